@@ -1,0 +1,103 @@
+"""Pins the CPU oracle against fixtures produced by the reference itself.
+
+tests/golden/make_golden.py ran the reference's core.py on the inputs of
+tests/golden/gen.py; here the oracle recomputes every output from the same
+seeds.  Integer outputs, fp32 centers, activations-derived scores and moments
+must agree bit for bit; the moments-router softmax and attention agree to a
+stated tolerance (the reference's exp and matmul orders are not restated).
+"""
+import hashlib
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from gen import unit_case
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+CASES = sorted(p.stem for p in GOLDEN.glob("u*.npz")) + ["cfg1"]
+
+
+def digest(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def load(name):
+    z = np.load(GOLDEN / f"{name}.npz")
+    return z, json.loads(str(z["meta"]))
+
+
+@pytest.fixture(scope="module", params=CASES)
+def case(request, oracle):
+    z, m = load(request.param)
+    c = unit_case(m["seed"], m["n"], m["d"], m["clusters"], m["F"], m["G"],
+                  tail=m["tail"] + m["append_n"], bf16=m["bf16"], key_mean=m["key_mean"])
+    sae = oracle.SAE(c["W"], c["b"], key_mean=m["key_mean"], query_topk=m["k"])
+    idx = oracle.build_index(c["keys"][:m["n"]], sae, 1.0)
+    return z, m, c, sae, idx
+
+
+def test_build_index_bit_exact(case):
+    z, m, c, sae, idx = case
+    assert np.array_equal(idx.center.view(np.uint32), z["center"].view(np.uint32))
+    assert np.array_equal(idx.counts, z["counts"])
+    assert idx.memberships == int(z["n_members"])
+    assert digest(idx.ids.astype(np.int64)) == str(z["ids_sha"])
+    assert digest(idx.mean) == str(z["mean_sha"])
+    assert digest(idx.variance) == str(z["var_sha"])
+
+
+def test_q_activation_route_bit_exact(case, oracle):
+    z, m, c, sae, idx = case
+    score, order = oracle.bucket_scores(c["q"], idx, router="q_activation", sae=sae, query_scale=1.0,
+                                        query_topk=m["k"])
+    assert np.array_equal(order, z["qact_order"])
+    nz = np.flatnonzero(score)
+    assert np.array_equal(nz, z["qact_score_nz_ids"])
+    assert np.array_equal(score[nz].view(np.uint32), z["qact_score_nz"].view(np.uint32))
+    assert digest(score) == str(z["qact_score_sha"])
+
+
+def test_moments_route(case, oracle):
+    z, m, c, sae, idx = case
+    score, order = oracle.bucket_scores(c["q"], idx, router="moments", query_topk=m["k"])
+    np.testing.assert_allclose(score, z["mom_score"], rtol=1e-5, atol=1e-7)
+    # Ordering given the reference's own scores is exact (level-1 parity).
+    lvl1 = oracle.order_live(z["mom_score"], idx.counts, m["k"])
+    assert np.array_equal(lvl1, z["mom_order"])
+
+
+def test_select_and_attend(case, oracle):
+    z, m, c, sae, idx = case
+    total = m["n"] + m["tail"]
+    for j, cap in enumerate(m["caps"]):
+        cap = None if cap < 0 else cap
+        ids, meta = oracle.select_buckets(c["q"], idx, unique_cap=cap, router="q_activation", sae=sae,
+                                          query_scale=1.0, query_topk=m["k"])
+        assert np.array_equal(ids, z[f"sel{j}_ids"].astype(np.int64))
+        assert meta["features"] == z[f"sel{j}_features"].tolist()
+        assert meta["raw"] == int(z[f"sel{j}_raw"])
+        assert meta["limit"] == int(z[f"sel{j}_limit"])
+        out = oracle.attend(c["q"], c["keys"][:total], c["values"][:total], ids, m["n"])
+        ref = z[f"sel{j}_attend"]
+        np.testing.assert_allclose(out, ref, rtol=1e-4, atol=1e-5)
+
+
+def test_append_index_bit_exact(case, oracle):
+    z, m, c, sae, idx = case
+    new = c["keys"][m["n"]:m["n"] + m["append_n"]]
+    merged = oracle.append_index(idx, new, sae, 1.0)
+    assert np.array_equal(merged.counts, z["app_counts"])
+    assert digest(merged.ids.astype(np.int64)) == str(z["app_ids_sha"])
+    assert digest(merged.mean) == str(z["app_mean_sha"])
+    assert digest(merged.variance) == str(z["app_var_sha"])
+
+
+def test_edge_cases(oracle):
+    z = np.load(GOLDEN / "edge.npz")
+    sae = oracle.SAE(np.array([[1., 0, 0, 0], [1., 0, 0, 0], [0, 1., 0, 0]], np.float32), np.zeros(3, np.float32),
+                     key_mean=2, query_topk=2)
+    idx = oracle.build_index(np.ones((9, 4), np.float32), sae, 1.0, center=np.zeros(4, np.float32))
+    assert np.array_equal(idx.counts, z["tie_counts"])
+    assert np.array_equal(idx.ids, z["tie_ids"])
