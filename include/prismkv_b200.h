@@ -1,0 +1,202 @@
+/*
+ * prismkv_b200.h -- C ABI of the B200 (sm_100a) PrismKV retrieval library.
+ *
+ * Conventions (the same as the reference's native bindings,
+ * src/prismkv/native8b.py:46-80 and kernels/cuda_sm90/native.py:16-35):
+ *   - every device buffer is passed as a uint64_t address owned by the caller;
+ *   - every call is asynchronous on the caller's CUDA stream (last argument)
+ *     and performs no host synchronisation and no allocation;
+ *   - the return value is 0 on success, a negative PK_ERR_* for an argument
+ *     error detected on the host, or a positive cudaError_t from the launch;
+ *   - conditions only the device can detect (a full bucket region, a full
+ *     boundary buffer, a history too long for the union's on-chip bitmap) are
+ *     OR-ed into a caller-provided int32 status word (PK_STATUS_*), which the
+ *     caller reads after synchronising.  Nothing is silently truncated.
+ *
+ * Index layout (one "unit" = one (batch row, KV head) of one layer):
+ *   offsets[U, F+1] int32  start of each bucket's region in ids; region f has
+ *                          capacity offsets[f+1] - offsets[f]
+ *   lens[U, F]      int32  bucket sizes (the reference's FeatureIndex.counts)
+ *   ids[U, ids_stride] int32 token ids, ascending within each bucket
+ *   center[U, d], mean/var[U, F, d] fp32 (moments are optional)
+ * This is the CSR interchange of native8b.py:66-69 with per-bucket slack so
+ * that append_index can extend buckets in place.
+ *
+ * Workspace buffers must be zero-filled before their first use; the kernels
+ * leave their counters zeroed again when they finish.
+ */
+#ifndef PRISMKV_B200_H
+#define PRISMKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Host-side return codes. */
+#define PK_OK 0
+#define PK_ERR_ARG (-1)          /* an argument is out of range               */
+#define PK_ERR_UNSUPPORTED (-2)  /* shape/dtype not compiled into this build  */
+#define PK_ERR_WORKSPACE (-3)    /* workspace smaller than *_workspace_bytes  */
+
+/* Device status bits (OR-ed into the caller's int32 status word). */
+#define PK_STATUS_BUCKET_FULL 1       /* append: a bucket region is full        */
+#define PK_STATUS_BOUNDARY_FULL 2     /* build: boundary buffer too small       */
+#define PK_STATUS_MEMBERS_FULL 4      /* build: member buffer too small         */
+#define PK_STATUS_BUCKET_TOO_BIG 8    /* build: a bucket exceeds the sort limit */
+#define PK_STATUS_OUT_FULL 16         /* union: output row too short            */
+#define PK_STATUS_HISTORY_TOO_LONG 32 /* union: history above max_history       */
+
+/* Element types. */
+#define PK_F32 0
+#define PK_BF16 1
+
+/* Router terms for pk_route_moments (core.py:117-126). */
+#define PK_TERM_COUNT 1
+#define PK_TERM_MEAN 2
+#define PK_TERM_VARIANCE 4
+
+/* Library build facts: target sm version * 100 + ABI revision; head dims. */
+int pk_version(void);
+int pk_supported_head_dim(int d);
+
+/* ------------------------------------------------------------------------
+ * q_activation routing (a1 + a2).
+ * Replaces the score stage of the native operators -- pack + torch.bmm +
+ * fused_norm_top (src/prismkv/native8b.py:82-87, kernels/ppu_8b/pack.cu:3-4,
+ * kernels/ppu_8b/route_parallel.cu:13-35; kernels/cuda_sm90/native.py:158-167)
+ * -- for the reference's q_activation router, src/prismkv/core.py:131-139.
+ *
+ * q[U, G, d] (PK_F32 or PK_BF16).  The heads of the listed units (units[n],
+ * int32, or 0 for all U) are encoded with one SAE: w_enc[F, d], b_enc[F] fp32.
+ * counts[U, F] int32 marks live buckets.  Outputs per listed unit u:
+ *   order[u, 0..n_order[u])  candidate buckets, descending score, ties by id
+ *   score[u, F]   (optional, 0 to skip) the reference's full score vector
+ *   topk[u, G, k] (optional) each head's picks in rank order
+ * ------------------------------------------------------------------------ */
+size_t pk_route_qact_workspace_bytes(int U, int G, int F, int k);
+int pk_route_qact(uint64_t q, int q_dtype, uint64_t units, int n_units,
+                  uint64_t w_enc, uint64_t b_enc, float query_scale, uint64_t counts,
+                  int U, int G, int d, int F, int k,
+                  uint64_t workspace, uint64_t workspace_bytes,
+                  uint64_t order, uint64_t n_order, int order_stride,
+                  uint64_t score, uint64_t topk, uint64_t stream);
+
+/* ------------------------------------------------------------------------
+ * moments routing (a9).
+ * Replaces pack + torch.bmm + fused_norm_top / HopperTop16
+ * (native8b.py:82-87; cuda_sm90/native.py:158-167; hopper_top16.cu:64-184)
+ * for src/prismkv/core.py:117-130.  mean/var[U, F, d] fp32, counts[U, F].
+ * score[U, F] fp32 is written (required).  order[u, 0..n_order[u]) holds
+ * the first k live buckets by descending score, ties by id.
+ * ------------------------------------------------------------------------ */
+size_t pk_route_moments_workspace_bytes(int U, int G, int F);
+int pk_route_moments(uint64_t q, int q_dtype, uint64_t mean, uint64_t var, uint64_t counts, int terms,
+                     int U, int G, int d, int F, int k,
+                     uint64_t workspace, uint64_t workspace_bytes,
+                     uint64_t score, uint64_t order, uint64_t n_order, int order_stride, uint64_t stream);
+
+/* ------------------------------------------------------------------------
+ * Budgeted bucket union (a3; a10 when limit >= history).
+ * Replaces launch_union_warp (kernels/ppu_8b/union.cu:39-49,
+ * kernels/cuda_sm90/native_sources/union.cu:52-62), extended from the
+ * unbudgeted OR of bitmaps to the greedy skip-overflow rule of
+ * src/prismkv/core.py:152-164.  For each unit u, buckets order[u, 0..n_order[u])
+ * are taken in turn; a bucket whose new (not yet chosen) tokens would push
+ * the chosen count past limit[u] (int64) is skipped.  Outputs:
+ * out_ids[u, 0..count[u]) ascending unique token ids, features[u, ..n_features[u])
+ * accepted buckets in acceptance order, raw[u] (int64) summed sizes of the
+ * accepted buckets.  history[u] (int32) bounds the token ids; the on-chip
+ * bitmap is sized for max_history.
+ * ------------------------------------------------------------------------ */
+int pk_union(uint64_t offsets, uint64_t lens, uint64_t ids, int64_t ids_stride,
+             uint64_t order, uint64_t n_order, int order_stride,
+             uint64_t history, uint64_t limit, int U, int F, int max_history,
+             uint64_t out_ids, int64_t out_stride, uint64_t out_count,
+             uint64_t features, uint64_t n_features, uint64_t raw,
+             uint64_t status, uint64_t stream);
+
+/* ------------------------------------------------------------------------
+ * Sparse attention over selected rows plus the dense tail (a4 + a11).
+ * Replaces attention_tuned (kernels/ppu_8b/av_tuned.cu:62-67), batch_av
+ * (kernels/cuda_sm90/native_sources/av.cu:92-103) and HopperAV
+ * (kernels/cuda_sm90/hopper_av.py:6-103); semantics of core.py:170-183.
+ * Unit u = (b, h) with h = u % kv_heads reads K/V rows at
+ *   base(u) = (u / kv_heads) * kv_batch_stride + (u % kv_heads) * kv_head_stride
+ *   row(p)  = base(u) + p * kv_row_stride       (elements)
+ * which covers both [U, total, d] and slot-major [slot, cap, H_kv, d].
+ * Rows attended: ids[u, 0..count[u]) then history[u]..length[u]-1.
+ * length[u] == 0 marks an inactive unit (output zeros).  q, k, v and out
+ * share `dtype`.  splits <= 0 picks a split count for the machine.
+ * With partial != 0 the kernel writes per-(u, head) partials
+ * (m, l, o[d]) fp32 to partial[U*G, d+2] instead of out (for pk_lse_merge).
+ * ------------------------------------------------------------------------ */
+size_t pk_sparse_av_workspace_bytes(int U, int G, int d, int splits);
+int pk_sparse_av(uint64_t q, uint64_t k, uint64_t v, int dtype,
+                 int kv_heads, int64_t kv_batch_stride, int64_t kv_head_stride, int64_t kv_row_stride,
+                 uint64_t ids, int64_t ids_stride, uint64_t count, uint64_t history, uint64_t length,
+                 int U, int G, int d, int splits,
+                 uint64_t workspace, uint64_t workspace_bytes,
+                 uint64_t out, uint64_t partial, uint64_t stream);
+
+/* Log-sum-exp merge of P partial states partial[P, UG, d+2] (m, l, o[d]) into
+ * out[UG, d] (dtype).  The cross-GPU step of the sequence-sharded decode;
+ * generalises the in-GPU split merge of av_tuned.cu:54-61. */
+int pk_lse_merge(uint64_t partial, int P, int UG, int d, uint64_t out, int dtype, uint64_t stream);
+
+/* ------------------------------------------------------------------------
+ * Index build (a5 + a6) and append (a7).
+ * Replaces IndexBuilder.group + Kernels.positive_top + moments + build_bits
+ * (kernels/cuda_sm90/native.py:37-82,99-115; native_sources/hist.cu:3-22,
+ * moments.cu:5-24; kernels/ppu_8b/pack.cu:5-6) with the exact semantics of
+ * src/prismkv/core.py:92-103 (global positive BatchTopK with the flat-index
+ * tie order of core.py:13-26) and core.py:186-201.
+ * Keys of unit u, row t: keys + u*unit_stride + t*row_stride (elements).
+ * ------------------------------------------------------------------------ */
+
+/* center[u, d] = mean of the unit's N key rows (core.py:98). */
+int pk_key_center(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride,
+                  int U, int64_t N, int d, uint64_t center, uint64_t stream);
+
+/* Builds buckets for U units sharing one SAE (w_enc[F, d], b_enc[F]).
+ * Token ids are written as token_base + t.  Bucket regions get
+ * ceil(len*slack_frac) + slack_min spare slots for later appends;
+ * ids_stride must be >= pk_build_ids_capacity(...).  */
+int64_t pk_build_ids_capacity(int64_t N, int F, int key_mean, float slack_frac, int slack_min);
+size_t pk_build_workspace_bytes(int U, int64_t N, int F, int key_mean, int64_t boundary_capacity);
+int pk_build_index(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride,
+                   uint64_t center, float key_scale, uint64_t w_enc, uint64_t b_enc,
+                   int U, int64_t N, int d, int F, int key_mean, int64_t token_base,
+                   float slack_frac, int slack_min,
+                   uint64_t offsets, uint64_t lens, uint64_t ids, int64_t ids_stride,
+                   int64_t boundary_capacity, uint64_t workspace, uint64_t workspace_bytes,
+                   uint64_t status, uint64_t stream);
+
+/* Population mean / variance of the ORIGINAL keys per bucket (core.py:76-89). */
+int pk_summarize(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride,
+                 uint64_t offsets, uint64_t lens, uint64_t ids, int64_t ids_stride,
+                 int U, int d, int F, uint64_t mean, uint64_t var, uint64_t stream);
+
+/* Appends a block of n_new keys per unit (rows at new_keys + u*unit_stride +
+ * t*row_stride) to an index built with history `history`: BatchTopK over the
+ * block only with the stored centers, bucket lists extended in place (token
+ * ids history + t), lens updated, and -- when mean/var are non-zero --
+ * moments merged with the parallel formula of core.py:194-199.  All or
+ * nothing: if any bucket region would overflow, the index is left unchanged
+ * and PK_STATUS_BUCKET_FULL is raised. */
+size_t pk_append_workspace_bytes(int U, int64_t n_new, int d, int F, int key_mean, int64_t boundary_capacity);
+int pk_append_index(uint64_t new_keys, int dtype, int64_t unit_stride, int64_t row_stride, int64_t n_new,
+                    uint64_t center, float key_scale, uint64_t w_enc, uint64_t b_enc,
+                    int U, int d, int F, int key_mean, int64_t history,
+                    uint64_t offsets, uint64_t lens, uint64_t ids, int64_t ids_stride,
+                    uint64_t mean, uint64_t var,
+                    int64_t boundary_capacity, uint64_t workspace, uint64_t workspace_bytes,
+                    uint64_t status, uint64_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PRISMKV_B200_H */

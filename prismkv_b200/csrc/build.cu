@@ -1,0 +1,687 @@
+// Key-side index build and append: src/prismkv/core.py:92-103 (build_index),
+// :13-26 (positive_global_topk), :76-89 (summarize), :186-201 (append_index).
+//
+// The encode a[t, f] = relu(((k_t - c) / s) . W_f + b_f) is recomputed in two
+// passes and never stored: pass 1 builds a 2048-bin histogram of the positive
+// activations' float bits (>> 20) per unit, which fixes the coarse bin that
+// holds the budget's threshold; pass 2 emits every activation above that bin
+// as a member and every activation inside it to a boundary buffer as a
+// 64-bit key (value descending, flat index ascending).  An exact radix
+// select over the boundary keys then takes the remaining members, which is
+// the reference's rule: all activations above the count-th largest value,
+// then ties at that value by ascending flat index, positives only.  The dot
+// products run as one sequential FMA chain over d, the order the reference's
+// F.linear takes for a many-row block, so memberships are bit-identical.
+#include "common.cuh"
+
+namespace pk {
+
+constexpr int kBD = 128;             // head dim compiled for the build
+constexpr int kBT = 128;             // tokens per CTA tile
+constexpr int kBF = 128;             // features per CTA tile
+constexpr int kBThreads = 256;       // 16 x 16 threads, 8 x 8 outputs each
+constexpr int kBPitch = kBT + 4;     // smem pitch (floats) of the k-major tiles
+constexpr int kHistBins = 2048;
+constexpr int kSortWarpCap = 1024;   // ids a warp sorts in shared memory
+constexpr int kSortBigCap = 32768;   // ids one CTA sorts (larger: error)
+
+struct BuildWs {
+    int* hist;          // [U, 2048]
+    int* cut;           // [U]
+    long long* need;    // [U]
+    int* n_members;     // [U]
+    int* n_boundary;    // [U]
+    int* fill;          // [U, F]
+    int* flag;          // [4]
+    long long* members; // [U, mcap]
+    long long* boundary;// [U, bcap]
+    int64_t mcap, bcap;
+};
+
+template <typename T>
+__device__ __forceinline__ float key_at(const T* keys, int64_t unit_stride, int64_t row_stride, int u, int64_t t,
+                                        int c) {
+    return load_f(keys, (int64_t)u * unit_stride + t * row_stride + c);
+}
+
+// center[u, c] = torch-order column mean of the unit's N rows.
+template <typename T>
+__global__ void center_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride, int64_t N, int d,
+                              float* __restrict__ center) {
+    const int u = blockIdx.x;
+    for (int c = threadIdx.x; c < d; c += blockDim.x) {
+        const float s =
+            torch_cascade_sum(N, [&](int64_t i) { return key_at(keys, unit_stride, row_stride, u, i, c); });
+        center[(int64_t)u * d + c] = __fdiv_rn(s, (float)N);
+    }
+}
+
+// One tile of 128 tokens x 128 features.  PASS 1: histogram; PASS 2: emit.
+template <int PASS, typename T>
+__global__ void __launch_bounds__(kBThreads)
+build_encode_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride, int64_t N,
+                    const float* __restrict__ center, float key_scale, const float* __restrict__ W,
+                    const float* __restrict__ bias, int F, BuildWs ws, int* __restrict__ lens,
+                    int* __restrict__ status) {
+    extern __shared__ __align__(16) float sm[];
+    float* Xs = sm;                       // [kBD][kBPitch]  x^T
+    float* Ws = sm + kBD * kBPitch;       // [kBD][kBPitch]  W^T
+    int* hist = reinterpret_cast<int*>(Ws + kBD * kBPitch);  // [2048] (pass 1)
+    const int tid = threadIdx.x;
+    const int f0 = blockIdx.x * kBF;
+    const int64_t t0 = (int64_t)blockIdx.y * kBT;
+    const int u = blockIdx.z;
+    const float* cu = center + (int64_t)u * kBD;
+
+    if (PASS == 1)
+        for (int i = tid; i < kHistBins; i += kBThreads) hist[i] = 0;
+    // x = (k - center) / key_scale (core.py:99), transposed into Xs.
+    for (int e = tid; e < kBT * kBD; e += kBThreads) {
+        const int tt = e / kBD, c = e % kBD;
+        const int64_t t = t0 + tt;
+        float x = 0.f;
+        if (t < N) x = __fdiv_rn(__fsub_rn(key_at(keys, unit_stride, row_stride, u, t, c), cu[c]), key_scale);
+        Xs[c * kBPitch + tt] = x;
+    }
+    for (int e = tid; e < kBF * kBD / 4; e += kBThreads) {
+        const int ff = e / (kBD / 4), c4 = e % (kBD / 4);
+        const int f = f0 + ff;
+        float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (f < F) w = reinterpret_cast<const float4*>(W + (int64_t)f * kBD)[c4];
+        Ws[(4 * c4 + 0) * kBPitch + ff] = w.x;
+        Ws[(4 * c4 + 1) * kBPitch + ff] = w.y;
+        Ws[(4 * c4 + 2) * kBPitch + ff] = w.z;
+        Ws[(4 * c4 + 3) * kBPitch + ff] = w.w;
+    }
+    __syncthreads();
+
+    const int tx = tid & 15, ty = tid >> 4;
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+#pragma unroll 2
+    for (int k = 0; k < kBD; ++k) {
+        const float4 xa = *reinterpret_cast<const float4*>(Xs + k * kBPitch + ty * 8);
+        const float4 xb = *reinterpret_cast<const float4*>(Xs + k * kBPitch + ty * 8 + 4);
+        const float4 wa = *reinterpret_cast<const float4*>(Ws + k * kBPitch + tx * 8);
+        const float4 wb = *reinterpret_cast<const float4*>(Ws + k * kBPitch + tx * 8 + 4);
+        const float xr[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+        const float wr[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(xr[i], wr[j], acc[i][j]);
+    }
+
+    const int cut = PASS == 2 ? ws.cut[u] : 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int64_t t = t0 + ty * 8 + i;
+        if (t >= N) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int f = f0 + tx * 8 + j;
+            if (f >= F) continue;
+            const float v = __fadd_rn(acc[i][j], bias[f]);
+            if (!(v > 0.f)) continue;
+            const uint32_t bits = __float_as_uint(v);
+            const int bin = (int)(bits >> 20);
+            if (PASS == 1) {
+                atomicAdd(&hist[bin], 1);
+            } else {
+                const long long flat = (long long)t * F + f;
+                if (bin > cut) {
+                    const int at = atomicAdd(&ws.n_members[u], 1);
+                    if (at < ws.mcap) {
+                        ws.members[(int64_t)u * ws.mcap + at] = flat;
+                        atomicAdd(&lens[(int64_t)u * F + f], 1);
+                    } else {
+                        atomicOr(status, PK_STATUS_MEMBERS_FULL);
+                    }
+                } else if (bin == cut) {
+                    const int at = atomicAdd(&ws.n_boundary[u], 1);
+                    if (at < ws.bcap) {
+                        const unsigned long long key =
+                            ((unsigned long long)(0xFFFFFu - (bits & 0xFFFFFu)) << 40) | (unsigned long long)flat;
+                        ws.boundary[(int64_t)u * ws.bcap + at] = (long long)key;
+                    } else {
+                        atomicOr(status, PK_STATUS_BOUNDARY_FULL);
+                    }
+                }
+            }
+        }
+    }
+    if (PASS == 1) {
+        __syncthreads();
+        for (int i = tid; i < kHistBins; i += kBThreads)
+            if (hist[i]) atomicAdd(&ws.hist[(int64_t)u * kHistBins + i], hist[i]);
+    }
+}
+
+// Coarse cut per unit: the bin holding the count-th largest positive value.
+__global__ void build_cut_kernel(BuildWs ws, long long count) {
+    const int u = blockIdx.x;
+    if (threadIdx.x != 0) return;
+    const int* h = ws.hist + (int64_t)u * kHistBins;
+    long long above = 0;
+    int b = kHistBins - 1;
+    for (; b >= 0; --b) {
+        if (above + h[b] >= count) break;
+        above += h[b];
+    }
+    if (b < 0) {
+        ws.cut[u] = -1;  // at most `count` positives: every one is a member
+        ws.need[u] = 0;
+    } else if (above + h[b] == count && b >= 0) {
+        ws.cut[u] = b;   // the bin fills the budget exactly: all of it
+        ws.need[u] = h[b];
+    } else {
+        ws.cut[u] = b;
+        ws.need[u] = count - above;
+    }
+}
+
+// Exact resolution of the boundary bin: the `need` smallest 64-bit keys.
+__global__ void __launch_bounds__(1024)
+build_resolve_kernel(BuildWs ws, int F, int* __restrict__ lens, int* __restrict__ status) {
+    const int u = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+    __shared__ int hist[256];
+    __shared__ unsigned long long s_prefix;
+    __shared__ long long s_need;
+    const long long need0 = ws.need[u];
+    const int nb = ws.n_boundary[u];
+    if (ws.cut[u] < 0 || need0 <= 0) return;
+    if (nb > ws.bcap) return;  // flagged by the encode pass
+    const long long* B = ws.boundary + (int64_t)u * ws.bcap;
+    unsigned long long prefix = ~0ull;  // take everything when need >= nb
+    if (need0 < nb) {
+        unsigned long long pre = 0, pmask = 0;
+        long long need = need0;
+        for (int pass = 0; pass < 8; ++pass) {
+            const int shift = 56 - 8 * pass;
+            for (int i = tid; i < 256; i += nt) hist[i] = 0;
+            __syncthreads();
+            for (int i = tid; i < nb; i += nt) {
+                const unsigned long long kk = (unsigned long long)B[i];
+                if ((kk & pmask) == pre) atomicAdd(&hist[(kk >> shift) & 255ull], 1);
+            }
+            __syncthreads();
+            if (tid == 0) {
+                long long acc = 0;
+                int dgt = 0;
+                for (; dgt < 256; ++dgt) {
+                    if (acc + hist[dgt] >= need) break;
+                    acc += hist[dgt];
+                }
+                s_prefix = pre | ((unsigned long long)dgt << shift);
+                s_need = need - acc;
+            }
+            __syncthreads();
+            pre = s_prefix;
+            pmask |= 0xFFull << shift;
+            need = s_need;
+            __syncthreads();
+        }
+        prefix = pre;
+    }
+    // Keys are unique (flat indices differ): take every key <= prefix.
+    for (int i = tid; i < nb; i += nt) {
+        const unsigned long long kk = (unsigned long long)B[i];
+        if (kk <= prefix) {
+            const long long flat = (long long)(kk & ((1ull << 40) - 1));
+            const int at = atomicAdd(&ws.n_members[u], 1);
+            if (at < ws.mcap) {
+                ws.members[(int64_t)u * ws.mcap + at] = flat;
+                atomicAdd(&lens[(int64_t)u * F + (int)(flat % F)], 1);
+            } else {
+                atomicOr(status, PK_STATUS_MEMBERS_FULL);
+            }
+        }
+    }
+}
+
+__host__ __device__ __forceinline__ int bucket_slack(int len, float frac, int smin) {
+    return (int)ceilf((float)len * frac) + smin;
+}
+
+// offsets[u, f] = exclusive scan of (len + slack) over f; offsets[u, F] = total.
+__global__ void __launch_bounds__(1024)
+build_offsets_kernel(const int* __restrict__ lens, int F, float frac, int smin, int* __restrict__ offsets,
+                     int64_t ids_stride, int* __restrict__ status) {
+    const int u = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+    __shared__ int scan[40];
+    const int per = (F + nt - 1) / nt;
+    const int b0 = min(F, tid * per), b1 = min(F, b0 + per);
+    long long mine = 0;
+    for (int f = b0; f < b1; ++f) {
+        const int l = lens[(int64_t)u * F + f];
+        mine += l + bucket_slack(l, frac, smin);
+    }
+    int total;
+    int at = block_exclusive_scan((int)min(mine, (long long)(INT32_MAX / 2)), scan, &total);
+    int* off = offsets + (int64_t)u * (F + 1);
+    for (int f = b0; f < b1; ++f) {
+        off[f] = at;
+        const int l = lens[(int64_t)u * F + f];
+        at += l + bucket_slack(l, frac, smin);
+    }
+    if (tid == 0) {
+        off[F] = total;
+        if ((int64_t)total > ids_stride) atomicOr(status, PK_STATUS_MEMBERS_FULL);
+    }
+}
+
+// Scatter members into their bucket regions at slot fill[u, f]++.
+__global__ void build_scatter_kernel(BuildWs ws, int F, const int* __restrict__ offsets, int* __restrict__ ids,
+                                     int64_t ids_stride, long long token_base) {
+    const int u = blockIdx.y;
+    const int n = (int)min((int64_t)ws.n_members[u], ws.mcap);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const long long flat = ws.members[(int64_t)u * ws.mcap + i];
+        const int f = (int)(flat % F);
+        const long long t = flat / F;
+        const int slot = atomicAdd(&ws.fill[(int64_t)u * F + f], 1);
+        ids[(int64_t)u * ids_stride + offsets[(int64_t)u * (F + 1) + f] + slot] = (int)(token_base + t);
+    }
+}
+
+__device__ __forceinline__ int next_pow2(int x) {
+    int p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+
+__device__ void bitonic_sort_shared(int* a, int n, int lane, int nthreads, bool warp_only) {
+    for (int size = 2; size <= n; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = lane; i < n / 2; i += nthreads) {
+                const int lo = 2 * i - (i & (stride - 1));
+                const int hi = lo + stride;
+                const bool up = (lo & size) == 0;
+                const int x = a[lo], y = a[hi];
+                if ((x > y) == up) { a[lo] = y; a[hi] = x; }
+            }
+            if (warp_only) __syncwarp(); else __syncthreads();
+        }
+    }
+}
+
+// Sort ids[off[f] + start[f] .. + cnt[f]) ascending, one warp per bucket for
+// buckets up to kSortWarpCap ids; larger ones go to the CTA sorter.
+__global__ void __launch_bounds__(256)
+sort_buckets_warp_kernel(int* __restrict__ ids, int64_t ids_stride, const int* __restrict__ offsets,
+                         const int* __restrict__ start, const int* __restrict__ cnt, int F) {
+    __shared__ int buf[8][kSortWarpCap];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int u = blockIdx.y;
+    const int f = blockIdx.x * 8 + warp;
+    if (f >= F) return;
+    const int L = cnt[(int64_t)u * F + f];
+    if (L <= 1 || L > kSortWarpCap) return;
+    int* a = buf[warp];
+    int* src = ids + (int64_t)u * ids_stride + offsets[(int64_t)u * (F + 1) + f] +
+               (start ? start[(int64_t)u * F + f] : 0);
+    const int n = next_pow2(L);
+    for (int i = lane; i < n; i += 32) a[i] = i < L ? src[i] : INT32_MAX;
+    __syncwarp();
+    bitonic_sort_shared(a, n, lane, 32, true);
+    for (int i = lane; i < L; i += 32) src[i] = a[i];
+}
+
+__global__ void __launch_bounds__(1024)
+sort_buckets_big_kernel(int* __restrict__ ids, int64_t ids_stride, const int* __restrict__ offsets,
+                        const int* __restrict__ start, const int* __restrict__ cnt, int F, int* __restrict__ status) {
+    extern __shared__ int big[];
+    const int u = blockIdx.y, f = blockIdx.x;
+    const int L = cnt[(int64_t)u * F + f];
+    if (L <= kSortWarpCap) return;
+    if (L > kSortBigCap) {
+        if (threadIdx.x == 0) atomicOr(status, PK_STATUS_BUCKET_TOO_BIG);
+        return;
+    }
+    int* src = ids + (int64_t)u * ids_stride + offsets[(int64_t)u * (F + 1) + f] +
+               (start ? start[(int64_t)u * F + f] : 0);
+    const int n = next_pow2(L);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) big[i] = i < L ? src[i] : INT32_MAX;
+    __syncthreads();
+    bitonic_sort_shared(big, n, threadIdx.x, blockDim.x, false);
+    for (int i = threadIdx.x; i < L; i += blockDim.x) src[i] = big[i];
+}
+
+// Moments of the ORIGINAL keys per bucket (core.py:84-88) in torch's order:
+// column cascade over the bucket's rows in list order, then / n.  One warp
+// per bucket; lane owns dims 4*lane .. 4*lane+3.
+template <typename T>
+__global__ void __launch_bounds__(256)
+summarize_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride,
+                 const int* __restrict__ offsets, const int* __restrict__ start, const int* __restrict__ cnt,
+                 const int* __restrict__ ids, int64_t ids_stride, long long token_base, int F,
+                 float* __restrict__ mean, float* __restrict__ var) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int u = blockIdx.y;
+    const int f = blockIdx.x * 8 + warp;
+    if (f >= F) return;
+    const int L = cnt[(int64_t)u * F + f];
+    const int* lst = ids + (int64_t)u * ids_stride + offsets[(int64_t)u * (F + 1) + f] +
+                     (start ? start[(int64_t)u * F + f] : 0);
+    float* mu = mean + ((int64_t)u * F + f) * kBD;
+    float* nu = var + ((int64_t)u * F + f) * kBD;
+    if (L == 0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) { mu[4 * lane + j] = 0.f; nu[4 * lane + j] = 0.f; }
+        return;
+    }
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j) {
+        const int c = 4 * lane + j;
+        const float s = torch_cascade_sum((int64_t)L, [&](int64_t i) {
+            return key_at(keys, unit_stride, row_stride, u, (int64_t)lst[i] - token_base, c);
+        });
+        const float mj = __fdiv_rn(s, (float)L);
+        const float s2 = torch_cascade_sum((int64_t)L, [&](int64_t i) {
+            const float x = __fsub_rn(key_at(keys, unit_stride, row_stride, u, (int64_t)lst[i] - token_base, c), mj);
+            return __fmul_rn(x, x);
+        });
+        mu[c] = mj;
+        nu[c] = __fdiv_rn(s2, (float)L);
+    }
+}
+
+// Parallel-formula merge of old and new bucket moments (core.py:194-199),
+// in the reference's operation order.  Skipped when the append was refused.
+__global__ void merge_moments_kernel(const int* __restrict__ lens_old, const int* __restrict__ cnt_new, int F,
+                                     float* __restrict__ mean, float* __restrict__ var,
+                                     const float* __restrict__ mean_new, const float* __restrict__ var_new,
+                                     const int* __restrict__ flag) {
+    if (*flag) return;
+    const int u = blockIdx.y;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)F * kBD) return;
+    const int f = (int)(i / kBD);
+    const float a = (float)lens_old[(int64_t)u * F + f], b = (float)cnt_new[(int64_t)u * F + f];
+    const float tot = __fadd_rn(a, b);
+    const float den = tot > 1.f ? tot : 1.f;
+    const int64_t j = (int64_t)u * F * kBD + i;
+    const float ma = mean[j], mb = mean_new[j], va = var[j], vb = var_new[j];
+    const float mu = __fdiv_rn(__fadd_rn(__fmul_rn(a, ma), __fmul_rn(b, mb)), den);
+    float nv = __fdiv_rn(__fadd_rn(__fmul_rn(a, va), __fmul_rn(b, vb)), den);
+    const float w = __fdiv_rn(__fmul_rn(a, b), __fmul_rn(den, den));
+    const float dm = __fsub_rn(ma, mb);
+    nv = __fadd_rn(nv, __fmul_rn(w, __fmul_rn(dm, dm)));
+    mean[j] = mu;
+    var[j] = nv;
+}
+
+// Append check: every bucket must fit its region; all-or-nothing.
+__global__ void append_check_kernel(const int* __restrict__ offsets, const int* __restrict__ lens,
+                                    const int* __restrict__ cnt_new, int F, int* __restrict__ flag) {
+    const int u = blockIdx.y;
+    for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < F; f += gridDim.x * blockDim.x) {
+        const int cap = offsets[(int64_t)u * (F + 1) + f + 1] - offsets[(int64_t)u * (F + 1) + f];
+        if (lens[(int64_t)u * F + f] + cnt_new[(int64_t)u * F + f] > cap) atomicOr(flag, 1);
+    }
+}
+
+// A refused append zeroes the new counts so nothing downstream (sort,
+// moments, commit) touches the index.
+__global__ void append_gate_kernel(const int* __restrict__ flag, int* __restrict__ cnt_new, int64_t n) {
+    if (!*flag) return;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        cnt_new[i] = 0;
+}
+
+__global__ void append_scatter_kernel(BuildWs ws, int F, const int* __restrict__ offsets, const int* __restrict__ lens,
+                                      int* __restrict__ ids, int64_t ids_stride, long long token_base) {
+    if (*ws.flag) return;
+    const int u = blockIdx.y;
+    const int n = (int)min((int64_t)ws.n_members[u], ws.mcap);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const long long flat = ws.members[(int64_t)u * ws.mcap + i];
+        const int f = (int)(flat % F);
+        const long long t = flat / F;
+        const int slot = atomicAdd(&ws.fill[(int64_t)u * F + f], 1);
+        ids[(int64_t)u * ids_stride + offsets[(int64_t)u * (F + 1) + f] + lens[(int64_t)u * F + f] + slot] =
+            (int)(token_base + t);
+    }
+}
+
+__global__ void append_commit_kernel(const int* __restrict__ flag, int* __restrict__ lens,
+                                     const int* __restrict__ cnt_new, int F, int* __restrict__ status) {
+    const int u = blockIdx.y;
+    const bool full = *flag != 0;
+    for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < F; f += gridDim.x * blockDim.x)
+        if (!full) lens[(int64_t)u * F + f] += cnt_new[(int64_t)u * F + f];
+    if (full && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicOr(status, PK_STATUS_BUCKET_FULL);
+}
+
+// ---------------------------------------------------------------------------
+// Host-side helpers
+// ---------------------------------------------------------------------------
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+size_t counters_bytes(int U, int F) {
+    return align256((size_t)U * kHistBins * 4) + align256((size_t)U * 4) + align256((size_t)U * 8) +
+           2 * align256((size_t)U * 4) + align256((size_t)U * F * 4) + align256(16);
+}
+
+size_t carve_bytes(int U, int F, int64_t mcap, int64_t bcap) {
+    return counters_bytes(U, F) + align256((size_t)U * mcap * 8) + align256((size_t)U * bcap * 8);
+}
+
+BuildWs carve(void* base, int U, int F, int64_t mcap, int64_t bcap) {
+    BuildWs w;
+    char* p = (char*)base;
+    w.hist = (int*)p; p += align256((size_t)U * kHistBins * 4);
+    w.cut = (int*)p; p += align256((size_t)U * 4);
+    w.need = (long long*)p; p += align256((size_t)U * 8);
+    w.n_members = (int*)p; p += align256((size_t)U * 4);
+    w.n_boundary = (int*)p; p += align256((size_t)U * 4);
+    w.fill = (int*)p; p += align256((size_t)U * F * 4);
+    w.flag = (int*)p; p += align256(16);
+    w.members = (long long*)p; p += align256((size_t)U * mcap * 8);
+    w.boundary = (long long*)p;
+    w.mcap = mcap;
+    w.bcap = bcap;
+    return w;
+}
+
+template <typename T>
+int run_encode_select(const T* keys, int64_t unit_stride, int64_t row_stride, int64_t N, const float* center,
+                      float key_scale, const float* W, const float* b, int U, int F, long long count, BuildWs ws,
+                      int* lens, int* status, cudaStream_t st) {
+    const size_t smem = (size_t)2 * kBD * kBPitch * sizeof(float) + kHistBins * sizeof(int);
+    dim3 grid((F + kBF - 1) / kBF, (unsigned)((N + kBT - 1) / kBT), U);
+    cudaFuncSetAttribute(build_encode_kernel<1, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(build_encode_kernel<2, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    build_encode_kernel<1, T><<<grid, kBThreads, smem, st>>>(keys, unit_stride, row_stride, N, center, key_scale, W,
+                                                             b, F, ws, lens, status);
+    PK_CHECK_LAUNCH();
+    build_cut_kernel<<<U, 32, 0, st>>>(ws, count);
+    PK_CHECK_LAUNCH();
+    build_encode_kernel<2, T><<<grid, kBThreads, smem, st>>>(keys, unit_stride, row_stride, N, center, key_scale, W,
+                                                             b, F, ws, lens, status);
+    PK_CHECK_LAUNCH();
+    build_resolve_kernel<<<U, 1024, 0, st>>>(ws, F, lens, status);
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}
+
+int sort_buckets(int* ids, int64_t ids_stride, const int* offsets, const int* start, const int* cnt, int U, int F,
+                 int* status, cudaStream_t st) {
+    sort_buckets_warp_kernel<<<dim3((F + 7) / 8, U), 256, 0, st>>>(ids, ids_stride, offsets, start, cnt, F);
+    PK_CHECK_LAUNCH();
+    const int smem = kSortBigCap * (int)sizeof(int);
+    cudaFuncSetAttribute(sort_buckets_big_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    sort_buckets_big_kernel<<<dim3(F, U), 1024, smem, st>>>(ids, ids_stride, offsets, start, cnt, F, status);
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}
+
+}  // namespace pk
+
+using namespace pk;
+
+extern "C" int pk_key_center(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride, int U, int64_t N,
+                             int d, uint64_t center, uint64_t stream) {
+    if (U < 1 || N < 1 || d < 1 || !keys || !center || row_stride < d) return PK_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int threads = d < 128 ? 32 * ((d + 31) / 32) : 128;
+    if (dtype == PK_BF16)
+        center_kernel<__nv_bfloat16><<<U, threads, 0, st>>>((const __nv_bfloat16*)keys, unit_stride, row_stride, N, d,
+                                                           (float*)center);
+    else if (dtype == PK_F32)
+        center_kernel<float><<<U, threads, 0, st>>>((const float*)keys, unit_stride, row_stride, N, d, (float*)center);
+    else
+        return PK_ERR_ARG;
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}
+
+extern "C" int64_t pk_build_ids_capacity(int64_t N, int F, int key_mean, float slack_frac, int slack_min) {
+    const int64_t members = N * (int64_t)key_mean;
+    return members + (int64_t)ceil((double)members * slack_frac) + (int64_t)F * (slack_min + 1) + 64;
+}
+
+extern "C" size_t pk_build_workspace_bytes(int U, int64_t N, int F, int key_mean, int64_t boundary_capacity) {
+    const int64_t mcap = N * (int64_t)key_mean;
+    return carve_bytes(U, F, mcap > 0 ? mcap : 1, boundary_capacity > 0 ? boundary_capacity : 1);
+}
+
+extern "C" int pk_build_index(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride, uint64_t center,
+                              float key_scale, uint64_t w_enc, uint64_t b_enc, int U, int64_t N, int d, int F,
+                              int key_mean, int64_t token_base, float slack_frac, int slack_min, uint64_t offsets,
+                              uint64_t lens, uint64_t ids, int64_t ids_stride, int64_t boundary_capacity,
+                              uint64_t workspace, uint64_t workspace_bytes, uint64_t status, uint64_t stream) {
+    if (U < 1 || N < 1 || F < 1 || key_mean < 1 || !(key_scale > 0.f) || slack_frac < 0.f || slack_min < 0)
+        return PK_ERR_ARG;
+    if (d != kBD) return PK_ERR_UNSUPPORTED;
+    if (!keys || !center || !w_enc || !b_enc || !offsets || !lens || !ids || !workspace || !status) return PK_ERR_ARG;
+    if ((long long)N * F >= (1ll << 40) || N > INT32_MAX || token_base + N > INT32_MAX || row_stride < d)
+        return PK_ERR_ARG;
+    if (boundary_capacity < 1) return PK_ERR_ARG;
+    if (ids_stride < pk_build_ids_capacity(N, F, key_mean, slack_frac, slack_min)) return PK_ERR_ARG;
+    if (workspace_bytes < pk_build_workspace_bytes(U, N, F, key_mean, boundary_capacity)) return PK_ERR_WORKSPACE;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int64_t mcap = N * (int64_t)key_mean;
+    BuildWs ws = carve((void*)workspace, U, F, mcap, boundary_capacity);
+    cudaMemsetAsync((void*)workspace, 0, counters_bytes(U, F), st);
+    cudaMemsetAsync((void*)lens, 0, (size_t)U * F * sizeof(int), st);
+    const long long count = (long long)N * key_mean;
+    int rc;
+    if (dtype == PK_BF16)
+        rc = run_encode_select((const __nv_bfloat16*)keys, unit_stride, row_stride, N, (const float*)center, key_scale,
+                               (const float*)w_enc, (const float*)b_enc, U, F, count, ws, (int*)lens, (int*)status, st);
+    else if (dtype == PK_F32)
+        rc = run_encode_select((const float*)keys, unit_stride, row_stride, N, (const float*)center, key_scale,
+                               (const float*)w_enc, (const float*)b_enc, U, F, count, ws, (int*)lens, (int*)status, st);
+    else
+        return PK_ERR_ARG;
+    if (rc) return rc;
+    build_offsets_kernel<<<U, 1024, 0, st>>>((const int*)lens, F, slack_frac, slack_min, (int*)offsets, ids_stride,
+                                             (int*)status);
+    PK_CHECK_LAUNCH();
+    build_scatter_kernel<<<dim3(64, U), 256, 0, st>>>(ws, F, (const int*)offsets, (int*)ids, ids_stride,
+                                                       (long long)token_base);
+    PK_CHECK_LAUNCH();
+    return sort_buckets((int*)ids, ids_stride, (const int*)offsets, nullptr, (const int*)lens, U, F, (int*)status, st);
+}
+
+extern "C" int pk_summarize(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride, uint64_t offsets,
+                            uint64_t lens, uint64_t ids, int64_t ids_stride, int U, int d, int F, uint64_t mean,
+                            uint64_t var, uint64_t stream) {
+    if (U < 1 || F < 1 || !keys || !offsets || !lens || !ids || !mean || !var) return PK_ERR_ARG;
+    if (d != kBD) return PK_ERR_UNSUPPORTED;
+    cudaStream_t st = (cudaStream_t)stream;
+    dim3 grid((F + 7) / 8, U);
+    if (dtype == PK_BF16)
+        summarize_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)keys, unit_stride, row_stride,
+                                                             (const int*)offsets, nullptr, (const int*)lens,
+                                                             (const int*)ids, ids_stride, 0, F, (float*)mean,
+                                                             (float*)var);
+    else if (dtype == PK_F32)
+        summarize_kernel<float><<<grid, 256, 0, st>>>((const float*)keys, unit_stride, row_stride, (const int*)offsets,
+                                                     nullptr, (const int*)lens, (const int*)ids, ids_stride, 0, F,
+                                                     (float*)mean, (float*)var);
+    else
+        return PK_ERR_ARG;
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}
+
+extern "C" size_t pk_append_workspace_bytes(int U, int64_t n_new, int d, int F, int key_mean,
+                                            int64_t boundary_capacity) {
+    const int64_t mcap = n_new * (int64_t)key_mean;
+    const size_t base = carve_bytes(U, F, mcap > 0 ? mcap : 1, boundary_capacity > 0 ? boundary_capacity : 1);
+    // + new-block counts [U, F] + new-block moments [2, U, F, d]
+    return base + align256((size_t)U * F * 4) + 2 * align256((size_t)U * F * d * 4);
+}
+
+extern "C" int pk_append_index(uint64_t new_keys, int dtype, int64_t unit_stride, int64_t row_stride, int64_t n_new,
+                               uint64_t center, float key_scale, uint64_t w_enc, uint64_t b_enc, int U, int d, int F,
+                               int key_mean, int64_t history, uint64_t offsets, uint64_t lens, uint64_t ids,
+                               int64_t ids_stride, uint64_t mean, uint64_t var, int64_t boundary_capacity,
+                               uint64_t workspace, uint64_t workspace_bytes, uint64_t status, uint64_t stream) {
+    if (U < 1 || n_new < 1 || F < 1 || key_mean < 1 || !(key_scale > 0.f) || history < 0) return PK_ERR_ARG;
+    if (d != kBD) return PK_ERR_UNSUPPORTED;
+    if (!new_keys || !center || !w_enc || !b_enc || !offsets || !lens || !ids || !workspace || !status)
+        return PK_ERR_ARG;
+    if ((mean == 0) != (var == 0)) return PK_ERR_ARG;
+    if ((long long)n_new * F >= (1ll << 40) || history + n_new > INT32_MAX || row_stride < d) return PK_ERR_ARG;
+    if (boundary_capacity < 1) return PK_ERR_ARG;
+    if (workspace_bytes < pk_append_workspace_bytes(U, n_new, d, F, key_mean, boundary_capacity))
+        return PK_ERR_WORKSPACE;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int64_t mcap = n_new * (int64_t)key_mean;
+    BuildWs ws = carve((void*)workspace, U, F, mcap, boundary_capacity);
+    char* extra = (char*)workspace + carve_bytes(U, F, mcap, boundary_capacity);
+    int* cnt_new = (int*)extra;
+    float* mean_new = (float*)(extra + align256((size_t)U * F * 4));
+    float* var_new = (float*)(extra + align256((size_t)U * F * 4) + align256((size_t)U * F * d * 4));
+    cudaMemsetAsync((void*)workspace, 0, counters_bytes(U, F), st);
+    cudaMemsetAsync(cnt_new, 0, (size_t)U * F * 4, st);
+    const long long count = (long long)n_new * key_mean;
+    int rc;
+    if (dtype == PK_BF16)
+        rc = run_encode_select((const __nv_bfloat16*)new_keys, unit_stride, row_stride, n_new, (const float*)center,
+                               key_scale, (const float*)w_enc, (const float*)b_enc, U, F, count, ws, cnt_new,
+                               (int*)status, st);
+    else if (dtype == PK_F32)
+        rc = run_encode_select((const float*)new_keys, unit_stride, row_stride, n_new, (const float*)center, key_scale,
+                               (const float*)w_enc, (const float*)b_enc, U, F, count, ws, cnt_new, (int*)status, st);
+    else
+        return PK_ERR_ARG;
+    if (rc) return rc;
+    dim3 g2((F + 255) / 256, U);
+    append_check_kernel<<<g2, 256, 0, st>>>((const int*)offsets, (const int*)lens, cnt_new, F, ws.flag);
+    PK_CHECK_LAUNCH();
+    append_scatter_kernel<<<dim3(64, U), 256, 0, st>>>(ws, F, (const int*)offsets, (const int*)lens, (int*)ids,
+                                                        ids_stride, (long long)history);
+    PK_CHECK_LAUNCH();
+    append_gate_kernel<<<256, 256, 0, st>>>(ws.flag, cnt_new, (int64_t)U * F);
+    PK_CHECK_LAUNCH();
+    // Sort only the appended tail of each bucket (it follows the old ids,
+    // which are all smaller).
+    rc = sort_buckets((int*)ids, ids_stride, (const int*)offsets, (const int*)lens, cnt_new, U, F, (int*)status, st);
+    if (rc) return rc;
+    if (mean) {
+        // New-block moments from the appended tails, then the merge.
+        if (dtype == PK_BF16)
+            summarize_kernel<__nv_bfloat16><<<dim3((F + 7) / 8, U), 256, 0, st>>>(
+                (const __nv_bfloat16*)new_keys, unit_stride, row_stride, (const int*)offsets, (const int*)lens,
+                cnt_new, (const int*)ids, ids_stride, (long long)history, F, mean_new, var_new);
+        else
+            summarize_kernel<float><<<dim3((F + 7) / 8, U), 256, 0, st>>>(
+                (const float*)new_keys, unit_stride, row_stride, (const int*)offsets, (const int*)lens, cnt_new,
+                (const int*)ids, ids_stride, (long long)history, F, mean_new, var_new);
+        PK_CHECK_LAUNCH();
+        merge_moments_kernel<<<dim3((unsigned)(((int64_t)F * kBD + 255) / 256), U), 256, 0, st>>>(
+            (const int*)lens, cnt_new, F, (float*)mean, (float*)var, mean_new, var_new, ws.flag);
+        PK_CHECK_LAUNCH();
+    }
+    append_commit_kernel<<<g2, 256, 0, st>>>(ws.flag, (int*)lens, cnt_new, F, (int*)status);
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}

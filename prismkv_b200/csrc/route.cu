@@ -1,0 +1,497 @@
+// Query-side routing kernels: q_activation (SAE encode + per-head top-k +
+// normalised aggregation) and the moments router.
+//
+// q_activation restates src/prismkv/core.py:131-139.  The encode reproduces
+// the fp32 dot-product order the reference's F.linear takes for a [G, d]
+// query block (G in 2..5: sixteen interleaved FMA chains folded pairwise;
+// G >= 6: one sequential chain), so the activations -- and with them the
+// routed bucket ids -- are bit-identical to the reference's.
+#include "common.cuh"
+#include "topk.cuh"
+
+namespace pk {
+
+constexpr int kEncD = 128;            // head dim compiled for the encoders
+constexpr int kEncHeads = 32;         // heads per CTA tile
+constexpr int kEncFeat = 128;         // features per CTA tile
+constexpr int kEncThreads = 128;      // 4 warps x (8 heads, 4 features/lane)
+constexpr int kWPitch = kEncD + 4;    // padded row pitch of the W tile (floats)
+
+enum DotOrder { kInterleaved16 = 0, kSequential = 1 };
+
+// Position of element k of a d=128 row in the chain-major layout used for the
+// interleaved order: chain j = k % 16 owns positions 8j .. 8j+7.
+__device__ __forceinline__ int perm16(int k) { return 8 * (k & 15) + (k >> 4); }
+
+template <int ORDER, typename QT>
+__global__ void __launch_bounds__(kEncThreads)
+qact_encode_kernel(const QT* __restrict__ q, const int* __restrict__ units, int n_units, int G,
+                   const float* __restrict__ W, const float* __restrict__ bias, float query_scale, int F,
+                   float* __restrict__ act) {
+    extern __shared__ __align__(16) float smem[];
+    float* Xs = smem;                          // [kEncHeads][kEncD]
+    float* Ws = smem + kEncHeads * kEncD;      // [kEncFeat][kWPitch]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int f0 = blockIdx.x * kEncFeat;
+    const int h0 = blockIdx.y * kEncHeads;
+    const int n_heads = n_units * G;
+
+    // Stage the query tile (x = q / query_scale, core.py:133) and W tile.
+    for (int e = tid; e < kEncHeads * kEncD; e += kEncThreads) {
+        const int hh = e / kEncD, kk = e % kEncD;
+        const int h = h0 + hh;
+        float x = 0.f;
+        if (h < n_heads) {
+            const int ui = h / G, g = h % G;
+            const int u = units ? units[ui] : ui;
+            x = __fdiv_rn(load_f(q, ((int64_t)u * G + g) * kEncD + kk), query_scale);
+        }
+        const int pos = ORDER == kInterleaved16 ? perm16(kk) : kk;
+        Xs[hh * kEncD + pos] = x;
+    }
+    for (int e = tid; e < kEncFeat * (kEncD / 4); e += kEncThreads) {
+        const int ff = e / (kEncD / 4), c = e % (kEncD / 4);
+        const int f = f0 + ff;
+        float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (f < F) w = reinterpret_cast<const float4*>(W + (int64_t)f * kEncD)[c];
+        float* row = Ws + ff * kWPitch;
+        const int k = 4 * c;
+        if (ORDER == kInterleaved16) {
+            row[perm16(k)] = w.x; row[perm16(k + 1)] = w.y; row[perm16(k + 2)] = w.z; row[perm16(k + 3)] = w.w;
+        } else {
+            *reinterpret_cast<float4*>(row + k) = w;
+        }
+    }
+    __syncthreads();
+
+    // Thread tile: heads warp*8 .. +7 (warp-uniform: broadcast loads),
+    // features lane + 32*i (i < 4; conflict-free with the padded pitch).
+    const float* xb = Xs + (warp * 8) * kEncD;
+    const float* wb = Ws + lane * kWPitch;
+    float res[8][4];
+
+    if (ORDER == kInterleaved16) {
+        float t0[8][4], t1[8][4], s[8][4];
+#pragma unroll 1
+        for (int l = 0; l < 4; ++l) {
+#pragma unroll 1
+            for (int uu = 0; uu < 4; ++uu) {
+                const int j = l + 4 * uu;
+                float acc[8][4];
+#pragma unroll
+                for (int a = 0; a < 8; ++a)
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const int p = 8 * j + 4 * half;
+                    float4 xv[8], wv[4];
+#pragma unroll
+                    for (int a = 0; a < 8; ++a) xv[a] = *reinterpret_cast<const float4*>(xb + a * kEncD + p);
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) wv[b] = *reinterpret_cast<const float4*>(wb + b * 32 * kWPitch + p);
+#pragma unroll
+                    for (int a = 0; a < 8; ++a)
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            acc[a][b] = fmaf(xv[a].x, wv[b].x, acc[a][b]);
+                            acc[a][b] = fmaf(xv[a].y, wv[b].y, acc[a][b]);
+                            acc[a][b] = fmaf(xv[a].z, wv[b].z, acc[a][b]);
+                            acc[a][b] = fmaf(xv[a].w, wv[b].w, acc[a][b]);
+                        }
+                }
+#pragma unroll
+                for (int a = 0; a < 8; ++a)
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) s[a][b] = uu == 0 ? acc[a][b] : __fadd_rn(s[a][b], acc[a][b]);
+            }
+#pragma unroll
+            for (int a = 0; a < 8; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    if (l == 0) t0[a][b] = s[a][b];
+                    else if (l == 1) t0[a][b] = __fadd_rn(t0[a][b], s[a][b]);
+                    else if (l == 2) t1[a][b] = s[a][b];
+                    else t1[a][b] = __fadd_rn(t1[a][b], s[a][b]);
+                }
+        }
+#pragma unroll
+        for (int a = 0; a < 8; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) res[a][b] = __fadd_rn(t0[a][b], t1[a][b]);
+    } else {
+#pragma unroll
+        for (int a = 0; a < 8; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) res[a][b] = 0.f;
+#pragma unroll 4
+        for (int p = 0; p < kEncD; p += 4) {
+            float4 xv[8], wv[4];
+#pragma unroll
+            for (int a = 0; a < 8; ++a) xv[a] = *reinterpret_cast<const float4*>(xb + a * kEncD + p);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) wv[b] = *reinterpret_cast<const float4*>(wb + b * 32 * kWPitch + p);
+#pragma unroll
+            for (int a = 0; a < 8; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    res[a][b] = fmaf(xv[a].x, wv[b].x, res[a][b]);
+                    res[a][b] = fmaf(xv[a].y, wv[b].y, res[a][b]);
+                    res[a][b] = fmaf(xv[a].z, wv[b].z, res[a][b]);
+                    res[a][b] = fmaf(xv[a].w, wv[b].w, res[a][b]);
+                }
+        }
+    }
+
+    // Epilogue: + bias, ReLU (core.py:48), store act[u, g, f].
+#pragma unroll
+    for (int a = 0; a < 8; ++a) {
+        const int h = h0 + warp * 8 + a;
+        if (h >= n_heads) continue;
+        const int ui = h / G, g = h % G;
+        const int u = units ? units[ui] : ui;
+        float* out = act + ((int64_t)u * G + g) * F;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int f = f0 + lane + 32 * b;
+            if (f < F) {
+                const float v = __fadd_rn(res[a][b], bias[f]);
+                out[f] = v > 0.f ? v : 0.f;
+            }
+        }
+    }
+}
+
+// Per (unit, head): exact top-k of the head's activations (stable descending,
+// ties -> lower feature id, core.py:134), normalisation by the k-slot sum in
+// the reference's summation order (core.py:136), division by G (core.py:137).
+// The last of the unit's G CTAs aggregates the heads in head order
+// (scatter_add_ of core.py:137), keeps score > 0 and live buckets, and emits
+// the candidate order (core.py:138-139).
+struct QactSmem {
+    TopkScratch tk;
+    int sel[256];
+    uint32_t selkey[256];
+    float val[256];
+    float norm;
+    int is_last;
+};
+
+__global__ void __launch_bounds__(256)
+qact_select_kernel(const float* __restrict__ act, const int* __restrict__ units, int G, int F, int k,
+                   const int* __restrict__ counts, int* __restrict__ head_ids, float* __restrict__ head_val,
+                   int* __restrict__ unit_done, int* __restrict__ order, int* __restrict__ n_order, int order_stride,
+                   float* __restrict__ score, int* __restrict__ topk_out) {
+    extern __shared__ __align__(16) uint32_t vbits[];  // [F] activation bits
+    __shared__ QactSmem sm;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const int ui = blockIdx.x / G, g = blockIdx.x % G;
+    const int u = units ? units[ui] : ui;
+    const float* a = act + ((int64_t)u * G + g) * F;
+    for (int i = tid; i < F; i += nt) vbits[i] = __float_as_uint(a[i]);
+    __syncthreads();
+
+    // Positive activations only: zero-valued picks add nothing to the score.
+    const int m = block_topk(
+        F, k, [&](int i) { return vbits[i]; }, [&](int i) { return __uint_as_float(vbits[i]) > 0.f; }, sm.sel,
+        sm.selkey, sm.tk);
+    // Slot values in rank order; slots past the positives hold zeros.
+    for (int r = tid; r < k; r += nt) sm.val[r] = r < m ? __uint_as_float(sm.selkey[r]) : 0.f;
+    __syncthreads();
+    if (tid == 0) {
+        const float s = torch_rowsum(sm.val, k);
+        const float floor_ = 1e-20f;
+        sm.norm = s < floor_ ? floor_ : s;
+    }
+    __syncthreads();
+    const float s = sm.norm;
+    int* hid = head_ids + ((int64_t)u * G + g) * k;
+    float* hv = head_val + ((int64_t)u * G + g) * k;
+    for (int r = tid; r < k; r += nt) {
+        float v = r < m ? __uint_as_float(sm.selkey[r]) : 0.f;
+        v = __fdiv_rn(v, s);
+        v = __fdiv_rn(v, (float)G);
+        hid[r] = r < m ? sm.sel[r] : -1;
+        hv[r] = v;
+    }
+    if (topk_out) {
+        // Zero-valued slots take the lowest feature ids whose value is not
+        // positive (the rest of the stable descending argsort).
+        int* tk = topk_out + ((int64_t)u * G + g) * k;
+        for (int r = tid; r < m; r += nt) tk[r] = sm.sel[r];
+        if (m < k) {
+            int base = 0;
+            for (int start = 0; start < F && base < k - m; start += nt) {
+                const int i = start + tid;
+                const bool z = i < F && !(__uint_as_float(vbits[i]) > 0.f);
+                int tot;
+                const int at = block_exclusive_scan(z ? 1 : 0, sm.tk.scan, &tot);
+                if (z && base + at < k - m) tk[m + base + at] = i;
+                base += tot;
+            }
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) sm.is_last = atomicAdd(&unit_done[u], 1) == G - 1;
+    __syncthreads();
+    if (!sm.is_last) return;
+    __threadfence();
+
+    // ---- Aggregation over the unit's G heads (this CTA arrived last). ----
+    const int E = G * k;  // <= 256
+    int* eid = reinterpret_cast<int*>(vbits);          // [E]
+    float* ev = reinterpret_cast<float*>(vbits) + E;   // [E]
+    float* sc = ev + E;                                // [E]
+    int* cand = reinterpret_cast<int*>(sc + E);        // [E]
+    __syncthreads();
+    for (int e = tid; e < E; e += nt) {
+        eid[e] = __ldcg(head_ids + (int64_t)u * E + e);
+        ev[e] = __ldcg(head_val + (int64_t)u * E + e);
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += nt) {
+        const int f = eid[e];
+        const int h = e / k;
+        bool first = f >= 0;
+        for (int e2 = 0; e2 < h * k && first; ++e2) first = eid[e2] != f;
+        float acc = 0.f;
+        if (first) {
+            for (int hh = 0; hh < G; ++hh)
+                for (int r = 0; r < k; ++r)
+                    if (eid[hh * k + r] == f) { acc = __fadd_rn(acc, ev[hh * k + r]); break; }
+        }
+        const bool keep = first && acc > 0.f && counts[(int64_t)u * F + f] > 0;
+        sc[e] = acc;
+        cand[e] = keep ? f : -1;
+        if (score && first) score[(int64_t)u * F + f] = acc;
+    }
+    __syncthreads();
+    // Rank the kept candidates by (score desc, feature asc).
+    for (int e = tid; e < E; e += nt) {
+        const int f = cand[e];
+        if (f < 0) continue;
+        const float v = sc[e];
+        int r = 0;
+        for (int e2 = 0; e2 < E; ++e2) {
+            const int f2 = cand[e2];
+            if (f2 < 0) continue;
+            const float v2 = sc[e2];
+            r += (v2 > v) || (v2 == v && f2 < f);
+        }
+        order[(int64_t)u * order_stride + r] = f;
+    }
+    int mine = 0;
+    for (int e = tid; e < E; e += nt) mine += cand[e] >= 0;
+    int tot;
+    block_exclusive_scan(mine, sm.tk.scan, &tot);
+    if (tid == 0) {
+        n_order[u] = tot;
+        unit_done[u] = 0;
+    }
+}
+
+__global__ void zero_rows_kernel(float* __restrict__ score, const int* __restrict__ units, int F) {
+    const int u = units ? units[blockIdx.x] : blockIdx.x;
+    for (int i = threadIdx.x; i < F; i += blockDim.x) score[(int64_t)u * F + i] = 0.f;
+}
+
+// ---------------------------------------------------------------------------
+// moments router (core.py:117-130)
+// ---------------------------------------------------------------------------
+
+// logits[u, g, f] = log(max(n,1)) + q.mu/sqrt(d) + (q*q).var/(2d), -inf for
+// empty buckets.  One warp per (unit, feature); lanes split d.
+template <typename QT>
+__global__ void moments_logits_kernel(const QT* __restrict__ q, const float* __restrict__ mean,
+                                      const float* __restrict__ var, const int* __restrict__ counts, int terms,
+                                      int G, int d, int F, float* __restrict__ logits) {
+    const int u = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int f = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (f >= F) return;
+    const int n = counts[(int64_t)u * F + f];
+    const float* mu = mean + ((int64_t)u * F + f) * d;
+    const float* nu = var + ((int64_t)u * F + f) * d;
+    const float sq = sqrtf((float)d);
+    for (int g = 0; g < G; ++g) {
+        float dm = 0.f, dv = 0.f;
+        for (int c = lane; c < d; c += 32) {
+            const float x = load_f(q, ((int64_t)u * G + g) * d + c);
+            if (terms & PK_TERM_MEAN) dm = fmaf(x, mu[c], dm);
+            if (terms & PK_TERM_VARIANCE) dv = fmaf(x * x, nu[c], dv);
+        }
+        dm = warp_sum(dm);
+        dv = warp_sum(dv);
+        if (lane == 0) {
+            float l = 0.f;
+            if (terms & PK_TERM_COUNT) l += logf((float)(n > 1 ? n : 1));
+            if (terms & PK_TERM_MEAN) l += dm / sq;
+            if (terms & PK_TERM_VARIANCE) l += dv / (float)(2 * d);
+            logits[((int64_t)u * G + g) * F + f] = n > 0 ? l : -INFINITY;
+        }
+    }
+}
+
+// score[u, f] = mean over heads of softmax(logits[u, g, :]); then the first k
+// live buckets by descending score (ties -> lower id).
+__global__ void __launch_bounds__(256)
+moments_select_kernel(const float* __restrict__ logits, const int* __restrict__ counts, int G, int F, int k,
+                      float* __restrict__ score, int* __restrict__ order, int* __restrict__ n_order,
+                      int order_stride) {
+    extern __shared__ __align__(16) uint32_t sbits[];  // [F]
+    __shared__ QactSmem sm;
+    __shared__ float red[32];
+    const int u = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+    bool any_live = false;
+    for (int i = tid; i < F; i += nt) any_live |= counts[(int64_t)u * F + i] > 0;
+    any_live = __syncthreads_or(any_live);
+    float* sc = score + (int64_t)u * F;
+    for (int i = tid; i < F; i += nt) sc[i] = 0.f;
+    __syncthreads();
+    if (any_live) {
+        for (int g = 0; g < G; ++g) {
+            const float* l = logits + ((int64_t)u * G + g) * F;
+            float mx = -INFINITY;
+            for (int i = tid; i < F; i += nt) mx = fmaxf(mx, l[i]);
+            mx = warp_max(mx);
+            if ((tid & 31) == 0) red[tid >> 5] = mx;
+            __syncthreads();
+            if (tid < 32) {
+                float v = tid < (nt >> 5) ? red[tid] : -INFINITY;
+                v = warp_max(v);
+                if (tid == 0) red[0] = v;
+            }
+            __syncthreads();
+            mx = red[0];
+            __syncthreads();
+            float z = 0.f;
+            for (int i = tid; i < F; i += nt) z += expf(l[i] - mx);
+            z = warp_sum(z);
+            if ((tid & 31) == 0) red[tid >> 5] = z;
+            __syncthreads();
+            if (tid < 32) {
+                float v = tid < (nt >> 5) ? red[tid] : 0.f;
+                v = warp_sum(v);
+                if (tid == 0) red[0] = v;
+            }
+            __syncthreads();
+            z = red[0];
+            __syncthreads();
+            for (int i = tid; i < F; i += nt) sc[i] += expf(l[i] - mx) / z;
+            __syncthreads();
+        }
+        for (int i = tid; i < F; i += nt) sc[i] = sc[i] / (float)G;
+        __syncthreads();
+    }
+    for (int i = tid; i < F; i += nt) sbits[i] = __float_as_uint(sc[i]);
+    __syncthreads();
+    const int m = block_topk(
+        F, k, [&](int i) { return sbits[i]; }, [&](int i) { return counts[(int64_t)u * F + i] > 0; }, sm.sel,
+        sm.selkey, sm.tk);
+    for (int r = tid; r < m; r += nt) order[(int64_t)u * order_stride + r] = sm.sel[r];
+    if (tid == 0) n_order[u] = m;
+}
+
+}  // namespace pk
+
+using namespace pk;
+
+extern "C" size_t pk_route_qact_workspace_bytes(int U, int G, int F, int k) {
+    const size_t act = (size_t)U * G * F * sizeof(float);
+    const size_t heads = (size_t)U * G * k * (sizeof(int) + sizeof(float));
+    const size_t done = (size_t)U * sizeof(int);
+    return (act + 255) / 256 * 256 + (heads + 255) / 256 * 256 + (done + 255) / 256 * 256;
+}
+
+extern "C" int pk_route_qact(uint64_t q, int q_dtype, uint64_t units, int n_units, uint64_t w_enc, uint64_t b_enc,
+                             float query_scale, uint64_t counts, int U, int G, int d, int F, int k,
+                             uint64_t workspace, uint64_t workspace_bytes, uint64_t order, uint64_t n_order,
+                             int order_stride, uint64_t score, uint64_t topk, uint64_t stream) {
+    if (U < 1 || G < 1 || F < 1 || k < 1 || n_units < 0 || n_units > U || !(query_scale > 0.f)) return PK_ERR_ARG;
+    if (k > F) k = F;
+    if (G * k > 256 || order_stride < G * k) return PK_ERR_ARG;
+    if (d != kEncD) return PK_ERR_UNSUPPORTED;
+    if ((size_t)F * sizeof(uint32_t) > 200 * 1024) return PK_ERR_UNSUPPORTED;
+    if (workspace_bytes < pk_route_qact_workspace_bytes(U, G, F, k)) return PK_ERR_WORKSPACE;
+    if (!q || !w_enc || !b_enc || !counts || !workspace || !order || !n_order) return PK_ERR_ARG;
+    if (n_units == 0) return PK_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    char* ws = (char*)workspace;
+    float* act = (float*)ws;
+    size_t off = ((size_t)U * G * F * sizeof(float) + 255) / 256 * 256;
+    int* hid = (int*)(ws + off);
+    float* hval = (float*)(hid + (size_t)U * G * k);
+    off += ((size_t)U * G * k * (sizeof(int) + sizeof(float)) + 255) / 256 * 256;
+    int* done = (int*)(ws + off);
+    const int* ul = (const int*)units;
+
+    // The order F.linear takes for a [G, d] block (see file header).
+    const bool inter = G >= 2 && G <= 5;
+    dim3 grid((F + kEncFeat - 1) / kEncFeat, (n_units * G + kEncHeads - 1) / kEncHeads);
+    const size_t smem = (size_t)(kEncHeads * kEncD + kEncFeat * kWPitch) * sizeof(float);
+#define PK_LAUNCH_ENC(ORD, QT)                                                                           \
+    do {                                                                                                 \
+        cudaFuncSetAttribute(qact_encode_kernel<ORD, QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
+                             (int)smem);                                                                 \
+        qact_encode_kernel<ORD, QT><<<grid, kEncThreads, smem, st>>>(                                    \
+            (const QT*)q, ul, n_units, G, (const float*)w_enc, (const float*)b_enc, query_scale, F, act); \
+    } while (0)
+    if (q_dtype == PK_BF16) {
+        if (inter) PK_LAUNCH_ENC(kInterleaved16, __nv_bfloat16); else PK_LAUNCH_ENC(kSequential, __nv_bfloat16);
+    } else if (q_dtype == PK_F32) {
+        if (inter) PK_LAUNCH_ENC(kInterleaved16, float); else PK_LAUNCH_ENC(kSequential, float);
+    } else {
+        return PK_ERR_ARG;
+    }
+#undef PK_LAUNCH_ENC
+    PK_CHECK_LAUNCH();
+    if (score) {
+        zero_rows_kernel<<<n_units, 256, 0, st>>>((float*)score, ul, F);
+        PK_CHECK_LAUNCH();
+    }
+    size_t ssmem = (size_t)F * sizeof(uint32_t);
+    const size_t agg = (size_t)4 * G * k * sizeof(float);
+    if (agg > ssmem) ssmem = agg;
+    cudaFuncSetAttribute(qact_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem);
+    qact_select_kernel<<<n_units * G, 256, ssmem, st>>>(act, ul, G, F, k, (const int*)counts, hid, hval, done,
+                                                        (int*)order, (int*)n_order, order_stride, (float*)score,
+                                                        (int*)topk);
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}
+
+extern "C" size_t pk_route_moments_workspace_bytes(int U, int G, int F) {
+    return ((size_t)U * G * F * sizeof(float) + 255) / 256 * 256;
+}
+
+extern "C" int pk_route_moments(uint64_t q, int q_dtype, uint64_t mean, uint64_t var, uint64_t counts, int terms,
+                                int U, int G, int d, int F, int k, uint64_t workspace, uint64_t workspace_bytes,
+                                uint64_t score, uint64_t order, uint64_t n_order, int order_stride,
+                                uint64_t stream) {
+    if (U < 1 || G < 1 || d < 1 || F < 1 || k < 1 || terms <= 0 || terms > 7) return PK_ERR_ARG;
+    if (k > F) k = F;
+    if (k > 256 || order_stride < k) return PK_ERR_ARG;
+    if ((size_t)F * sizeof(uint32_t) > 200 * 1024) return PK_ERR_UNSUPPORTED;
+    if (workspace_bytes < pk_route_moments_workspace_bytes(U, G, F)) return PK_ERR_WORKSPACE;
+    if (!q || !mean || !var || !counts || !workspace || !score || !order || !n_order) return PK_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    float* logits = (float*)workspace;
+    dim3 grid((F + 7) / 8, U);
+    if (q_dtype == PK_BF16)
+        moments_logits_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)q, (const float*)mean,
+                                                                   (const float*)var, (const int*)counts, terms,
+                                                                   G, d, F, logits);
+    else if (q_dtype == PK_F32)
+        moments_logits_kernel<float><<<grid, 256, 0, st>>>((const float*)q, (const float*)mean, (const float*)var,
+                                                           (const int*)counts, terms, G, d, F, logits);
+    else
+        return PK_ERR_ARG;
+    PK_CHECK_LAUNCH();
+    const size_t ssmem = (size_t)F * sizeof(uint32_t);
+    cudaFuncSetAttribute(moments_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem);
+    moments_select_kernel<<<U, 256, ssmem, st>>>(logits, (const int*)counts, G, F, k, (float*)score, (int*)order,
+                                                 (int*)n_order, order_stride);
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}

@@ -1,0 +1,499 @@
+// Sparse attention over the selected history rows plus the dense generated
+// tail: softmax((Q K_rows^T)/sqrt(d)) V_rows for the G query heads of a unit
+// (src/prismkv/core.py:170-183), split across CTAs along the row list with an
+// exact log-sum-exp merge (the split-KV scheme of kernels/ppu_8b/av_tuned.cu).
+//
+// bf16 path: the CTA gathers 64 K rows and 64 V rows per pipeline stage with
+// 16-byte cp.async (rows addressed through the id list), three stages deep;
+// each warp runs QK^T and PV for 16 rows with mma.sync m16n8k16 (the G heads
+// fill the M=16 rows), keeps an fp32 online softmax, and feeds P to the PV
+// product as a bf16 hi/lo pair so the weights keep ~16 bits.  The last CTA of
+// a unit merges the split partials.
+#include "common.cuh"
+
+namespace pk {
+
+constexpr int kAvD = 128;
+constexpr int kAvThreads = 128;
+constexpr int kAvTile = 64;
+constexpr int kAvStages = 3;
+constexpr int kAvRowBytes = kAvD * 2;
+constexpr int kAvStageBytes = kAvTile * kAvRowBytes * 2;   // K + V
+constexpr int kAvMaxG = 16;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct AvParams {
+    const void* q;
+    const void* k;
+    const void* v;
+    int kv_heads;
+    int64_t kv_batch_stride, kv_head_stride, kv_row_stride;
+    const int* ids;
+    int64_t ids_stride;
+    const int* count;
+    const int* history;
+    const int* length;
+    int G, S;
+    float* part;    // [U*G, S, D+2] split partials (log2 domain)
+    int* done;      // [U] arrival counters
+    void* out;      // [U, G, D] (dtype of q)
+    float* xpart;   // [U*G, D+2] exported partial (natural-log m), or null
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+    const int n = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(n));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&t);
+}
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Byte offset of (row, 16-byte chunk) inside a 64-row x 256-byte tile, the
+// chunk index XOR-swizzled by the row so ldmatrix is bank-conflict free.
+__device__ __forceinline__ uint32_t tile_off(int row, int chunk) {
+    return (uint32_t)(row * kAvRowBytes + ((chunk ^ (row & 7)) << 4));
+}
+
+template <typename OT>
+__device__ __forceinline__ OT to_out(float x);
+template <>
+__device__ __forceinline__ float to_out<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 to_out<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+// Combine per-warp (m, l, o) states held in shared memory into this CTA's
+// state, then either finish (single split) or store the split partial and
+// let the last CTA of the unit merge.  m is in log2 units.
+template <typename OT>
+__device__ void av_finish(const AvParams& p, int u, int s, const float* red, int nwarps) {
+    const int G = p.G, S = p.S, tid = threadIdx.x;
+    const float* rm = red;
+    const float* rl = red + nwarps * kAvMaxG;
+    const float* ro = red + 2 * nwarps * kAvMaxG;
+    __shared__ int is_last;
+    const int dim = tid;  // kAvThreads == kAvD
+    for (int h = 0; h < G; ++h) {
+        float M = -INFINITY;
+        for (int w = 0; w < nwarps; ++w) M = fmaxf(M, rm[w * kAvMaxG + h]);
+        float L = 0.f, O = 0.f;
+        for (int w = 0; w < nwarps; ++w) {
+            const float mw = rm[w * kAvMaxG + h];
+            const float sc = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+            L = fmaf(sc, rl[w * kAvMaxG + h], L);
+            O = fmaf(sc, ro[(w * kAvMaxG + h) * kAvD + dim], O);
+        }
+        const int64_t uh = (int64_t)u * G + h;
+        if (S == 1) {
+            if (p.xpart) {
+                float* xp = p.xpart + uh * (kAvD + 2);
+                if (dim == 0) { xp[0] = M == -INFINITY ? -INFINITY : M / kLog2e; xp[1] = L; }
+                xp[2 + dim] = O;
+            } else {
+                OT* o = (OT*)p.out + uh * kAvD;
+                o[dim] = to_out<OT>(L > 0.f ? O / L : 0.f);
+            }
+        } else {
+            float* pp = p.part + (uh * S + s) * (kAvD + 2);
+            if (dim == 0) { pp[0] = M; pp[1] = L; }
+            pp[2 + dim] = O;
+        }
+    }
+    if (S == 1) return;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) is_last = atomicAdd(&p.done[u], 1) == S - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    for (int h = 0; h < G; ++h) {
+        const int64_t uh = (int64_t)u * G + h;
+        const float* pp = p.part + uh * S * (kAvD + 2);
+        float M = -INFINITY;
+        for (int j = 0; j < S; ++j) M = fmaxf(M, __ldcg(pp + j * (kAvD + 2)));
+        float L = 0.f, O = 0.f;
+        for (int j = 0; j < S; ++j) {
+            const float mj = __ldcg(pp + j * (kAvD + 2));
+            const float sc = (mj == -INFINITY) ? 0.f : exp2f(mj - M);
+            L = fmaf(sc, __ldcg(pp + j * (kAvD + 2) + 1), L);
+            O = fmaf(sc, __ldcg(pp + j * (kAvD + 2) + 2 + dim), O);
+        }
+        if (p.xpart) {
+            float* xp = p.xpart + uh * (kAvD + 2);
+            if (dim == 0) { xp[0] = M == -INFINITY ? -INFINITY : M / kLog2e; xp[1] = L; }
+            xp[2 + dim] = O;
+        } else {
+            OT* o = (OT*)p.out + uh * kAvD;
+            o[dim] = to_out<OT>(L > 0.f ? O / L : 0.f);
+        }
+    }
+    if (tid == 0) p.done[u] = 0;
+}
+
+__global__ void __launch_bounds__(kAvThreads)
+sparse_av_bf16_kernel(AvParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int s = blockIdx.x, u = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = p.G;
+    const int H = p.history[u], len = p.length[u], cnt = p.count[u];
+    const int rows = len > 0 ? cnt + max(len - H, 0) : 0;
+    const int per = (rows + p.S - 1) / p.S;
+    const int span = (per + kAvTile - 1) / kAvTile * kAvTile;
+    const int r0 = min(rows, s * span), r1 = min(rows, r0 + span);
+    const int ntiles = (r1 - r0 + kAvTile - 1) / kAvTile;
+    const int64_t ubase = (int64_t)(u / p.kv_heads) * p.kv_batch_stride + (int64_t)(u % p.kv_heads) * p.kv_head_stride;
+    const __nv_bfloat16* kb = (const __nv_bfloat16*)p.k + ubase;
+    const __nv_bfloat16* vb = (const __nv_bfloat16*)p.v + ubase;
+    const int* idp = p.ids + (int64_t)u * p.ids_stride;
+    const __nv_bfloat16* qp = (const __nv_bfloat16*)p.q + (int64_t)u * G * kAvD;
+
+    // Q as the MMA A operand: rows = heads, columns = dims.
+    uint32_t qa[8][4];
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int hh = (lane >> 2) + (r & 1) * 8;
+            const int dim = kk * 16 + 2 * (lane & 3) + (r >> 1) * 8;
+            qa[kk][r] = hh < G ? *reinterpret_cast<const uint32_t*>(qp + hh * kAvD + dim) : 0u;
+        }
+
+    // Loader: two threads per row; each moves 8 K chunks and 8 V chunks.
+    const int ld_row = tid >> 1, ld_c0 = (tid & 1) * 8;
+    auto row_pos = [&](int t) -> int {
+        const int r = r0 + t * kAvTile + ld_row;
+        if (r >= r1) return -1;
+        return r < cnt ? idp[r] : H + (r - cnt);
+    };
+    auto issue = [&](int t, int pos) {
+        uint8_t* st = smem + (t % kAvStages) * kAvStageBytes;
+        const uint32_t kd = smem_u32(st), vd = smem_u32(st + kAvTile * kAvRowBytes);
+        const bool valid = pos >= 0;
+        const int64_t off = valid ? (int64_t)pos * p.kv_row_stride : 0;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const int ch = ld_c0 + c;
+            cp_async16(kd + tile_off(ld_row, ch), kb + off + ch * 8, valid);
+            cp_async16(vd + tile_off(ld_row, ch), vb + off + ch * 8, valid);
+        }
+    };
+
+    int pos0 = 0 < ntiles ? row_pos(0) : -1;
+    int pos1 = 1 < ntiles ? row_pos(1) : -1;
+    int prefetched = 2 < ntiles ? row_pos(2) : -1;
+    if (0 < ntiles) issue(0, pos0);
+    cp_async_commit();
+    if (1 < ntiles) issue(1, pos1);
+    cp_async_commit();
+
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+    float o[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    const float scale = kLog2e / sqrtf((float)kAvD);
+
+    for (int t = 0; t < ntiles; ++t) {
+        const int tn = t + kAvStages - 1;
+        if (tn < ntiles) issue(tn, prefetched);
+        cp_async_commit();
+        prefetched = tn + 1 < ntiles ? row_pos(tn + 1) : -1;
+        cp_async_wait<kAvStages - 1>();
+        __syncthreads();
+
+        const uint8_t* st = smem + (t % kAvStages) * kAvStageBytes;
+        const uint32_t kbase = smem_u32(st), vbase = smem_u32(st + kAvTile * kAvRowBytes);
+        const int wrow = warp * 16;
+        float sacc[2][4];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            uint32_t b[4];
+            const int mi = lane >> 3, r = lane & 7;
+            const int row = wrow + (mi >> 1) * 8 + r;
+            ldmatrix_x4(kbase + tile_off(row, 2 * kk + (mi & 1)), b);
+            mma_bf16(sacc[0], qa[kk], b[0], b[1]);
+            mma_bf16(sacc[1], qa[kk], b[2], b[3]);
+        }
+        // Scale, mask rows past the split end, online softmax per head.
+        const int base_r = r0 + t * kAvTile + wrow;
+        float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const bool ok = base_r + 8 * j + 2 * (lane & 3) + e < r1;
+                sacc[j][e] = ok ? sacc[j][e] * scale : -INFINITY;
+                sacc[j][2 + e] = ok ? sacc[j][2 + e] * scale : -INFINITY;
+                mx_a = fmaxf(mx_a, sacc[j][e]);
+                mx_b = fmaxf(mx_b, sacc[j][2 + e]);
+            }
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+        const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+        const float al_a = mn_a == -INFINITY ? 1.f : exp2f(m_a - mn_a);
+        const float al_b = mn_b == -INFINITY ? 1.f : exp2f(m_b - mn_b);
+        float pr[2][4];
+        float ps_a = 0.f, ps_b = 0.f;
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                pr[j][e] = mn_a == -INFINITY ? 0.f : exp2f(sacc[j][e] - mn_a);
+                pr[j][2 + e] = mn_b == -INFINITY ? 0.f : exp2f(sacc[j][2 + e] - mn_b);
+                ps_a += pr[j][e];
+                ps_b += pr[j][2 + e];
+            }
+        ps_a += __shfl_xor_sync(0xffffffffu, ps_a, 1);
+        ps_a += __shfl_xor_sync(0xffffffffu, ps_a, 2);
+        ps_b += __shfl_xor_sync(0xffffffffu, ps_b, 1);
+        ps_b += __shfl_xor_sync(0xffffffffu, ps_b, 2);
+        l_a = fmaf(l_a, al_a, ps_a);
+        l_b = fmaf(l_b, al_b, ps_b);
+        m_a = mn_a;
+        m_b = mn_b;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            o[j][0] *= al_a; o[j][1] *= al_a;
+            o[j][2] *= al_b; o[j][3] *= al_b;
+        }
+        // P as the A operand (rows = heads, k = the 16 rows), hi + lo parts.
+        uint32_t ph[4], pl[4];
+        {
+            const float h00 = bf16_round(pr[0][0]), h01 = bf16_round(pr[0][1]);
+            const float h02 = bf16_round(pr[0][2]), h03 = bf16_round(pr[0][3]);
+            const float h10 = bf16_round(pr[1][0]), h11 = bf16_round(pr[1][1]);
+            const float h12 = bf16_round(pr[1][2]), h13 = bf16_round(pr[1][3]);
+            ph[0] = pack_bf16(h00, h01); ph[1] = pack_bf16(h02, h03);
+            ph[2] = pack_bf16(h10, h11); ph[3] = pack_bf16(h12, h13);
+            pl[0] = pack_bf16(pr[0][0] - h00, pr[0][1] - h01); pl[1] = pack_bf16(pr[0][2] - h02, pr[0][3] - h03);
+            pl[2] = pack_bf16(pr[1][0] - h10, pr[1][1] - h11); pl[3] = pack_bf16(pr[1][2] - h12, pr[1][3] - h13);
+        }
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {
+            uint32_t b[4];
+            const int mi = lane >> 3, r = lane & 7;
+            const int row = wrow + (mi & 1) * 8 + r;
+            ldmatrix_x4_trans(vbase + tile_off(row, 2 * np + (mi >> 1)), b);
+            mma_bf16(o[2 * np], ph, b[0], b[1]);
+            mma_bf16(o[2 * np + 1], ph, b[2], b[3]);
+            mma_bf16(o[2 * np], pl, b[0], b[1]);
+            mma_bf16(o[2 * np + 1], pl, b[2], b[3]);
+        }
+        __syncthreads();
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // Per-warp states to shared memory (reusing the stage buffers).
+    float* red = reinterpret_cast<float*>(smem);
+    float* rm = red;
+    float* rl = red + 4 * kAvMaxG;
+    float* ro = red + 2 * 4 * kAvMaxG;
+    const int ha = lane >> 2, hb = ha + 8;
+    if ((lane & 3) == 0) {
+        if (ha < G) { rm[warp * kAvMaxG + ha] = m_a; rl[warp * kAvMaxG + ha] = l_a; }
+        if (hb < G) { rm[warp * kAvMaxG + hb] = m_b; rl[warp * kAvMaxG + hb] = l_b; }
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const int dim = 8 * j + 2 * (lane & 3);
+        if (ha < G) {
+            ro[(warp * kAvMaxG + ha) * kAvD + dim] = o[j][0];
+            ro[(warp * kAvMaxG + ha) * kAvD + dim + 1] = o[j][1];
+        }
+        if (hb < G) {
+            ro[(warp * kAvMaxG + hb) * kAvD + dim] = o[j][2];
+            ro[(warp * kAvMaxG + hb) * kAvD + dim + 1] = o[j][3];
+        }
+    }
+    __syncthreads();
+    av_finish<__nv_bfloat16>(p, u, s, red, 4);
+}
+
+// fp32 K/V path (parity shapes such as the CPU fp32 config): one warp per
+// row at a time, lane-owned dims, warp-reduced dot products.
+__global__ void __launch_bounds__(kAvThreads)
+sparse_av_f32_kernel(AvParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int s = blockIdx.x, u = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = p.G;
+    const int H = p.history[u], len = p.length[u], cnt = p.count[u];
+    const int rows = len > 0 ? cnt + max(len - H, 0) : 0;
+    const int per = (rows + p.S - 1) / p.S;
+    const int r0 = min(rows, s * per), r1 = min(rows, r0 + per);
+    const int64_t ubase = (int64_t)(u / p.kv_heads) * p.kv_batch_stride + (int64_t)(u % p.kv_heads) * p.kv_head_stride;
+    const float* kb = (const float*)p.k + ubase;
+    const float* vb = (const float*)p.v + ubase;
+    const int* idp = p.ids + (int64_t)u * p.ids_stride;
+    const float* qp = (const float*)p.q + (int64_t)u * G * kAvD;
+    float* red = reinterpret_cast<float*>(smem);
+    float* rm = red;
+    float* rl = red + 4 * kAvMaxG;
+    float* ro = red + 2 * 4 * kAvMaxG;
+    const float scale = kLog2e / sqrtf((float)kAvD);
+    // Heads in groups of four to bound register use.
+    for (int h0 = 0; h0 < G; h0 += 4) {
+        float4 qv[4], ov[4];
+        float m[4], l[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            const int h = h0 + a;
+            qv[a] = h < G ? reinterpret_cast<const float4*>(qp + h * kAvD)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+            ov[a] = make_float4(0.f, 0.f, 0.f, 0.f);
+            m[a] = -INFINITY;
+            l[a] = 0.f;
+        }
+        for (int r = r0 + warp; r < r1; r += 4) {
+            const int pos = r < cnt ? idp[r] : H + (r - cnt);
+            const float4 kv = reinterpret_cast<const float4*>(kb + (int64_t)pos * p.kv_row_stride)[lane];
+            const float4 vv = reinterpret_cast<const float4*>(vb + (int64_t)pos * p.kv_row_stride)[lane];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                float d = qv[a].x * kv.x + qv[a].y * kv.y + qv[a].z * kv.z + qv[a].w * kv.w;
+                d = warp_sum(d) * scale;
+                const float mn = fmaxf(m[a], d);
+                const float al = exp2f(m[a] - mn), pr = exp2f(d - mn);
+                l[a] = l[a] * al + pr;
+                ov[a].x = ov[a].x * al + pr * vv.x;
+                ov[a].y = ov[a].y * al + pr * vv.y;
+                ov[a].z = ov[a].z * al + pr * vv.z;
+                ov[a].w = ov[a].w * al + pr * vv.w;
+                m[a] = mn;
+            }
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            const int h = h0 + a;
+            if (h >= G) break;
+            if (lane == 0) { rm[warp * kAvMaxG + h] = m[a]; rl[warp * kAvMaxG + h] = l[a]; }
+            reinterpret_cast<float4*>(ro + (warp * kAvMaxG + h) * kAvD)[lane] = ov[a];
+        }
+    }
+    __syncthreads();
+    av_finish<float>(p, u, s, red, 4);
+}
+
+__global__ void lse_merge_kernel(const float* __restrict__ part, int P, int UG, float* __restrict__ out_f,
+                                 __nv_bfloat16* __restrict__ out_b) {
+    const int uh = blockIdx.x, dim = threadIdx.x;
+    float M = -INFINITY;
+    for (int j = 0; j < P; ++j) M = fmaxf(M, part[((int64_t)j * UG + uh) * (kAvD + 2)]);
+    float L = 0.f, O = 0.f;
+    for (int j = 0; j < P; ++j) {
+        const float* pp = part + ((int64_t)j * UG + uh) * (kAvD + 2);
+        const float sc = pp[0] == -INFINITY ? 0.f : expf(pp[0] - M);
+        L = fmaf(sc, pp[1], L);
+        O = fmaf(sc, pp[2 + dim], O);
+    }
+    const float r = L > 0.f ? O / L : 0.f;
+    if (out_f) out_f[(int64_t)uh * kAvD + dim] = r;
+    else out_b[(int64_t)uh * kAvD + dim] = __float2bfloat16_rn(r);
+}
+
+int default_splits(int U) {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    // About three resident CTAs per SM across all units.
+    const int s = (3 * sms + U - 1) / U;
+    return s < 1 ? 1 : (s > 256 ? 256 : s);
+}
+
+}  // namespace pk
+
+using namespace pk;
+
+extern "C" size_t pk_sparse_av_workspace_bytes(int U, int G, int d, int splits) {
+    if (splits <= 0) splits = 256;
+    const size_t part = (size_t)U * G * splits * (d + 2) * sizeof(float);
+    return (part + 255) / 256 * 256 + ((size_t)U * sizeof(int) + 255) / 256 * 256;
+}
+
+extern "C" int pk_sparse_av(uint64_t q, uint64_t k, uint64_t v, int dtype, int kv_heads, int64_t kv_batch_stride,
+                            int64_t kv_head_stride, int64_t kv_row_stride, uint64_t ids, int64_t ids_stride,
+                            uint64_t count, uint64_t history, uint64_t length, int U, int G, int d, int splits,
+                            uint64_t workspace, uint64_t workspace_bytes, uint64_t out, uint64_t partial,
+                            uint64_t stream) {
+    if (U < 1 || G < 1 || G > kAvMaxG || kv_heads < 1 || kv_row_stride < d) return PK_ERR_ARG;
+    if (d != kAvD) return PK_ERR_UNSUPPORTED;
+    if (!q || !k || !v || !ids || !count || !history || !length || (!out && !partial)) return PK_ERR_ARG;
+    if (splits <= 0) splits = default_splits(U);
+    if (splits > 256) return PK_ERR_ARG;
+    if (splits > 1 && (!workspace || workspace_bytes < pk_sparse_av_workspace_bytes(U, G, d, splits)))
+        return PK_ERR_WORKSPACE;
+    AvParams p;
+    p.q = (const void*)q; p.k = (const void*)k; p.v = (const void*)v;
+    p.kv_heads = kv_heads;
+    p.kv_batch_stride = kv_batch_stride; p.kv_head_stride = kv_head_stride; p.kv_row_stride = kv_row_stride;
+    p.ids = (const int*)ids; p.ids_stride = ids_stride;
+    p.count = (const int*)count; p.history = (const int*)history; p.length = (const int*)length;
+    p.G = G; p.S = splits;
+    const size_t part_bytes = (size_t)U * G * splits * (d + 2) * sizeof(float);
+    p.part = (float*)workspace;
+    p.done = workspace ? (int*)((char*)workspace + (part_bytes + 255) / 256 * 256) : nullptr;
+    p.out = (void*)out;
+    p.xpart = (float*)partial;
+    cudaStream_t st = (cudaStream_t)stream;
+    dim3 grid(splits, U);
+    if (dtype == PK_BF16) {
+        if (kv_row_stride % 8 || kv_batch_stride % 8 || kv_head_stride % 8 || (k | v) % 16) return PK_ERR_ARG;
+        const int smem = kAvStages * kAvStageBytes;
+        cudaFuncSetAttribute(sparse_av_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        sparse_av_bf16_kernel<<<grid, kAvThreads, smem, st>>>(p);
+    } else if (dtype == PK_F32) {
+        if (kv_row_stride % 4 || kv_batch_stride % 4 || kv_head_stride % 4 || (k | v | q) % 16) return PK_ERR_ARG;
+        const int smem = (2 * 4 * kAvMaxG + 4 * kAvMaxG * kAvD) * (int)sizeof(float);
+        cudaFuncSetAttribute(sparse_av_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        sparse_av_f32_kernel<<<grid, kAvThreads, smem, st>>>(p);
+    } else {
+        return PK_ERR_ARG;
+    }
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}
+
+extern "C" int pk_lse_merge(uint64_t partial, int P, int UG, int d, uint64_t out, int dtype, uint64_t stream) {
+    if (P < 1 || UG < 1 || !partial || !out) return PK_ERR_ARG;
+    if (d != kAvD) return PK_ERR_UNSUPPORTED;
+    if (dtype != PK_F32 && dtype != PK_BF16) return PK_ERR_ARG;
+    lse_merge_kernel<<<UG, kAvD, 0, (cudaStream_t)stream>>>(
+        (const float*)partial, P, UG, dtype == PK_F32 ? (float*)out : nullptr,
+        dtype == PK_BF16 ? (__nv_bfloat16*)out : nullptr);
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}

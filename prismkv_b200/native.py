@@ -1,0 +1,151 @@
+"""ctypes binding of libprismkv_b200.so (the C ABI of include/prismkv_b200.h).
+
+The same calling convention as the reference's bindings
+(src/prismkv/native8b.py:46-80, kernels/cuda_sm90/native.py:16-35): raw device
+addresses, the current CUDA stream last, and a nonzero return raised as
+RuntimeError.  There is no fallback: if the library is missing or cannot be
+loaded, every operation raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libprismkv_b200.so"
+
+PK_F32, PK_BF16 = 0, 1
+PK_TERM_COUNT, PK_TERM_MEAN, PK_TERM_VARIANCE = 1, 2, 4
+STATUS_BITS = {
+    1: "bucket region full (append)",
+    2: "boundary buffer full (build)",
+    4: "member buffer full (build)",
+    8: "bucket larger than the sort limit (build)",
+    16: "union output row too short",
+    32: "history longer than the union bitmap",
+}
+
+# name: (argument codes including the trailing stream, restype).
+# P = device address / size_t, i = int, l = int64, f = float.
+SIGNATURES = {
+    "pk_version": ("", ctypes.c_int),
+    "pk_supported_head_dim": ("i", ctypes.c_int),
+    "pk_route_qact_workspace_bytes": ("iiii", ctypes.c_size_t),
+    "pk_route_qact": ("PiPiPPfPiiiiiPPPPiPPP", ctypes.c_int),
+    "pk_route_moments_workspace_bytes": ("iii", ctypes.c_size_t),
+    "pk_route_moments": ("PiPPPiiiiiiPPPPPiP", ctypes.c_int),
+    "pk_union": ("PPPlPPiPPiiiPlPPPPPP", ctypes.c_int),
+    "pk_sparse_av_workspace_bytes": ("iiii", ctypes.c_size_t),
+    "pk_sparse_av": ("PPPiilllPlPPPiiiiPPPPP", ctypes.c_int),
+    "pk_lse_merge": ("PiiiPiP", ctypes.c_int),
+    "pk_key_center": ("PilliliPP", ctypes.c_int),
+    "pk_build_ids_capacity": ("liifi", ctypes.c_int64),
+    "pk_build_workspace_bytes": ("iliil", ctypes.c_size_t),
+    "pk_build_index": ("PillPfPPiliiilfiPPPllPPPP", ctypes.c_int),
+    "pk_summarize": ("PillPPPliiiPPP", ctypes.c_int),
+    "pk_append_workspace_bytes": ("iliiil", ctypes.c_size_t),
+    "pk_append_index": ("PilllPfPPiiiilPPPlPPlPPPP", ctypes.c_int),
+}
+_CT = {"P": ctypes.c_uint64, "i": ctypes.c_int, "l": ctypes.c_int64, "f": ctypes.c_float}
+# Entry points that take the stream as their last argument.
+_ASYNC = {n for n, (c, r) in SIGNATURES.items() if r is ctypes.c_int and c.endswith("P") and n not in
+          ("pk_version", "pk_supported_head_dim")}
+
+_lib = None
+
+
+class NativeError(RuntimeError):
+    pass
+
+
+def lib():
+    """Load the library once; raise if it is absent (no CPU fallback)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise NativeError(f"{LIB_PATH} is missing: build it with `python -m prismkv_b200.build`")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (codes, res) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = [_CT[c] for c in codes]
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def addr(x) -> int:
+    if x is None:
+        return 0
+    if isinstance(x, torch.Tensor):
+        if x.numel() and not x.is_cuda:
+            raise ValueError("device tensor required")
+        return x.data_ptr()
+    return int(x)
+
+
+def stream_handle() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def call(name: str, *args) -> None:
+    """Calls an asynchronous entry point; tensor arguments pass their
+    data_ptr and the current stream is appended.  Nonzero return ->
+    RuntimeError (as native8b.py:79)."""
+    fn = getattr(lib(), name)
+    codes = SIGNATURES[name][0]
+    if len(args) != len(codes) - 1:
+        raise TypeError(f"{name} takes {len(codes) - 1} arguments, got {len(args)}")
+    conv = []
+    for a, c in zip(args, codes):
+        if c == "P":
+            conv.append(addr(a))
+        elif c == "f":
+            conv.append(float(a))
+        else:
+            conv.append(int(a))
+    conv.append(stream_handle())
+    rc = fn(*conv)
+    if rc:
+        raise RuntimeError(f"{name}: {'argument error' if rc < 0 else 'CUDA error'} {rc}")
+
+
+def query(name: str, *args):
+    """Calls a host-only entry point (sizes, capacities, facts)."""
+    return getattr(lib(), name)(*args)
+
+
+def check_status(status: torch.Tensor, what: str) -> None:
+    """Raise if a kernel flagged a condition in the device status word."""
+    v = int(status.item())
+    if v:
+        msgs = [m for b, m in STATUS_BITS.items() if v & b]
+        raise RuntimeError(f"{what}: " + "; ".join(msgs))
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return PK_F32
+    if t.dtype == torch.bfloat16:
+        return PK_BF16
+    raise ValueError(f"unsupported dtype {t.dtype}: float32 or bfloat16 required")
+
+
+class Workspace:
+    """Zero-initialised device scratch buffers, kept across calls.  The kernels
+    leave their counters zeroed, so a buffer is cleared only when created."""
+
+    def __init__(self, device=None):
+        self.device = torch.device(device or "cuda")
+        self.buffers: dict[str, torch.Tensor] = {}
+
+    def get(self, name: str, nbytes: int) -> torch.Tensor:
+        nbytes = max(int(nbytes), 256)
+        buf = self.buffers.get(name)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+            self.buffers[name] = buf
+        return buf
+
+    def bytes(self) -> int:
+        return sum(b.numel() for b in self.buffers.values())
