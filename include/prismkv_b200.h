@@ -23,7 +23,10 @@
  * that append_index can extend buckets in place.
  *
  * Workspace buffers must be zero-filled before their first use; the kernels
- * leave their counters zeroed again when they finish.
+ * leave their counters zeroed again when they finish.  Counter positions
+ * depend on the call's shape, so a workspace reused for a different shape
+ * must be zero-filled again.  Calls that share a workspace must not overlap
+ * on the GPU.
  */
 #ifndef PRISMKV_B200_H
 #define PRISMKV_B200_H

@@ -193,7 +193,12 @@ build_resolve_kernel(BuildWs ws, int F, int* __restrict__ lens, int* __restrict_
     const long long need0 = ws.need[u];
     const int nb = ws.n_boundary[u];
     if (ws.cut[u] < 0 || need0 <= 0) return;
-    if (nb > ws.bcap) return;  // flagged by the encode pass
+    if (nb > ws.bcap) {
+        // Status already flagged by the encode pass; also stop an append
+        // from committing an incomplete member list.
+        if (tid == 0) atomicOr(ws.flag, 2);
+        return;
+    }
     const long long* B = ws.boundary + (int64_t)u * ws.bcap;
     unsigned long long prefix = ~0ull;  // take everything when need >= nb
     if (need0 < nb) {
@@ -453,7 +458,7 @@ __global__ void append_commit_kernel(const int* __restrict__ flag, int* __restri
     const bool full = *flag != 0;
     for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < F; f += gridDim.x * blockDim.x)
         if (!full) lens[(int64_t)u * F + f] += cnt_new[(int64_t)u * F + f];
-    if (full && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicOr(status, PK_STATUS_BUCKET_FULL);
+    if ((*flag & 1) && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicOr(status, PK_STATUS_BUCKET_FULL);
 }
 
 // ---------------------------------------------------------------------------

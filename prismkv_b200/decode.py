@@ -1,0 +1,166 @@
+"""Batched decode-time retrieval over the U units of one layer.
+
+The device operator of the reference (src/prismkv/native8b.py:34-111
+``Native8B``; kernels/cuda_sm90/native.py:122-189 ``DecodeOps``), shape-
+parametric: a constructor that takes the layer's index and preallocates every
+output, ``route(q)`` (router + budgeted union), ``attention(q, k, v)`` (sparse
+attention with split-KV), ``__call__`` (both) and ``buffer_bytes()``.  Every
+call is asynchronous on the current stream with no host synchronisation, so a
+whole decode step can be captured in a CUDA graph.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import native as nv
+from .index import DeviceIndex, SAEParams, budget_limit
+
+
+class SparseDecode:
+    def __init__(self, index: DeviceIndex, sae, *, heads_per_unit: int = 4, router: str = "q_activation",
+                 query_scale: float = 1.0, query_topk: int | None = None, unique_cap: float | None = None,
+                 budget: int | None = None, terms=("count", "mean", "variance"), splits: int | None = None,
+                 max_history: int | None = None, workspace: nv.Workspace | None = None):
+        if router not in ("q_activation", "moments"):
+            raise ValueError("router must be 'q_activation' or 'moments'")
+        if unique_cap is not None and budget is not None:
+            raise ValueError("give unique_cap or budget, not both")
+        if unique_cap is not None and not 0 <= unique_cap <= 1:
+            raise ValueError("unique_cap must be a fraction in [0,1]")
+        self.index = index
+        self.sae = SAEParams.of(sae, index.device)
+        self.router = router
+        self.G = heads_per_unit
+        self.U, self.F, self.d = index.U, index.F, index.d
+        self.k = min(query_topk or self.sae.query_topk, self.F)
+        self.query_scale = float(query_scale)
+        self.terms = terms
+        self.splits = splits
+        self.ws = workspace or nv.Workspace(index.device)
+        dev = index.device
+        U, G, k = self.U, self.G, self.k
+        self.width = G * k if router == "q_activation" else k
+        self.max_history = int(max_history or index.history)
+        self.order = torch.zeros(U, self.width, dtype=torch.int32, device=dev)
+        self.n_order = torch.zeros(U, dtype=torch.int32, device=dev)
+        self.features = torch.zeros(U, self.width, dtype=torch.int32, device=dev)
+        self.n_features = torch.zeros(U, dtype=torch.int32, device=dev)
+        self.raw = torch.zeros(U, dtype=torch.int64, device=dev)
+        self.count = torch.zeros(U, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.history = torch.full((U,), index.history, dtype=torch.int32, device=dev)
+        self.unique_cap, self.budget = unique_cap, budget
+        lim = budget if budget is not None else budget_limit(index.history, unique_cap)
+        self.limit = torch.full((U,), int(lim), dtype=torch.int64, device=dev)
+        self.id_width = int(min(self.max_history, lim)) if (budget is not None or unique_cap is not None) \
+            else self.max_history
+        self.ids = torch.zeros(U, max(1, self.id_width), dtype=torch.int32, device=dev)
+        self.score = torch.zeros(U, self.F, device=dev) if router == "moments" else None
+        self.out = None
+
+    def sync_history(self) -> None:
+        """Refresh per-unit history and limits after the index grew (append)."""
+        H = self.index.history
+        if H > self.max_history:
+            raise ValueError("index history exceeds max_history given at construction")
+        self.history.fill_(H)
+        lim = self.budget if self.budget is not None else budget_limit(H, self.unique_cap)
+        self.limit.fill_(int(lim))
+
+    # ---------------------------------------------------------------- route
+    def route(self, q: torch.Tensor) -> None:
+        """Router + budgeted union for every unit (core.py:142-167)."""
+        U, G, d, F, k = self.U, self.G, self.d, self.F, self.k
+        if q.shape != (U, G, d) or not q.is_contiguous():
+            raise ValueError(f"contiguous Q[{U},{G},{d}] required")
+        idx = self.index
+        if self.router == "q_activation":
+            nbytes = nv.query("pk_route_qact_workspace_bytes", U, G, F, k)
+            nv.call("pk_route_qact", q, nv.dtype_code(q), None, U, self.sae.W_enc, self.sae.b_enc, self.query_scale,
+                    idx.lens, U, G, d, F, k, self.ws.get(("qact", U, G, F, k), nbytes), nbytes, self.order,
+                    self.n_order, self.width, None, None)
+        else:
+            bits = ((nv.PK_TERM_COUNT if "count" in self.terms else 0)
+                    | (nv.PK_TERM_MEAN if "mean" in self.terms else 0)
+                    | (nv.PK_TERM_VARIANCE if "variance" in self.terms else 0))
+            nbytes = nv.query("pk_route_moments_workspace_bytes", U, G, F)
+            nv.call("pk_route_moments", q, nv.dtype_code(q), idx.mean, idx.var, idx.lens, bits, U, G, d, F, k,
+                    self.ws.get(("moments", U, G, F), nbytes), nbytes, self.score, self.order, self.n_order,
+                    self.width)
+        nv.call("pk_union", idx.offsets, idx.lens, idx.ids, idx.ids.stride(0), self.order, self.n_order, self.width,
+                self.history, self.limit, U, F, self.max_history, self.ids, self.ids.shape[1], self.count,
+                self.features, self.n_features, self.raw, self.status)
+
+    # ------------------------------------------------------------ attention
+    def attention(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, length=None, splits=None,
+                  partial: torch.Tensor | None = None) -> torch.Tensor:
+        """Sparse attention over the routed ids plus the dense tail.
+
+        k, v: [U, total, d] (rows of each unit contiguous) or slot-major
+        [B, total, H_kv, d] with U = B * H_kv.  length: rows per unit
+        (history + tail), an int or an int32 tensor [U]; default all rows.
+        With ``partial`` ([U*G, d+2] fp32) the per-head (m, l, o) partial is
+        written instead of the output (for the sequence-sharded merge)."""
+        U, G, d = self.U, self.G, self.d
+        if k.shape != v.shape or k.stride() != v.stride():
+            raise ValueError("K and V must share shape and strides")
+        if k.dtype != q.dtype or v.dtype != q.dtype:
+            raise ValueError("Q, K and V must share a dtype")
+        if k.dim() == 3:
+            if k.shape[0] != U or k.shape[2] != d:
+                raise ValueError(f"K/V[{U},total,{d}] required")
+            kv_heads, bs, hs, rs, total = 1, k.stride(0), 0, k.stride(1), k.shape[1]
+        elif k.dim() == 4:
+            B, total, Hkv, dd = k.shape
+            if B * Hkv != U or dd != d:
+                raise ValueError("slot-major K/V[B,total,H_kv,d] with B*H_kv == U required")
+            kv_heads, bs, hs, rs = Hkv, k.stride(0), k.stride(2), k.stride(1)
+        else:
+            raise ValueError("K/V must be 3-D or 4-D")
+        if k.stride(-1) != 1:
+            raise ValueError("K/V with contiguous head dimension required")
+        if total < self.index.history:
+            raise ValueError("K/V shorter than the indexed history")
+        if length is None:
+            length = total
+        if isinstance(length, int):
+            lt = self._length_buf(length)
+        else:
+            lt = length
+        S = splits or self.splits or 0
+        if S <= 0:
+            S = max(1, min(256, (3 * 148 + U - 1) // U))
+        nbytes = nv.query("pk_sparse_av_workspace_bytes", U, G, d, S)
+        out = None
+        if partial is None:
+            if self.out is None or self.out.dtype != q.dtype:
+                self.out = torch.empty(U, G, d, dtype=q.dtype, device=q.device)
+            out = self.out
+        nv.call("pk_sparse_av", q, k, v, nv.dtype_code(q), kv_heads, bs, hs, rs, self.ids, self.ids.shape[1],
+                self.count, self.history, lt, U, G, d, S, self.ws.get(("av", U, G, d, S), nbytes), nbytes, out,
+                partial)
+        return out if partial is None else partial
+
+    def _length_buf(self, n: int) -> torch.Tensor:
+        buf = getattr(self, "_len", None)
+        if buf is None:
+            buf = self._len = torch.empty(self.U, dtype=torch.int32, device=self.index.device)
+            self._len_val = None
+        if self._len_val != n:
+            buf.fill_(n)
+            self._len_val = n
+        return buf
+
+    def __call__(self, q, k, v, **kwargs):
+        self.route(q)
+        return self.attention(q, k, v, **kwargs)
+
+    def check(self) -> None:
+        """Synchronise and raise on any condition the kernels flagged."""
+        nv.check_status(self.status, "decode")
+
+    def buffer_bytes(self) -> dict:
+        """Live tensors owned here (index, K/V and model weights excluded)."""
+        out = {name: t.numel() * t.element_size() for name, t in vars(self).items() if isinstance(t, torch.Tensor)}
+        out["workspace"] = self.ws.bytes()
+        return out

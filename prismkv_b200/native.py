@@ -17,6 +17,8 @@ LIB_PATH = Path(__file__).resolve().parent / "libprismkv_b200.so"
 
 PK_F32, PK_BF16 = 0, 1
 PK_TERM_COUNT, PK_TERM_MEAN, PK_TERM_VARIANCE = 1, 2, 4
+STATUS_BUCKET_FULL, STATUS_BOUNDARY_FULL, STATUS_MEMBERS_FULL = 1, 2, 4
+STATUS_BUCKET_TOO_BIG, STATUS_OUT_FULL, STATUS_HISTORY_TOO_LONG = 8, 16, 32
 STATUS_BITS = {
     1: "bucket region full (append)",
     2: "boundary buffer full (build)",
@@ -133,13 +135,15 @@ def dtype_code(t: torch.Tensor) -> int:
 
 class Workspace:
     """Zero-initialised device scratch buffers, kept across calls.  The kernels
-    leave their counters zeroed, so a buffer is cleared only when created."""
+    leave their counters zeroed, so a buffer is cleared only when created; the
+    key names the call and its shape, because counter positions inside a
+    workspace depend on the shape."""
 
     def __init__(self, device=None):
         self.device = torch.device(device or "cuda")
-        self.buffers: dict[str, torch.Tensor] = {}
+        self.buffers: dict = {}
 
-    def get(self, name: str, nbytes: int) -> torch.Tensor:
+    def get(self, name, nbytes: int) -> torch.Tensor:
         nbytes = max(int(nbytes), 256)
         buf = self.buffers.get(name)
         if buf is None or buf.numel() < nbytes:

@@ -1,0 +1,219 @@
+"""GPU tests of the batched decode operator and the edge cases of the path,
+checked against the CPU oracle on the same seeded inputs (integer outputs
+exact; attention within 2e-2 relative L2 in bf16, 1e-3 in fp32)."""
+import numpy as np
+import pytest
+import torch
+
+from gen import bf16_round
+
+pytestmark = pytest.mark.gpu
+TOL_F32, TOL_BF16 = 1e-3, 2e-2
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def pk():
+    from prismkv_b200 import build as b
+    b.build()
+    import prismkv_b200
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return prismkv_b200
+
+
+def clustered(rs, U, n, d, C, G):
+    centers = rs.standard_normal((U, C, d)).astype(np.float32)
+    cid = rs.randint(0, C, size=(U, n))
+    uu = np.arange(U)[:, None]
+    keys = centers[uu, cid] + np.float32(0.3) * rs.standard_normal((U, n, d))
+    vals = rs.standard_normal((U, n, d))
+    qc = rs.randint(0, C, size=(U, G))
+    q = centers[uu, qc] + np.float32(0.3) * rs.standard_normal((U, G, d))
+    return (bf16_round(keys.astype(np.float32)), bf16_round(vals.astype(np.float32)),
+            bf16_round(q.astype(np.float32)))
+
+
+@pytest.fixture(scope="module")
+def batch(pk, oracle):
+    rs = np.random.RandomState(7)
+    U, N, tail, d, C, F, G, k = 8, 4096, 16, 128, 64, 512, 4, 16
+    keys, vals, q = clustered(rs, U, N + tail, d, C, G)
+    W = (rs.standard_normal((F, d)) / np.sqrt(d)).astype(np.float32)
+    b = np.zeros(F, np.float32)
+    dev = torch.device("cuda")
+    K = torch.from_numpy(keys).to(dev).to(torch.bfloat16)
+    V = torch.from_numpy(vals).to(dev).to(torch.bfloat16)
+    Q = torch.from_numpy(q).to(dev).to(torch.bfloat16).contiguous()
+    sae = pk.SAEParams(torch.from_numpy(W).to(dev), torch.from_numpy(b).to(dev), key_mean=8, query_topk=k)
+    idx = pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=True)
+    osae = oracle.SAE(W, b, key_mean=8, query_topk=k)
+    oidx = [oracle.build_index(keys[u, :N], osae, 1.0) for u in range(U)]
+    return dict(U=U, N=N, tail=tail, d=d, F=F, G=G, k=k, keys=keys, vals=vals, q=q, K=K, V=V, Q=Q, sae=sae,
+                idx=idx, osae=osae, oidx=oidx)
+
+
+@pytest.mark.parametrize("budget", [None, 256, 1024])
+def test_batched_decode_matches_oracle(pk, oracle, batch, budget):
+    B = batch
+    cap = None if budget is None else budget / B["N"]
+    op = pk.SparseDecode(B["idx"], B["sae"], heads_per_unit=B["G"], query_scale=1.0, unique_cap=cap)
+    out = op(B["Q"], B["K"], B["V"])
+    torch.cuda.synchronize()
+    op.check()
+    for u in range(B["U"]):
+        counts, ids = B["idx"].csr(u)
+        assert np.array_equal(counts, B["oidx"][u].counts)
+        assert np.array_equal(ids, B["oidx"][u].ids)
+        oids, meta = oracle.select_buckets(B["q"][u], B["oidx"][u], unique_cap=cap, router="q_activation",
+                                           sae=B["osae"], query_scale=1.0, query_topk=B["k"])
+        c = int(op.count[u])
+        assert np.array_equal(op.ids[u, :c].cpu().numpy().astype(np.int64), oids)
+        assert op.features[u, :int(op.n_features[u])].cpu().tolist() == meta["features"]
+        assert int(op.raw[u]) == meta["raw"]
+        ref = oracle.attend(B["q"][u], B["keys"][u], B["vals"][u], oids, B["N"])
+        assert rel_l2(out[u].float().cpu().numpy(), ref) < TOL_BF16
+
+
+def test_splits_agree(pk, batch):
+    B = batch
+    op = pk.SparseDecode(B["idx"], B["sae"], heads_per_unit=B["G"], unique_cap=512 / B["N"])
+    op.route(B["Q"])
+    outs = [op.attention(B["Q"], B["K"], B["V"], splits=s).float().clone() for s in (1, 3, 16, 64)]
+    for o in outs[1:]:
+        assert rel_l2(o.cpu().numpy(), outs[0].cpu().numpy()) < 1e-5
+
+
+def test_sequence_shard_partials_merge(pk, batch):
+    """Emulates the sequence-sharded decode on one GPU: each shard attends
+    over its own id range and the LSE merge of the partials equals the
+    unsharded result."""
+    B = batch
+    U, G, d = B["U"], B["G"], B["d"]
+    op = pk.SparseDecode(B["idx"], B["sae"], heads_per_unit=G, unique_cap=None)
+    full = op(B["Q"], B["K"], B["V"]).float().clone()
+    ids = op.ids.clone()
+    count = op.count.clone()
+    P = 3
+    parts = torch.empty(P, U * G, d + 2, device="cuda")
+    for r in range(P):
+        lo, hi = r * B["N"] // P, (r + 1) * B["N"] // P
+        sel = [(ids[u, :count[u]][(ids[u, :count[u]] >= lo) & (ids[u, :count[u]] < hi)]) for u in range(U)]
+        op.ids.zero_()
+        for u in range(U):
+            op.ids[u, :len(sel[u])] = sel[u]
+            op.count[u] = len(sel[u])
+        # The dense tail belongs to the last shard only.
+        length = torch.full((U,), B["N"] + B["tail"] if r == P - 1 else B["N"], dtype=torch.int32, device="cuda")
+        op.attention(B["Q"], B["K"], B["V"], length=length, partial=parts[r])
+    merged = torch.empty(U * G, d, dtype=torch.float32, device="cuda")
+    from prismkv_b200 import native as nv
+    nv.call("pk_lse_merge", parts, P, U * G, d, merged, nv.PK_F32)
+    assert rel_l2(merged.view(U, G, d).cpu().numpy(), full.cpu().numpy()) < 1e-5
+
+
+def test_slot_major_layout_and_inactive_unit(pk, batch):
+    B = batch
+    U, G, d = B["U"], B["G"], B["d"]
+    Hkv = 4
+    K4 = B["K"].view(U // Hkv, Hkv, -1, d).transpose(1, 2).contiguous()  # [B, T, Hkv, d]
+    V4 = B["V"].view(U // Hkv, Hkv, -1, d).transpose(1, 2).contiguous()
+    op = pk.SparseDecode(B["idx"], B["sae"], heads_per_unit=G, unique_cap=512 / B["N"])
+    op.route(B["Q"])
+    ref = op.attention(B["Q"], B["K"], B["V"]).float().clone()
+    got = op.attention(B["Q"], K4, V4).float().clone()
+    assert rel_l2(got.cpu().numpy(), ref.cpu().numpy()) < 1e-6
+    length = torch.full((U,), B["N"] + B["tail"], dtype=torch.int32, device="cuda")
+    length[-1] = 0
+    masked = op.attention(B["Q"], K4, V4, length=length)
+    assert torch.count_nonzero(masked[-1]).item() == 0
+    assert rel_l2(masked[:-1].float().cpu().numpy(), ref[:-1].cpu().numpy()) < 1e-6
+
+
+def test_fp32_decode_path(pk, oracle, batch):
+    B = batch
+    K, V, Q = B["K"].float(), B["V"].float(), B["Q"].float().contiguous()
+    op = pk.SparseDecode(B["idx"], B["sae"], heads_per_unit=B["G"], unique_cap=256 / B["N"])
+    out = op(Q, K, V)
+    for u in range(B["U"]):
+        oids, _ = oracle.select_buckets(B["q"][u], B["oidx"][u], unique_cap=256 / B["N"], router="q_activation",
+                                        sae=B["osae"], query_scale=1.0, query_topk=B["k"])
+        ref = oracle.attend(B["q"][u], B["keys"][u], B["vals"][u], oids, B["N"])
+        assert rel_l2(out[u].cpu().numpy(), ref) < TOL_F32
+
+
+def test_empty_index_zero_budget_and_tail_only(pk, oracle):
+    dev = torch.device("cuda")
+    rs = np.random.RandomState(3)
+    n, d, F = 300, 128, 64
+    keys = bf16_round(rs.standard_normal((n + 5, d)).astype(np.float32))
+    vals = bf16_round(rs.standard_normal((n + 5, d)).astype(np.float32))
+    q = bf16_round(rs.standard_normal((4, d)).astype(np.float32))
+    W = -np.abs(rs.standard_normal((F, d))).astype(np.float32) * 0
+    b = np.full(F, -1.0, np.float32)  # every activation <= 0: empty index
+    sae = pk.SAEParams(torch.from_numpy(W).to(dev), torch.from_numpy(b).to(dev), key_mean=8, query_topk=8)
+    K = torch.from_numpy(keys).to(dev).bfloat16()
+    V = torch.from_numpy(vals).to(dev).bfloat16()
+    Q = torch.from_numpy(q).to(dev).bfloat16()
+    idx = pk.build_index(K[:n], sae, 1.0)
+    assert int(idx.counts.sum()) == 0
+    ids, meta = pk.select_buckets(Q, idx, router="q_activation", sae=sae, query_scale=1.0, query_topk=8)
+    assert len(ids) == 0 and meta["features"] == [] and meta["candidate_buckets"] == 0
+    out = pk.attend(Q, K, V, ids, n)
+    ref = oracle.attend(q, keys, vals, np.zeros(0, np.int64), n)
+    assert rel_l2(out.float().cpu().numpy(), ref) < TOL_BF16
+    # zero budget on a populated index
+    W2 = (rs.standard_normal((F, d)) / np.sqrt(d)).astype(np.float32)
+    sae2 = pk.SAEParams(torch.from_numpy(W2).to(dev), torch.zeros(F, device=dev), key_mean=8, query_topk=8)
+    idx2 = pk.build_index(K[:n], sae2, 1.0)
+    ids2, meta2 = pk.select_buckets(Q, idx2, unique_cap=0.0, router="q_activation", sae=sae2, query_scale=1.0,
+                                    query_topk=8)
+    assert len(ids2) == 0 and meta2["raw"] == 0 and meta2["limit"] == 0
+    # no old rows and no tail: zeros (core.py:180-181)
+    out0 = pk.attend(Q, K[:n], V[:n], ids2, n)
+    assert torch.count_nonzero(out0).item() == 0
+
+
+def test_tied_activations_follow_flat_index_order(pk, oracle):
+    """All activations equal: the budget takes ties by ascending flat index
+    (core.py:24), as the reference's own tie fixture."""
+    dev = torch.device("cuda")
+    d = 128
+    W = np.zeros((3, d), np.float32)
+    W[0, 0] = W[1, 0] = W[2, 1] = 1.0
+    keys = np.ones((9, d), np.float32)
+    sae = pk.SAEParams(torch.from_numpy(W).to(dev), torch.zeros(3, device=dev), key_mean=2, query_topk=2)
+    idx = pk.build_index(torch.from_numpy(keys).to(dev), sae, 1.0, center=torch.zeros(d, device=dev))
+    osae = oracle.SAE(W, np.zeros(3, np.float32), key_mean=2, query_topk=2)
+    oidx = oracle.build_index(keys, osae, 1.0, center=np.zeros(d, np.float32))
+    counts, ids = idx.dev.csr(0)
+    assert counts.tolist() == [6, 6, 6] == oidx.counts.tolist()
+    assert np.array_equal(ids, oidx.ids)
+
+
+def test_append_grows_regions_when_full(pk, oracle):
+    """Appends that overflow a bucket region repack the index and retry;
+    the result equals the oracle's append_index."""
+    dev = torch.device("cuda")
+    rs = np.random.RandomState(11)
+    n, d, F = 512, 128, 64
+    keys = bf16_round((rs.standard_normal((n + 256, d)) + 1).astype(np.float32))
+    W = (rs.standard_normal((F, d)) / np.sqrt(d)).astype(np.float32)
+    sae = pk.SAEParams(torch.from_numpy(W).to(dev), torch.zeros(F, device=dev), key_mean=8, query_topk=8)
+    K = torch.from_numpy(keys).to(dev).bfloat16()
+    idx = pk.DeviceIndex.build(K[:n], sae, 1.0, moments=True, slack_frac=0.0, slack_min=0)
+    osae = oracle.SAE(W, np.zeros(F, np.float32), key_mean=8, query_topk=8)
+    oidx = oracle.build_index(keys[:n], osae, 1.0)
+    for lo in range(n, n + 256, 64):
+        idx.append(K[lo:lo + 64], sae, 1.0)
+        oidx = oracle.append_index(oidx, keys[lo:lo + 64], osae, 1.0)
+    counts, ids = idx.csr(0)
+    assert idx.history == oidx.history
+    assert np.array_equal(counts, oidx.counts)
+    assert np.array_equal(ids, oidx.ids)
+    assert np.array_equal(idx.mean[0].cpu().numpy().view(np.uint32), oidx.mean.view(np.uint32))
+    assert np.array_equal(idx.var[0].cpu().numpy().view(np.uint32), oidx.variance.view(np.uint32))
