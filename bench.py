@@ -1,0 +1,471 @@
+#!/usr/bin/env python
+"""Decode-attention benchmark: tokens/s at 128K context, config-3 shapes.
+
+One decode step = for each of 32 layers: q_activation routing (SAE encode +
+per-head top-32 + aggregation), budgeted bucket union (4096 tokens), and
+sparse attention over the selected rows plus the dense generated tail, for
+B=4 sequences x 8 KV heads (U = 32 units) with 4 query heads each, history
+131072 tokens, F = 16384 SAE features.  Inputs are seeded synthetic tensors
+with the config's shapes (clustered keys, iid values); the index is built by
+this library's own build kernels before timing.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU (torchrun, one rank per GPU): every rank serves its own batch of
+B=4 sequences (batch x KV-head sharding, no collective on the path), so the
+job's tokens/s is the sum over ranks -- weak scaling.  Timing is on the
+device with CUDA events, max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode attn tokens/s/GPU at 128K ctx; sparse-AV HBM GB/s vs 8 TB/s peak"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--layers", type=int, default=32)
+    p.add_argument("--batch", type=int, default=4)
+    p.add_argument("--kv-heads", type=int, default=8)
+    p.add_argument("--q-per-kv", type=int, default=4)
+    p.add_argument("--history", type=int, default=131072)
+    p.add_argument("--features", type=int, default=16384)
+    p.add_argument("--query-topk", type=int, default=32)
+    p.add_argument("--key-mean", type=int, default=8)
+    p.add_argument("--budget", type=int, default=4096)
+    p.add_argument("--clusters", type=int, default=1024)
+    p.add_argument("--max-steps", type=int, default=256, help="decode positions the KV cache holds")
+    p.add_argument("--update-interval", type=int, default=4096, help="index append cadence (tokens)")
+    p.add_argument("--no-graph", action="store_true", help="eager launches instead of CUDA-graph replay")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--seed", type=int, default=0)
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler
+# ---------------------------------------------------------------------------
+
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), [x.strip() for x in line.split(",")]))
+
+    def mark(self):
+        return time.time()
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0, t1):
+        rows = [s for t, s in self.samples if t0 - 0.05 <= t <= t1 + 0.05]
+        if not rows:
+            rows = [s for t, s in self.samples][-3:]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = sorted(v for v in (num(r[1]) for r in rows) if v is not None)
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": num(rows[0][2]),
+                "power_w_max": max((num(r[3]) or 0) for r in rows), "reasons": sorted(reasons),
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+
+def gen_layer(torch, dev, g, U, T, d, C):
+    """Clustered keys (centers ~ N(0,1), noise sigma 0.3) and iid values, bf16."""
+    centers = torch.randn(U, C, d, device=dev, generator=g)
+    cid = torch.randint(0, C, (U, T), device=dev, generator=g)
+    K = torch.empty(U, T, d, device=dev, dtype=torch.bfloat16)
+    V = torch.empty(U, T, d, device=dev, dtype=torch.bfloat16)
+    chunk = 16384
+    for lo in range(0, T, chunk):
+        hi = min(T, lo + chunk)
+        c = torch.gather(centers, 1, cid[:, lo:hi, None].expand(U, hi - lo, d))
+        K[:, lo:hi] = (c + 0.3 * torch.randn(U, hi - lo, d, device=dev, generator=g)).to(torch.bfloat16)
+        V[:, lo:hi] = torch.randn(U, hi - lo, d, device=dev, generator=g).to(torch.bfloat16)
+    return centers, K, V
+
+
+def gen_queries(torch, dev, g, centers, n, G):
+    U, C, d = centers.shape
+    cid = torch.randint(0, C, (n, U, G), device=dev, generator=g)
+    c = centers[torch.arange(U, device=dev)[None, :, None], cid]
+    return (c + 0.3 * torch.randn(n, U, G, d, device=dev, generator=g)).to(torch.bfloat16)
+
+
+def run_ours(a):
+    import torch
+    import torch.distributed as dist
+    import prismkv_b200 as pk
+    from prismkv_b200 import native as nv
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+
+    L, B, Hkv, G, d = a.layers, a.batch, a.kv_heads, a.q_per_kv, 128
+    U = B * Hkv
+    N, F, k = a.history, a.features, a.query_topk
+    T = N + a.max_steps
+    total_steps = a.warmup + a.steps
+    if total_steps > a.max_steps:
+        raise SystemExit("warmup + steps exceeds the KV cache's decode positions (--max-steps)")
+    g = torch.Generator(device=dev)
+    t_setup = time.time()
+    layers = []
+    ws = nv.Workspace(dev)
+    build_s = 0.0
+    for l in range(L):
+        g.manual_seed(a.seed * 1_000_003 + rank * 10_007 + l)
+        centers, K, V = gen_layer(torch, dev, g, U, T, d, a.clusters)
+        W = torch.randn(F, d, device=dev, generator=g) / math.sqrt(d)
+        sae = pk.SAEParams(W, torch.zeros(F, device=dev), key_mean=a.key_mean, query_topk=k)
+        torch.cuda.synchronize()
+        tb = time.time()
+        idx = pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=False, workspace=ws)
+        torch.cuda.synchronize()
+        build_s += time.time() - tb
+        op = pk.SparseDecode(idx, sae, heads_per_unit=G, query_scale=1.0, budget=a.budget,
+                             max_history=N + a.max_steps, workspace=ws)
+        Q = gen_queries(torch, dev, g, centers, total_steps, G)
+        layers.append(dict(K=K, V=V, idx=idx, op=op, Q=Q))
+        del centers
+    ws.buffers.pop(("build",), None)
+    for key in [k_ for k_ in ws.buffers if isinstance(k_, tuple) and k_[0] == "build"]:
+        del ws.buffers[key]
+    torch.cuda.empty_cache()
+    # Per-step lengths: history + the tokens generated so far (dense tail).
+    lens = torch.stack([torch.full((U,), N + s + 1, dtype=torch.int32, device=dev) for s in range(total_steps)])
+    setup_s = time.time() - t_setup
+
+    # Static inputs for graph replay.
+    q_static = torch.stack([lay["Q"][0] for lay in layers]).contiguous()   # [L, U, G, d]
+    len_static = lens[0].clone()
+    outs = torch.empty(L, U, G, d, dtype=torch.bfloat16, device=dev)
+
+    def step_body(av_events=None):
+        for l, lay in enumerate(layers):
+            q = q_static[l]
+            lay["op"].route(q)
+            if av_events is not None:
+                av_events[l][0].record()
+            o = lay["op"].attention(q, lay["K"], lay["V"], length=len_static)
+            if av_events is not None:
+                av_events[l][1].record()
+            outs[l].copy_(o)
+
+    def load_step(s):
+        for l, lay in enumerate(layers):
+            q_static[l].copy_(lay["Q"][s])
+        len_static.copy_(lens[s])
+
+    # Warm up eagerly once (creates every workspace), then capture.
+    load_step(0)
+    step_body()
+    torch.cuda.synchronize()
+    for lay in layers:
+        lay["op"].check()
+    graph = None
+    if not a.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        s_cap = torch.cuda.Stream()
+        s_cap.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s_cap):
+            with torch.cuda.graph(graph, stream=s_cap):
+                step_body()
+        torch.cuda.current_stream().wait_stream(s_cap)
+        torch.cuda.synchronize()
+
+    def run_step(s):
+        load_step(s)
+        if graph is not None:
+            graph.replay()
+        else:
+            step_body()
+
+    for s in range(a.warmup):
+        run_step(s)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.2)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.time()
+    e0.record()
+    for s in range(a.warmup, total_steps):
+        run_step(s)
+    e1.record()
+    torch.cuda.synchronize()
+    t1 = time.time()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    for lay in layers:
+        lay["op"].check()
+
+    # Per-launch sparse-attention timing: the same steps, eager, with an
+    # event pair around every attention launch; and the algorithmic bytes of
+    # each launch from the routed counts.
+    av_ms, av_bytes, step_eager_ms = [], [], []
+    for s in range(a.warmup, total_steps):
+        load_step(s)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+        es0, es1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        es0.record()
+        step_body(evs)
+        es1.record()
+        torch.cuda.synchronize()
+        step_eager_ms.append(es0.elapsed_time(es1))
+        tail = s + 1
+        for l, lay in enumerate(layers):
+            av_ms.append(evs[l][0].elapsed_time(evs[l][1]))
+            cnt = lay["op"].count.long()
+            rows = int(cnt.sum().item()) + U * tail
+            av_bytes.append(rows * d * 2 * 2 + 4 * int(cnt.sum().item()) + 2 * U * G * d * 2)
+    clocks_t1 = time.time()
+
+    # End to end through the public API with host buffers: pinned host
+    # queries -> device, full step, outputs -> pinned host, every step.
+    h_q = torch.stack([torch.stack([lay["Q"][s] for lay in layers]) for s in range(total_steps)]).cpu().pin_memory()
+    h_out = torch.empty(L, U, G, d, dtype=torch.bfloat16).pin_memory()
+    ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ee0.record()
+    for s in range(a.warmup, total_steps):
+        q_static.copy_(h_q[s], non_blocking=True)
+        len_static.copy_(lens[s])
+        if graph is not None:
+            graph.replay()
+        else:
+            step_body()
+        h_out.copy_(outs, non_blocking=True)
+    ee1.record()
+    torch.cuda.synchronize()
+    e2e_ms = ee0.elapsed_time(ee1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    clocks.stop()
+    clk = clocks.summary(t0, t1)
+
+    tokens = world * B * a.steps
+    value = tokens / (ms / 1e3)
+    e2e = tokens / (e2e_ms / 1e3)
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get("hbm_gbs", 6650.0)
+    mean_av_ms = sum(av_ms) / len(av_ms)
+    mean_bytes = sum(av_bytes) / len(av_bytes)
+    achieved = mean_bytes / (mean_av_ms / 1e3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "sparse_av_traffic.json"
+    if tfile.exists():
+        try:
+            tj = json.loads(tfile.read_text())
+            traffic = tj["dram_bytes_per_row"] * (mean_bytes / (d * 2 * 2))
+        except (OSError, ValueError, KeyError):
+            traffic = None
+    launches_per_step = L * 4  # encode + select + union + attention per layer
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": a.steps,
+        "warmup": a.warmup,
+        "ms_per_step": round(ms / a.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded clustered keys, iid values, random-init SAE)",
+        "config": {"workload": "config3: Llama-3-8B-shaped decode attention path, 32 layers",
+                   "layers": L, "batch_per_gpu": B, "kv_heads": Hkv, "q_per_kv": G, "head_dim": d,
+                   "history": N, "features": F, "query_topk": k, "budget": a.budget, "key_mean": a.key_mean,
+                   "router": "q_activation", "update_interval": a.update_interval,
+                   "graph": graph is not None, "l2": "inputs larger than L2 (KV and index per step >> 126 MB)",
+                   "parallelism": f"units{world}", "setup_s": round(setup_s, 1), "build_s": round(build_s, 1)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": "sparse_av_bf16_kernel", "avg_launch_us": round(mean_av_ms * 1e3, 2),
+                     "algorithmic_bytes_per_launch": int(mean_bytes),
+                     "share_of_eager_step": round(sum(av_ms) / sum(step_eager_ms), 3),
+                     "peak_source": "measured" if "hbm_gbs" in peaks else "fallback"},
+        "e2e": {"value": round(e2e, 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(L * U * G * d * 2 + U * 4),
+                "d2h_bytes_per_step": int(L * U * G * d * 2)},
+        "gpu_launches": launches_per_step * a.steps,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_rate(a, seconds=a.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        del graph
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference path restated by the oracle, on a bounded sample
+# ---------------------------------------------------------------------------
+
+def cpu_rate(a, seconds: float = 10.0) -> dict:
+    """Times the oracle's route + select + attend for a sample of config-3
+    units on the host cores (one unit per thread) and scales to a full
+    decode step (all units x layers).  The sample's bucket index is a
+    synthetic CSR with key_mean memberships per token (its build is not
+    timed)."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    import oracle
+    from gen import bf16_round
+
+    cores = os.cpu_count() or 1
+    n_units = max(1, min(cores, a.batch * a.kv_heads))
+    N, F, d, G, k = a.history, a.features, 128, a.q_per_kv, a.query_topk
+    tail = 128
+    rs = np.random.RandomState(1234)
+    W = (rs.standard_normal((F, d)) / np.sqrt(d)).astype(np.float32)
+    sae = oracle.SAE(W, np.zeros(F, np.float32), key_mean=a.key_mean, query_topk=k)
+    units = []
+    for u in range(n_units):
+        C = a.clusters
+        centers = rs.standard_normal((C, d)).astype(np.float32)
+        cid = rs.randint(0, C, N + tail)
+        keys = bf16_round(centers[cid] + np.float32(0.3) * rs.standard_normal((N + tail, d)).astype(np.float32))
+        vals = bf16_round(rs.standard_normal((N + tail, d)).astype(np.float32))
+        q = bf16_round(centers[rs.randint(0, C, G)] + np.float32(0.3) * rs.standard_normal((G, d)).astype(np.float32))
+        feats = rs.randint(0, F, size=(N, a.key_mean))
+        tok = np.repeat(np.arange(N), a.key_mean)
+        order = np.lexsort((tok, feats.reshape(-1)))
+        fs, ts = feats.reshape(-1)[order], tok[order]
+        keep = np.ones(len(fs), bool)
+        keep[1:] = (fs[1:] != fs[:-1]) | (ts[1:] != ts[:-1])
+        fs, ts = fs[keep], ts[keep]
+        counts = np.bincount(fs, minlength=F).astype(np.int64)
+        offsets = np.zeros(F + 1, np.int64)
+        np.cumsum(counts, out=offsets[1:])
+        idx = oracle.FeatureIndex(N, np.zeros(d, np.float32), counts, None, None, offsets, ts.astype(np.int64))
+        units.append((q, keys, vals, idx))
+    cap = a.budget / N
+
+    def one(unit):
+        q, keys, vals, idx = unit
+        ids, _ = oracle.select_buckets(q, idx, unique_cap=cap, router="q_activation", sae=sae, query_scale=1.0,
+                                       query_topk=k)
+        oracle.attend(q, keys, vals, ids, N)
+
+    reps, t_total = 0, 0.0
+    with ThreadPoolExecutor(max_workers=n_units) as ex:
+        list(ex.map(one, units))  # warm
+        while t_total < seconds or reps == 0:
+            t0 = time.perf_counter()
+            list(ex.map(one, units))
+            t_total += time.perf_counter() - t0
+            reps += 1
+    per_batch = t_total / reps                       # n_units units in parallel
+    U_total = a.batch * a.kv_heads * a.layers
+    step_s = per_batch * U_total / n_units
+    return {"value": round(a.batch / step_s, 4), "unit": "tokens/s", "cores": n_units, "kind": "port",
+            "sample": f"{n_units} config-3 units (history {N}, F {F}, k {k}, budget {a.budget}, tail {tail}) "
+                      f"x {reps} reps, one unit per thread, scaled to {U_total} units per step; synthetic CSR "
+                      f"index, build not timed"}
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    base = cpu_rate(a, seconds=max(1.0, a.cpu_seconds))
+    line = {"metric": METRIC, "value": base["value"], "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps,
+            "warmup": a.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "config3: Llama-3-8B-shaped decode attention path, 32 layers",
+                       "history": a.history, "features": a.features, "budget": a.budget},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)

@@ -124,8 +124,13 @@ class SparseDecode:
         if length is None:
             length = total
         if isinstance(length, int):
+            if not self.index.history <= length <= total and length != 0:
+                raise ValueError("length must lie in [history, K/V rows] (0 marks an inactive unit)")
             lt = self._length_buf(length)
         else:
+            # Device lengths are the caller's contract: each in [history, rows] or 0.
+            if length.dtype != torch.int32 or tuple(length.shape) != (U,):
+                raise ValueError(f"length tensor must be int32 [{U}]")
             lt = length
         S = splits or self.splits or 0
         if S <= 0:

@@ -152,7 +152,7 @@ class DeviceIndex:
         dt = nv.dtype_code(new_keys)
         for _ in range(6):
             nbytes = nv.query("pk_append_workspace_bytes", U, n, d, self.F, sae.key_mean, bcap)
-            buf = ws.get(("append", U, n, F, bcap), nbytes)
+            buf = ws.get(("append", U, n, self.F, bcap), nbytes)
             status.zero_()
             nv.call("pk_append_index", new_keys, dt, us, rs, n, self.center, float(key_scale), sae.W_enc, sae.b_enc,
                     U, d, self.F, sae.key_mean, self.history, self.offsets, self.lens, self.ids, self.ids.stride(0),
