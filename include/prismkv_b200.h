@@ -149,6 +149,29 @@ int pk_sparse_av(uint64_t q, uint64_t k, uint64_t v, int dtype,
  * generalises the in-GPU split merge of av_tuned.cu:54-61. */
 int pk_lse_merge(uint64_t partial, int P, int UG, int d, uint64_t out, int dtype, uint64_t stream);
 
+/* Sparse attention for callers that cannot allocate device memory.
+ * This entry point has no counterpart in the reference.  It exists for
+ * embedders that cannot hand the library a workspace: a host that reserved
+ * all device memory for its own pool up front (where an extra cudaMalloc
+ * would fail or fragment it), or a foreign-language caller that binds only
+ * this C ABI and has no device allocator of its own.
+ * Same arguments and results as pk_sparse_av without the workspace and the
+ * partial output; the split scratch lives in a library-owned device array of
+ * PK_SPARSE_AV_NOALLOC_SCRATCH_BYTES (4 MiB) that every GPU loading the
+ * library holds until exit.  A shape whose scratch
+ * (pk_sparse_av_workspace_bytes) exceeds that returns
+ * PK_ERR_SCRATCH_LIMIT; pass fewer splits (splits == 1 needs none).
+ * The first call on each device looks the array up with the device current;
+ * make that first call before any stream capture.  All calls share the one
+ * array, so calls that overlap on the GPU (other streams, other threads)
+ * race: serialise them.  Nothing is allocated or freed. */
+#define PK_SPARSE_AV_NOALLOC_SCRATCH_BYTES (4u << 20)
+#define PK_ERR_SCRATCH_LIMIT (-4)
+int pk_sparse_av_noalloc(uint64_t q, uint64_t k, uint64_t v, int dtype,
+                         int kv_heads, int64_t kv_batch_stride, int64_t kv_head_stride, int64_t kv_row_stride,
+                         uint64_t ids, int64_t ids_stride, uint64_t count, uint64_t history, uint64_t length,
+                         int U, int G, int d, int splits, uint64_t out, uint64_t stream);
+
 /* ------------------------------------------------------------------------
  * Index build (a5 + a6) and append (a7).
  * Replaces IndexBuilder.group + Kernels.positive_top + moments + build_bits

@@ -497,3 +497,67 @@ extern "C" int pk_lse_merge(uint64_t partial, int P, int UG, int d, uint64_t out
     PK_CHECK_LAUNCH();
     return PK_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant (no counterpart in the reference).  Some embedders
+// cannot give the library a workspace -- a host that pre-reserved all device
+// memory for its own pool, or a foreign-language caller of this C ABI with no
+// device allocator -- so the split scratch lives here, in a file-scope device
+// array every GPU that loads the library keeps until exit.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace pk {
+static __device__ __align__(256) unsigned char g_av_noalloc_scratch[PK_SPARSE_AV_NOALLOC_SCRATCH_BYTES];
+
+// The array's name is only a host-side stand-in; its device address is looked
+// up once per device, with that device current.
+static void* noalloc_scratch_address(int* rc) {
+    static std::mutex mu;
+    static void* addr[128] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 128) {
+        *rc = e != cudaSuccess ? (int)e : PK_ERR_ARG;
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_av_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            *rc = e != cudaSuccess ? (int)e : PK_ERR_ARG;
+            return nullptr;
+        }
+        addr[dev] = p;
+    }
+    *rc = 0;
+    return addr[dev];
+}
+}  // namespace pk
+
+extern "C" int pk_sparse_av_noalloc(uint64_t q, uint64_t k, uint64_t v, int dtype, int kv_heads,
+                                    int64_t kv_batch_stride, int64_t kv_head_stride, int64_t kv_row_stride,
+                                    uint64_t ids, int64_t ids_stride, uint64_t count, uint64_t history,
+                                    uint64_t length, int U, int G, int d, int splits, uint64_t out,
+                                    uint64_t stream) {
+    if (U < 1 || G < 1 || G > kAvMaxG || !out) return PK_ERR_ARG;
+    if (splits <= 0) splits = default_splits(U);
+    if (splits > 256) return PK_ERR_ARG;
+    const size_t need = pk_sparse_av_workspace_bytes(U, G, d, splits);
+    if (splits > 1 && need > PK_SPARSE_AV_NOALLOC_SCRATCH_BYTES) return PK_ERR_SCRATCH_LIMIT;
+    int rc = 0;
+    void* scratch = noalloc_scratch_address(&rc);
+    if (!scratch) return rc;
+    if (splits > 1) {
+        // The arrival counters must start at zero; the array keeps whatever
+        // the previous call left, so clear them on this call's stream.
+        const size_t part = (size_t)U * G * splits * (d + 2) * sizeof(float);
+        const size_t counters = (part + 255) / 256 * 256;
+        cudaError_t e = cudaMemsetAsync((char*)scratch + counters, 0, (size_t)U * sizeof(int), (cudaStream_t)stream);
+        if (e != cudaSuccess) return (int)e;
+    }
+    return pk_sparse_av(q, k, v, dtype, kv_heads, kv_batch_stride, kv_head_stride, kv_row_stride, ids, ids_stride,
+                        count, history, length, U, G, d, splits, (uint64_t)scratch,
+                        (uint64_t)PK_SPARSE_AV_NOALLOC_SCRATCH_BYTES, out, 0, stream);
+}
