@@ -51,6 +51,7 @@ extern "C" {
 #define PK_STATUS_BUCKET_TOO_BIG 8    /* build: a bucket exceeds the sort limit */
 #define PK_STATUS_OUT_FULL 16         /* union: output row too short            */
 #define PK_STATUS_HISTORY_TOO_LONG 32 /* union: history above max_history       */
+#define PK_STATUS_NEEDS_EXACT 64      /* build: bounds undecided, rerun exactly  */
 
 /* Element types. */
 #define PK_F32 0
@@ -78,10 +79,18 @@ int pk_supported_head_dim(int d);
  *   order[u, 0..n_order[u])  candidate buckets, descending score, ties by id
  *   score[u, F]   (optional, 0 to skip) the reference's full score vector
  *   topk[u, G, k] (optional) each head's picks in rank order
+ * With w_bf16[F, d] and w_norm[F] from pk_sae_prepare (both non-zero, topk
+ * not requested) the activations are first approximated on the tensor cores
+ * and only features whose error-bounded value can reach the top-k are
+ * recomputed exactly -- the same results, far fewer fp32 operations.
  * ------------------------------------------------------------------------ */
+/* Per-SAE preparation for the fast routing path: bf16 copy of W_enc and an
+ * upper bound of each row's L2 norm. */
+int pk_sae_prepare(uint64_t w_enc, int F, int d, uint64_t w_bf16, uint64_t w_norm, uint64_t stream);
 size_t pk_route_qact_workspace_bytes(int U, int G, int F, int k);
 int pk_route_qact(uint64_t q, int q_dtype, uint64_t units, int n_units,
-                  uint64_t w_enc, uint64_t b_enc, float query_scale, uint64_t counts,
+                  uint64_t w_enc, uint64_t b_enc, uint64_t w_bf16, uint64_t w_norm,
+                  float query_scale, uint64_t counts,
                   int U, int G, int d, int F, int k,
                   uint64_t workspace, uint64_t workspace_bytes,
                   uint64_t order, uint64_t n_order, int order_stride,
@@ -187,6 +196,12 @@ int pk_key_center(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_str
                   int U, int64_t N, int d, uint64_t center, uint64_t stream);
 
 /* Builds buckets for U units sharing one SAE (w_enc[F, d], b_enc[F]).
+ * With w_bf16 and w_norm from pk_sae_prepare (both non-zero), activations
+ * are first approximated on the tensor cores with a per-entry error bound;
+ * only entries the bounds cannot place above or below the budget threshold
+ * are recomputed exactly (same memberships).  If the bounds cannot bracket
+ * the threshold (degenerate inputs) PK_STATUS_NEEDS_EXACT is raised and the
+ * caller reruns without w_bf16 / w_norm (append_index then changes nothing).
  * Token ids are written as token_base + t.  Bucket regions get
  * ceil(len*slack_frac) + slack_min spare slots for later appends;
  * ids_stride must be >= pk_build_ids_capacity(...).  */
@@ -194,6 +209,7 @@ int64_t pk_build_ids_capacity(int64_t N, int F, int key_mean, float slack_frac, 
 size_t pk_build_workspace_bytes(int U, int64_t N, int F, int key_mean, int64_t boundary_capacity);
 int pk_build_index(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride,
                    uint64_t center, float key_scale, uint64_t w_enc, uint64_t b_enc,
+                   uint64_t w_bf16, uint64_t w_norm,
                    int U, int64_t N, int d, int F, int key_mean, int64_t token_base,
                    float slack_frac, int slack_min,
                    uint64_t offsets, uint64_t lens, uint64_t ids, int64_t ids_stride,
@@ -215,6 +231,7 @@ int pk_summarize(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stri
 size_t pk_append_workspace_bytes(int U, int64_t n_new, int d, int F, int key_mean, int64_t boundary_capacity);
 int pk_append_index(uint64_t new_keys, int dtype, int64_t unit_stride, int64_t row_stride, int64_t n_new,
                     uint64_t center, float key_scale, uint64_t w_enc, uint64_t b_enc,
+                    uint64_t w_bf16, uint64_t w_norm,
                     int U, int d, int F, int key_mean, int64_t history,
                     uint64_t offsets, uint64_t lens, uint64_t ids, int64_t ids_stride,
                     uint64_t mean, uint64_t var,

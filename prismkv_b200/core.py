@@ -140,8 +140,10 @@ def _route(q, dev: DeviceIndex, *, router, sae, query_scale, query_topk, terms, 
     order = torch.empty(1, max(1, G * k), dtype=torch.int32, device=device)
     n = torch.empty(1, dtype=torch.int32, device=device)
     nbytes = nv.query("pk_route_qact_workspace_bytes", 1, G, F, k)
-    nv.call("pk_route_qact", qc, nv.dtype_code(qc), None, 1, p.W_enc, p.b_enc, float(query_scale), dev.lens, 1, G, d,
-            F, k, ws.get(("qact", 1, G, F, k), nbytes), nbytes, order, n, order.shape[1], score if want_score else None, None)
+    wb, wn = p.prepared()
+    nv.call("pk_route_qact", qc, nv.dtype_code(qc), None, 1, p.W_enc, p.b_enc, wb, wn, float(query_scale), dev.lens, 1,
+            G, d, F, k, ws.get(("qact", 1, G, F, k), nbytes), nbytes, order, n, order.shape[1],
+            score if want_score else None, None)
     return score[0], order[0, :int(n.item())]
 
 

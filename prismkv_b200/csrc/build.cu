@@ -13,10 +13,11 @@
 // products run as one sequential FMA chain over d, the order the reference's
 // F.linear takes for a many-row block, so memberships are bit-identical.
 #include "common.cuh"
+#include "mma.cuh"
 
 namespace pk {
 
-constexpr int kBD = 128;             // head dim compiled for the build
+constexpr int kBD = 128;            // head dim compiled for the build
 constexpr int kBT = 128;             // tokens per CTA tile
 constexpr int kBF = 128;             // features per CTA tile
 constexpr int kBThreads = 256;       // 16 x 16 threads, 8 x 8 outputs each
@@ -429,6 +430,11 @@ __global__ void append_check_kernel(const int* __restrict__ offsets, const int* 
     }
 }
 
+__global__ void status_gate_kernel(const int* __restrict__ status, int* __restrict__ flag) {
+    if (threadIdx.x == 0 && (*status & (PK_STATUS_NEEDS_EXACT | PK_STATUS_BOUNDARY_FULL | PK_STATUS_MEMBERS_FULL)))
+        atomicOr(flag, 2);
+}
+
 // A refused append zeroes the new counts so nothing downstream (sort,
 // moments, commit) touches the index.
 __global__ void append_gate_kernel(const int* __restrict__ flag, int* __restrict__ cnt_new, int64_t n) {
@@ -514,6 +520,354 @@ int run_encode_select(const T* keys, int64_t unit_stride, int64_t row_stride, in
     return PK_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Bound-filtered build: approximate activations on the tensor cores with a
+// per-entry error bound, global thresholds that bracket the exact budget
+// threshold, exact recomputation of only the entries the bounds cannot decide.
+// ---------------------------------------------------------------------------
+
+constexpr int kFBins = 8192;          // bins of the bounds' float bits >> 18
+constexpr int kFShift = 18;
+constexpr int kFThreads = 256;        // 8 warps x 16 tokens, 128 features
+
+struct FastWs {
+    int* histL;         // [U, 8192] positive lower bounds
+    int* histU;         // [U, 8192] positive upper bounds
+    int* cutL;          // [U] bin of the count-th largest lower bound (-1: fewer positives)
+    int* cutU;          // [U] same for the upper bound
+    int* n_amb;         // [U]
+    long long* amb;     // [U, acap] flat indices to recompute exactly
+    int64_t acap;
+};
+
+size_t fast_counters_bytes(int U) {
+    return 2 * align256((size_t)U * kFBins * 4) + 3 * align256((size_t)U * 4);
+}
+size_t fast_bytes(int U, int64_t acap) { return fast_counters_bytes(U) + align256((size_t)U * acap * 8); }
+
+FastWs carve_fast(void* base, int U, int64_t acap) {
+    FastWs w;
+    char* p = (char*)base;
+    w.histL = (int*)p; p += align256((size_t)U * kFBins * 4);
+    w.histU = (int*)p; p += align256((size_t)U * kFBins * 4);
+    w.cutL = (int*)p; p += align256((size_t)U * 4);
+    w.cutU = (int*)p; p += align256((size_t)U * 4);
+    w.n_amb = (int*)p; p += align256((size_t)U * 4);
+    w.amb = (long long*)p;
+    w.acap = acap;
+    return w;
+}
+
+__device__ __forceinline__ int fbin(float v) { return (int)(__float_as_uint(v) >> kFShift); }
+
+// Tile of 128 tokens x 128 features; warp w owns tokens 16w..16w+15.
+// v ~= x . W_f + b_f from bf16 operands (mma.sync, fp32 accumulate),
+// |v - exact| <= e = 2^-6 |x| |W_f| + 2^-20 |v|  (operand rounding 2^-8
+// each, accumulation, and the exact order's own rounding, with margin).
+// PASS 1: histograms of the positive bounds L = v - e and U = v + e.
+// PASS 2: L above every upper bound's cut -> member; U below the lower
+// bound's cut -> not a member; otherwise recompute exactly.
+template <int PASS, typename T>
+__global__ void __launch_bounds__(kFThreads)
+build_approx_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride, int64_t N,
+                    const float* __restrict__ center, float key_scale, const __nv_bfloat16* __restrict__ Wb,
+                    const float* __restrict__ bias, const float* __restrict__ wn, int F, BuildWs ws, FastWs fw,
+                    int* __restrict__ lens, int* __restrict__ status) {
+    extern __shared__ __align__(128) uint8_t fsm[];
+    uint8_t* Xs = fsm;                          // [128 rows][256 B] swizzled
+    uint8_t* Wt = fsm + 128 * 256;              // [128 rows][256 B] swizzled
+    float* xn = reinterpret_cast<float*>(fsm + 2 * 128 * 256);   // [128]
+    float* wnt = xn + 128;                                       // [128]
+    float* bt = wnt + 128;                                       // [128]
+    int* hL = reinterpret_cast<int*>(bt + 128);                  // [8192] (pass 1)
+    int* hU = hL + kFBins;                                       // [8192]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int f0 = blockIdx.x * 128;
+    const int64_t t0 = (int64_t)blockIdx.y * 128;
+    const int u = blockIdx.z;
+    const float* cu = center + (int64_t)u * kBD;
+
+    for (int c = tid; c < 128 * 16; c += kFThreads) {
+        const int row = c >> 4, ch = c & 15;
+        const int f = f0 + row;
+        const bool valid = f < F;
+        cp_async_16(smem_addr(Wt) + swz(row, ch), Wb + (int64_t)(valid ? f : 0) * kBD + ch * 8, valid);
+    }
+    cp_async_commit_group();
+    if (PASS == 1)
+        for (int i = tid; i < 2 * kFBins; i += kFThreads) hL[i] = 0;
+    for (int j = tid; j < 128; j += kFThreads) {
+        const int f = f0 + j;
+        wnt[j] = f < F ? wn[f] : 0.f;
+        bt[j] = f < F ? bias[f] : 0.f;
+    }
+    // x = (k - center) / key_scale in fp32 (core.py:99), rounded to bf16 for
+    // the tensor cores; the row norm bound uses the fp32 values.
+    const bool unit_scale = key_scale == 1.0f;
+    for (int rr = 0; rr < 16; ++rr) {
+        const int row = warp * 16 + rr;
+        const int64_t t = t0 + row;
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        if (t < N) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int c = 4 * lane + e;
+                const float k = key_at(keys, unit_stride, row_stride, u, t, c);
+                const float dlt = __fsub_rn(k, cu[c]);
+                x[e] = unit_scale ? dlt : __fdiv_rn(dlt, key_scale);
+            }
+        }
+        float ss = fmaf(x[0], x[0], fmaf(x[1], x[1], fmaf(x[2], x[2], x[3] * x[3])));
+        ss = warp_sum(ss);
+        if (lane == 0) xn[row] = sqrtf(ss) * (1.0f + 1.0f / 4096.0f);
+        __nv_bfloat162 p0 = __floats2bfloat162_rn(x[0], x[1]), p1 = __floats2bfloat162_rn(x[2], x[3]);
+        uint2 pk2;
+        pk2.x = *reinterpret_cast<uint32_t*>(&p0);
+        pk2.y = *reinterpret_cast<uint32_t*>(&p1);
+        *reinterpret_cast<uint2*>(Xs + swz(row, lane >> 1) + (lane & 1) * 8) = pk2;
+    }
+    cp_async_wait_group<0>();
+    __syncthreads();
+
+    float acc[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    const int mi = lane >> 3, r8 = lane & 7;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+        uint32_t a[4];
+        ldsm_x4(smem_addr(Xs) + swz(warp * 16 + (mi & 1) * 8 + r8, 2 * kk + (mi >> 1)), a);
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {
+            uint32_t b[4];
+            ldsm_x4(smem_addr(Wt) + swz(np * 16 + (mi >> 1) * 8 + r8, 2 * kk + (mi & 1)), b);
+            mma_16816(acc[2 * np], a, b[0], b[1]);
+            mma_16816(acc[2 * np + 1], a, b[2], b[3]);
+        }
+    }
+
+    const int cutL = PASS == 2 ? fw.cutL[u] : 0, cutU = PASS == 2 ? fw.cutU[u] : 0;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        const int row = warp * 16 + (lane >> 2) + half * 8;
+        const int64_t t = t0 + row;
+        if (t >= N) continue;
+        const float xr = xn[row];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int col = 8 * j + 2 * (lane & 3) + e;
+                const int f = f0 + col;
+                if (f >= F) continue;
+                const float v = acc[j][2 * half + e] + bt[col];
+                const float err = fmaf(0.015625f * xr, wnt[col], 9.5367431640625e-07f * fabsf(v));
+                const float lo = v - err, hi = v + err;
+                if (PASS == 1) {
+                    if (hi > 0.f) atomicAdd(&hU[fbin(hi)], 1);
+                    if (lo > 0.f) atomicAdd(&hL[fbin(lo)], 1);
+                } else {
+                    if (!(hi > 0.f) || fbin(hi) < cutL) continue;          // surely not a member
+                    const long long flat = (long long)t * F + f;
+                    if (lo > 0.f && fbin(lo) > cutU) {                    // surely a member
+                        const int at = atomicAdd(&ws.n_members[u], 1);
+                        if (at < ws.mcap) {
+                            ws.members[(int64_t)u * ws.mcap + at] = flat;
+                            atomicAdd(&lens[(int64_t)u * F + f], 1);
+                        } else {
+                            atomicOr(status, PK_STATUS_MEMBERS_FULL);
+                        }
+                    } else {
+                        const int at = atomicAdd(&fw.n_amb[u], 1);
+                        if (at < fw.acap) fw.amb[(int64_t)u * fw.acap + at] = flat;
+                        else atomicOr(status, PK_STATUS_NEEDS_EXACT);
+                    }
+                }
+            }
+    }
+    if (PASS == 1) {
+        __syncthreads();
+        for (int i = tid; i < kFBins; i += kFThreads) {
+            if (hL[i]) atomicAdd(&fw.histL[(int64_t)u * kFBins + i], hL[i]);
+            if (hU[i]) atomicAdd(&fw.histU[(int64_t)u * kFBins + i], hU[i]);
+        }
+    }
+}
+
+// Per unit: the bins holding the count-th largest lower / upper bound.  The
+// exact threshold T lies between them; fewer than `count` positive lower
+// bounds leaves no useful lower cut, and the exact path is needed.
+__global__ void build_fast_cut_kernel(FastWs fw, long long count, int* __restrict__ status) {
+    const int u = blockIdx.x;
+    if (threadIdx.x != 0) return;
+    for (int which = 0; which < 2; ++which) {
+        const int* h = (which ? fw.histU : fw.histL) + (int64_t)u * kFBins;
+        long long above = 0;
+        int b = kFBins - 1;
+        for (; b >= 0; --b) {
+            if (above + h[b] >= count) break;
+            above += h[b];
+        }
+        (which ? fw.cutU : fw.cutL)[u] = b;  // -1 when fewer than count positives
+    }
+    if (fw.cutL[u] < 0 && fw.cutU[u] >= 0) atomicOr(status, PK_STATUS_NEEDS_EXACT);
+}
+
+// Exact activations of the undecided entries (sequential FMA over d, as the
+// reference); entries the exact value decides go straight to members or are
+// dropped, the rest become 64-bit boundary keys (value descending within the
+// band, flat index ascending).
+template <typename T>
+__global__ void build_exact_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride,
+                                   const float* __restrict__ center, float key_scale, const float* __restrict__ W,
+                                   const float* __restrict__ bias, int F, BuildWs ws, FastWs fw,
+                                   int* __restrict__ lens, int* __restrict__ status) {
+    const int u = blockIdx.y;
+    const int n = (int)min((int64_t)fw.n_amb[u], fw.acap);
+    const int cutL = fw.cutL[u], cutU = fw.cutU[u];
+    if (cutL < 0 && cutU >= 0) return;  // the exact path runs instead
+    const float* cu = center + (int64_t)u * kBD;
+    const bool unit_scale = key_scale == 1.0f;
+    const uint32_t hi_bits = cutU >= 0 ? ((uint32_t)(cutU + 1) << kFShift) : 0x7F800000u;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const long long flat = fw.amb[(int64_t)u * fw.acap + i];
+        const long long t = flat / F;
+        const int f = (int)(flat % F);
+        const float* w = W + (int64_t)f * kBD;
+        float acc = 0.f;
+#pragma unroll 8
+        for (int c = 0; c < kBD; ++c) {
+            const float dlt = __fsub_rn(key_at(keys, unit_stride, row_stride, u, t, c), cu[c]);
+            const float x = unit_scale ? dlt : __fdiv_rn(dlt, key_scale);
+            acc = fmaf(x, w[c], acc);
+        }
+        const float y = __fadd_rn(acc, bias[f]);
+        if (!(y > 0.f) || fbin(y) < cutL) continue;                 // below the threshold
+        if (cutU < 0 || fbin(y) > cutU) {                           // above it (or all positives count)
+            const int at = atomicAdd(&ws.n_members[u], 1);
+            if (at < ws.mcap) {
+                ws.members[(int64_t)u * ws.mcap + at] = flat;
+                atomicAdd(&lens[(int64_t)u * F + f], 1);
+            } else {
+                atomicOr(status, PK_STATUS_MEMBERS_FULL);
+            }
+            continue;
+        }
+        const uint32_t span = hi_bits - __float_as_uint(y);          // > 0: y lies below the band's top
+        if (span >= (1u << 28) || flat >= (1ll << 36)) {
+            atomicOr(status, PK_STATUS_NEEDS_EXACT);
+            continue;
+        }
+        const int at = atomicAdd(&ws.n_boundary[u], 1);
+        if (at < ws.bcap)
+            ws.boundary[(int64_t)u * ws.bcap + at] =
+                (long long)(((unsigned long long)span << 36) | (unsigned long long)flat);
+        else
+            atomicOr(status, PK_STATUS_BOUNDARY_FULL);
+    }
+}
+
+// need = count - members so far (the boundary supplies the rest); cut >= 0
+// so that the resolve kernel runs.
+__global__ void build_fast_need_kernel(BuildWs ws, FastWs fw, long long count) {
+    const int u = blockIdx.x;
+    if (threadIdx.x != 0) return;
+    const long long have = ws.n_members[u];
+    ws.need[u] = count - have;
+    ws.cut[u] = fw.cutU[u] >= 0 ? 0 : -1;  // all positives: nothing to resolve
+}
+
+// Resolve with the fast keys: the `need` smallest keys of the boundary are
+// members; key bits [36, 64) hold the value's distance below the band top.
+__global__ void __launch_bounds__(1024)
+build_fast_resolve_kernel(BuildWs ws, int F, int* __restrict__ lens, int* __restrict__ status) {
+    const int u = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+    __shared__ int hist[256];
+    __shared__ unsigned long long s_prefix;
+    __shared__ long long s_need;
+    const long long need0 = ws.need[u];
+    const int nb = ws.n_boundary[u];
+    if (ws.cut[u] < 0 || need0 <= 0 || nb > ws.bcap) return;
+    if (need0 > nb) {
+        // The bounds should always leave enough candidates: flag, never guess.
+        if (tid == 0) atomicOr(status, PK_STATUS_NEEDS_EXACT);
+        return;
+    }
+    const long long* B = ws.boundary + (int64_t)u * ws.bcap;
+    unsigned long long prefix = ~0ull;
+    if (need0 < nb) {
+        unsigned long long pre = 0, pmask = 0;
+        long long need = need0;
+        for (int pass = 0; pass < 8; ++pass) {
+            const int shift = 56 - 8 * pass;
+            for (int i = tid; i < 256; i += nt) hist[i] = 0;
+            __syncthreads();
+            for (int i = tid; i < nb; i += nt) {
+                const unsigned long long kk = (unsigned long long)B[i];
+                if ((kk & pmask) == pre) atomicAdd(&hist[(kk >> shift) & 255ull], 1);
+            }
+            __syncthreads();
+            if (tid == 0) {
+                long long acc = 0;
+                int dgt = 0;
+                for (; dgt < 256; ++dgt) {
+                    if (acc + hist[dgt] >= need) break;
+                    acc += hist[dgt];
+                }
+                s_prefix = pre | ((unsigned long long)dgt << shift);
+                s_need = need - acc;
+            }
+            __syncthreads();
+            pre = s_prefix;
+            pmask |= 0xFFull << shift;
+            need = s_need;
+            __syncthreads();
+        }
+        prefix = pre;
+    }
+    for (int i = tid; i < nb; i += nt) {
+        const unsigned long long kk = (unsigned long long)B[i];
+        if (kk <= prefix) {
+            const long long flat = (long long)(kk & ((1ull << 36) - 1));
+            const int at = atomicAdd(&ws.n_members[u], 1);
+            if (at < ws.mcap) {
+                ws.members[(int64_t)u * ws.mcap + at] = flat;
+                atomicAdd(&lens[(int64_t)u * F + (int)(flat % F)], 1);
+            } else {
+                atomicOr(status, PK_STATUS_MEMBERS_FULL);
+            }
+        }
+    }
+}
+
+template <typename T>
+int run_encode_select_fast(const T* keys, int64_t unit_stride, int64_t row_stride, int64_t N, const float* center,
+                           float key_scale, const float* W, const __nv_bfloat16* Wb, const float* wn,
+                           const float* b, int U, int F, long long count, BuildWs ws, FastWs fw, int* lens,
+                           int* status, cudaStream_t st) {
+    const int smem1 = 2 * 128 * 256 + 3 * 128 * 4 + 2 * kFBins * 4;
+    const int smem2 = 2 * 128 * 256 + 3 * 128 * 4;
+    dim3 grid((F + 127) / 128, (unsigned)((N + 127) / 128), U);
+    cudaFuncSetAttribute(build_approx_kernel<1, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1);
+    cudaFuncSetAttribute(build_approx_kernel<2, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2);
+    build_approx_kernel<1, T><<<grid, kFThreads, smem1, st>>>(keys, unit_stride, row_stride, N, center, key_scale,
+                                                              Wb, b, wn, F, ws, fw, lens, status);
+    PK_CHECK_LAUNCH();
+    build_fast_cut_kernel<<<U, 32, 0, st>>>(fw, count, status);
+    PK_CHECK_LAUNCH();
+    build_approx_kernel<2, T><<<grid, kFThreads, smem2, st>>>(keys, unit_stride, row_stride, N, center, key_scale,
+                                                              Wb, b, wn, F, ws, fw, lens, status);
+    PK_CHECK_LAUNCH();
+    build_exact_kernel<T><<<dim3(512, U), 256, 0, st>>>(keys, unit_stride, row_stride, center, key_scale, W, b, F,
+                                                        ws, fw, lens, status);
+    PK_CHECK_LAUNCH();
+    build_fast_need_kernel<<<U, 32, 0, st>>>(ws, fw, count);
+    PK_CHECK_LAUNCH();
+    build_fast_resolve_kernel<<<U, 1024, 0, st>>>(ws, F, lens, status);
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}
+
 int sort_buckets(int* ids, int64_t ids_stride, const int* offsets, const int* start, const int* cnt, int U, int F,
                  int* status, cudaStream_t st) {
     sort_buckets_warp_kernel<<<dim3((F + 7) / 8, U), 256, 0, st>>>(ids, ids_stride, offsets, start, cnt, F);
@@ -552,11 +906,13 @@ extern "C" int64_t pk_build_ids_capacity(int64_t N, int F, int key_mean, float s
 
 extern "C" size_t pk_build_workspace_bytes(int U, int64_t N, int F, int key_mean, int64_t boundary_capacity) {
     const int64_t mcap = N * (int64_t)key_mean;
-    return carve_bytes(U, F, mcap > 0 ? mcap : 1, boundary_capacity > 0 ? boundary_capacity : 1);
+    const int64_t bcap = boundary_capacity > 0 ? boundary_capacity : 1;
+    return carve_bytes(U, F, mcap > 0 ? mcap : 1, bcap) + fast_bytes(U, bcap);
 }
 
 extern "C" int pk_build_index(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride, uint64_t center,
-                              float key_scale, uint64_t w_enc, uint64_t b_enc, int U, int64_t N, int d, int F,
+                              float key_scale, uint64_t w_enc, uint64_t b_enc, uint64_t w_bf16, uint64_t w_norm,
+                              int U, int64_t N, int d, int F,
                               int key_mean, int64_t token_base, float slack_frac, int slack_min, uint64_t offsets,
                               uint64_t lens, uint64_t ids, int64_t ids_stride, int64_t boundary_capacity,
                               uint64_t workspace, uint64_t workspace_bytes, uint64_t status, uint64_t stream) {
@@ -572,11 +928,24 @@ extern "C" int pk_build_index(uint64_t keys, int dtype, int64_t unit_stride, int
     cudaStream_t st = (cudaStream_t)stream;
     const int64_t mcap = N * (int64_t)key_mean;
     BuildWs ws = carve((void*)workspace, U, F, mcap, boundary_capacity);
+    void* fbase = (char*)workspace + carve_bytes(U, F, mcap, boundary_capacity);
+    FastWs fw = carve_fast(fbase, U, boundary_capacity);
     cudaMemsetAsync((void*)workspace, 0, counters_bytes(U, F), st);
+    cudaMemsetAsync(fbase, 0, fast_counters_bytes(U), st);
     cudaMemsetAsync((void*)lens, 0, (size_t)U * F * sizeof(int), st);
     const long long count = (long long)N * key_mean;
     int rc;
-    if (dtype == PK_BF16)
+    const bool fast = w_bf16 && w_norm;
+    if (fast && dtype == PK_BF16)
+        rc = run_encode_select_fast((const __nv_bfloat16*)keys, unit_stride, row_stride, N, (const float*)center,
+                                    key_scale, (const float*)w_enc, (const __nv_bfloat16*)w_bf16,
+                                    (const float*)w_norm, (const float*)b_enc, U, F, count, ws, fw, (int*)lens,
+                                    (int*)status, st);
+    else if (fast && dtype == PK_F32)
+        rc = run_encode_select_fast((const float*)keys, unit_stride, row_stride, N, (const float*)center, key_scale,
+                                    (const float*)w_enc, (const __nv_bfloat16*)w_bf16, (const float*)w_norm,
+                                    (const float*)b_enc, U, F, count, ws, fw, (int*)lens, (int*)status, st);
+    else if (dtype == PK_BF16)
         rc = run_encode_select((const __nv_bfloat16*)keys, unit_stride, row_stride, N, (const float*)center, key_scale,
                                (const float*)w_enc, (const float*)b_enc, U, F, count, ws, (int*)lens, (int*)status, st);
     else if (dtype == PK_F32)
@@ -619,13 +988,15 @@ extern "C" int pk_summarize(uint64_t keys, int dtype, int64_t unit_stride, int64
 extern "C" size_t pk_append_workspace_bytes(int U, int64_t n_new, int d, int F, int key_mean,
                                             int64_t boundary_capacity) {
     const int64_t mcap = n_new * (int64_t)key_mean;
-    const size_t base = carve_bytes(U, F, mcap > 0 ? mcap : 1, boundary_capacity > 0 ? boundary_capacity : 1);
+    const int64_t bcap = boundary_capacity > 0 ? boundary_capacity : 1;
+    const size_t base = carve_bytes(U, F, mcap > 0 ? mcap : 1, bcap) + fast_bytes(U, bcap);
     // + new-block counts [U, F] + new-block moments [2, U, F, d]
     return base + align256((size_t)U * F * 4) + 2 * align256((size_t)U * F * d * 4);
 }
 
 extern "C" int pk_append_index(uint64_t new_keys, int dtype, int64_t unit_stride, int64_t row_stride, int64_t n_new,
-                               uint64_t center, float key_scale, uint64_t w_enc, uint64_t b_enc, int U, int d, int F,
+                               uint64_t center, float key_scale, uint64_t w_enc, uint64_t b_enc, uint64_t w_bf16,
+                               uint64_t w_norm, int U, int d, int F,
                                int key_mean, int64_t history, uint64_t offsets, uint64_t lens, uint64_t ids,
                                int64_t ids_stride, uint64_t mean, uint64_t var, int64_t boundary_capacity,
                                uint64_t workspace, uint64_t workspace_bytes, uint64_t status, uint64_t stream) {
@@ -641,15 +1012,29 @@ extern "C" int pk_append_index(uint64_t new_keys, int dtype, int64_t unit_stride
     cudaStream_t st = (cudaStream_t)stream;
     const int64_t mcap = n_new * (int64_t)key_mean;
     BuildWs ws = carve((void*)workspace, U, F, mcap, boundary_capacity);
-    char* extra = (char*)workspace + carve_bytes(U, F, mcap, boundary_capacity);
+    void* fbase = (char*)workspace + carve_bytes(U, F, mcap, boundary_capacity);
+    FastWs fw = carve_fast(fbase, U, boundary_capacity);
+    char* extra = (char*)fbase + fast_bytes(U, boundary_capacity);
     int* cnt_new = (int*)extra;
     float* mean_new = (float*)(extra + align256((size_t)U * F * 4));
     float* var_new = (float*)(extra + align256((size_t)U * F * 4) + align256((size_t)U * F * d * 4));
     cudaMemsetAsync((void*)workspace, 0, counters_bytes(U, F), st);
     cudaMemsetAsync(cnt_new, 0, (size_t)U * F * 4, st);
+    cudaMemsetAsync(fbase, 0, fast_counters_bytes(U), st);
     const long long count = (long long)n_new * key_mean;
     int rc;
-    if (dtype == PK_BF16)
+    const bool fast = w_bf16 && w_norm;
+    if (fast && dtype == PK_BF16)
+        rc = run_encode_select_fast((const __nv_bfloat16*)new_keys, unit_stride, row_stride, n_new,
+                                    (const float*)center, key_scale, (const float*)w_enc,
+                                    (const __nv_bfloat16*)w_bf16, (const float*)w_norm, (const float*)b_enc, U, F,
+                                    count, ws, fw, cnt_new, (int*)status, st);
+    else if (fast && dtype == PK_F32)
+        rc = run_encode_select_fast((const float*)new_keys, unit_stride, row_stride, n_new, (const float*)center,
+                                    key_scale, (const float*)w_enc, (const __nv_bfloat16*)w_bf16,
+                                    (const float*)w_norm, (const float*)b_enc, U, F, count, ws, fw, cnt_new,
+                                    (int*)status, st);
+    else if (dtype == PK_BF16)
         rc = run_encode_select((const __nv_bfloat16*)new_keys, unit_stride, row_stride, n_new, (const float*)center,
                                key_scale, (const float*)w_enc, (const float*)b_enc, U, F, count, ws, cnt_new,
                                (int*)status, st);
@@ -659,6 +1044,10 @@ extern "C" int pk_append_index(uint64_t new_keys, int dtype, int64_t unit_stride
     else
         return PK_ERR_ARG;
     if (rc) return rc;
+    // An incomplete member list (boundary full, or bounds that need the exact
+    // path) must not be committed.
+    status_gate_kernel<<<1, 32, 0, st>>>((const int*)status, ws.flag);
+    PK_CHECK_LAUNCH();
     dim3 g2((F + 255) / 256, U);
     append_check_kernel<<<g2, 256, 0, st>>>((const int*)offsets, (const int*)lens, cnt_new, F, ws.flag);
     PK_CHECK_LAUNCH();

@@ -20,6 +20,7 @@ constexpr int kAvStages = 3;
 constexpr int kAvRowBytes = kAvD * 2;
 constexpr int kAvStageBytes = kAvTile * kAvRowBytes * 2;   // K + V
 constexpr int kAvMaxG = 16;
+constexpr int kAvIdsCap = 2048;   // row ids staged per CTA (longer splits read the rest directly)
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct AvParams {
@@ -185,32 +186,37 @@ sparse_av_bf16_kernel(AvParams p) {
             qa[kk][r] = hh < G ? *reinterpret_cast<const uint32_t*>(qp + hh * kAvD + dim) : 0u;
         }
 
-    // Loader: two threads per row; each moves 8 K chunks and 8 V chunks.
-    const int ld_row = tid >> 1, ld_c0 = (tid & 1) * 8;
-    auto row_pos = [&](int t) -> int {
-        const int r = r0 + t * kAvTile + ld_row;
+    // The split's row ids, staged once in shared memory (one coalesced read)
+    // so that issuing a tile's copies never waits on a global load.
+    int* sids = reinterpret_cast<int*>(smem + kAvStages * kAvStageBytes);
+    const int n_staged = min(max(0, min(r1, cnt) - r0), kAvIdsCap);
+    for (int i = tid; i < n_staged; i += kAvThreads) sids[i] = idp[r0 + i];
+    __syncthreads();
+    auto pos_of = [&](int r) -> int {
         if (r >= r1) return -1;
-        return r < cnt ? idp[r] : H + (r - cnt);
+        if (r >= cnt) return H + (r - cnt);
+        return r - r0 < kAvIdsCap ? sids[r - r0] : idp[r];
     };
-    auto issue = [&](int t, int pos) {
+    // Loader: each warp moves its 16 rows of the tile, two 256-byte rows per
+    // instruction (16 lanes x 16 bytes per row: fully coalesced).
+    const int ld_sub = lane >> 4, ld_ch = lane & 15;
+    auto issue = [&](int t) {
         uint8_t* st = smem + (t % kAvStages) * kAvStageBytes;
         const uint32_t kd = smem_u32(st), vd = smem_u32(st + kAvTile * kAvRowBytes);
-        const bool valid = pos >= 0;
-        const int64_t off = valid ? (int64_t)pos * p.kv_row_stride : 0;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const int ch = ld_c0 + c;
-            cp_async16(kd + tile_off(ld_row, ch), kb + off + ch * 8, valid);
-            cp_async16(vd + tile_off(ld_row, ch), vb + off + ch * 8, valid);
+        for (int i = 0; i < 8; ++i) {
+            const int row = warp * 16 + 2 * i + ld_sub;
+            const int pos = pos_of(r0 + t * kAvTile + row);
+            const bool valid = pos >= 0;
+            const int64_t off = valid ? (int64_t)pos * p.kv_row_stride : 0;
+            cp_async16(kd + tile_off(row, ld_ch), kb + off + ld_ch * 8, valid);
+            cp_async16(vd + tile_off(row, ld_ch), vb + off + ld_ch * 8, valid);
         }
     };
 
-    int pos0 = 0 < ntiles ? row_pos(0) : -1;
-    int pos1 = 1 < ntiles ? row_pos(1) : -1;
-    int prefetched = 2 < ntiles ? row_pos(2) : -1;
-    if (0 < ntiles) issue(0, pos0);
+    if (0 < ntiles) issue(0);
     cp_async_commit();
-    if (1 < ntiles) issue(1, pos1);
+    if (1 < ntiles) issue(1);
     cp_async_commit();
 
     float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
@@ -221,9 +227,8 @@ sparse_av_bf16_kernel(AvParams p) {
 
     for (int t = 0; t < ntiles; ++t) {
         const int tn = t + kAvStages - 1;
-        if (tn < ntiles) issue(tn, prefetched);
+        if (tn < ntiles) issue(tn);
         cp_async_commit();
-        prefetched = tn + 1 < ntiles ? row_pos(tn + 1) : -1;
         cp_async_wait<kAvStages - 1>();
         __syncthreads();
 
@@ -472,7 +477,7 @@ extern "C" int pk_sparse_av(uint64_t q, uint64_t k, uint64_t v, int dtype, int k
     dim3 grid(splits, U);
     if (dtype == PK_BF16) {
         if (kv_row_stride % 8 || kv_batch_stride % 8 || kv_head_stride % 8 || (k | v) % 16) return PK_ERR_ARG;
-        const int smem = kAvStages * kAvStageBytes;
+        const int smem = kAvStages * kAvStageBytes + kAvIdsCap * (int)sizeof(int);
         cudaFuncSetAttribute(sparse_av_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         sparse_av_bf16_kernel<<<grid, kAvThreads, smem, st>>>(p);
     } else if (dtype == PK_F32) {

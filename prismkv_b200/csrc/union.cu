@@ -3,36 +3,34 @@
 // over the unit's history and compacted to ascending token ids by a block
 // scan (the order of core.py:164's chosen.nonzero()).
 //
-// The greedy is sequential by definition -- bucket i is accepted iff its
-// tokens not yet chosen fit the remaining budget -- but it is computed here
-// in parallel, exactly:
-//   1. every staged (bucket, token) entry is inserted into a shared-memory
-//      hash table that keeps each token's first candidate (atomicMin);
-//   2. while no bucket has been skipped, bucket i's new tokens are exactly
-//      its tokens whose first candidate is i, so one prefix sum over the
-//      candidates finds the first bucket that overflows (i*);
-//   3. after i*, the new-token counts of all remaining buckets are recounted
-//      in parallel against the bitmap; a warp ballot finds the next bucket
-//      that fits; accepting a bucket with no new tokens leaves the bitmap --
-//      and so every count -- unchanged, otherwise the bitmap is updated and
-//      the remaining counts recounted.
-// When the staged lists or the history do not fit on chip, the greedy runs
-// in one warp over lists staged chunk by chunk (same result).
+// The candidates' bucket lists are first staged in shared memory with one
+// fully parallel copy.  The greedy -- sequential by definition: bucket i is
+// accepted iff its tokens not yet chosen fit the remaining budget -- is then
+// computed exactly in two phases:
+//   1. while no bucket has been skipped, bucket i's new tokens are its tokens
+//      that are neither in the bitmap (earlier rounds) nor in an earlier
+//      bucket of the current round.  Rounds take as many buckets as a shared-
+//      memory hash (token -> first bucket of the round, atomicMin) can hold;
+//      a warp prefix sum over the round's counts finds the first bucket that
+//      would overflow (i*), and the buckets before it are OR-ed in.
+//   2. after i*, every remaining bucket's new-token count is computed once in
+//      parallel; then one warp walks the buckets in order.  A bucket whose
+//      count minus the tokens added since cannot fit is skipped at once; any
+//      other is re-counted against the current bitmap and taken if it fits.
+// Lists that do not fit the staging area are read from global memory by the
+// same code paths.
 #include "common.cuh"
 
 namespace pk {
 
 constexpr int kUnionThreads = 512;
-constexpr int kStage = 8192;      // staged token ids (32 KB)
 constexpr int kMaxCand = 256;     // candidates per unit (G * k)
-constexpr int kHashSlots = 16384; // 2x the staged entries
-constexpr int kHashBits = 14;
 
 struct UnionSmem {
     int cand_bucket[kMaxCand];
     int cand_start[kMaxCand];
     int cand_len[kMaxCand];
-    int stage_off[kMaxCand + 1];
+    int cand_stage[kMaxCand];     // offset in the staging area, or -1
     int newc[kMaxCand];
     int scan[40];
     long long red[32];
@@ -41,33 +39,39 @@ struct UnionSmem {
 
 __device__ __forceinline__ bool test_bit(const uint32_t* bm, int t) { return (bm[t >> 5] >> (t & 31)) & 1u; }
 __device__ __forceinline__ void set_bit(uint32_t* bm, int t) { atomicOr(&bm[t >> 5], 1u << (t & 31)); }
-__device__ __forceinline__ int hash_slot(int t) { return (int)(((uint32_t)t * 2654435761u) >> (32 - kHashBits)); }
 
-__device__ __forceinline__ void hash_insert(int* hkey, int* hown, int t, int c) {
-    int s = hash_slot(t);
-    while (true) {
-        const int old = atomicCAS(&hkey[s], -1, t);
-        if (old == -1 || old == t) {
-            atomicMin(&hown[s], c);
-            return;
+struct Hash {
+    int* key;
+    int* own;
+    int bits;
+    __device__ __forceinline__ int slot(int t) const { return (int)(((uint32_t)t * 2654435761u) >> (32 - bits)); }
+    __device__ __forceinline__ void insert(int t, int c) const {
+        const int mask = (1 << bits) - 1;
+        int s = slot(t);
+        while (true) {
+            const int old = atomicCAS(&key[s], -1, t);
+            if (old == -1 || old == t) {
+                atomicMin(&own[s], c);
+                return;
+            }
+            s = (s + 1) & mask;
         }
-        s = (s + 1) & (kHashSlots - 1);
     }
-}
-
-__device__ __forceinline__ int hash_owner(const int* hkey, const int* hown, int t) {
-    int s = hash_slot(t);
-    while (hkey[s] != t) s = (s + 1) & (kHashSlots - 1);
-    return hown[s];
-}
+    __device__ __forceinline__ int owner(int t) const {
+        const int mask = (1 << bits) - 1;
+        int s = slot(t);
+        while (key[s] != t) s = (s + 1) & mask;
+        return own[s];
+    }
+};
 
 __global__ void __launch_bounds__(kUnionThreads)
 union_kernel(const int* __restrict__ offsets, const int* __restrict__ lens, const int* __restrict__ ids,
              int64_t ids_stride, const int* __restrict__ order, const int* __restrict__ n_order, int order_stride,
              const int* __restrict__ history, const long long* __restrict__ limit, int F, int max_history,
-             int use_hash, int* __restrict__ out_ids, int64_t out_stride, int* __restrict__ out_count,
-             int* __restrict__ features, int* __restrict__ n_features, long long* __restrict__ raw,
-             int* __restrict__ status) {
+             int hash_bits, int stage_cap, int* __restrict__ out_ids, int64_t out_stride,
+             int* __restrict__ out_count, int* __restrict__ features, int* __restrict__ n_features,
+             long long* __restrict__ raw, int* __restrict__ status) {
     extern __shared__ __align__(16) uint32_t dyn[];
     __shared__ UnionSmem sm;
     const int u = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
@@ -85,10 +89,10 @@ union_kernel(const int* __restrict__ offsets, const int* __restrict__ lens, cons
     }
     const int W = (H + 31) >> 5;
     const int Wmax = (max_history + 31) >> 5;
-    uint32_t* bm = dyn;                                             // [W]
-    int* stage = reinterpret_cast<int*>(dyn + ((Wmax + 3) & ~3));   // [kStage]
-    int* hkey = stage + kStage;                                     // [kHashSlots] (use_hash)
-    int* hown = hkey + kHashSlots;                                  // [kHashSlots]
+    uint32_t* bm = dyn;                                               // [W]
+    int* hkeys = reinterpret_cast<int*>(dyn + ((Wmax + 3) & ~3));     // [2^hash_bits]
+    int* hown = hkeys + (1 << hash_bits);                             // [2^hash_bits]
+    int* stage = hown + (1 << hash_bits);                             // [stage_cap]
     const int n = min(n_order[u], kMaxCand);
     const long long lim = limit[u];
     const int* uid = ids + (int64_t)u * ids_stride;
@@ -104,14 +108,29 @@ union_kernel(const int* __restrict__ offsets, const int* __restrict__ lens, cons
     __syncthreads();
     if (tid == 0) {
         long long s = 0;
-        sm.stage_off[0] = 0;
+        int staged = 0;
         for (int c = 0; c < n; ++c) {
-            s += sm.cand_len[c];
-            sm.stage_off[c + 1] = (int)min(s, (long long)INT32_MAX);
+            const int L = sm.cand_len[c];
+            s += L;
+            if (staged + L <= stage_cap) { sm.cand_stage[c] = staged; staged += L; }
+            else sm.cand_stage[c] = -1;
         }
         sm.red[0] = s;
     }
     __syncthreads();
+    // Stage: one warp per candidate, every load independent.
+    for (int c = warp; c < n; c += nw) {
+        const int off = sm.cand_stage[c];
+        if (off < 0) continue;
+        const int L = sm.cand_len[c];
+        const int* src = uid + sm.cand_start[c];
+        for (int i = lane; i < L; i += 32) stage[off + i] = src[i];
+    }
+    __syncthreads();
+    auto list = [&](int c) -> const int* {
+        const int off = sm.cand_stage[c];
+        return off >= 0 ? stage + off : uid + sm.cand_start[c];
+    };
     const long long raw_total = sm.red[0];
     long long raw_acc = 0;
     int nf = 0;
@@ -120,92 +139,104 @@ union_kernel(const int* __restrict__ offsets, const int* __restrict__ lens, cons
         // Every candidate fits whatever the overlap: the unbudgeted union.
         for (int c = warp; c < n; c += nw) {
             const int L = sm.cand_len[c];
-            const int* src = uid + sm.cand_start[c];
+            const int* lst = list(c);
             for (int i = lane; i < L; i += 32) {
-                const int t = src[i];
+                const int t = lst[i];
                 if ((unsigned)t < (unsigned)H) set_bit(bm, t);
             }
         }
         for (int c = tid; c < n; c += nt) feat[c] = sm.cand_bucket[c];
         nf = n;
         raw_acc = raw_total;
-    } else if (use_hash && raw_total <= kStage) {
-        // ---- 1. stage the lists and record each token's first candidate.
-        for (int i = tid; i < kHashSlots; i += nt) { hkey[i] = -1; hown[i] = INT32_MAX; }
-        for (int c = warp; c < n; c += nw) {
-            const int L = sm.cand_len[c];
-            const int* src = uid + sm.cand_start[c];
-            int* dst = stage + sm.stage_off[c];
-            for (int i = lane; i < L; i += 32) dst[i] = src[i];
-        }
-        __syncthreads();
-        for (int c = warp; c < n; c += nw) {
-            const int* lst = stage + sm.stage_off[c];
-            const int L = sm.cand_len[c];
-            for (int i = lane; i < L; i += 32) {
-                const int t = lst[i];
-                if ((unsigned)t < (unsigned)H) hash_insert(hkey, hown, t, c);
-            }
-        }
-        __syncthreads();
-        // ---- 2. new tokens per candidate while every earlier one is taken.
-        for (int c = warp; c < n; c += nw) {
-            const int* lst = stage + sm.stage_off[c];
-            const int L = sm.cand_len[c];
-            int cnt = 0;
-            for (int i = lane; i < L; i += 32) {
-                const int t = lst[i];
-                cnt += ((unsigned)t < (unsigned)H && hash_owner(hkey, hown, t) == c) ? 1 : 0;
-            }
-            cnt = warp_sum(cnt);
-            if (lane == 0) sm.newc[c] = cnt;
-        }
-        __syncthreads();
-        if (warp == 0) {
-            // Prefix sum in candidate order; i* = first candidate that overflows.
-            long long run = 0;
-            int istar = n;
-            for (int base = 0; base < n; base += 32) {
-                const int c = base + lane;
-                int v = c < n ? sm.newc[c] : 0;
-                int inc = warp_inclusive_scan(v);
-                const bool over = c < n && run + inc > lim;
-                const unsigned om = __ballot_sync(0xffffffffu, over);
-                if (om) {
-                    istar = base + __ffs(om) - 1;
-                    const int before = __shfl_sync(0xffffffffu, inc - v, istar - base);
-                    run += before;
-                    break;
+    } else {
+        Hash hs{hkeys, hown, hash_bits};
+        const int round_cap = 1 << (hash_bits - 1);  // load factor <= 1/2
+        long long count = 0;
+        int c0 = 0, istar = n;
+        // ---- 1. rounds while every bucket so far was accepted.
+        while (c0 < n) {
+            if (tid == 0) {
+                int c1 = c0, filled = 0;
+                while (c1 < n && (filled + sm.cand_len[c1] <= round_cap || c1 == c0)) {
+                    filled += sm.cand_len[c1];
+                    ++c1;
                 }
-                run += __shfl_sync(0xffffffffu, inc, 31);
+                sm.flags[0] = c1;
             }
-            if (lane == 0) {
-                sm.flags[0] = istar;
-                sm.red[1] = run;   // chosen count after the accepted prefix
+            __syncthreads();
+            const int c1 = sm.flags[0];
+            const bool single = c1 - c0 == 1;
+            if (!single) {
+                for (int i = tid; i < (1 << hash_bits); i += nt) { hs.key[i] = -1; hs.own[i] = INT32_MAX; }
+                __syncthreads();
+                for (int c = c0 + warp; c < c1; c += nw) {
+                    const int* lst = list(c);
+                    const int L = sm.cand_len[c];
+                    for (int i = lane; i < L; i += 32) {
+                        const int t = lst[i];
+                        if ((unsigned)t < (unsigned)H && !test_bit(bm, t)) hs.insert(t, c);
+                    }
+                }
+                __syncthreads();
             }
+            for (int c = c0 + warp; c < c1; c += nw) {
+                const int* lst = list(c);
+                const int L = sm.cand_len[c];
+                int cnt = 0;
+                for (int i = lane; i < L; i += 32) {
+                    const int t = lst[i];
+                    cnt += ((unsigned)t < (unsigned)H && !test_bit(bm, t) && (single || hs.owner(t) == c)) ? 1 : 0;
+                }
+                cnt = warp_sum(cnt);
+                if (lane == 0) sm.newc[c] = cnt;
+            }
+            __syncthreads();
+            if (warp == 0) {
+                long long run = count;
+                int first_over = c1;
+                for (int base = c0; base < c1; base += 32) {
+                    const int c = base + lane;
+                    const int v = c < c1 ? sm.newc[c] : 0;
+                    const int inc = warp_inclusive_scan(v);
+                    const bool over = c < c1 && run + inc > lim;
+                    const unsigned om = __ballot_sync(0xffffffffu, over);
+                    if (om) {
+                        first_over = base + __ffs(om) - 1;
+                        run += __shfl_sync(0xffffffffu, inc - v, first_over - base);
+                        break;
+                    }
+                    run += __shfl_sync(0xffffffffu, inc, 31);
+                }
+                if (lane == 0) {
+                    sm.flags[1] = first_over;
+                    sm.red[1] = run;
+                }
+            }
+            __syncthreads();
+            const int acc_end = sm.flags[1];
+            count = sm.red[1];
+            for (int c = c0 + warp; c < acc_end; c += nw) {
+                const int* lst = list(c);
+                const int L = sm.cand_len[c];
+                for (int i = lane; i < L; i += 32) {
+                    const int t = lst[i];
+                    if ((unsigned)t < (unsigned)H) set_bit(bm, t);
+                }
+            }
+            for (int c = c0 + tid; c < acc_end; c += nt) feat[c] = sm.cand_bucket[c];
+            for (int c = c0; c < acc_end; ++c) raw_acc += sm.cand_len[c];
+            nf = acc_end;
+            __syncthreads();
+            if (acc_end < c1) {
+                istar = acc_end;
+                break;
+            }
+            c0 = c1;
         }
-        __syncthreads();
-        const int istar = sm.flags[0];
-        long long count = sm.red[1];
-        // Accepted prefix: its tokens into the bitmap.
-        for (int c = warp; c < istar; c += nw) {
-            const int* lst = stage + sm.stage_off[c];
-            const int L = sm.cand_len[c];
-            for (int i = lane; i < L; i += 32) {
-                const int t = lst[i];
-                if ((unsigned)t < (unsigned)H) set_bit(bm, t);
-            }
-        }
-        for (int c = tid; c < istar; c += nt) feat[c] = sm.cand_bucket[c];
-        nf = istar;
-        raw_acc = sm.stage_off[istar];
-        __syncthreads();
-        // ---- 3. the tail after the first skipped candidate.
-        int pos = istar + 1;
-        while (pos < n) {
-            // Recount new tokens of candidates pos.. against the bitmap.
-            for (int c = pos + warp; c < n; c += nw) {
-                const int* lst = stage + sm.stage_off[c];
+        // ---- 2. the tail after the first skipped bucket.
+        if (istar + 1 < n) {
+            for (int c = istar + 1 + warp; c < n; c += nw) {
+                const int* lst = list(c);
                 const int L = sm.cand_len[c];
                 int cnt = 0;
                 for (int i = lane; i < L; i += 32) {
@@ -217,111 +248,45 @@ union_kernel(const int* __restrict__ offsets, const int* __restrict__ lens, cons
             }
             __syncthreads();
             if (warp == 0) {
-                // Scan for the next fitting candidate; zero-new acceptances
-                // change nothing and are taken inline.
-                int next = n;
-                while (pos < n) {
-                    const int c = pos + lane;
-                    const bool fits = c < n && count + sm.newc[c] <= lim;
-                    const unsigned fm = __ballot_sync(0xffffffffu, fits);
-                    if (!fm) { pos += 32; continue; }
-                    const int a = pos + __ffs(fm) - 1;
-                    const int add = sm.newc[a];
-                    if (lane == 0) feat[nf] = sm.cand_bucket[a];
-                    ++nf;
-                    raw_acc += sm.cand_len[a];
-                    pos = a + 1;
-                    if (add > 0) {
-                        count += add;
-                        next = a;
-                        break;
-                    }
-                }
-                if (lane == 0) {
-                    sm.flags[1] = next;
-                    sm.flags[2] = nf;
-                    sm.flags[3] = min(pos, n);
-                    sm.red[2] = raw_acc;
-                    sm.red[3] = count;
-                }
-            }
-            __syncthreads();
-            const int a = sm.flags[1];
-            nf = sm.flags[2];
-            pos = sm.flags[3];
-            raw_acc = sm.red[2];
-            count = sm.red[3];
-            if (a >= n) break;
-            // Candidate a added tokens: set them, then recount.
-            {
-                const int* lst = stage + sm.stage_off[a];
-                const int L = sm.cand_len[a];
-                for (int i = tid; i < L; i += nt) {
-                    const int t = lst[i];
-                    if ((unsigned)t < (unsigned)H) set_bit(bm, t);
-                }
-            }
-            __syncthreads();
-        }
-    } else {
-        // Sequential greedy over lists staged chunk by chunk.
-        long long count = 0;
-        int c = 0;
-        while (c < n) {
-            if (tid == 0) {
-                int c_end = c, filled = 0;
-                sm.flags[4] = 0;
-                sm.stage_off[c] = 0;
-                while (c_end < n && (filled + sm.cand_len[c_end] <= kStage || c_end == c)) {
-                    filled += min(sm.cand_len[c_end], kStage);
-                    ++c_end;
-                    sm.stage_off[c_end] = filled;
-                }
-                sm.flags[0] = c_end;
-            }
-            __syncthreads();
-            const int c_end = sm.flags[0];
-            for (int cc = c; cc < c_end; ++cc) {
-                const int L = min(sm.cand_len[cc], kStage);
-                const int* src = uid + sm.cand_start[cc];
-                int* dst = stage + sm.stage_off[cc];
-                for (int i = tid; i < L; i += nt) dst[i] = src[i];
-            }
-            __syncthreads();
-            if (warp == 0) {
-                for (int cc = c; cc < c_end; ++cc) {
-                    const int L = sm.cand_len[cc];
-                    const int* src = L <= kStage ? stage + sm.stage_off[cc] : uid + sm.cand_start[cc];
+                // newc[c] was exact when counted; the bitmap has grown by
+                // `added` tokens since, so newc[c] - added <= true count.
+                long long added = 0;
+                for (int c = istar + 1; c < n; ++c) {
+                    if ((long long)sm.newc[c] - added > lim - count) continue;
+                    const int* lst = list(c);
+                    const int L = sm.cand_len[c];
                     int fresh = 0;
-                    for (int i = lane; i < L; i += 32) {
-                        const int t = src[i];
-                        fresh += ((unsigned)t < (unsigned)H && !test_bit(bm, t)) ? 1 : 0;
-                    }
-                    fresh = warp_sum(fresh);
-                    if (count + fresh <= lim) {
+                    if (added == 0) {
+                        fresh = sm.newc[c];
+                    } else {
                         for (int i = lane; i < L; i += 32) {
-                            const int t = src[i];
+                            const int t = lst[i];
+                            fresh += ((unsigned)t < (unsigned)H && !test_bit(bm, t)) ? 1 : 0;
+                        }
+                        fresh = warp_sum(fresh);
+                    }
+                    if (count + fresh > lim) continue;
+                    if (fresh > 0) {
+                        for (int i = lane; i < L; i += 32) {
+                            const int t = lst[i];
                             if ((unsigned)t < (unsigned)H) set_bit(bm, t);
                         }
                         __syncwarp();
-                        count += fresh;
-                        raw_acc += L;
-                        if (lane == 0) feat[nf] = sm.cand_bucket[cc];
-                        ++nf;
                     }
+                    count += fresh;
+                    added += fresh;
+                    raw_acc += L;
+                    if (lane == 0) feat[nf] = sm.cand_bucket[c];
+                    ++nf;
                 }
                 if (lane == 0) {
-                    sm.flags[1] = nf;
-                    sm.red[1] = raw_acc;
-                    sm.red[2] = count;
+                    sm.flags[3] = nf;
+                    sm.red[2] = raw_acc;
                 }
             }
             __syncthreads();
-            nf = sm.flags[1];
-            raw_acc = sm.red[1];
-            count = sm.red[2];
-            c = c_end;
-            __syncthreads();
+            nf = sm.flags[3];
+            raw_acc = sm.red[2];
         }
     }
     __syncthreads();
@@ -366,16 +331,20 @@ extern "C" int pk_union(uint64_t offsets, uint64_t lens, uint64_t ids, int64_t i
         !features || !n_features || !raw)
         return PK_ERR_ARG;
     const int Wmax = (max_history + 31) / 32;
-    const size_t base = (size_t)((Wmax + 3) & ~3) * 4 + (size_t)kStage * 4;
-    const size_t with_hash = base + (size_t)2 * kHashSlots * 4;
+    const size_t bitmap = (size_t)((Wmax + 3) & ~3) * 4;
     const size_t cap = 200 * 1024;
-    if (base > cap) return PK_ERR_UNSUPPORTED;
-    const int use_hash = with_hash <= cap ? 1 : 0;
-    const size_t smem = use_hash ? with_hash : base;
-    cudaFuncSetAttribute(union_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    union_kernel<<<U, kUnionThreads, smem, (cudaStream_t)stream>>>(
+    // Hash of 2^13 slots (rounds of <= 4096 list entries) when the bitmap
+    // leaves room, else 2^10; the rest stages lists (at least 2048 ids).
+    int bits = 0;
+    for (int b = 13; b >= 10; --b)
+        if (bitmap + ((size_t)2 << b) * 4 + 2048 * 4 <= cap) { bits = b; break; }
+    if (!bits) return PK_ERR_UNSUPPORTED;
+    const size_t used = bitmap + ((size_t)2 << bits) * 4;
+    const int stage_cap = (int)((cap - used) / 4);
+    cudaFuncSetAttribute(union_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cap);
+    union_kernel<<<U, kUnionThreads, cap, (cudaStream_t)stream>>>(
         (const int*)offsets, (const int*)lens, (const int*)ids, ids_stride, (const int*)order, (const int*)n_order,
-        order_stride, (const int*)history, (const long long*)limit, F, max_history, use_hash, (int*)out_ids,
+        order_stride, (const int*)history, (const long long*)limit, F, max_history, bits, stage_cap, (int*)out_ids,
         out_stride, (int*)out_count, (int*)features, (int*)n_features, (long long*)raw, (int*)status);
     PK_CHECK_LAUNCH();
     return PK_OK;

@@ -20,7 +20,8 @@ class SparseDecode:
     def __init__(self, index: DeviceIndex, sae, *, heads_per_unit: int = 4, router: str = "q_activation",
                  query_scale: float = 1.0, query_topk: int | None = None, unique_cap: float | None = None,
                  budget: int | None = None, terms=("count", "mean", "variance"), splits: int | None = None,
-                 max_history: int | None = None, workspace: nv.Workspace | None = None):
+                 max_history: int | None = None, workspace: nv.Workspace | None = None,
+                 exact_encode: bool = False):
         if router not in ("q_activation", "moments"):
             raise ValueError("router must be 'q_activation' or 'moments'")
         if unique_cap is not None and budget is not None:
@@ -57,6 +58,9 @@ class SparseDecode:
         self.ids = torch.zeros(U, max(1, self.id_width), dtype=torch.int32, device=dev)
         self.score = torch.zeros(U, self.F, device=dev) if router == "moments" else None
         self.out = None
+        # Bound-filtered routing (tensor-core approximation + exact recompute
+        # of the candidates) unless the all-features exact encode is asked for.
+        self.prep = (None, None) if exact_encode else self.sae.prepared()
 
     def sync_history(self) -> None:
         """Refresh per-unit history and limits after the index grew (append)."""
@@ -76,8 +80,8 @@ class SparseDecode:
         idx = self.index
         if self.router == "q_activation":
             nbytes = nv.query("pk_route_qact_workspace_bytes", U, G, F, k)
-            nv.call("pk_route_qact", q, nv.dtype_code(q), None, U, self.sae.W_enc, self.sae.b_enc, self.query_scale,
-                    idx.lens, U, G, d, F, k, self.ws.get(("qact", U, G, F, k), nbytes), nbytes, self.order,
+            nv.call("pk_route_qact", q, nv.dtype_code(q), None, U, self.sae.W_enc, self.sae.b_enc, self.prep[0],
+                    self.prep[1], self.query_scale, idx.lens, U, G, d, F, k, self.ws.get(("qact", U, G, F, k), nbytes), nbytes, self.order,
                     self.n_order, self.width, None, None)
         else:
             bits = ((nv.PK_TERM_COUNT if "count" in self.terms else 0)

@@ -45,6 +45,17 @@ class SAEParams:
     def to(self, device) -> "SAEParams":
         return SAEParams(self.W_enc.to(device), self.b_enc.to(device), self.key_mean, self.query_topk)
 
+    def prepared(self):
+        """(W_bf16[F, d], w_norm[F]) for the bound-filtered routing path,
+        computed once on the device (pk_sae_prepare)."""
+        cached = getattr(self, "_prep", None)
+        if cached is None or cached[0].device != self.W_enc.device:
+            wb = torch.empty(self.W_enc.shape, dtype=torch.bfloat16, device=self.W_enc.device)
+            wn = torch.empty(self.features, dtype=torch.float32, device=self.W_enc.device)
+            nv.call("pk_sae_prepare", self.W_enc, self.features, self.head_dim, wb, wn)
+            cached = self._prep = (wb, wn)
+        return cached
+
     @classmethod
     def of(cls, sae, device=None) -> "SAEParams":
         """Accepts an SAEParams or any object with the reference SharedSAE's
@@ -90,8 +101,10 @@ class DeviceIndex:
     @classmethod
     def build(cls, keys: torch.Tensor, sae, key_scale: float = 1.0, *, center=None, moments: bool = True,
               slack_frac: float = 0.0, slack_min: int = 0, workspace: nv.Workspace | None = None,
-              boundary_capacity: int | None = None) -> "DeviceIndex":
-        """Index every unit's keys (core.py:92-103 per unit)."""
+              boundary_capacity: int | None = None, exact: bool = False) -> "DeviceIndex":
+        """Index every unit's keys (core.py:92-103 per unit).  By default the
+        activations are bounded on the tensor cores and only undecided
+        entries recomputed; exact=True computes every activation in fp32."""
         keys, U, N, d, us, rs = _unit_view(keys)
         if N == 0 or key_scale <= 0:
             raise ValueError("nonempty [history,head_dim] keys and positive scale required")
@@ -109,28 +122,33 @@ class DeviceIndex:
             c = torch.as_tensor(center, dtype=torch.float32, device=keys.device).reshape(-1, d)
             idx.center.copy_(c.expand(U, d))
         idx._encode(keys, dt, us, rs, N, sae, key_scale, token_base=0, workspace=workspace,
-                    boundary_capacity=boundary_capacity)
+                    boundary_capacity=boundary_capacity, exact=exact)
         idx.history = N
         if moments:
             nv.call("pk_summarize", keys, dt, us, rs, idx.offsets, idx.lens, idx.ids, idx.ids.stride(0), U, d, F,
                     idx.mean, idx.var)
         return idx
 
-    def _encode(self, keys, dt, us, rs, N, sae, key_scale, token_base, workspace, boundary_capacity):
+    def _encode(self, keys, dt, us, rs, N, sae, key_scale, token_base, workspace, boundary_capacity, exact=False):
         U, F, d = self.U, self.F, self.d
         ws = workspace or nv.Workspace(keys.device)
         status = torch.zeros(1, dtype=torch.int32, device=keys.device)
-        bcap = boundary_capacity or (2 * N * sae.key_mean + 65536)
-        for _ in range(4):
+        bcap = boundary_capacity or (4 * N * sae.key_mean + 65536)
+        wb, wn = (None, None) if exact else sae.prepared()
+        for _ in range(6):
             nbytes = nv.query("pk_build_workspace_bytes", U, N, F, sae.key_mean, bcap)
             buf = ws.get(("build", U, N, F, bcap), nbytes)
             status.zero_()
-            nv.call("pk_build_index", keys, dt, us, rs, self.center, float(key_scale), sae.W_enc, sae.b_enc, U, N, d,
-                    F, sae.key_mean, token_base, self.slack_frac, self.slack_min, self.offsets, self.lens, self.ids,
-                    self.ids.stride(0), bcap, buf, nbytes, status)
+            nv.call("pk_build_index", keys, dt, us, rs, self.center, float(key_scale), sae.W_enc, sae.b_enc, wb, wn, U,
+                    N, d, F, sae.key_mean, token_base, self.slack_frac, self.slack_min, self.offsets, self.lens,
+                    self.ids, self.ids.stride(0), bcap, buf, nbytes, status)
             v = int(status.item())
             if v & nv.STATUS_BOUNDARY_FULL:
                 bcap *= 4
+                continue
+            if v & nv.STATUS_NEEDS_EXACT and wb is not None:
+                # The bounds could not bracket the threshold: exact encode.
+                wb, wn = None, None
                 continue
             nv.check_status(status, "build_index")
             return
@@ -148,18 +166,22 @@ class DeviceIndex:
         sae = SAEParams.of(sae, new_keys.device)
         ws = workspace or nv.Workspace(new_keys.device)
         status = torch.zeros(1, dtype=torch.int32, device=new_keys.device)
-        bcap = 2 * n * sae.key_mean + 65536
+        bcap = 4 * n * sae.key_mean + 65536
         dt = nv.dtype_code(new_keys)
-        for _ in range(6):
+        wb, wn = sae.prepared()
+        for _ in range(8):
             nbytes = nv.query("pk_append_workspace_bytes", U, n, d, self.F, sae.key_mean, bcap)
             buf = ws.get(("append", U, n, self.F, bcap), nbytes)
             status.zero_()
             nv.call("pk_append_index", new_keys, dt, us, rs, n, self.center, float(key_scale), sae.W_enc, sae.b_enc,
-                    U, d, self.F, sae.key_mean, self.history, self.offsets, self.lens, self.ids, self.ids.stride(0),
-                    self.mean, self.var, bcap, buf, nbytes, status)
+                    wb, wn, U, d, self.F, sae.key_mean, self.history, self.offsets, self.lens, self.ids,
+                    self.ids.stride(0), self.mean, self.var, bcap, buf, nbytes, status)
             v = int(status.item())
             if v & nv.STATUS_BOUNDARY_FULL:
                 bcap *= 4
+                continue
+            if v & nv.STATUS_NEEDS_EXACT and wb is not None:
+                wb, wn = None, None
                 continue
             if v & nv.STATUS_BUCKET_FULL:
                 # Nothing was written: make room and retry.

@@ -19,6 +19,7 @@ PK_F32, PK_BF16 = 0, 1
 PK_TERM_COUNT, PK_TERM_MEAN, PK_TERM_VARIANCE = 1, 2, 4
 STATUS_BUCKET_FULL, STATUS_BOUNDARY_FULL, STATUS_MEMBERS_FULL = 1, 2, 4
 STATUS_BUCKET_TOO_BIG, STATUS_OUT_FULL, STATUS_HISTORY_TOO_LONG = 8, 16, 32
+STATUS_NEEDS_EXACT = 64
 STATUS_BITS = {
     1: "bucket region full (append)",
     2: "boundary buffer full (build)",
@@ -26,6 +27,7 @@ STATUS_BITS = {
     8: "bucket larger than the sort limit (build)",
     16: "union output row too short",
     32: "history longer than the union bitmap",
+    64: "bounds could not bracket the threshold: exact build needed",
 }
 
 # name: (argument codes including the trailing stream, restype).
@@ -34,7 +36,8 @@ SIGNATURES = {
     "pk_version": ("", ctypes.c_int),
     "pk_supported_head_dim": ("i", ctypes.c_int),
     "pk_route_qact_workspace_bytes": ("iiii", ctypes.c_size_t),
-    "pk_route_qact": ("PiPiPPfPiiiiiPPPPiPPP", ctypes.c_int),
+    "pk_route_qact": ("PiPiPPPPfPiiiiiPPPPiPPP", ctypes.c_int),
+    "pk_sae_prepare": ("PiiPPP", ctypes.c_int),
     "pk_route_moments_workspace_bytes": ("iii", ctypes.c_size_t),
     "pk_route_moments": ("PiPPPiiiiiiPPPPPiP", ctypes.c_int),
     "pk_union": ("PPPlPPiPPiiiPlPPPPPP", ctypes.c_int),
@@ -45,10 +48,10 @@ SIGNATURES = {
     "pk_key_center": ("PilliliPP", ctypes.c_int),
     "pk_build_ids_capacity": ("liifi", ctypes.c_int64),
     "pk_build_workspace_bytes": ("iliil", ctypes.c_size_t),
-    "pk_build_index": ("PillPfPPiliiilfiPPPllPPPP", ctypes.c_int),
+    "pk_build_index": ("PillPfPPPPiliiilfiPPPllPPPP", ctypes.c_int),
     "pk_summarize": ("PillPPPliiiPPP", ctypes.c_int),
     "pk_append_workspace_bytes": ("iliiil", ctypes.c_size_t),
-    "pk_append_index": ("PilllPfPPiiiilPPPlPPlPPPP", ctypes.c_int),
+    "pk_append_index": ("PilllPfPPPPiiiilPPPlPPlPPPP", ctypes.c_int),
 }
 _CT = {"P": ctypes.c_uint64, "i": ctypes.c_int, "l": ctypes.c_int64, "f": ctypes.c_float}
 # Entry points that take the stream as their last argument.

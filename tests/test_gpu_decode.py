@@ -223,3 +223,92 @@ def test_append_grows_regions_when_full(pk, oracle):
     assert np.array_equal(ids, oidx.ids)
     assert np.array_equal(idx.mean[0].cpu().numpy().view(np.uint32), oidx.mean.view(np.uint32))
     assert np.array_equal(idx.var[0].cpu().numpy().view(np.uint32), oidx.variance.view(np.uint32))
+
+
+def test_bound_filtered_routing_equals_exact_encode(pk, batch):
+    """The tensor-core-filtered router and the all-features exact encode
+    give identical candidate orders and unions on many queries."""
+    B = batch
+    fast = pk.SparseDecode(B["idx"], B["sae"], heads_per_unit=B["G"], unique_cap=512 / B["N"])
+    exact = pk.SparseDecode(B["idx"], B["sae"], heads_per_unit=B["G"], unique_cap=512 / B["N"], exact_encode=True)
+    g = torch.Generator(device="cuda").manual_seed(9)
+    for rep in range(20):
+        q = (B["Q"].float() + 0.5 * torch.randn(B["Q"].shape, device="cuda", generator=g)).bfloat16().contiguous()
+        fast.route(q)
+        exact.route(q)
+        torch.cuda.synchronize()
+        assert torch.equal(fast.n_order, exact.n_order), rep
+        for u in range(B["U"]):
+            n = int(exact.n_order[u])
+            assert torch.equal(fast.order[u, :n], exact.order[u, :n]), (rep, u)
+            c = int(exact.count[u])
+            assert int(fast.count[u]) == c
+            assert torch.equal(fast.ids[u, :c], exact.ids[u, :c])
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_union_greedy_matches_oracle_on_large_buckets(pk, oracle, seed):
+    """Budgeted union on synthetic CSR indexes whose buckets are large and
+    overlap heavily (multi-round hash path, single-bucket rounds, accepted
+    buckets after the first skip), against the oracle's greedy."""
+    from prismkv_b200 import native as nv
+    rs = np.random.RandomState(100 + seed)
+    U, H, F, n_cand = 6, 60000, 300, 200
+    dev = torch.device("cuda")
+    lists_all, orders = [], []
+    for u in range(U):
+        sizes = rs.choice([3, 40, 300, 2000, 9000], size=F, p=[0.2, 0.4, 0.3, 0.08, 0.02])
+        hot = rs.randint(0, H, size=3000)  # shared tokens -> overlap between buckets
+        lists = []
+        for f in range(F):
+            pool = np.concatenate([hot, rs.randint(0, H, size=int(sizes[f]))])
+            lists.append(np.unique(rs.choice(pool, size=min(len(pool), int(sizes[f])), replace=False)))
+        lists_all.append(lists)
+        orders.append(rs.permutation(F)[:n_cand])
+    dindex = pk.index.from_lists([[torch.from_numpy(x) for x in l] for l in lists_all], H, 128, dev)
+    order = torch.tensor(np.stack(orders), dtype=torch.int32, device=dev)
+    n_order = torch.full((U,), n_cand, dtype=torch.int32, device=dev)
+    hist = torch.full((U,), H, dtype=torch.int32, device=dev)
+    for lim in (0, 500, 4096, 20000, 10 ** 9):
+        limit = torch.full((U,), lim, dtype=torch.int64, device=dev)
+        out = torch.empty(U, H, dtype=torch.int32, device=dev)
+        cnt = torch.empty(U, dtype=torch.int32, device=dev)
+        feats = torch.empty(U, n_cand, dtype=torch.int32, device=dev)
+        nf = torch.empty(U, dtype=torch.int32, device=dev)
+        raw = torch.empty(U, dtype=torch.int64, device=dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        nv.call("pk_union", dindex.offsets, dindex.lens, dindex.ids, dindex.ids.stride(0), order, n_order, n_cand,
+                hist, limit, U, F, H, out, H, cnt, feats, nf, raw, status)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        for u in range(U):
+            oi = oracle.index_from_lists(H, np.zeros(128, np.float32), lists_all[u])
+            ids, fts, rw = oracle.select_from_order(orders[u], oi, lim)
+            c = int(cnt[u])
+            assert np.array_equal(out[u, :c].cpu().numpy().astype(np.int64), ids), (lim, u)
+            assert feats[u, :int(nf[u])].cpu().tolist() == fts, (lim, u)
+            assert int(raw[u]) == rw, (lim, u)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_bound_filtered_build_equals_exact_build(pk, dtype):
+    """Tensor-core bounds + exact recompute of the undecided band give the
+    same memberships as computing every activation exactly."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(21)
+    U, N, d, F, C = 4, 6000, 128, 1024, 48
+    centers = torch.randn(U, C, d, device=dev, generator=g)
+    cid = torch.randint(0, C, (U, N), device=dev, generator=g)
+    keys = (torch.gather(centers, 1, cid[..., None].expand(U, N, d)) +
+            0.3 * torch.randn(U, N, d, device=dev, generator=g)).to(dtype)
+    W = torch.randn(F, d, device=dev, generator=g) / d ** 0.5
+    b = 0.05 * torch.randn(F, device=dev, generator=g)
+    sae = pk.SAEParams(W, b, key_mean=8, query_topk=16)
+    fast = pk.DeviceIndex.build(keys, sae, 1.3, moments=False)
+    exact = pk.DeviceIndex.build(keys, sae, 1.3, moments=False, exact=True)
+    assert torch.equal(fast.center, exact.center)
+    for u in range(U):
+        cf, idf = fast.csr(u)
+        ce, ide = exact.csr(u)
+        assert np.array_equal(cf, ce), u
+        assert np.array_equal(idf, ide), u

@@ -60,16 +60,18 @@ def raw(lib, name, *args):
 
 def test_argument_errors_are_negative(lib):
     # U = 0, head dim 64, zero scale: rejected before any launch.
-    assert raw(lib, "pk_route_qact", 1, 1, 0, 0, 1, 1, 1.0, 1, 0, 4, 128, 64, 8, 1, 1 << 20, 1, 1, 32, 0, 0, 0) < 0
-    assert raw(lib, "pk_route_qact", 1, 1, 0, 1, 1, 1, 1.0, 1, 1, 4, 64, 64, 8, 1, 1 << 20, 1, 1, 32, 0, 0, 0) == -2
-    assert raw(lib, "pk_route_qact", 1, 1, 0, 1, 1, 1, 0.0, 1, 1, 4, 128, 64, 8, 1, 1 << 20, 1, 1, 32, 0, 0, 0) < 0
-    assert raw(lib, "pk_route_qact", 1, 1, 0, 1, 1, 1, 1.0, 1, 1, 4, 128, 64, 8, 1, 16, 1, 1, 32, 0, 0, 0) == -3
+    qa = "pk_route_qact"
+    assert raw(lib, qa, 1, 1, 0, 0, 1, 1, 0, 0, 1.0, 1, 0, 4, 128, 64, 8, 1, 1 << 20, 1, 1, 32, 0, 0, 0) < 0
+    assert raw(lib, qa, 1, 1, 0, 1, 1, 1, 0, 0, 1.0, 1, 1, 4, 64, 64, 8, 1, 1 << 20, 1, 1, 32, 0, 0, 0) == -2
+    assert raw(lib, qa, 1, 1, 0, 1, 1, 1, 0, 0, 0.0, 1, 1, 4, 128, 64, 8, 1, 1 << 20, 1, 1, 32, 0, 0, 0) < 0
+    assert raw(lib, qa, 1, 1, 0, 1, 1, 1, 0, 0, 1.0, 1, 1, 4, 128, 64, 8, 1, 16, 1, 1, 32, 0, 0, 0) == -3
+    assert raw(lib, "pk_sae_prepare", 1, 64, 64, 1, 1, 0) == -2
     assert raw(lib, "pk_sparse_av", 1, 1, 1, 1, 1, 0, 0, 64, 1, 1, 1, 1, 1, 1, 4, 64, 1, 0, 0, 1, 0, 0) == -2
     assert raw(lib, "pk_sparse_av", 1, 1, 1, 1, 1, 0, 0, 128, 1, 1, 1, 1, 1, 1, 17, 128, 1, 0, 0, 1, 0, 0) == -1
     assert raw(lib, "pk_union", 0, 0, 0, 0, 0, 0, 1, 0, 0, 1, 8, 64, 0, 0, 0, 0, 0, 0, 0, 0) == -1
     assert raw(lib, "pk_lse_merge", 1, 0, 4, 128, 1, 1, 0) == -1
-    assert raw(lib, "pk_build_index", 1, 1, 0, 128, 1, 1.0, 1, 1, 1, 100, 128, 64, 8, 0, 0.0, 0, 1, 1, 1, 10, 1,
-               1, 1 << 30, 1, 0) == -1  # ids_stride below capacity
+    assert raw(lib, "pk_build_index", 1, 1, 0, 128, 1, 1.0, 1, 1, 0, 0, 1, 100, 128, 64, 8, 0, 0.0, 0, 1, 1, 1, 10,
+               1, 1, 1 << 30, 1, 0) == -1  # ids_stride below capacity
 
 
 def test_missing_library_fails_loudly(lib, monkeypatch, tmp_path):
