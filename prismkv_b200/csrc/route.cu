@@ -195,14 +195,24 @@ __device__ void head_finish(int u, int g, int G, int F, int k, int m, QactSmem& 
     }
     __syncthreads();
     const float s = sm.norm;
+    // Stored in feature order, unused slots INT_MAX, for the binary
+    // searches of the aggregation below.
     int* hid = head_ids + ((int64_t)u * G + g) * k;
     float* hv = head_val + ((int64_t)u * G + g) * k;
     for (int r = tid; r < k; r += nt) {
-        float v = r < m ? __uint_as_float(sm.selkey[r]) : 0.f;
-        v = __fdiv_rn(v, s);
-        v = __fdiv_rn(v, (float)G);
-        hid[r] = r < m ? sm.sel[r] : -1;
-        hv[r] = v;
+        if (r < m) {
+            const int f = sm.sel[r];
+            int pos = 0;
+            for (int r2 = 0; r2 < m; ++r2) pos += sm.sel[r2] < f;
+            float v = __uint_as_float(sm.selkey[r]);
+            v = __fdiv_rn(v, s);
+            v = __fdiv_rn(v, (float)G);
+            hid[pos] = f;
+            hv[pos] = v;
+        } else {
+            hid[r] = INT32_MAX;
+            hv[r] = 0.f;
+        }
     }
     __threadfence();
     __syncthreads();
@@ -221,16 +231,31 @@ __device__ void head_finish(int u, int g, int G, int F, int k, int m, QactSmem& 
         ev[e] = __ldcg(head_val + (int64_t)u * E + e);
     }
     __syncthreads();
+    // Position of feature f in head hh's sorted picks, or -1.
+    auto find = [&](int hh, int f) -> int {
+        const int* seg = eid + hh * k;
+        int lo = 0, hi = k;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (seg[mid] < f) lo = mid + 1;
+            else hi = mid;
+        }
+        return lo < k && seg[lo] == f ? lo : -1;
+    };
+    // score[f] = 0 + v_h1 + v_h2 + ... over the heads that picked f, in head
+    // order (scatter_add_ of core.py:137), kept at f's first entry.
     for (int e = tid; e < E; e += nt) {
         const int f = eid[e];
         const int h = e / k;
-        bool first = f >= 0;
-        for (int e2 = 0; e2 < h * k && first; ++e2) first = eid[e2] != f;
+        bool first = f != INT32_MAX;
+        for (int hh = 0; hh < h && first; ++hh) first = find(hh, f) < 0;
         float acc = 0.f;
         if (first) {
-            for (int hh = 0; hh < G; ++hh)
-                for (int r = 0; r < k; ++r)
-                    if (eid[hh * k + r] == f) { acc = __fadd_rn(acc, ev[hh * k + r]); break; }
+            acc = ev[e];
+            for (int hh = h + 1; hh < G; ++hh) {
+                const int i = find(hh, f);
+                if (i >= 0) acc = __fadd_rn(acc, ev[hh * k + i]);
+            }
         }
         const bool keep = first && acc > 0.f && counts[(int64_t)u * F + f] > 0;
         sc[e] = acc;
@@ -238,19 +263,29 @@ __device__ void head_finish(int u, int g, int G, int F, int k, int m, QactSmem& 
         if (score && first) score[(int64_t)u * F + f] = acc;
     }
     __syncthreads();
-    // Rank the kept candidates by (score desc, feature asc).
-    for (int e = tid; e < E; e += nt) {
-        const int f = cand[e];
-        if (f < 0) continue;
-        const float v = sc[e];
-        int r = 0;
-        for (int e2 = 0; e2 < E; ++e2) {
-            const int f2 = cand[e2];
-            if (f2 < 0) continue;
-            const float v2 = sc[e2];
-            r += (v2 > v) || (v2 == v && f2 < f);
+    // Rank the kept candidates by (score desc, feature asc); P threads
+    // (a power of two within a warp) share each entry's comparisons.
+    int P = 1;
+    while (P < 32 && 2 * P * E <= nt) P *= 2;
+    {
+        const int e = tid / P, part = tid % P;
+        int f = -1;
+        float v = 0.f;
+        if (e < E) {
+            f = cand[e];
+            v = sc[e];
         }
-        order[(int64_t)u * order_stride + r] = f;
+        int r = 0;
+        if (f >= 0) {
+            for (int e2 = part; e2 < E; e2 += P) {
+                const int f2 = cand[e2];
+                if (f2 < 0) continue;
+                const float v2 = sc[e2];
+                r += (v2 > v) || (v2 == v && f2 < f);
+            }
+        }
+        for (int o = 1; o < P; o <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+        if (f >= 0 && part == 0) order[(int64_t)u * order_stride + r] = f;
     }
     int mine = 0;
     for (int e = tid; e < E; e += nt) mine += cand[e] >= 0;
@@ -325,15 +360,61 @@ __global__ void sae_prepare_kernel(const float* __restrict__ W, int F, __nv_bflo
 }
 
 constexpr int kApxHeads = 64, kApxFeat = 128, kApxThreads = 128;
+constexpr int kMaxGroups = 512;
 
-// v[u, g, f] ~= (q/scale) . W_f + b_f with bf16 operands on mma.sync and fp32
-// accumulation: a 64-head x 128-feature tile per CTA, 16 heads per warp.
+__device__ __forceinline__ uint32_t fkey(float x) {
+    const uint32_t b = __float_as_uint(x);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float fkey_inv(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+// Features per group for the routing threshold estimate: the largest of
+// 128..8 that still leaves at least k groups (at most kMaxGroups), 0 if none.
+__host__ __device__ __forceinline__ int select_group_size(int F, int k) {
+    for (int gs = 128; gs >= 8; gs >>= 1)
+        if ((F + gs - 1) / gs >= k && (F + gs - 1) / gs <= kMaxGroups) return gs;
+    return 0;
+}
+
+// Eight consecutive query values as floats (16-byte bf16 or 2x16-byte fp32
+// loads; query rows are 16-byte aligned).
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&x)[8]) {
+    const uint4 r = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(b[j]);
+        x[2 * j] = f.x;
+        x[2 * j + 1] = f.y;
+    }
+}
+__device__ __forceinline__ void load8(const float* p, float (&x)[8]) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
+// Tensor-core approximation of the query activations with rigorous bounds.
+// v[u, g, f] = (q/scale) . W_f + b_f with bf16 operands on mma.sync and fp32
+// accumulation (a 64-head x 128-feature tile per CTA, 16 heads per warp)
+// differs from the exact fp32 activation by at most
+//     e_f = 2^-6 |x| |W_f| + 2^-20 |v|
+// (bf16 rounding of both operands, 2^-8 relative each, fp32 accumulation and
+// the exact order's own rounding, with a 2x margin; |x| is rounded up by
+// 2^-12 and |W_f| comes from pk_sae_prepare).  The kernel writes the upper
+// bound U = v + e for every feature and, per head, the maximum lower bound
+// L = v - e of every group of gs consecutive features (order-preserving
+// keys; gs = 0 skips the groups).
 template <typename QT>
 __global__ void __launch_bounds__(kApxThreads)
 qact_approx_kernel(const QT* __restrict__ q, const int* __restrict__ units, int n_units, int G,
-                   const __nv_bfloat16* __restrict__ Wb, const float* __restrict__ bias, float query_scale, int F,
-                   float* __restrict__ act) {
+                   const __nv_bfloat16* __restrict__ Wb, const float* __restrict__ bias, const float* __restrict__ wn,
+                   float query_scale, int F, int gs, int ngroups, float* __restrict__ upper,
+                   uint32_t* __restrict__ gmax) {
     extern __shared__ __align__(128) uint8_t apx_smem[];
+    __shared__ float sxn[kApxHeads];
     uint8_t* Xs = apx_smem;                     // [64 rows][256 B] swizzled
     uint8_t* Wt = apx_smem + kApxHeads * 256;   // [128 rows][256 B] swizzled
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -346,18 +427,44 @@ qact_approx_kernel(const QT* __restrict__ q, const int* __restrict__ units, int 
         cp_async_16(smem_addr(Wt) + swz(row, ch), Wb + (int64_t)(valid ? f : 0) * kEncD + ch * 8, valid);
     }
     cp_async_commit_group();
-    for (int e = tid; e < kApxHeads * 64; e += kApxThreads) {
-        const int row = e >> 6, pc = e & 63;
+    // The 64 query rows, 16-byte chunks of 8 values (all loads of a thread
+    // issued before any is used), scaled, rounded to bf16, and their norms.
+    constexpr int kChunks = kApxHeads * 16 / kApxThreads;
+    float xv[kChunks][8];
+#pragma unroll
+    for (int t = 0; t < kChunks; ++t) {
+        const int c = tid + t * kApxThreads, row = c >> 4, ch = c & 15;
         const int h = h0 + row;
-        float x0 = 0.f, x1 = 0.f;
         if (h < n_heads) {
             const int ui = h / G, g = h % G;
             const int u = units ? units[ui] : ui;
-            const int64_t base = ((int64_t)u * G + g) * kEncD + 2 * pc;
-            x0 = __fdiv_rn(load_f(q, base), query_scale);
-            x1 = __fdiv_rn(load_f(q, base + 1), query_scale);
+            load8(q + ((int64_t)u * G + g) * kEncD + ch * 8, xv[t]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) xv[t][j] = 0.f;
         }
-        *reinterpret_cast<__nv_bfloat162*>(Xs + swz(row, pc >> 2) + (pc & 3) * 4) = __floats2bfloat162_rn(x0, x1);
+    }
+    // x = q * (1/scale): within a few ulp of the exact quotient, far inside
+    // the bound's margins (the norm's 2^-12, the operands' 2^-8).
+    const float inv_scale = 1.0f / query_scale;
+#pragma unroll
+    for (int t = 0; t < kChunks; ++t) {
+        const int c = tid + t * kApxThreads, row = c >> 4, ch = c & 15;
+        uint4 packed;
+        uint32_t* pw = reinterpret_cast<uint32_t*>(&packed);
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float xa = xv[t][2 * j] * inv_scale, xb = xv[t][2 * j + 1] * inv_scale;
+            ss = fmaf(xa, xa, fmaf(xb, xb, ss));
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(xa, xb);
+            pw[j] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+        *reinterpret_cast<uint4*>(Xs + swz(row, ch)) = packed;
+        // The 16 chunks of a row sit in 16 consecutive lanes.
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (ch == 0) sxn[row] = sqrtf(ss) * (1.0f + 1.0f / 4096.0f);
     }
     cp_async_wait_group<0>();
     __syncthreads();
@@ -378,32 +485,66 @@ qact_approx_kernel(const QT* __restrict__ q, const int* __restrict__ units, int 
             mma_16816(acc[2 * np + 1], a, b[2], b[3]);
         }
     }
+    // acc[j][2*half + e] is feature f0 + 8j + 2(lane&3) + e of local row
+    // warp*16 + (lane>>2) + 8*half.
+    float bv[16][2], wv[16][2];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int f = f0 + 8 * j + 2 * (lane & 3) + e;
+            bv[j][e] = f < F ? bias[f] : 0.f;
+            wv[j][e] = f < F ? wn[f] : 0.f;
+        }
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
-        const int h = h0 + warp * 16 + (lane >> 2) + half * 8;
-        if (h >= n_heads) continue;
-        const int ui = h / G, g = h % G;
-        const int u = units ? units[ui] : ui;
-        float* out = act + ((int64_t)u * G + g) * F;
+        const int lrow = warp * 16 + (lane >> 2) + half * 8;
+        const int h = h0 + lrow;
+        const bool hv = h < n_heads;
+        int u = 0, g = 0;
+        if (hv) {
+            const int ui = h / G;
+            g = h % G;
+            u = units ? units[ui] : ui;
+        }
+        const float xn = sxn[lrow];
+        float* out = upper + ((int64_t)u * G + g) * F;
+        const int per = gs >> 3, g0 = gs ? f0 / gs : 0;   // 8-feature blocks per group
+        uint32_t* gm = gmax + ((int64_t)u * G + g) * ngroups;
+        const bool writer = gs && hv && (lane & 3) == 0;
+        uint32_t run = 0u;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
             const int f = f0 + 8 * j + 2 * (lane & 3);
-            if (f + 1 < F) {
-                *reinterpret_cast<float2*>(out + f) =
-                    make_float2(acc[j][2 * half] + bias[f], acc[j][2 * half + 1] + bias[f + 1]);
-            } else if (f < F) {
-                out[f] = acc[j][2 * half] + bias[f];
+            float up[2];
+            uint32_t lk = 0u;
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const float v = acc[j][2 * half + e] + bv[j][e];
+                const float err = 0.015625f * xn * wv[j][e] + 9.5367431640625e-07f * fabsf(v);
+                up[e] = v + err;
+                if (f + e < F) lk = max(lk, fkey(v - err));
+            }
+            if (hv) {
+                if ((F & 1) == 0 && f + 1 < F) {
+                    *reinterpret_cast<float2*>(out + f) = make_float2(up[0], up[1]);
+                } else {
+                    if (f < F) out[f] = up[0];
+                    if (f + 1 < F) out[f + 1] = up[1];
+                }
+            }
+            // At a group's last 8-feature block, reduce over the quad
+            // (the four lanes holding the row's features of each block).
+            run = max(run, lk);
+            if (gs && ((j + 1) & (per - 1)) == 0) {
+                run = max(run, __shfl_xor_sync(0xffffffffu, run, 1));
+                run = max(run, __shfl_xor_sync(0xffffffffu, run, 2));
+                const int gi = g0 + (j + 1) / per - 1;
+                if (writer && gi < ngroups) gm[gi] = run;
+                run = 0u;
             }
         }
     }
-}
-
-__device__ __forceinline__ uint32_t fkey(float x) {
-    const uint32_t b = __float_as_uint(x);
-    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-__device__ __forceinline__ float fkey_inv(uint32_t k) {
-    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
 template <int ORDER>
@@ -446,100 +587,148 @@ __device__ __forceinline__ float exact_dot(const float* __restrict__ x, const fl
 }
 
 constexpr int kCandCap = 2048;
+constexpr int kSelThreads = 256;
+constexpr int kWarpCand = kCandCap / (kSelThreads / 32);   // candidate slots per warp
 
 struct FastSmem {
     QactSmem q;
     float x[kEncD];
-    float red[32];
     int cand[kCandCap];
     float cval[kCandCap];
+    uint32_t gkey[kMaxGroups];
     int wc[32];
-    int ncand;
+    float lam;
 };
 
-// Per (unit, head): lambda = k-th largest lower bound; candidates = features
-// whose upper bound reaches lambda (a superset of the exact top-k, ties
-// included); exact fp32 activations for the candidates in the reference's
-// dot-product order; exact top-k among them.  Too many candidates (near-
-// degenerate inputs): every feature is recomputed exactly instead.
+// Per (unit, head), the exact top-k of the activations from the bounds of
+// qact_approx_kernel (L_f <= exact_f <= U_f):
+//   lambda' = the k-th largest of the per-group maxima of L.  At least k
+//             features have L >= lambda', so lambda' <= the k-th largest L
+//             <= the k-th largest exact activation.
+//   candidates = features with U >= lambda' (and U > 0): every feature whose
+//             exact value reaches the k-th largest -- ties included -- is a
+//             candidate, so the exact top-k among them (stable descending,
+//             ties -> lower feature id, core.py:134) is the exact top-k.
+// Candidates get exact fp32 activations in the reference's dot-product
+// order.  Too many candidates (near-degenerate inputs): every feature is
+// recomputed.
 template <int ORDER, typename QT>
-__global__ void __launch_bounds__(256)
-qact_select_fast_kernel(const QT* __restrict__ q, const float* __restrict__ act, const int* __restrict__ units, int G,
-                        const float* __restrict__ W, const float* __restrict__ bias, const float* __restrict__ wn,
-                        float query_scale, int F, int k, const int* __restrict__ counts, int* __restrict__ head_ids,
-                        float* __restrict__ head_val, int* __restrict__ unit_done, int* __restrict__ order,
-                        int* __restrict__ n_order, int order_stride, float* __restrict__ score, int store_up) {
-    // sA[F]: order-preserving keys of the lower bounds (later: exact values
-    // if every feature is recomputed); sB[F]: upper bounds when they fit.
+__global__ void __launch_bounds__(kSelThreads)
+qact_select_fast_kernel(const QT* __restrict__ q, const float* __restrict__ upper,
+                        const uint32_t* __restrict__ gmax, int ngroups, const int* __restrict__ units, int G,
+                        const float* __restrict__ W, const float* __restrict__ bias, float query_scale, int F, int k,
+                        const int* __restrict__ counts, int* __restrict__ head_ids, float* __restrict__ head_val,
+                        int* __restrict__ unit_done, int* __restrict__ order, int* __restrict__ n_order,
+                        int order_stride, float* __restrict__ score) {
+    // sA[F]: exact values when every feature is recomputed; head_finish's
+    // aggregation scratch.
     extern __shared__ __align__(16) uint32_t sA[];
-    float* sB = reinterpret_cast<float*>(sA + F);
     __shared__ FastSmem sm;
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
     const int ui = blockIdx.x / G, g = blockIdx.x % G;
     const int u = units ? units[ui] : ui;
-    const float* a = act + ((int64_t)u * G + g) * F;
-    float ss = 0.f;
-    for (int c = tid; c < kEncD; c += nt) {
-        const float x = __fdiv_rn(load_f(q, ((int64_t)u * G + g) * kEncD + c), query_scale);
-        sm.x[c] = x;
-        ss = fmaf(x, x, ss);
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) sm.red[warp] = ss;
+    const float* up = upper + ((int64_t)u * G + g) * F;
+    const uint32_t* gk = gmax + ((int64_t)u * G + g) * ngroups;
+    for (int i = tid; i < ngroups; i += nt) sm.gkey[i] = gk[i];
+    for (int c = tid; c < kEncD; c += nt) sm.x[c] = __fdiv_rn(load_f(q, ((int64_t)u * G + g) * kEncD + c), query_scale);
+    if (tid == 0) sm.lam = -INFINITY;
     __syncthreads();
-    if (tid == 0) {
-        float t = 0.f;
-        for (int w = 0; w < nw; ++w) t += sm.red[w];
-        sm.red[0] = sqrtf(t) * (1.0f + 1.0f / 4096.0f);
-    }
-    __syncthreads();
-    const float xn = sm.red[0];
-    // |v_approx - v_exact| <= eps_f: bf16 operand rounding (2^-8 each),
-    // fp32 accumulation and the exact order's own rounding, x2 margin.
-    auto eps = [&](int f, float v) { return 0.015625f * xn * wn[f] + 9.5367431640625e-07f * fabsf(v); };
-    // One streaming pass (independent, coalesced loads) computes both bounds.
-    for (int i = tid; i < F; i += nt) {
-        const float v = a[i];
-        const float e = eps(i, v);
-        sA[i] = fkey(v - e);
-        if (store_up) sB[i] = v + e;
-    }
-    __syncthreads();
-    auto upper = [&](int i) { return store_up ? sB[i] : a[i] + eps(i, a[i]); };
-    const int m0 = block_topk(
-        F, k, [&](int i) { return sA[i]; }, [&](int i) { return true; }, sm.q.sel, sm.q.selkey, sm.q.tk);
-    const float lam = m0 >= k ? fkey_inv(sm.q.selkey[k - 1]) : -INFINITY;
-    const bool pos_only = !(lam > 0.f);
-    // Ordered gather of the candidates (feature order).
-    const int seg = ((F + nw - 1) / nw + 31) / 32 * 32;
-    const int w0 = min(F, warp * seg), w1 = min(F, w0 + seg);
-    int mine = 0;
-    for (int base = w0; base < w1; base += 32) {
-        const int i = base + lane;
-        bool c = false;
-        if (i < w1) {
-            const float up = upper(i);
-            c = pos_only ? up > 0.f : up >= lam;
+    // lambda' = k-th largest group maximum (rank by value, then group index);
+    // no groups (too few features): -inf, every positive U is a candidate.
+    for (int i = tid; i < ngroups; i += nt) {
+        const uint32_t ki = sm.gkey[i];
+        int r = 0;
+        for (int j = 0; j < ngroups; ++j) {
+            const uint32_t kj = sm.gkey[j];
+            r += (kj > ki) || (kj == ki && j < i);
         }
-        mine += __popc(__ballot_sync(0xffffffffu, c));
+        if (r == k - 1) sm.lam = fkey_inv(ki);
+    }
+    __syncthreads();
+    const float lam = sm.lam;
+    const bool pos_only = !(lam > 0.f);
+    auto is_cand = [&](float u_) { return pos_only ? u_ > 0.f : u_ >= lam; };
+
+    // One pass over U: each warp owns a contiguous segment (a multiple of
+    // 128 features) and appends its candidates, in feature order, to its own
+    // slots; 16-byte loads, sixteen per lane in flight, when rows are aligned.
+    const bool vec = (F & 3) == 0 && (reinterpret_cast<uintptr_t>(up) & 15) == 0;
+    const int seg = ((F + nw - 1) / nw + 127) / 128 * 128;
+    const int s0 = min(F, warp * seg), s1 = min(F, s0 + seg);
+    int* wslot = sm.cand + warp * kWarpCand;
+    int mine = 0;
+    auto take = [&](int base, const float (&v)[4]) {
+        unsigned m = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            if (base + 4 * lane + c < s1 && is_cand(v[c])) m |= 1u << c;
+        const int cnt = __popc(m);
+        if (__ballot_sync(0xffffffffu, cnt != 0)) {
+            const int inc = warp_inclusive_scan(cnt);
+            int at = mine + inc - cnt;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                if (m & (1u << c)) {
+                    if (at < kWarpCand) wslot[at] = base + 4 * lane + c;
+                    ++at;
+                }
+            mine += __shfl_sync(0xffffffffu, inc, 31);
+        }
+    };
+    if (vec) {
+        constexpr int kBatch = 16;  // 16-byte loads in flight per lane
+        for (int b0 = s0; b0 < s1; b0 += 128 * kBatch) {
+            float4 va[kBatch];
+#pragma unroll
+            for (int t = 0; t < kBatch; ++t) {
+                const int i = b0 + 128 * t + 4 * lane;
+                va[t] = i < s1 ? *reinterpret_cast<const float4*>(up + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int t = 0; t < kBatch; ++t) {
+                if (b0 + 128 * t >= s1) break;
+                const float v[4] = {va[t].x, va[t].y, va[t].z, va[t].w};
+                take(b0 + 128 * t, v);
+            }
+        }
+    } else {
+        for (int b = s0; b < s1; b += 128) {
+            float v[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int i = b + 4 * lane + c;
+                v[c] = i < s1 ? up[i] : 0.f;
+            }
+            take(b, v);
+        }
     }
     if (lane == 0) sm.wc[warp] = mine;
     __syncthreads();
-    int before = 0, total = 0;
-    for (int w = 0; w < nw; ++w) { if (w < warp) before += sm.wc[w]; total += sm.wc[w]; }
-    const bool all_exact = total > kCandCap;
+    int total = 0;
+    bool all_exact = false;
+    for (int w = 0; w < nw; ++w) {
+        total += sm.wc[w];
+        all_exact |= sm.wc[w] > kWarpCand;
+    }
     if (!all_exact) {
-        int out = before;
-        for (int base = w0; base < w1; base += 32) {
-            const int i = base + lane;
-            bool c = false;
-            if (i < w1) {
-                const float up = upper(i);
-                c = pos_only ? up > 0.f : up >= lam;
+        // Compact the per-warp slots into feature order.
+        constexpr int kPer = kCandCap / kSelThreads;
+        int vals[kPer];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int p = tid + i * nt;
+            vals[i] = -1;
+            if (p < total) {
+                int w = 0, before = 0;
+                while (before + sm.wc[w] <= p) { before += sm.wc[w]; ++w; }
+                vals[i] = sm.cand[w * kWarpCand + (p - before)];
             }
-            const unsigned cm = __ballot_sync(0xffffffffu, c);
-            if (c) sm.cand[out + __popc(cm & lanemask_lt())] = i;
-            out += __popc(cm);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int p = tid + i * nt;
+            if (p < total) sm.cand[p] = vals[i];
         }
     }
     __syncthreads();
@@ -551,10 +740,34 @@ qact_select_fast_kernel(const QT* __restrict__ q, const float* __restrict__ act,
             sm.cval[c] = z > 0.f ? z : 0.f;
         }
         __syncthreads();
-        m = block_topk(
-            total, k, [&](int i) { return __float_as_uint(sm.cval[i]); }, [&](int i) { return sm.cval[i] > 0.f; },
-            sm.q.sel, sm.q.selkey, sm.q.tk);
-        for (int r = tid; r < m; r += nt) sm.q.sel[r] = sm.cand[sm.q.sel[r]];
+        if (total <= 512) {
+            // Exact rank among the candidates: (value desc, feature asc),
+            // positive values only; the candidates are in feature order.
+            int npos = 0;
+            for (int c = tid; c < total; c += nt) npos += sm.cval[c] > 0.f;
+            npos = warp_sum(npos);
+            if (lane == 0) sm.wc[warp] = npos;
+            __syncthreads();
+            int all_pos = 0;
+            for (int w = 0; w < nw; ++w) all_pos += sm.wc[w];
+            m = min(k, all_pos);
+            for (int c = tid; c < total; c += nt) {
+                const float vc = sm.cval[c];
+                if (!(vc > 0.f)) continue;
+                int r = 0;
+                for (int j = 0; j < total; ++j) {
+                    const float vj = sm.cval[j];
+                    r += (vj > vc) || (vj == vc && j < c);
+                }
+                if (r < m) { sm.q.sel[r] = sm.cand[c]; sm.q.selkey[r] = __float_as_uint(vc); }
+            }
+            __syncthreads();
+        } else {
+            m = block_topk(
+                total, k, [&](int i) { return __float_as_uint(sm.cval[i]); },
+                [&](int i) { return sm.cval[i] > 0.f; }, sm.q.sel, sm.q.selkey, sm.q.tk);
+            for (int r = tid; r < m; r += nt) sm.q.sel[r] = sm.cand[sm.q.sel[r]];
+        }
     } else {
         for (int f = tid; f < F; f += nt) {
             const float z = __fadd_rn(exact_dot<ORDER>(sm.x, W + (int64_t)f * kEncD), bias[f]);
@@ -676,11 +889,21 @@ moments_select_kernel(const float* __restrict__ logits, const int* __restrict__ 
 
 using namespace pk;
 
+// Workspace: activations or upper bounds [U*G, F] fp32, the heads' picks,
+// the per-unit arrival counters, the group maxima [U*G, ngroups].
+static size_t route_groups(int F, int k) {
+    if (k > F) k = F;
+    const int gs = select_group_size(F, k);
+    return gs ? (size_t)(F + gs - 1) / gs : 0;
+}
+
 extern "C" size_t pk_route_qact_workspace_bytes(int U, int G, int F, int k) {
     const size_t act = (size_t)U * G * F * sizeof(float);
     const size_t heads = (size_t)U * G * k * (sizeof(int) + sizeof(float));
     const size_t done = (size_t)U * sizeof(int);
-    return (act + 255) / 256 * 256 + (heads + 255) / 256 * 256 + (done + 255) / 256 * 256;
+    const size_t groups = (size_t)U * G * route_groups(F, k) * sizeof(uint32_t);
+    return (act + 255) / 256 * 256 + (heads + 255) / 256 * 256 + (done + 255) / 256 * 256 +
+           (groups + 255) / 256 * 256;
 }
 
 extern "C" int pk_sae_prepare(uint64_t w_enc, int F, int d, uint64_t w_bf16, uint64_t w_norm, uint64_t stream) {
@@ -713,6 +936,10 @@ extern "C" int pk_route_qact(uint64_t q, int q_dtype, uint64_t units, int n_unit
     float* hval = (float*)(hid + (size_t)U * G * k);
     off += ((size_t)U * G * k * (sizeof(int) + sizeof(float)) + 255) / 256 * 256;
     int* done = (int*)(ws + off);
+    off += ((size_t)U * sizeof(int) + 255) / 256 * 256;
+    uint32_t* gmax = (uint32_t*)(ws + off);
+    const int gs = select_group_size(F, k);
+    const int ngroups = (int)route_groups(F, k);
     const int* ul = (const int*)units;
 
     // The order F.linear takes for a [G, d] block (see file header).
@@ -721,36 +948,35 @@ extern "C" int pk_route_qact(uint64_t q, int q_dtype, uint64_t units, int n_unit
         // Bound-filtered path: approximate encode on the tensor cores, exact
         // recomputation of the features that can reach the top-k.
         if (q_dtype != PK_BF16 && q_dtype != PK_F32) return PK_ERR_ARG;
+        if (q % 16 || w_bf16 % 16) return PK_ERR_ARG;   // 16-byte row loads
         dim3 ag((F + kApxFeat - 1) / kApxFeat, (n_units * G + kApxHeads - 1) / kApxHeads);
         const int asmem = (kApxHeads + kApxFeat) * 256;
         if (q_dtype == PK_BF16) {
             cudaFuncSetAttribute(qact_approx_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, asmem);
             qact_approx_kernel<__nv_bfloat16><<<ag, kApxThreads, asmem, st>>>(
                 (const __nv_bfloat16*)q, ul, n_units, G, (const __nv_bfloat16*)w_bf16, (const float*)b_enc,
-                query_scale, F, act);
+                (const float*)w_norm, query_scale, F, gs, ngroups, act, gmax);
         } else {
             cudaFuncSetAttribute(qact_approx_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, asmem);
-            qact_approx_kernel<float><<<ag, kApxThreads, asmem, st>>>((const float*)q, ul, n_units, G,
-                                                                      (const __nv_bfloat16*)w_bf16,
-                                                                      (const float*)b_enc, query_scale, F, act);
+            qact_approx_kernel<float><<<ag, kApxThreads, asmem, st>>>(
+                (const float*)q, ul, n_units, G, (const __nv_bfloat16*)w_bf16, (const float*)b_enc,
+                (const float*)w_norm, query_scale, F, gs, ngroups, act, gmax);
         }
         PK_CHECK_LAUNCH();
         if (score) {
             zero_rows_kernel<<<n_units, 256, 0, st>>>((float*)score, ul, F);
             PK_CHECK_LAUNCH();
         }
-        // Lower-bound keys always; upper bounds too when both fit on chip.
-        const int store_up = (size_t)8 * F <= 160 * 1024 ? 1 : 0;
-        size_t fsmem = (size_t)(store_up ? 8 : 4) * F;
+        // Shared memory for the all-features fallback and the aggregation.
+        size_t fsmem = (size_t)4 * F;
         if ((size_t)16 * G * k > fsmem) fsmem = (size_t)16 * G * k;
 #define PK_LAUNCH_FAST(ORD, QT)                                                                                  \
     do {                                                                                                         \
         cudaFuncSetAttribute(qact_select_fast_kernel<ORD, QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
                              (int)fsmem);                                                                        \
-        qact_select_fast_kernel<ORD, QT><<<n_units * G, 256, fsmem, st>>>(                                       \
-            (const QT*)q, act, ul, G, (const float*)w_enc, (const float*)b_enc, (const float*)w_norm,            \
-            query_scale, F, k, (const int*)counts, hid, hval, done, (int*)order, (int*)n_order, order_stride,    \
-            (float*)score, store_up);                                                                            \
+        qact_select_fast_kernel<ORD, QT><<<n_units * G, kSelThreads, fsmem, st>>>(                               \
+            (const QT*)q, act, gmax, ngroups, ul, G, (const float*)w_enc, (const float*)b_enc, query_scale, F,   \
+            k, (const int*)counts, hid, hval, done, (int*)order, (int*)n_order, order_stride, (float*)score);    \
     } while (0)
         if (q_dtype == PK_BF16) {
             if (inter) PK_LAUNCH_FAST(kInterleaved16, __nv_bfloat16); else PK_LAUNCH_FAST(kSequential, __nv_bfloat16);

@@ -7,8 +7,12 @@
 // 16-byte cp.async (rows addressed through the id list), three stages deep;
 // each warp runs QK^T and PV for 16 rows with mma.sync m16n8k16 (the G heads
 // fill the M=16 rows), keeps an fp32 online softmax, and feeds P to the PV
-// product as a bf16 hi/lo pair so the weights keep ~16 bits.  The last CTA of
-// a unit merges the split partials.
+// product in bf16.  The S split CTAs of a unit form a thread-block cluster
+// and merge their states through distributed shared memory (S <= 16); for
+// more splits, the last CTA of a unit to finish merges partials from global
+// memory.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace pk {
@@ -21,6 +25,7 @@ constexpr int kAvRowBytes = kAvD * 2;
 constexpr int kAvStageBytes = kAvTile * kAvRowBytes * 2;   // K + V
 constexpr int kAvMaxG = 16;
 constexpr int kAvIdsCap = 2048;   // row ids staged per CTA (longer splits read the rest directly)
+constexpr int kAvMaxCluster = 16; // splits merged through distributed shared memory
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct AvParams {
@@ -49,6 +54,9 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool v
     const int n = valid ? 16 : 0;
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(n));
 }
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(dst), "l"(src));
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
@@ -74,7 +82,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&t);
 }
-__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 // Byte offset of (row, 16-byte chunk) inside a 64-row x 256-byte tile, the
 // chunk index XOR-swizzled by the row so ldmatrix is bank-conflict free.
@@ -93,7 +100,7 @@ __device__ __forceinline__ __nv_bfloat16 to_out<__nv_bfloat16>(float x) { return
 // state, then either finish (single split) or store the split partial and
 // let the last CTA of the unit merge.  m is in log2 units.
 template <typename OT>
-__device__ void av_finish(const AvParams& p, int u, int s, const float* red, int nwarps) {
+__device__ void av_finish(const AvParams& p, int u, int s, float* red, int nwarps) {
     const int G = p.G, S = p.S, tid = threadIdx.x;
     const float* rm = red;
     const float* rl = red + nwarps * kAvMaxG;
@@ -133,18 +140,42 @@ __device__ void av_finish(const AvParams& p, int u, int s, const float* red, int
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    for (int h = 0; h < G; ++h) {
-        const int64_t uh = (int64_t)u * G + h;
-        const float* pp = p.part + uh * S * (kAvD + 2);
+    // Merge the unit's G x S split partials.  Every load is independent of
+    // the others, so they are issued in parallel: first all (m, l) pairs into
+    // shared memory (reusing `red`, whose per-warp states were consumed
+    // above), then the o columns in batches of 16 per thread.  Within a head
+    // the splits are still accumulated in ascending order.
+    const int GS = G * S;
+    float* wt = red;                       // [G*S] m, then merge weights
+    float* lt = wt + GS;                   // [G*S] l
+    float* Mh = lt + GS;                   // [G]
+    float* Lh = Mh + G;                    // [G]
+    const float* pu = p.part + (int64_t)u * GS * (kAvD + 2);
+    for (int e = tid; e < GS; e += kAvThreads) {
+        wt[e] = __ldcg(pu + (int64_t)e * (kAvD + 2));
+        lt[e] = __ldcg(pu + (int64_t)e * (kAvD + 2) + 1);
+    }
+    __syncthreads();
+    const int lane = tid & 31, warp = tid >> 5;
+    for (int h = warp; h < G; h += kAvThreads / 32) {
         float M = -INFINITY;
-        for (int j = 0; j < S; ++j) M = fmaxf(M, __ldcg(pp + j * (kAvD + 2)));
-        float L = 0.f, O = 0.f;
-        for (int j = 0; j < S; ++j) {
-            const float mj = __ldcg(pp + j * (kAvD + 2));
+        for (int j = lane; j < S; j += 32) M = fmaxf(M, wt[h * S + j]);
+        M = warp_max(M);
+        __syncwarp();
+        float L = 0.f;
+        for (int j = lane; j < S; j += 32) {
+            const float mj = wt[h * S + j];
             const float sc = (mj == -INFINITY) ? 0.f : exp2f(mj - M);
-            L = fmaf(sc, __ldcg(pp + j * (kAvD + 2) + 1), L);
-            O = fmaf(sc, __ldcg(pp + j * (kAvD + 2) + 2 + dim), O);
+            wt[h * S + j] = sc;
+            L = fmaf(sc, lt[h * S + j], L);
         }
+        L = warp_sum(L);
+        if (lane == 0) { Mh[h] = M; Lh[h] = L; }
+    }
+    __syncthreads();
+    auto emit = [&](int h, float O) {
+        const int64_t uh = (int64_t)u * G + h;
+        const float M = Mh[h], L = Lh[h];
         if (p.xpart) {
             float* xp = p.xpart + uh * (kAvD + 2);
             if (dim == 0) { xp[0] = M == -INFINITY ? -INFINITY : M / kLog2e; xp[1] = L; }
@@ -153,10 +184,97 @@ __device__ void av_finish(const AvParams& p, int u, int s, const float* red, int
             OT* o = (OT*)p.out + uh * kAvD;
             o[dim] = to_out<OT>(L > 0.f ? O / L : 0.f);
         }
+    };
+    constexpr int kBatch = 16;
+    float O = 0.f;
+    int hcur = 0;
+    for (int e0 = 0; e0 < GS; e0 += kBatch) {
+        float v[kBatch];
+#pragma unroll
+        for (int t = 0; t < kBatch; ++t)
+            v[t] = e0 + t < GS ? __ldcg(pu + (int64_t)(e0 + t) * (kAvD + 2) + 2 + dim) : 0.f;
+#pragma unroll
+        for (int t = 0; t < kBatch; ++t) {
+            const int e = e0 + t;
+            if (e < GS) {
+                const int h = e / S;
+                if (h != hcur) { emit(hcur, O); O = 0.f; hcur = h; }
+                O = fmaf(wt[e], v[t], O);
+            }
+        }
     }
+    emit(hcur, O);
     if (tid == 0) p.done[u] = 0;
 }
 
+// Cluster merge: the CTA combines its warps' states into shared memory
+// (st: m[kAvMaxG], l[kAvMaxG], o[kAvMaxG][D]), then the cluster's CTAs share
+// out the G*D outputs and each reads the S states of its outputs from the
+// CTAs' shared memory, accumulating in split order (the same arithmetic as
+// the global merge).  The second cluster barrier keeps every CTA's shared
+// memory alive until all reads are done.
+template <typename OT>
+__device__ void av_finish_cluster(const AvParams& p, int u, int s, const float* red, int nwarps, float* st) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int G = p.G, S = p.S, tid = threadIdx.x;
+    const float* rm = red;
+    const float* rl = red + nwarps * kAvMaxG;
+    const float* ro = red + 2 * nwarps * kAvMaxG;
+    const int dim = tid;  // kAvThreads == kAvD
+    for (int h = 0; h < G; ++h) {
+        float M = -INFINITY;
+        for (int w = 0; w < nwarps; ++w) M = fmaxf(M, rm[w * kAvMaxG + h]);
+        float L = 0.f, O = 0.f;
+        for (int w = 0; w < nwarps; ++w) {
+            const float mw = rm[w * kAvMaxG + h];
+            const float sc = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+            L = fmaf(sc, rl[w * kAvMaxG + h], L);
+            O = fmaf(sc, ro[(w * kAvMaxG + h) * kAvD + dim], O);
+        }
+        if (dim == 0) { st[h] = M; st[kAvMaxG + h] = L; }
+        st[2 * kAvMaxG + h * kAvD + dim] = O;
+    }
+    cluster.sync();
+    for (int e = s * kAvThreads + tid; e < G * kAvD; e += S * kAvThreads) {
+        const int h = e / kAvD, d = e % kAvD;
+        float mj[kAvMaxCluster], lj[kAvMaxCluster], oj[kAvMaxCluster];
+#pragma unroll
+        for (int j = 0; j < kAvMaxCluster; ++j) {
+            if (j < S) {
+                const float* rst = cluster.map_shared_rank(st, j);
+                mj[j] = rst[h];
+                lj[j] = rst[kAvMaxG + h];
+                oj[j] = rst[2 * kAvMaxG + h * kAvD + d];
+            }
+        }
+        float M = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < kAvMaxCluster; ++j)
+            if (j < S) M = fmaxf(M, mj[j]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int j = 0; j < kAvMaxCluster; ++j) {
+            if (j < S) {
+                const float sc = (mj[j] == -INFINITY) ? 0.f : exp2f(mj[j] - M);
+                L = fmaf(sc, lj[j], L);
+                O = fmaf(sc, oj[j], O);
+            }
+        }
+        const int64_t uh = (int64_t)u * G + h;
+        if (p.xpart) {
+            float* xp = p.xpart + uh * (kAvD + 2);
+            if (d == 0) { xp[0] = M == -INFINITY ? -INFINITY : M / kLog2e; xp[1] = L; }
+            xp[2 + d] = O;
+        } else {
+            OT* o = (OT*)p.out + uh * kAvD;
+            o[d] = to_out<OT>(L > 0.f ? O / L : 0.f);
+        }
+    }
+    cluster.sync();
+}
+
+template <bool kCluster>
 __global__ void __launch_bounds__(kAvThreads)
 sparse_av_bf16_kernel(AvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -186,11 +304,13 @@ sparse_av_bf16_kernel(AvParams p) {
             qa[kk][r] = hh < G ? *reinterpret_cast<const uint32_t*>(qp + hh * kAvD + dim) : 0u;
         }
 
-    // The split's row ids, staged once in shared memory (one coalesced read)
-    // so that issuing a tile's copies never waits on a global load.
+    // The split's row ids, staged once in shared memory (all copies in flight
+    // together) so that issuing a tile's copies never waits on a global load.
     int* sids = reinterpret_cast<int*>(smem + kAvStages * kAvStageBytes);
     const int n_staged = min(max(0, min(r1, cnt) - r0), kAvIdsCap);
-    for (int i = tid; i < n_staged; i += kAvThreads) sids[i] = idp[r0 + i];
+    for (int i = tid; i < n_staged; i += kAvThreads) cp_async4(smem_u32(sids + i), idp + r0 + i);
+    cp_async_commit();
+    cp_async_wait<0>();
     __syncthreads();
     auto pos_of = [&](int r) -> int {
         if (r >= r1) return -1;
@@ -291,18 +411,12 @@ sparse_av_bf16_kernel(AvParams p) {
             o[j][0] *= al_a; o[j][1] *= al_a;
             o[j][2] *= al_b; o[j][3] *= al_b;
         }
-        // P as the A operand (rows = heads, k = the 16 rows), hi + lo parts.
-        uint32_t ph[4], pl[4];
-        {
-            const float h00 = bf16_round(pr[0][0]), h01 = bf16_round(pr[0][1]);
-            const float h02 = bf16_round(pr[0][2]), h03 = bf16_round(pr[0][3]);
-            const float h10 = bf16_round(pr[1][0]), h11 = bf16_round(pr[1][1]);
-            const float h12 = bf16_round(pr[1][2]), h13 = bf16_round(pr[1][3]);
-            ph[0] = pack_bf16(h00, h01); ph[1] = pack_bf16(h02, h03);
-            ph[2] = pack_bf16(h10, h11); ph[3] = pack_bf16(h12, h13);
-            pl[0] = pack_bf16(pr[0][0] - h00, pr[0][1] - h01); pl[1] = pack_bf16(pr[0][2] - h02, pr[0][3] - h03);
-            pl[2] = pack_bf16(pr[1][0] - h10, pr[1][1] - h11); pl[3] = pack_bf16(pr[1][2] - h12, pr[1][3] - h13);
-        }
+        // P as the A operand (rows = heads, k = the 16 rows), rounded to
+        // bf16 (relative error 2^-9 per weight, the output's own rounding);
+        // l above sums the unrounded fp32 weights.
+        uint32_t ph[4];
+        ph[0] = pack_bf16(pr[0][0], pr[0][1]); ph[1] = pack_bf16(pr[0][2], pr[0][3]);
+        ph[2] = pack_bf16(pr[1][0], pr[1][1]); ph[3] = pack_bf16(pr[1][2], pr[1][3]);
 #pragma unroll
         for (int np = 0; np < 8; ++np) {
             uint32_t b[4];
@@ -311,8 +425,6 @@ sparse_av_bf16_kernel(AvParams p) {
             ldmatrix_x4_trans(vbase + tile_off(row, 2 * np + (mi >> 1)), b);
             mma_bf16(o[2 * np], ph, b[0], b[1]);
             mma_bf16(o[2 * np + 1], ph, b[2], b[3]);
-            mma_bf16(o[2 * np], pl, b[0], b[1]);
-            mma_bf16(o[2 * np + 1], pl, b[2], b[3]);
         }
         __syncthreads();
     }
@@ -342,7 +454,10 @@ sparse_av_bf16_kernel(AvParams p) {
         }
     }
     __syncthreads();
-    av_finish<__nv_bfloat16>(p, u, s, red, 4);
+    if constexpr (kCluster)
+        av_finish_cluster<__nv_bfloat16>(p, u, s, red, 4, red + 2 * 4 * kAvMaxG + 4 * kAvMaxG * kAvD);
+    else
+        av_finish<__nv_bfloat16>(p, u, s, red, 4);
 }
 
 // fp32 K/V path (parity shapes such as the CPU fp32 config): one warp per
@@ -426,6 +541,36 @@ __global__ void lse_merge_kernel(const float* __restrict__ part, int P, int UG, 
     else out_b[(int64_t)uh * kAvD + dim] = __float2bfloat16_rn(r);
 }
 
+// Whether a cluster of S split CTAs (S <= 16; above 8 the non-portable
+// cluster sizes) can be resident; answered once per S and kept.
+bool cluster_fits(int S, int smem) {
+    static int known[kAvMaxCluster + 1] = {};   // 0 unknown, 1 yes, 2 no
+    if (S < 2 || S > kAvMaxCluster) return false;
+    if (!known[S]) {
+        auto fn = sparse_av_bf16_kernel<true>;
+        bool ok = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess;
+        if (ok && S > 8) ok = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+        int clusters = 0;
+        if (ok) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(S, 1);
+            cfg.blockDim = dim3(kAvThreads);
+            cfg.dynamicSmemBytes = smem;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = S;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            ok = cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) == cudaSuccess && clusters > 0;
+        }
+        cudaGetLastError();   // a refused query leaves no sticky error
+        known[S] = ok ? 1 : 2;
+    }
+    return known[S] == 1;
+}
+
 int default_splits(int U) {
     static int sms = 0;
     if (!sms) {
@@ -434,9 +579,12 @@ int default_splits(int U) {
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (sms <= 0) sms = 148;
     }
-    // About three resident CTAs per SM across all units.
-    const int s = (3 * sms + U - 1) / U;
-    return s < 1 ? 1 : (s > 256 ? 256 : s);
+    // About one wave of two CTAs per SM across all units, at most 8 splits
+    // (portable clusters, merged on chip): each split pays a fixed prologue
+    // (ids, Q, first tile), so more splits than resident slots only add
+    // overhead, and clusters above 8 CTAs schedule poorly.
+    const int s = (2 * sms) / U;
+    return s < 1 ? 1 : (s > 8 ? 8 : s);
 }
 
 }  // namespace pk
@@ -478,8 +626,25 @@ extern "C" int pk_sparse_av(uint64_t q, uint64_t k, uint64_t v, int dtype, int k
     if (dtype == PK_BF16) {
         if (kv_row_stride % 8 || kv_batch_stride % 8 || kv_head_stride % 8 || (k | v) % 16) return PK_ERR_ARG;
         const int smem = kAvStages * kAvStageBytes + kAvIdsCap * (int)sizeof(int);
-        cudaFuncSetAttribute(sparse_av_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        sparse_av_bf16_kernel<<<grid, kAvThreads, smem, st>>>(p);
+        if (splits >= 2 && cluster_fits(splits, smem)) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = grid;
+            cfg.blockDim = dim3(kAvThreads);
+            cfg.dynamicSmemBytes = smem;
+            cfg.stream = st;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = splits;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            const cudaError_t e = cudaLaunchKernelEx(&cfg, sparse_av_bf16_kernel<true>, p);
+            if (e != cudaSuccess) return (int)e;
+        } else {
+            cudaFuncSetAttribute(sparse_av_bf16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            sparse_av_bf16_kernel<false><<<grid, kAvThreads, smem, st>>>(p);
+        }
     } else if (dtype == PK_F32) {
         if (kv_row_stride % 4 || kv_batch_stride % 4 || kv_head_stride % 4 || (k | v | q) % 16) return PK_ERR_ARG;
         const int smem = (2 * 4 * kAvMaxG + 4 * kAvMaxG * kAvD) * (int)sizeof(float);

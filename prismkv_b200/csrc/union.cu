@@ -3,75 +3,67 @@
 // over the unit's history and compacted to ascending token ids by a block
 // scan (the order of core.py:164's chosen.nonzero()).
 //
-// The candidates' bucket lists are first staged in shared memory with one
-// fully parallel copy.  The greedy -- sequential by definition: bucket i is
-// accepted iff its tokens not yet chosen fit the remaining budget -- is then
-// computed exactly in two phases:
-//   1. while no bucket has been skipped, bucket i's new tokens are its tokens
-//      that are neither in the bitmap (earlier rounds) nor in an earlier
-//      bucket of the current round.  Rounds take as many buckets as a shared-
-//      memory hash (token -> first bucket of the round, atomicMin) can hold;
-//      a warp prefix sum over the round's counts finds the first bucket that
-//      would overflow (i*), and the buckets before it are OR-ed in.
-//   2. after i*, every remaining bucket's new-token count is computed once in
-//      parallel; then one warp walks the buckets in order.  A bucket whose
-//      count minus the tokens added since cannot fit is skipped at once; any
-//      other is re-counted against the current bitmap and taken if it fits.
-// Lists that do not fit the staging area are read from global memory by the
-// same code paths.
+// Candidate bucket i is accepted iff its tokens not yet chosen fit the
+// remaining budget.  The kernel computes that sequential rule exactly in two
+// phases, with the whole block working on every step:
+//   1. the prefix of buckets accepted before the first skip (i*) is found by
+//      galloping probes: a probe ORs a range of lists into the bitmap at once
+//      and counts the bits it turned on (atomicOr returns the old word, so a
+//      token shared by several lists of the range is counted once); if the
+//      count overflows the budget the probe's bits are turned off again (each
+//      staged entry that turned a bit on carries a flag), and the range
+//      halves.  Ranges of more than one bucket run on lists staged in shared
+//      memory; a one-bucket probe counts its tokens missing from the bitmap.
+//   2. after i*, rounds: every remaining bucket's count of tokens missing
+//      from the bitmap is taken in parallel; the first bucket whose count
+//      fits is accepted (its count is exact: nothing changed since), the ones
+//      before it are skipped, and every bucket whose count exceeds the
+//      remaining budget is dropped for good (its count can shrink by at most
+//      what the budget shrinks).  Rounds = accepted tail buckets + 1.
 #include "common.cuh"
+#include "mma.cuh"
 
 namespace pk {
 
 constexpr int kUnionThreads = 512;
 constexpr int kMaxCand = 256;     // candidates per unit (G * k)
+constexpr uint32_t kFlipFlag = 0x80000000u;
 
 struct UnionSmem {
     int cand_bucket[kMaxCand];
     int cand_start[kMaxCand];
     int cand_len[kMaxCand];
-    int cand_stage[kMaxCand];     // offset in the staging area, or -1
+    int cand_pre[kMaxCand + 1];   // exclusive prefix of the list lengths
     int newc[kMaxCand];
+    unsigned char dead[kMaxCand];
     int scan[40];
-    long long red[32];
+    int red[32];
     int flags[8];
+    long long lred[2];
 };
 
 __device__ __forceinline__ bool test_bit(const uint32_t* bm, int t) { return (bm[t >> 5] >> (t & 31)) & 1u; }
 __device__ __forceinline__ void set_bit(uint32_t* bm, int t) { atomicOr(&bm[t >> 5], 1u << (t & 31)); }
 
-struct Hash {
-    int* key;
-    int* own;
-    int bits;
-    __device__ __forceinline__ int slot(int t) const { return (int)(((uint32_t)t * 2654435761u) >> (32 - bits)); }
-    __device__ __forceinline__ void insert(int t, int c) const {
-        const int mask = (1 << bits) - 1;
-        int s = slot(t);
-        while (true) {
-            const int old = atomicCAS(&key[s], -1, t);
-            if (old == -1 || old == t) {
-                atomicMin(&own[s], c);
-                return;
-            }
-            s = (s + 1) & mask;
-        }
-    }
-    __device__ __forceinline__ int owner(int t) const {
-        const int mask = (1 << bits) - 1;
-        int s = slot(t);
-        while (key[s] != t) s = (s + 1) & mask;
-        return own[s];
-    }
-};
+// Sum of one int per thread, returned to every thread (two barriers).
+__device__ __forceinline__ int block_sum(int v, int* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    int s = 0;
+    for (int w = 0; w < nw; ++w) s += red[w];
+    return s;
+}
 
 __global__ void __launch_bounds__(kUnionThreads)
 union_kernel(const int* __restrict__ offsets, const int* __restrict__ lens, const int* __restrict__ ids,
              int64_t ids_stride, const int* __restrict__ order, const int* __restrict__ n_order, int order_stride,
              const int* __restrict__ history, const long long* __restrict__ limit, int F, int max_history,
-             int hash_bits, int stage_cap, int* __restrict__ out_ids, int64_t out_stride,
-             int* __restrict__ out_count, int* __restrict__ features, int* __restrict__ n_features,
-             long long* __restrict__ raw, int* __restrict__ status) {
+             int stage_cap, int* __restrict__ out_ids, int64_t out_stride, int* __restrict__ out_count,
+             int* __restrict__ features, int* __restrict__ n_features, long long* __restrict__ raw,
+             int* __restrict__ status) {
     extern __shared__ __align__(16) uint32_t dyn[];
     __shared__ UnionSmem sm;
     const int u = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
@@ -89,10 +81,8 @@ union_kernel(const int* __restrict__ offsets, const int* __restrict__ lens, cons
     }
     const int W = (H + 31) >> 5;
     const int Wmax = (max_history + 31) >> 5;
-    uint32_t* bm = dyn;                                               // [W]
-    int* hkeys = reinterpret_cast<int*>(dyn + ((Wmax + 3) & ~3));     // [2^hash_bits]
-    int* hown = hkeys + (1 << hash_bits);                             // [2^hash_bits]
-    int* stage = hown + (1 << hash_bits);                             // [stage_cap]
+    uint32_t* bm = dyn;                                                   // [W]
+    uint32_t* stage = dyn + ((Wmax + 3) & ~3);                            // [stage_cap]
     const int n = min(n_order[u], kMaxCand);
     const long long lim = limit[u];
     const int* uid = ids + (int64_t)u * ids_stride;
@@ -104,44 +94,83 @@ union_kernel(const int* __restrict__ offsets, const int* __restrict__ lens, cons
         sm.cand_bucket[c] = b;
         sm.cand_start[c] = offsets[(int64_t)u * (F + 1) + b];
         sm.cand_len[c] = lens[(int64_t)u * F + b];
+        sm.dead[c] = 0;
     }
     __syncthreads();
-    if (tid == 0) {
-        long long s = 0;
-        int staged = 0;
-        for (int c = 0; c < n; ++c) {
-            const int L = sm.cand_len[c];
-            s += L;
-            if (staged + L <= stage_cap) { sm.cand_stage[c] = staged; staged += L; }
-            else sm.cand_stage[c] = -1;
+    if (warp == 0) {
+        int run = 0;
+        for (int base = 0; base < n; base += 32) {
+            const int c = base + lane;
+            const int L = c < n ? sm.cand_len[c] : 0;
+            const int inc = warp_inclusive_scan(L);
+            if (c < n) sm.cand_pre[c] = run + inc - L;
+            run += __shfl_sync(0xffffffffu, inc, 31);
         }
-        sm.red[0] = s;
+        if (lane == 0) sm.cand_pre[n] = run;
     }
     __syncthreads();
-    // Stage: one warp per candidate, every load independent.
-    for (int c = warp; c < n; c += nw) {
-        const int off = sm.cand_stage[c];
-        if (off < 0) continue;
-        const int L = sm.cand_len[c];
-        const int* src = uid + sm.cand_start[c];
-        for (int i = lane; i < L; i += 32) stage[off + i] = src[i];
-    }
-    __syncthreads();
-    auto list = [&](int c) -> const int* {
-        const int off = sm.cand_stage[c];
-        return off >= 0 ? stage + off : uid + sm.cand_start[c];
+
+    // Staging window: buckets [ws0, ws1) whose lists lie back to back in
+    // shared memory (entry i of bucket c at cand_pre[c] - cand_pre[ws0] + i).
+    int ws0 = 0, ws1 = 0;
+    auto stage_from = [&](int c0) {
+        // Every warp finds the same window end (the first bucket whose list
+        // would end past stage_cap); copies are asynchronous.
+        const int base = sm.cand_pre[c0];
+        int c1 = n;
+        for (int b = c0 + 1; b <= n; b += 32) {
+            const int c = b + lane;
+            const bool over = c <= n && sm.cand_pre[c] - base > stage_cap;
+            const unsigned om = __ballot_sync(0xffffffffu, over);
+            if (om) {
+                c1 = b + __ffs(om) - 2;
+                break;
+            }
+        }
+        for (int c = c0 + warp; c < c1; c += nw) {
+            const int off = sm.cand_pre[c] - base;
+            const int L = sm.cand_len[c];
+            const int* src = uid + sm.cand_start[c];
+            for (int i = lane; i < L; i += 32) cp_async_4(smem_addr(stage + off + i), src + i);
+        }
+        cp_async_wait_all();
+        __syncthreads();
+        ws0 = c0;
+        ws1 = c1;
     };
-    const long long raw_total = sm.red[0];
+    // Token i of bucket c (flag bit masked off).
+    auto token = [&](int c, int i) -> int {
+        if (c >= ws0 && c < ws1) return (int)(stage[sm.cand_pre[c] - sm.cand_pre[ws0] + i] & ~kFlipFlag);
+        return uid[sm.cand_start[c] + i];
+    };
+    // Tokens of bucket c not in the bitmap (lists hold distinct tokens).
+    auto missing = [&](int c) -> int {
+        const int L = sm.cand_len[c];
+        int m = 0;
+        for (int i = tid; i < L; i += nt) {
+            const int t = token(c, i);
+            m += ((unsigned)t < (unsigned)H && !test_bit(bm, t)) ? 1 : 0;
+        }
+        return block_sum(m, sm.red);
+    };
+    auto or_bucket = [&](int c) {
+        const int L = sm.cand_len[c];
+        for (int i = tid; i < L; i += nt) {
+            const int t = token(c, i);
+            if ((unsigned)t < (unsigned)H) set_bit(bm, t);
+        }
+    };
+    stage_from(0);
+
+    const long long raw_total = sm.cand_pre[n];
     long long raw_acc = 0;
     int nf = 0;
-
     if (raw_total <= lim) {
         // Every candidate fits whatever the overlap: the unbudgeted union.
         for (int c = warp; c < n; c += nw) {
             const int L = sm.cand_len[c];
-            const int* lst = list(c);
             for (int i = lane; i < L; i += 32) {
-                const int t = lst[i];
+                const int t = token(c, i);
                 if ((unsigned)t < (unsigned)H) set_bit(bm, t);
             }
         }
@@ -149,144 +178,232 @@ union_kernel(const int* __restrict__ offsets, const int* __restrict__ lens, cons
         nf = n;
         raw_acc = raw_total;
     } else {
-        Hash hs{hkeys, hown, hash_bits};
-        const int round_cap = 1 << (hash_bits - 1);  // load factor <= 1/2
-        long long count = 0;
-        int c0 = 0, istar = n;
-        // ---- 1. rounds while every bucket so far was accepted.
-        while (c0 < n) {
-            if (tid == 0) {
-                int c1 = c0, filled = 0;
-                while (c1 < n && (filled + sm.cand_len[c1] <= round_cap || c1 == c0)) {
-                    filled += sm.cand_len[c1];
-                    ++c1;
-                }
-                sm.flags[0] = c1;
-            }
-            __syncthreads();
-            const int c1 = sm.flags[0];
-            const bool single = c1 - c0 == 1;
-            if (!single) {
-                for (int i = tid; i < (1 << hash_bits); i += nt) { hs.key[i] = -1; hs.own[i] = INT32_MAX; }
-                __syncthreads();
-                for (int c = c0 + warp; c < c1; c += nw) {
-                    const int* lst = list(c);
-                    const int L = sm.cand_len[c];
-                    for (int i = lane; i < L; i += 32) {
-                        const int t = lst[i];
-                        if ((unsigned)t < (unsigned)H && !test_bit(bm, t)) hs.insert(t, c);
-                    }
-                }
-                __syncthreads();
-            }
-            for (int c = c0 + warp; c < c1; c += nw) {
-                const int* lst = list(c);
-                const int L = sm.cand_len[c];
-                int cnt = 0;
-                for (int i = lane; i < L; i += 32) {
-                    const int t = lst[i];
-                    cnt += ((unsigned)t < (unsigned)H && !test_bit(bm, t) && (single || hs.owner(t) == c)) ? 1 : 0;
-                }
-                cnt = warp_sum(cnt);
-                if (lane == 0) sm.newc[c] = cnt;
-            }
-            __syncthreads();
-            if (warp == 0) {
-                long long run = count;
-                int first_over = c1;
-                for (int base = c0; base < c1; base += 32) {
-                    const int c = base + lane;
-                    const int v = c < c1 ? sm.newc[c] : 0;
-                    const int inc = warp_inclusive_scan(v);
-                    const bool over = c < c1 && run + inc > lim;
-                    const unsigned om = __ballot_sync(0xffffffffu, over);
-                    if (om) {
-                        first_over = base + __ffs(om) - 1;
-                        run += __shfl_sync(0xffffffffu, inc - v, first_over - base);
-                        break;
-                    }
-                    run += __shfl_sync(0xffffffffu, inc, 31);
-                }
-                if (lane == 0) {
-                    sm.flags[1] = first_over;
-                    sm.red[1] = run;
-                }
-            }
-            __syncthreads();
-            const int acc_end = sm.flags[1];
-            count = sm.red[1];
-            for (int c = c0 + warp; c < acc_end; c += nw) {
-                const int* lst = list(c);
-                const int L = sm.cand_len[c];
-                for (int i = lane; i < L; i += 32) {
-                    const int t = lst[i];
-                    if ((unsigned)t < (unsigned)H) set_bit(bm, t);
-                }
-            }
-            for (int c = c0 + tid; c < acc_end; c += nt) feat[c] = sm.cand_bucket[c];
-            for (int c = c0; c < acc_end; ++c) raw_acc += sm.cand_len[c];
-            nf = acc_end;
-            __syncthreads();
-            if (acc_end < c1) {
-                istar = acc_end;
+        // ---- 1. the prefix accepted before i*.  Buckets whose lists, counted
+        // with repeats, fit the budget are accepted whatever the overlap:
+        // they are ORed in one pass.
+        int sure = n;
+        for (int b = 0; b < n; b += 32) {
+            const int c = b + lane;
+            const unsigned om = __ballot_sync(0xffffffffu, c < n && (long long)sm.cand_pre[c + 1] > lim);
+            if (om) {
+                sure = b + __ffs(om) - 1;
                 break;
             }
-            c0 = c1;
         }
-        // ---- 2. the tail after the first skipped bucket.
-        if (istar + 1 < n) {
-            for (int c = istar + 1 + warp; c < n; c += nw) {
-                const int* lst = list(c);
-                const int L = sm.cand_len[c];
-                int cnt = 0;
-                for (int i = lane; i < L; i += 32) {
-                    const int t = lst[i];
-                    cnt += ((unsigned)t < (unsigned)H && !test_bit(bm, t)) ? 1 : 0;
+        int flips = 0;
+        for (int c = warp; c < sure; c += nw) {
+            const int L = sm.cand_len[c];
+            for (int i = lane; i < L; i += 32) {
+                const int t = token(c, i);
+                if ((unsigned)t < (unsigned)H) {
+                    const uint32_t bit = 1u << (t & 31);
+                    flips += (atomicOr(&bm[t >> 5], bit) & bit) ? 0 : 1;
                 }
-                cnt = warp_sum(cnt);
-                if (lane == 0) sm.newc[c] = cnt;
+            }
+        }
+        long long count = block_sum(flips, sm.red);
+        // Galloping probes from there; the first range is sized by the
+        // overlap seen so far (tokens per listed entry).
+        int lo = sure, fail_hi = n + 1, istar = n;
+        int step = 8;
+        bool predicted = false;
+        if (sure > 0 && sure < n) {
+            // Predicted i*: the first bucket whose entries, thinned by the
+            // ratio seen so far, exceed the room left.
+            const double ratio = (double)count / (double)max(1, sm.cand_pre[sure]);
+            const double room = (double)(lim - count) / fmax(ratio, 1e-3);
+            int c = n;
+            for (int b = sure; b < n; b += 32) {
+                const int cc = b + lane;
+                const unsigned om = __ballot_sync(
+                    0xffffffffu, cc < n && (double)(sm.cand_pre[cc + 1] - sm.cand_pre[sure]) > room);
+                if (om) {
+                    c = b + __ffs(om) - 1;
+                    break;
+                }
+            }
+            step = max(1, c - sure);
+            predicted = true;
+        }
+        __syncthreads();
+        while (lo < n) {
+            if (fail_hi == lo + 1) { istar = lo; break; }
+            int hi = min(min(lo + step, fail_hi - 1), n);
+            if (hi > lo + 1 && hi > ws1) {
+                if (lo >= ws1) stage_from(lo);
+                hi = max(lo + 1, min(hi, ws1));
+            }
+            if (hi == lo + 1) {
+                const int m = missing(lo);
+                if (count + m <= lim) {
+                    or_bucket(lo);
+                    count += m;
+                    lo = hi;
+                    step = predicted ? 1 : step * 2;
+                    predicted = false;
+                    __syncthreads();
+                } else {
+                    istar = lo;
+                    break;
+                }
+            } else {
+                const int e0 = sm.cand_pre[lo] - sm.cand_pre[ws0], e1 = sm.cand_pre[hi] - sm.cand_pre[ws0];
+                int flips = 0;
+                for (int e = e0 + tid; e < e1; e += nt) {
+                    const uint32_t t = stage[e] & ~kFlipFlag;
+                    if (t < (uint32_t)H) {
+                        const uint32_t bit = 1u << (t & 31);
+                        if (!(atomicOr(&bm[t >> 5], bit) & bit)) {
+                            stage[e] = t | kFlipFlag;
+                            ++flips;
+                        }
+                    }
+                }
+                const int m = block_sum(flips, sm.red);
+                if (count + m <= lim) {
+                    count += m;
+                    lo = hi;
+                    step = predicted ? 1 : step * 2;
+                    predicted = false;
+                } else {
+                    for (int e = e0 + tid; e < e1; e += nt) {
+                        const uint32_t t = stage[e];
+                        if (t & kFlipFlag) {
+                            const uint32_t tt = t & ~kFlipFlag;
+                            stage[e] = tt;
+                            atomicAnd(&bm[tt >> 5], ~(1u << (tt & 31)));
+                        }
+                    }
+                    fail_hi = hi;
+                    step = max(1, (hi - lo) / 2);
+                    predicted = false;
+                }
+                __syncthreads();
+            }
+        }
+        for (int c = tid; c < istar; c += nt) feat[c] = sm.cand_bucket[c];
+        nf = istar;
+        raw_acc = sm.cand_pre[istar];
+        // ---- 2. after the first skipped bucket.
+        int cpos = istar + 1;
+        if (cpos < n && (cpos < ws0 || cpos >= ws1)) stage_from(cpos);
+        // Preferred: one warp walks the remaining buckets in order with each
+        // bucket's exact count of tokens missing from the bitmap, kept exact
+        // by a multimap token -> tail entries (a chained hash over the
+        // entries whose token is still missing): accepting a bucket
+        // decrements the count of every later bucket holding a token it
+        // added.  It needs the tail staged and room for the multimap after
+        // the staged lists; otherwise the rounds below run instead.
+        // Chain heads: about one per tail entry (only entries whose token is
+        // still missing are chained), fewer if space is short.
+        const int T = cpos < n ? sm.cand_pre[n] - sm.cand_pre[cpos] : 0;
+        const int used = ws1 > ws0 ? sm.cand_pre[ws1] - sm.cand_pre[ws0] : 0;
+        int hb_bits = 8;
+        while (hb_bits < 16 && (1 << hb_bits) < T) ++hb_bits;
+        while (hb_bits > 8 && used + (1 << hb_bits) + T + (T + 3) / 4 > stage_cap) --hb_bits;
+        const int need = (1 << hb_bits) + T + (T + 3) / 4;
+        if (cpos < n && ws1 == n && cpos >= ws0 && used + need <= stage_cap) {
+            int* heads = reinterpret_cast<int*>(stage + used);
+            int* nxt = heads + (1 << hb_bits);
+            unsigned char* own = reinterpret_cast<unsigned char*>(nxt + T);
+            const uint32_t* tail = stage + (sm.cand_pre[cpos] - sm.cand_pre[ws0]);
+            for (int i = tid; i < (1 << hb_bits); i += nt) heads[i] = -1;
+            __syncthreads();
+            auto slot = [&](uint32_t t) { return (int)((t * 2654435761u) >> (32 - hb_bits)); };
+            for (int c = cpos + warp; c < n; c += nw) {
+                const int L = sm.cand_len[c];
+                const int e0 = sm.cand_pre[c] - sm.cand_pre[cpos];
+                int m = 0;
+                for (int i = lane; i < L; i += 32) {
+                    const uint32_t t = tail[e0 + i] & ~kFlipFlag;
+                    if (t < (uint32_t)H && !test_bit(bm, (int)t)) {
+                        ++m;
+                        own[e0 + i] = (unsigned char)c;
+                        nxt[e0 + i] = atomicExch(&heads[slot(t)], e0 + i);
+                    }
+                }
+                m = warp_sum(m);
+                if (lane == 0) sm.newc[c] = m;
+            }
+            __syncthreads();
+            // Every warp finds the same next bucket whose exact count fits
+            // (ballots over the counts), then the whole block adds its tokens
+            // and, for each token it turns on, decrements the counts of the
+            // later buckets holding it.
+            long long cnt = count;
+            for (int c = cpos; c < n; ++c) {
+                const long long rem = lim - cnt;
+                int next = n;
+                for (int b = c; b < n; b += 32) {
+                    const int cc = b + lane;
+                    const unsigned fm = __ballot_sync(0xffffffffu, cc < n && (long long)sm.newc[cc] <= rem);
+                    if (fm) {
+                        next = b + __ffs(fm) - 1;
+                        break;
+                    }
+                }
+                if (next >= n) break;
+                c = next;
+                const int miss = sm.newc[c];
+                __syncthreads();   // every warp has read the counts it scanned
+                cnt += miss;
+                raw_acc += sm.cand_len[c];
+                if (tid == 0) feat[nf] = sm.cand_bucket[c];
+                ++nf;
+                const int L = sm.cand_len[c];
+                const int e0 = sm.cand_pre[c] - sm.cand_pre[cpos];
+                for (int i = tid; i < L; i += nt) {
+                    const uint32_t t = tail[e0 + i] & ~kFlipFlag;
+                    if (t >= (uint32_t)H) continue;
+                    const uint32_t bit = 1u << (t & 31);
+                    if (atomicOr(&bm[t >> 5], bit) & bit) continue;
+                    for (int e = heads[slot(t)]; e >= 0; e = nxt[e]) {
+                        const int oc = own[e];
+                        if (oc > c && (tail[e] & ~kFlipFlag) == t) atomicSub(&sm.newc[oc], 1);
+                    }
+                }
+                __syncthreads();
+            }
+            cpos = n;
+        }
+        while (cpos < n) {
+            for (int c = cpos + warp; c < n; c += nw) {
+                if (sm.dead[c]) continue;
+                const int L = sm.cand_len[c];
+                int m = 0;
+                for (int i = lane; i < L; i += 32) {
+                    const int t = token(c, i);
+                    m += ((unsigned)t < (unsigned)H && !test_bit(bm, t)) ? 1 : 0;
+                }
+                m = warp_sum(m);
+                if (lane == 0) sm.newc[c] = m;
             }
             __syncthreads();
             if (warp == 0) {
-                // newc[c] was exact when counted; the bitmap has grown by
-                // `added` tokens since, so newc[c] - added <= true count.
-                long long added = 0;
-                for (int c = istar + 1; c < n; ++c) {
-                    if ((long long)sm.newc[c] - added > lim - count) continue;
-                    const int* lst = list(c);
-                    const int L = sm.cand_len[c];
-                    int fresh = 0;
-                    if (added == 0) {
-                        fresh = sm.newc[c];
-                    } else {
-                        for (int i = lane; i < L; i += 32) {
-                            const int t = lst[i];
-                            fresh += ((unsigned)t < (unsigned)H && !test_bit(bm, t)) ? 1 : 0;
-                        }
-                        fresh = warp_sum(fresh);
+                const long long rem = lim - count;
+                int first = n;
+                for (int base = cpos; base < n; base += 32) {
+                    const int c = base + lane;
+                    bool fits = false;
+                    if (c < n && !sm.dead[c]) {
+                        if ((long long)sm.newc[c] <= rem) fits = true;
+                        else sm.dead[c] = 1;
                     }
-                    if (count + fresh > lim) continue;
-                    if (fresh > 0) {
-                        for (int i = lane; i < L; i += 32) {
-                            const int t = lst[i];
-                            if ((unsigned)t < (unsigned)H) set_bit(bm, t);
-                        }
-                        __syncwarp();
-                    }
-                    count += fresh;
-                    added += fresh;
-                    raw_acc += L;
-                    if (lane == 0) feat[nf] = sm.cand_bucket[c];
-                    ++nf;
+                    const unsigned fm = __ballot_sync(0xffffffffu, fits);
+                    if (fm && first == n) first = base + __ffs(fm) - 1;
                 }
-                if (lane == 0) {
-                    sm.flags[3] = nf;
-                    sm.red[2] = raw_acc;
-                }
+                if (lane == 0) sm.flags[0] = first;
             }
             __syncthreads();
-            nf = sm.flags[3];
-            raw_acc = sm.red[2];
+            const int c = sm.flags[0];
+            if (c >= n) break;
+            or_bucket(c);
+            count += sm.newc[c];
+            raw_acc += sm.cand_len[c];
+            if (tid == 0) feat[nf] = sm.cand_bucket[c];
+            ++nf;
+            cpos = c + 1;
+            __syncthreads();
         }
     }
     __syncthreads();
@@ -333,18 +450,13 @@ extern "C" int pk_union(uint64_t offsets, uint64_t lens, uint64_t ids, int64_t i
     const int Wmax = (max_history + 31) / 32;
     const size_t bitmap = (size_t)((Wmax + 3) & ~3) * 4;
     const size_t cap = 200 * 1024;
-    // Hash of 2^13 slots (rounds of <= 4096 list entries) when the bitmap
-    // leaves room, else 2^10; the rest stages lists (at least 2048 ids).
-    int bits = 0;
-    for (int b = 13; b >= 10; --b)
-        if (bitmap + ((size_t)2 << b) * 4 + 2048 * 4 <= cap) { bits = b; break; }
-    if (!bits) return PK_ERR_UNSUPPORTED;
-    const size_t used = bitmap + ((size_t)2 << bits) * 4;
-    const int stage_cap = (int)((cap - used) / 4);
+    // The bitmap, then as many staged list entries as fit (at least 2048).
+    if (bitmap + 2048 * 4 > cap) return PK_ERR_UNSUPPORTED;
+    const int stage_cap = (int)((cap - bitmap) / 4);
     cudaFuncSetAttribute(union_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cap);
     union_kernel<<<U, kUnionThreads, cap, (cudaStream_t)stream>>>(
         (const int*)offsets, (const int*)lens, (const int*)ids, ids_stride, (const int*)order, (const int*)n_order,
-        order_stride, (const int*)history, (const long long*)limit, F, max_history, bits, stage_cap, (int*)out_ids,
+        order_stride, (const int*)history, (const long long*)limit, F, max_history, stage_cap, (int*)out_ids,
         out_stride, (int*)out_count, (int*)features, (int*)n_features, (long long*)raw, (int*)status);
     PK_CHECK_LAUNCH();
     return PK_OK;

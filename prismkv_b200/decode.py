@@ -138,7 +138,10 @@ class SparseDecode:
             lt = length
         S = splits or self.splits or 0
         if S <= 0:
-            S = max(1, min(256, (3 * 148 + U - 1) // U))
+            # The library's default: one wave of two CTAs per SM over all
+            # units, at most 8 splits (one on-chip merged cluster per unit).
+            sms = torch.cuda.get_device_properties(q.device).multi_processor_count
+            S = max(1, min(8, (2 * sms) // U))
         nbytes = nv.query("pk_sparse_av_workspace_bytes", U, G, d, S)
         out = None
         if partial is None:
