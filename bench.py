@@ -349,7 +349,9 @@ def run_ours(a):
     if tfile.exists():
         try:
             tj = json.loads(tfile.read_text())
-            traffic = tj["dram_bytes_per_row"] * (mean_bytes / (d * 2 * 2))
+            # One ncu capture's DRAM bytes per algorithmic byte, applied to
+            # this run's mean launch (same kernel, same per-row traffic).
+            traffic = round(tj["dram_bytes_per_algorithmic_byte"] * mean_bytes)
         except (OSError, ValueError, KeyError):
             traffic = None
     launches_per_step = L * 4  # encode + select + union + attention per layer
