@@ -45,16 +45,56 @@ __device__ __forceinline__ float key_at(const T* keys, int64_t unit_stride, int6
     return load_f(keys, (int64_t)u * unit_stride + t * row_stride + c);
 }
 
-// center[u, c] = torch-order column mean of the unit's N rows.
+// center[u, c] = torch-order column mean of the unit's N rows.  The cascade
+// of torch_cascade_sum (blocks of 2^lp rows, 4 levels) splits into chunks of
+// 2^(3 lp) rows that each add one independent sum to the top accumulator:
+// the chunks' sums run in parallel (warp w of the CTA takes chunks w, w+nw,
+// ...; lane = column), then lane 0..31 of warp 0 adds them in chunk order
+// and runs the cascade over the remaining rows.  Same arithmetic, same order.
 template <typename T>
-__global__ void center_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride, int64_t N, int d,
-                              float* __restrict__ center) {
-    const int u = blockIdx.x;
-    for (int c = threadIdx.x; c < d; c += blockDim.x) {
-        const float s =
-            torch_cascade_sum(N, [&](int64_t i) { return key_at(keys, unit_stride, row_stride, u, i, c); });
-        center[(int64_t)u * d + c] = __fdiv_rn(s, (float)N);
+__global__ void __launch_bounds__(1024)
+center_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride, int64_t N, int d,
+              float* __restrict__ center) {
+    extern __shared__ float part[];   // [nchunks][32]
+    const int u = blockIdx.y, lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int c = blockIdx.x * 32 + lane;
+    int lp = ceil_log2_i64(N) / 4;
+    if (lp < 4) lp = 4;
+    const int64_t step = (int64_t)1 << lp, chunk = step * step * step, mask = step - 1;
+    const int64_t nchunks = N / chunk;
+    auto get = [&](int64_t i) { return key_at(keys, unit_stride, row_stride, u, i, c); };
+    if (c < d) {
+        for (int64_t ch = w; ch < nchunks; ch += nw) {
+            int64_t i = ch * chunk;
+            float a2 = 0.f;
+            for (int64_t g = 0; g < step; ++g) {
+                float a1 = 0.f;
+                for (int64_t b = 0; b < step; ++b) {
+                    float a0 = 0.f;
+                    for (int64_t s = 0; s < step; ++s, ++i) a0 = __fadd_rn(a0, get(i));
+                    a1 = __fadd_rn(a1, a0);
+                }
+                a2 = __fadd_rn(a2, a1);
+            }
+            part[ch * 32 + lane] = a2;
+        }
     }
+    __syncthreads();
+    if (w != 0 || c >= d) return;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int64_t ch = 0; ch < nchunks; ++ch) acc[3] = __fadd_rn(acc[3], part[ch * 32 + lane]);
+    int64_t i = nchunks * chunk;
+    while (i + step <= N) {
+        for (int64_t s = 0; s < step; ++s, ++i) acc[0] = __fadd_rn(acc[0], get(i));
+        for (int j = 1; j < 4; ++j) {
+            acc[j] = __fadd_rn(acc[j], acc[j - 1]);
+            acc[j - 1] = 0.f;
+            if ((i & (mask << (j * lp))) != 0) break;
+        }
+    }
+    for (; i < N; ++i) acc[0] = __fadd_rn(acc[0], get(i));
+    for (int j = 1; j < 4; ++j) acc[0] = __fadd_rn(acc[0], acc[j]);
+    center[(int64_t)u * d + c] = __fdiv_rn(acc[0], (float)N);
 }
 
 // One tile of 128 tokens x 128 features.  PASS 1: histogram; PASS 2: emit.
@@ -524,32 +564,53 @@ int run_encode_select(const T* keys, int64_t unit_stride, int64_t row_stride, in
 // Bound-filtered build: approximate activations on the tensor cores with a
 // per-entry error bound, global thresholds that bracket the exact budget
 // threshold, exact recomputation of only the entries the bounds cannot decide.
+//
+// Each CTA holds 128 tokens of one unit (x = (k - c) / s, rounded to bf16)
+// and streams every 128-feature tile of W through a double buffer, so a
+// token block's histogram or members are gathered once per CTA.
+//   MODE 0 (sample): histogram of the positive upper bounds of a strided
+//     sample of token blocks and feature tiles, all 8192 bins; it places a
+//     floor well below the budget threshold.
+//   MODE 1: histograms of the lower and upper bounds at or above the floor
+//     (a 1024-bin window; the top bin collects everything above) and the
+//     counts of positive bounds.
+//   MODE 2: L above the upper bounds' cut -> member; U below the lower
+//     bounds' cut -> not a member; otherwise recompute exactly.
 // ---------------------------------------------------------------------------
 
 constexpr int kFBins = 8192;          // bins of the bounds' float bits >> 18
 constexpr int kFShift = 18;
-constexpr int kFThreads = 256;        // 8 warps x 16 tokens, 128 features
+constexpr int kFWin = 1024;           // histogram window above the floor (32 octaves)
+constexpr int kFThreads = 256;        // 8 warps x 16 tokens, 128 features a tile
+constexpr int kFSampleMargin = 8;     // floor: 8x the sample's share of the budget
 
 struct FastWs {
-    int* histL;         // [U, 8192] positive lower bounds
-    int* histU;         // [U, 8192] positive upper bounds
-    int* cutL;          // [U] bin of the count-th largest lower bound (-1: fewer positives)
-    int* cutU;          // [U] same for the upper bound
-    int* n_amb;         // [U]
-    long long* amb;     // [U, acap] flat indices to recompute exactly
+    int* histL;                 // [U, kFWin] lower bounds from floor_bin up
+    int* histU;                 // [U, kFWin] upper bounds from floor_bin up
+    int* histS;                 // [U, kFBins] sampled positive upper bounds
+    int* floor_bin;             // [U]
+    unsigned long long* pos;    // [U, 2] positive upper / lower bounds
+    int* cutL;                  // [U] bin of the count-th largest lower bound (-1: fewer positives)
+    int* cutU;                  // [U] same for the upper bound
+    int* n_amb;                 // [U]
+    long long* amb;             // [U, acap] flat indices to recompute exactly
     int64_t acap;
 };
 
 size_t fast_counters_bytes(int U) {
-    return 2 * align256((size_t)U * kFBins * 4) + 3 * align256((size_t)U * 4);
+    return 2 * align256((size_t)U * kFWin * 4) + align256((size_t)U * kFBins * 4) + align256((size_t)U * 4) +
+           align256((size_t)U * 16) + 3 * align256((size_t)U * 4);
 }
 size_t fast_bytes(int U, int64_t acap) { return fast_counters_bytes(U) + align256((size_t)U * acap * 8); }
 
 FastWs carve_fast(void* base, int U, int64_t acap) {
     FastWs w;
     char* p = (char*)base;
-    w.histL = (int*)p; p += align256((size_t)U * kFBins * 4);
-    w.histU = (int*)p; p += align256((size_t)U * kFBins * 4);
+    w.histL = (int*)p; p += align256((size_t)U * kFWin * 4);
+    w.histU = (int*)p; p += align256((size_t)U * kFWin * 4);
+    w.histS = (int*)p; p += align256((size_t)U * kFBins * 4);
+    w.floor_bin = (int*)p; p += align256((size_t)U * 4);
+    w.pos = (unsigned long long*)p; p += align256((size_t)U * 16);
     w.cutL = (int*)p; p += align256((size_t)U * 4);
     w.cutU = (int*)p; p += align256((size_t)U * 4);
     w.n_amb = (int*)p; p += align256((size_t)U * 4);
@@ -559,48 +620,69 @@ FastWs carve_fast(void* base, int U, int64_t acap) {
 }
 
 __device__ __forceinline__ int fbin(float v) { return (int)(__float_as_uint(v) >> kFShift); }
+__device__ __forceinline__ unsigned lane_below() {
+    unsigned m;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+    return m;
+}
 
-// Tile of 128 tokens x 128 features; warp w owns tokens 16w..16w+15.
-// v ~= x . W_f + b_f from bf16 operands (mma.sync, fp32 accumulate),
-// |v - exact| <= e = 2^-6 |x| |W_f| + 2^-20 |v|  (operand rounding 2^-8
-// each, accumulation, and the exact order's own rounding, with margin).
-// PASS 1: histograms of the positive bounds L = v - e and U = v + e.
-// PASS 2: L above every upper bound's cut -> member; U below the lower
-// bound's cut -> not a member; otherwise recompute exactly.
-template <int PASS, typename T>
-__global__ void __launch_bounds__(kFThreads)
-build_approx_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride, int64_t N,
-                    const float* __restrict__ center, float key_scale, const __nv_bfloat16* __restrict__ Wb,
-                    const float* __restrict__ bias, const float* __restrict__ wn, int F, BuildWs ws, FastWs fw,
-                    int* __restrict__ lens, int* __restrict__ status) {
+struct TileSample {
+    int tb_stride, ft_stride;   // MODE 0: token blocks and feature tiles sampled
+};
+
+// Shared memory bytes per mode.
+__host__ __device__ constexpr int tile_smem(int mode) {
+    return 128 * 256 + 2 * 128 * 256 + 2 * 2 * 128 * 4 + 128 * 4 + 32 * 4 +
+           (mode == 0 ? kFBins * 4 : mode == 1 ? 2 * kFWin * 4 : 0);
+}
+
+template <int MODE, typename T>
+__global__ void __launch_bounds__(kFThreads, 2)
+build_tile_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride, int64_t N,
+                  const float* __restrict__ center, float key_scale, const __nv_bfloat16* __restrict__ Wb,
+                  const float* __restrict__ bias, const float* __restrict__ wn, int F, BuildWs ws, FastWs fw,
+                  TileSample smp, int* __restrict__ lens, int* __restrict__ status) {
     extern __shared__ __align__(128) uint8_t fsm[];
-    uint8_t* Xs = fsm;                          // [128 rows][256 B] swizzled
-    uint8_t* Wt = fsm + 128 * 256;              // [128 rows][256 B] swizzled
-    float* xn = reinterpret_cast<float*>(fsm + 2 * 128 * 256);   // [128]
-    float* wnt = xn + 128;                                       // [128]
-    float* bt = wnt + 128;                                       // [128]
-    int* hL = reinterpret_cast<int*>(bt + 128);                  // [8192] (pass 1)
-    int* hU = hL + kFBins;                                       // [8192]
+    uint8_t* Xs = fsm;                                            // [128 rows][256 B] swizzled
+    uint8_t* Wt = fsm + 128 * 256;                                // [2][128 rows][256 B] swizzled
+    float* wnt = reinterpret_cast<float*>(fsm + 3 * 128 * 256);   // [2][128]
+    float* bt = wnt + 2 * 128;                                    // [2][128]
+    float* xn = bt + 2 * 128;                                     // [128]
+    float* wmax = xn + 128;                                       // [2] per tile max of |W_f|
+    int* hA = reinterpret_cast<int*>(wmax + 32);                  // MODE 0: [kFBins]; MODE 1: L [kFWin]
+    int* hB = hA + kFWin;                                         // MODE 1: U [kFWin]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int f0 = blockIdx.x * 128;
-    const int64_t t0 = (int64_t)blockIdx.y * 128;
-    const int u = blockIdx.z;
+    const int u = blockIdx.y;
+    const int64_t t0 = (int64_t)blockIdx.x * (MODE == 0 ? smp.tb_stride : 1) * 128;
     const float* cu = center + (int64_t)u * kBD;
+    const int nft = (F + 127) / 128;
+    const int fstep = MODE == 0 ? smp.ft_stride : 1;
 
-    for (int c = tid; c < 128 * 16; c += kFThreads) {
-        const int row = c >> 4, ch = c & 15;
-        const int f = f0 + row;
-        const bool valid = f < F;
-        cp_async_16(smem_addr(Wt) + swz(row, ch), Wb + (int64_t)(valid ? f : 0) * kBD + ch * 8, valid);
-    }
+    auto load_w = [&](int ft, int buf) {
+        const int f0 = ft * 128;
+        uint8_t* dst = Wt + buf * 128 * 256;
+        for (int c = tid; c < 128 * 16; c += kFThreads) {
+            const int row = c >> 4, ch = c & 15;
+            const int f = f0 + row;
+            const bool valid = f < F;
+            cp_async_16(smem_addr(dst) + swz(row, ch), Wb + (int64_t)(valid ? f : 0) * kBD + ch * 8, valid);
+        }
+        if (tid < 128) {
+            const int f = f0 + tid;
+            const float w = f < F ? wn[f] : 0.f;
+            wnt[buf * 128 + tid] = w;
+            bt[buf * 128 + tid] = f < F ? bias[f] : 0.f;
+            const float m = warp_max(w);
+            if (lane == 0) wmax[buf * 16 + warp] = m;
+        }
+    };
+    const int ft_first = MODE == 0 ? (int)(blockIdx.x % fstep) : 0;
+    load_w(ft_first, 0);
     cp_async_commit_group();
-    if (PASS == 1)
-        for (int i = tid; i < 2 * kFBins; i += kFThreads) hL[i] = 0;
-    for (int j = tid; j < 128; j += kFThreads) {
-        const int f = f0 + j;
-        wnt[j] = f < F ? wn[f] : 0.f;
-        bt[j] = f < F ? bias[f] : 0.f;
-    }
+    if (MODE == 0)
+        for (int i = tid; i < kFBins; i += kFThreads) hA[i] = 0;
+    if (MODE == 1)
+        for (int i = tid; i < 2 * kFWin; i += kFThreads) hA[i] = 0;
     // x = (k - center) / key_scale in fp32 (core.py:99), rounded to bf16 for
     // the tensor cores; the row norm bound uses the fp32 values.
     const bool unit_scale = key_scale == 1.0f;
@@ -626,120 +708,311 @@ build_approx_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row
         pk2.y = *reinterpret_cast<uint32_t*>(&p1);
         *reinterpret_cast<uint2*>(Xs + swz(row, lane >> 1) + (lane & 1) * 8) = pk2;
     }
-    cp_async_wait_group<0>();
-    __syncthreads();
-
-    float acc[16][4];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    const int floor_bin = MODE == 1 ? fw.floor_bin[u] : 0;
+    const int cutL = MODE == 2 ? fw.cutL[u] : 0, cutU = MODE == 2 ? fw.cutU[u] : 0;
+    unsigned long long posU = 0, posL = 0;
     const int mi = lane >> 3, r8 = lane & 7;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-        uint32_t a[4];
-        ldsm_x4(smem_addr(Xs) + swz(warp * 16 + (mi & 1) * 8 + r8, 2 * kk + (mi >> 1)), a);
-#pragma unroll
-        for (int np = 0; np < 8; ++np) {
-            uint32_t b[4];
-            ldsm_x4(smem_addr(Wt) + swz(np * 16 + (mi >> 1) * 8 + r8, 2 * kk + (mi & 1)), b);
-            mma_16816(acc[2 * np], a, b[0], b[1]);
-            mma_16816(acc[2 * np + 1], a, b[2], b[3]);
-        }
-    }
 
-    const int cutL = PASS == 2 ? fw.cutL[u] : 0, cutU = PASS == 2 ? fw.cutU[u] : 0;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-        const int row = warp * 16 + (lane >> 2) + half * 8;
-        const int64_t t = t0 + row;
-        if (t >= N) continue;
-        const float xr = xn[row];
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int col = 8 * j + 2 * (lane & 3) + e;
-                const int f = f0 + col;
-                if (f >= F) continue;
-                const float v = acc[j][2 * half + e] + bt[col];
-                const float err = fmaf(0.015625f * xr, wnt[col], 9.5367431640625e-07f * fabsf(v));
-                const float lo = v - err, hi = v + err;
-                if (PASS == 1) {
-                    if (hi > 0.f) atomicAdd(&hU[fbin(hi)], 1);
-                    if (lo > 0.f) atomicAdd(&hL[fbin(lo)], 1);
-                } else {
-                    if (!(hi > 0.f) || fbin(hi) < cutL) continue;          // surely not a member
-                    const long long flat = (long long)t * F + f;
-                    if (lo > 0.f && fbin(lo) > cutU) {                    // surely a member
-                        const int at = atomicAdd(&ws.n_members[u], 1);
-                        if (at < ws.mcap) {
-                            ws.members[(int64_t)u * ws.mcap + at] = flat;
-                            atomicAdd(&lens[(int64_t)u * F + f], 1);
-                        } else {
-                            atomicOr(status, PK_STATUS_MEMBERS_FULL);
-                        }
-                    } else {
-                        const int at = atomicAdd(&fw.n_amb[u], 1);
-                        if (at < fw.acap) fw.amb[(int64_t)u * fw.acap + at] = flat;
-                        else atomicOr(status, PK_STATUS_NEEDS_EXACT);
-                    }
-                }
-            }
-    }
-    if (PASS == 1) {
+    int buf = 0;
+    for (int ft = ft_first; ft < nft; ft += fstep, buf ^= 1) {
+        const int ftn = ft + fstep;
+        if (ftn < nft) load_w(ftn, buf ^ 1);
+        cp_async_commit_group();
+        cp_async_wait_group<1>();
         __syncthreads();
-        for (int i = tid; i < kFBins; i += kFThreads) {
-            if (hL[i]) atomicAdd(&fw.histL[(int64_t)u * kFBins + i], hL[i]);
-            if (hU[i]) atomicAdd(&fw.histU[(int64_t)u * kFBins + i], hU[i]);
+        const uint8_t* W = Wt + buf * 128 * 256;
+        const float* wnb = wnt + buf * 128;
+        const float* bb = bt + buf * 128;
+        float acc[16][4];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            uint32_t a[4];
+            ldsm_x4(smem_addr(Xs) + swz(warp * 16 + (mi & 1) * 8 + r8, 2 * kk + (mi >> 1)), a);
+#pragma unroll
+            for (int np = 0; np < 8; ++np) {
+                uint32_t b[4];
+                ldsm_x4(smem_addr(W) + swz(np * 16 + (mi >> 1) * 8 + r8, 2 * kk + (mi & 1)), b);
+                mma_16816(acc[2 * np], a, b[0], b[1]);
+                mma_16816(acc[2 * np + 1], a, b[2], b[3]);
+            }
+        }
+        const int f0 = ft * 128;
+        const float wm = fmaxf(fmaxf(wmax[buf * 16 + 0], wmax[buf * 16 + 1]), fmaxf(wmax[buf * 16 + 2], wmax[buf * 16 + 3]));
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const int row = warp * 16 + (lane >> 2) + half * 8;
+            const int64_t t = t0 + row;
+            const bool trow = t < N;
+            const float cx = 0.015625f * xn[row];
+            // |err| <= E + 2^-20 |v| for every feature of the tile; the row
+            // tests below use E with the relative term folded in.
+            const float E = cx * wm * (1.0f + 1.0f / 65536.0f);
+            auto err_of = [&](int col, float v) { return fmaf(cx, wnb[col], 9.5367431640625e-07f * fabsf(v)); };
+            if (MODE == 0) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int col = 8 * j + 2 * (lane & 3) + e;
+                        const float v = acc[j][2 * half + e] + bb[col];
+                        if (!trow || f0 + col >= F || !(v > -2.f * E)) continue;
+                        const float hi = v + err_of(col, v);
+                        if (hi > 0.f) atomicAdd(&hA[fbin(hi)], 1);
+                    }
+            } else if (MODE == 1) {
+                // Bounds at or above the floor value are binned; positives
+                // are counted, exactly only where |v| is within the error.
+                // v below vfloor => U below the floor value: U <= v + E +
+                // 2^-20|v|, and |v| <= 4(fval + E) there or U is negative.
+                const float fval = __uint_as_float((uint32_t)floor_bin << kFShift);
+                const float vfloor = fval - 1.001f * E - 3.814697265625e-06f * (fval + E);
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int col = 8 * j + 2 * (lane & 3) + e;
+                        const float v = acc[j][2 * half + e] + bb[col];
+                        if (!trow || f0 + col >= F) continue;
+                        if (v > 2.f * E) {
+                            ++posU;
+                            ++posL;
+                        } else if (v >= -2.f * E) {
+                            const float err = err_of(col, v);
+                            posU += (v + err > 0.f) ? 1 : 0;
+                            posL += (v - err > 0.f) ? 1 : 0;
+                        }
+                        if (v >= vfloor) {
+                            const float err = err_of(col, v);
+                            const float lo = v - err, hi = v + err;
+                            if (hi > 0.f) {
+                                const int bh = fbin(hi) - floor_bin;
+                                if (bh >= 0) atomicAdd(&hB[min(bh, kFWin - 1)], 1);
+                            }
+                            if (lo > 0.f) {
+                                const int bl = fbin(lo) - floor_bin;
+                                if (bl >= 0) atomicAdd(&hA[min(bl, kFWin - 1)], 1);
+                            }
+                        }
+                    }
+            } else {
+                // Entries that can reach the lower bounds' cut (or be positive
+                // when there is none); the warp skips the tile-half when none.
+                if (cutL == INT32_MAX) continue;   // this unit takes the exact path
+                const float cval = cutL >= 0 ? __uint_as_float((uint32_t)cutL << kFShift) : 0.f;
+                const float vcut = cutL >= 0 ? cval - 1.001f * E - 3.814697265625e-06f * (cval + E) : -2.f * E;
+                bool any = false;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int col = 8 * j + 2 * (lane & 3) + e;
+                        any |= trow && f0 + col < F && acc[j][2 * half + e] + bb[col] >= vcut;
+                    }
+                if (!__any_sync(0xffffffffu, any)) continue;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int col = 8 * j + 2 * (lane & 3) + e;
+                        const int f = f0 + col;
+                        const bool valid = trow && f < F;
+                        const float v = acc[j][2 * half + e] + bb[col];
+                        const float err = err_of(col, v);
+                        const float lo = v - err, hi = v + err;
+                        // Surely not a member: U not positive or below the
+                        // lower bounds' cut.  Surely a member: L above the
+                        // upper bounds' cut.  Appends are aggregated per warp.
+                        const bool out = !valid || !(hi > 0.f) || fbin(hi) < cutL;
+                        const bool mem = !out && lo > 0.f && fbin(lo) > cutU;
+                        const bool amb = !out && !mem;
+                        const long long flat = t * F + f;
+                        const unsigned mm = __ballot_sync(0xffffffffu, mem);
+                        if (mm) {
+                            const int lead = __ffs(mm) - 1;
+                            int base = 0;
+                            if (lane == lead) base = atomicAdd(&ws.n_members[u], __popc(mm));
+                            base = __shfl_sync(0xffffffffu, base, lead);
+                            if (mem) {
+                                const int at = base + __popc(mm & lane_below());
+                                if (at < ws.mcap) {
+                                    ws.members[(int64_t)u * ws.mcap + at] = flat;
+                                    atomicAdd(&lens[(int64_t)u * F + f], 1);
+                                } else {
+                                    atomicOr(status, PK_STATUS_MEMBERS_FULL);
+                                }
+                            }
+                        }
+                        const unsigned am = __ballot_sync(0xffffffffu, amb);
+                        if (am) {
+                            const int lead = __ffs(am) - 1;
+                            int base = 0;
+                            if (lane == lead) base = atomicAdd(&fw.n_amb[u], __popc(am));
+                            base = __shfl_sync(0xffffffffu, base, lead);
+                            if (amb) {
+                                const int at = base + __popc(am & lane_below());
+                                if (at < fw.acap) fw.amb[(int64_t)u * fw.acap + at] = flat;
+                                else atomicOr(status, PK_STATUS_BOUNDARY_FULL);
+                            }
+                        }
+                    }
+            }
+        }
+        __syncthreads();   // the buffer is refilled two tiles on
+    }
+    cp_async_wait_group<0>();
+    if (MODE == 0) {
+        for (int i = tid; i < kFBins; i += kFThreads)
+            if (hA[i]) atomicAdd(&fw.histS[(int64_t)u * kFBins + i], hA[i]);
+    } else if (MODE == 1) {
+        posU = warp_sum(posU);
+        posL = warp_sum(posL);
+        if (lane == 0) {
+            atomicAdd(&fw.pos[2 * u], posU);
+            atomicAdd(&fw.pos[2 * u + 1], posL);
+        }
+        for (int i = tid; i < kFWin; i += kFThreads) {
+            if (hA[i]) atomicAdd(&fw.histL[(int64_t)u * kFWin + i], hA[i]);
+            if (hB[i]) atomicAdd(&fw.histU[(int64_t)u * kFWin + i], hB[i]);
         }
     }
 }
 
-// Per unit: the bins holding the count-th largest lower / upper bound.  The
-// exact threshold T lies between them; fewer than `count` positive lower
-// bounds leaves no useful lower cut, and the exact path is needed.
+// Per unit: the floor bin.  Scanning the sample's upper-bound histogram from
+// the top, the floor is the bin where the count reaches kFSampleMargin times
+// the sample's share of the budget (or the lowest sampled positive bin).
+// Any floor is correct -- the cut kernel checks that enough bounds lie above
+// it -- a low one only costs histogram work.
+__global__ void build_floor_kernel(FastWs fw, long long count, double sample_frac) {
+    const int u = blockIdx.x;
+    if (threadIdx.x != 0) return;
+    const int* h = fw.histS + (int64_t)u * kFBins;
+    const double target = fmax(1.0, kFSampleMargin * (double)count * sample_frac);
+    double acc = 0.0;
+    int b = kFBins - 1, lowest = 0;
+    int fb = -1;
+    for (; b >= 0; --b) {
+        if (h[b]) lowest = b;
+        acc += h[b];
+        if (fb < 0 && acc >= target) fb = b;
+    }
+    fw.floor_bin[u] = fb >= 0 ? fb : lowest;
+}
+
+// Per unit: the bins holding the count-th largest lower / upper bound,
+// inside the window above the floor.  When fewer than `count` bounds reach
+// the floor: if fewer are positive at all, every positive counts (cut -1);
+// otherwise the floor was too high and the exact path is needed.  A cut in
+// the window's top bin (which merges everything above) is unusable too.
 __global__ void build_fast_cut_kernel(FastWs fw, long long count, int* __restrict__ status) {
     const int u = blockIdx.x;
     if (threadIdx.x != 0) return;
+    const int fb = fw.floor_bin[u];
+    bool bad = false;
     for (int which = 0; which < 2; ++which) {
-        const int* h = (which ? fw.histU : fw.histL) + (int64_t)u * kFBins;
+        const int* h = (which ? fw.histU : fw.histL) + (int64_t)u * kFWin;
+        const unsigned long long npos = fw.pos[2 * u + (which ? 0 : 1)];
         long long above = 0;
-        int b = kFBins - 1;
+        int b = kFWin - 1;
         for (; b >= 0; --b) {
             if (above + h[b] >= count) break;
             above += h[b];
         }
-        (which ? fw.cutU : fw.cutL)[u] = b;  // -1 when fewer than count positives
+        int cut;
+        if (b >= 0) {
+            cut = fb + b;
+            if (b == kFWin - 1) bad = true;
+        } else {
+            cut = -1;
+            if ((long long)npos >= count) bad = true;
+        }
+        (which ? fw.cutU : fw.cutL)[u] = cut;
     }
-    if (fw.cutL[u] < 0 && fw.cutU[u] >= 0) atomicOr(status, PK_STATUS_NEEDS_EXACT);
+    if (bad || (fw.cutL[u] < 0 && fw.cutU[u] >= 0)) {
+        // The exact path runs instead: classify nothing.
+        atomicOr(status, PK_STATUS_NEEDS_EXACT);
+        fw.cutL[u] = INT32_MAX;
+        fw.cutU[u] = INT32_MAX;
+    }
 }
 
 // Exact activations of the undecided entries (sequential FMA over d, as the
 // reference); entries the exact value decides go straight to members or are
 // dropped, the rest become 64-bit boundary keys (value descending within the
-// band, flat index ascending).
+// band, flat index ascending).  Key and W rows are read 32 values at a time
+// with 16-byte loads when the key rows are 16-byte aligned.
 template <typename T>
-__global__ void build_exact_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride,
-                                   const float* __restrict__ center, float key_scale, const float* __restrict__ W,
-                                   const float* __restrict__ bias, int F, BuildWs ws, FastWs fw,
-                                   int* __restrict__ lens, int* __restrict__ status) {
+__device__ __forceinline__ void load32(const T* p, bool vec, float (&x)[32]) {
+    if constexpr (sizeof(T) == 2) {
+        if (vec) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint4 r = reinterpret_cast<const uint4*>(p)[q];
+                const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 f = __bfloat1622float2(b[j]);
+                    x[8 * q + 2 * j] = f.x;
+                    x[8 * q + 2 * j + 1] = f.y;
+                }
+            }
+            return;
+        }
+    } else {
+        if (vec) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 r = reinterpret_cast<const float4*>(p)[q];
+                x[4 * q] = r.x; x[4 * q + 1] = r.y; x[4 * q + 2] = r.z; x[4 * q + 3] = r.w;
+            }
+            return;
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < 32; ++c) x[c] = load_f(p, c);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+build_exact_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride,
+                   const float* __restrict__ center, float key_scale, const float* __restrict__ W,
+                   const float* __restrict__ bias, int F, BuildWs ws, FastWs fw, int* __restrict__ lens,
+                   int* __restrict__ status, int vec_keys) {
+    __shared__ float cs[kBD];
     const int u = blockIdx.y;
+    for (int c = threadIdx.x; c < kBD; c += blockDim.x) cs[c] = center[(int64_t)u * kBD + c];
+    __syncthreads();
     const int n = (int)min((int64_t)fw.n_amb[u], fw.acap);
     const int cutL = fw.cutL[u], cutU = fw.cutU[u];
-    if (cutL < 0 && cutU >= 0) return;  // the exact path runs instead
-    const float* cu = center + (int64_t)u * kBD;
+    if (cutL == INT32_MAX) return;  // the exact path runs instead
     const bool unit_scale = key_scale == 1.0f;
     const uint32_t hi_bits = cutU >= 0 ? ((uint32_t)(cutU + 1) << kFShift) : 0x7F800000u;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const long long flat = fw.amb[(int64_t)u * fw.acap + i];
         const long long t = flat / F;
         const int f = (int)(flat % F);
-        const float* w = W + (int64_t)f * kBD;
+        const T* krow = keys + (int64_t)u * unit_stride + t * row_stride;
+        const float4* wrow = reinterpret_cast<const float4*>(W + (int64_t)f * kBD);
         float acc = 0.f;
-#pragma unroll 8
-        for (int c = 0; c < kBD; ++c) {
-            const float dlt = __fsub_rn(key_at(keys, unit_stride, row_stride, u, t, c), cu[c]);
-            const float x = unit_scale ? dlt : __fdiv_rn(dlt, key_scale);
-            acc = fmaf(x, w[c], acc);
+#pragma unroll 1
+        for (int c0 = 0; c0 < kBD; c0 += 32) {
+            float kv[32];
+            load32(krow + c0, vec_keys != 0, kv);
+            float4 wv[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) wv[q] = wrow[c0 / 4 + q];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float w4[4] = {wv[q].x, wv[q].y, wv[q].z, wv[q].w};
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int c = 4 * q + r;
+                    const float dlt = __fsub_rn(kv[c], cs[c0 + c]);
+                    const float x = unit_scale ? dlt : __fdiv_rn(dlt, key_scale);
+                    acc = fmaf(x, w4[r], acc);
+                }
+            }
         }
         const float y = __fadd_rn(acc, bias[f]);
         if (!(y > 0.f) || fbin(y) < cutL) continue;                 // below the threshold
@@ -845,21 +1118,36 @@ int run_encode_select_fast(const T* keys, int64_t unit_stride, int64_t row_strid
                            float key_scale, const float* W, const __nv_bfloat16* Wb, const float* wn,
                            const float* b, int U, int F, long long count, BuildWs ws, FastWs fw, int* lens,
                            int* status, cudaStream_t st) {
-    const int smem1 = 2 * 128 * 256 + 3 * 128 * 4 + 2 * kFBins * 4;
-    const int smem2 = 2 * 128 * 256 + 3 * 128 * 4;
-    dim3 grid((F + 127) / 128, (unsigned)((N + 127) / 128), U);
-    cudaFuncSetAttribute(build_approx_kernel<1, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1);
-    cudaFuncSetAttribute(build_approx_kernel<2, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2);
-    build_approx_kernel<1, T><<<grid, kFThreads, smem1, st>>>(keys, unit_stride, row_stride, N, center, key_scale,
-                                                              Wb, b, wn, F, ws, fw, lens, status);
+    const int nblocks = (int)((N + 127) / 128);
+    const int nft = (F + 127) / 128;
+    // Floor sample: about 64 token blocks, a quarter of the feature tiles.
+    TileSample smp;
+    smp.tb_stride = nblocks > 64 ? nblocks / 64 : 1;
+    smp.ft_stride = nft >= 4 ? 4 : 1;
+    const int nsample = (nblocks + smp.tb_stride - 1) / smp.tb_stride;
+    const double frac = fmin(1.0, (double)nsample * 128.0 / (double)N) / (double)smp.ft_stride;
+    const TileSample none = {1, 1};
+    cudaFuncSetAttribute(build_tile_kernel<0, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tile_smem(0));
+    cudaFuncSetAttribute(build_tile_kernel<1, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tile_smem(1));
+    cudaFuncSetAttribute(build_tile_kernel<2, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tile_smem(2));
+    build_tile_kernel<0, T><<<dim3(nsample, U), kFThreads, tile_smem(0), st>>>(
+        keys, unit_stride, row_stride, N, center, key_scale, Wb, b, wn, F, ws, fw, smp, lens, status);
+    PK_CHECK_LAUNCH();
+    build_floor_kernel<<<U, 32, 0, st>>>(fw, count, frac);
+    PK_CHECK_LAUNCH();
+    build_tile_kernel<1, T><<<dim3(nblocks, U), kFThreads, tile_smem(1), st>>>(
+        keys, unit_stride, row_stride, N, center, key_scale, Wb, b, wn, F, ws, fw, none, lens, status);
     PK_CHECK_LAUNCH();
     build_fast_cut_kernel<<<U, 32, 0, st>>>(fw, count, status);
     PK_CHECK_LAUNCH();
-    build_approx_kernel<2, T><<<grid, kFThreads, smem2, st>>>(keys, unit_stride, row_stride, N, center, key_scale,
-                                                              Wb, b, wn, F, ws, fw, lens, status);
+    build_tile_kernel<2, T><<<dim3(nblocks, U), kFThreads, tile_smem(2), st>>>(
+        keys, unit_stride, row_stride, N, center, key_scale, Wb, b, wn, F, ws, fw, none, lens, status);
     PK_CHECK_LAUNCH();
+    const size_t esz = sizeof(T);
+    const int vec = ((uint64_t)keys % 16 == 0 && (unit_stride * (int64_t)esz) % 16 == 0 &&
+                     (row_stride * (int64_t)esz) % 16 == 0) ? 1 : 0;
     build_exact_kernel<T><<<dim3(512, U), 256, 0, st>>>(keys, unit_stride, row_stride, center, key_scale, W, b, F,
-                                                        ws, fw, lens, status);
+                                                        ws, fw, lens, status, vec);
     PK_CHECK_LAUNCH();
     build_fast_need_kernel<<<U, 32, 0, st>>>(ws, fw, count);
     PK_CHECK_LAUNCH();
@@ -887,14 +1175,24 @@ extern "C" int pk_key_center(uint64_t keys, int dtype, int64_t unit_stride, int6
                              int d, uint64_t center, uint64_t stream) {
     if (U < 1 || N < 1 || d < 1 || !keys || !center || row_stride < d) return PK_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;
-    const int threads = d < 128 ? 32 * ((d + 31) / 32) : 128;
-    if (dtype == PK_BF16)
-        center_kernel<__nv_bfloat16><<<U, threads, 0, st>>>((const __nv_bfloat16*)keys, unit_stride, row_stride, N, d,
-                                                           (float*)center);
-    else if (dtype == PK_F32)
-        center_kernel<float><<<U, threads, 0, st>>>((const float*)keys, unit_stride, row_stride, N, d, (float*)center);
-    else
+    // 32 columns per CTA, 32 warps share the cascade's independent chunks.
+    int lp = ceil_log2_i64(N) / 4;
+    if (lp < 4) lp = 4;
+    const int64_t nchunks = N >> (3 * lp);
+    const size_t smem = (size_t)(nchunks > 0 ? nchunks : 1) * 32 * sizeof(float);
+    if (smem > 200 * 1024) return PK_ERR_UNSUPPORTED;
+    dim3 grid((d + 31) / 32, U);
+    if (dtype == PK_BF16) {
+        cudaFuncSetAttribute(center_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        center_kernel<__nv_bfloat16><<<grid, 1024, smem, st>>>((const __nv_bfloat16*)keys, unit_stride, row_stride, N,
+                                                               d, (float*)center);
+    } else if (dtype == PK_F32) {
+        cudaFuncSetAttribute(center_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        center_kernel<float><<<grid, 1024, smem, st>>>((const float*)keys, unit_stride, row_stride, N, d,
+                                                       (float*)center);
+    } else {
         return PK_ERR_ARG;
+    }
     PK_CHECK_LAUNCH();
     return PK_OK;
 }
