@@ -41,6 +41,8 @@ def parse():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", type=int, choices=[3, 4], default=3,
+                   help="3: Llama-3-8B-shaped 32-layer decode (default); 4: 1M-token sequence-sharded decode")
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--batch", type=int, default=4)
     p.add_argument("--kv-heads", type=int, default=8)
@@ -182,7 +184,7 @@ def run_ours(a):
         sae = pk.SAEParams(W, torch.zeros(F, device=dev), key_mean=a.key_mean, query_topk=k)
         torch.cuda.synchronize()
         tb = time.time()
-        idx = pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=False, workspace=ws)
+        idx = pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=False, workspace=ws, slack_frac=0.25, slack_min=4)
         torch.cuda.synchronize()
         build_s += time.time() - tb
         op = pk.SparseDecode(idx, sae, heads_per_unit=G, query_scale=1.0, budget=a.budget,
@@ -517,8 +519,151 @@ def run_reference(a):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# config 4: million-token single-layer decode, KV cache sequence-sharded
+# ---------------------------------------------------------------------------
+
+def run_seqshard(a):
+    """Config 4: B=1, 32/8 heads (U = 8 units of 4 query heads), context
+    1048576, F = 32768, 64 features per query, budget 8192, clustered keys
+    with 4096 clusters.  Rank r of P holds tokens [r*N/P, (r+1)*N/P) of every
+    unit and its shard-local bucket index; a decode step routes (replicated),
+    unions its shard's buckets with budget 8192/P, attends over its rows and
+    merges the P log-sum-exp partials after one NCCL all-gather.  The total
+    context is fixed: strong scaling."""
+    import torch
+    import torch.distributed as dist
+    import prismkv_b200 as pk
+    from prismkv_b200 import native as nv
+    from prismkv_b200.shard import ShardedDecode, token_ranges
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from datetime import timedelta
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+    B, Hkv, G, d = 1, 8, 4, 128
+    U = B * Hkv
+    N, F, k, budget, C = 1 << 20, 32768, 64, 8192, 4096
+    steps_total = a.warmup + a.steps
+    lo, hi = token_ranges(N, world)[rank]
+    tail = steps_total if rank == world - 1 else 0
+    n_local = hi - lo
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed * 7919 + 1)
+    centers = torch.randn(U, C, d, device=dev, generator=g)
+    W = torch.randn(F, d, device=dev, generator=g) / math.sqrt(d)
+    Q = (centers[torch.arange(U, device=dev)[None, :, None],
+                 torch.randint(0, C, (steps_total, U, G), device=dev, generator=g)]
+         + 0.3 * torch.randn(steps_total, U, G, d, device=dev, generator=g)).to(torch.bfloat16)
+    g.manual_seed(a.seed * 7919 + 1000 + rank)
+    T = n_local + tail
+    K = torch.empty(U, T, d, device=dev, dtype=torch.bfloat16)
+    V = torch.empty(U, T, d, device=dev, dtype=torch.bfloat16)
+    for c0 in range(0, T, 16384):
+        c1 = min(T, c0 + 16384)
+        cid = torch.randint(0, C, (U, c1 - c0), device=dev, generator=g)
+        cc = torch.gather(centers, 1, cid[:, :, None].expand(U, c1 - c0, d))
+        K[:, c0:c1] = (cc + 0.3 * torch.randn(U, c1 - c0, d, device=dev, generator=g)).to(torch.bfloat16)
+        V[:, c0:c1] = torch.randn(U, c1 - c0, d, device=dev, generator=g).to(torch.bfloat16)
+    sae = pk.SAEParams(W, torch.zeros(F, device=dev), key_mean=8, query_topk=k)
+    ws = nv.Workspace(dev)
+    torch.cuda.synchronize()
+    tb = time.time()
+    idx = pk.DeviceIndex.build(K[:, :n_local], sae, 1.0, moments=False, workspace=ws)
+    torch.cuda.synchronize()
+    build_s = time.time() - tb
+    for key in [k_ for k_ in ws.buffers if isinstance(k_, tuple) and k_[0] == "build"]:
+        del ws.buffers[key]
+    torch.cuda.empty_cache()
+    sd = ShardedDecode(idx, sae, heads_per_unit=G, budget=budget, max_history=n_local, workspace=ws)
+    q_static = Q[0].clone()
+    len_static = torch.full((U,), n_local + (1 if tail else 0), dtype=torch.int32, device=dev)
+
+    def step(s):
+        q_static.copy_(Q[s])
+        len_static.fill_(n_local + (s + 1 if tail else 0))
+        return sd(q_static, K, V, length=len_static)
+
+    for s_ in range(a.warmup):
+        step(s_)
+    torch.cuda.synchronize()
+    sd.check()
+    barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.2)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.time()
+    e0.record()
+    for s_ in range(a.warmup, steps_total):
+        out = step(s_)
+    e1.record()
+    torch.cuda.synchronize()
+    t1 = time.time()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    # End to end with host buffers: the query in, the merged output out.
+    h_q = Q.cpu().pin_memory()
+    h_out = torch.empty(U, G, d, dtype=torch.bfloat16).pin_memory()
+    torch.cuda.synchronize()
+    barrier()
+    ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ee0.record()
+    for s_ in range(a.warmup, steps_total):
+        q_static.copy_(h_q[s_], non_blocking=True)
+        len_static.fill_(n_local + (s_ + 1 if tail else 0))
+        o = sd(q_static, K, V, length=len_static)
+        h_out.copy_(o, non_blocking=True)
+    ee1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(ee0.elapsed_time(ee1))
+    clocks.stop()
+    sd.check()
+    tokens = B * a.steps
+    line = {
+        "metric": "config4 decode tokens/s at 1M ctx (sequence-sharded)", "value": round(tokens / (ms / 1e3), 2),
+        "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": round(ms / a.steps, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded clustered keys, iid values, random-init SAE)",
+        "config": {"workload": "config4: 1M-token single-layer decode, KV cache sequence-sharded",
+                   "batch": B, "kv_heads": Hkv, "q_per_kv": G, "history": N, "features": F, "query_topk": k,
+                   "budget": budget, "budget_per_shard": budget // world, "clusters": C,
+                   "tokens_per_shard": n_local, "build_s": round(build_s, 2),
+                   "index": "shard-local build (per-shard BatchTopK threshold)",
+                   "parallelism": f"seq{world}", "l2": "KV rows gathered per step are scattered over >> L2"},
+        "e2e": {"value": round(tokens / (e2e_ms / 1e3), 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(U * G * d * 2), "d2h_bytes_per_step": int(U * G * d * 2)},
+        "gpu_launches": 5 * a.steps,
+        "clocks": clocks.summary(t0, t1),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 if __name__ == "__main__":
     args = parse()
+    if args.impl == "ours" and args.config == 4:
+        run_seqshard(args)
+        sys.exit(0)
     if args.impl == "reference":
         run_reference(args)
     else:

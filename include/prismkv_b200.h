@@ -195,13 +195,18 @@ int pk_sparse_av_noalloc(uint64_t q, uint64_t k, uint64_t v, int dtype,
 int pk_key_center(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride,
                   int U, int64_t N, int d, uint64_t center, uint64_t stream);
 
+/* w_enc rounded to fp16 [F, d] for the bound-filtered build and append (no
+ * counterpart in the reference: an internal operand copy, made once per SAE). */
+int pk_sae_prepare_half(uint64_t w_enc, int F, int d, uint64_t w_half, uint64_t stream);
+
 /* Builds buckets for U units sharing one SAE (w_enc[F, d], b_enc[F]).
- * With w_bf16 and w_norm from pk_sae_prepare (both non-zero), activations
- * are first approximated on the tensor cores with a per-entry error bound;
- * only entries the bounds cannot place above or below the budget threshold
- * are recomputed exactly (same memberships).  If the bounds cannot bracket
- * the threshold (degenerate inputs) PK_STATUS_NEEDS_EXACT is raised and the
- * caller reruns without w_bf16 / w_norm (append_index then changes nothing).
+ * With w_half from pk_sae_prepare_half and w_norm from pk_sae_prepare (both
+ * non-zero), activations are first approximated on the tensor cores (fp16
+ * operands) with a per-entry error bound; only entries the bounds cannot
+ * place above or below the budget threshold are recomputed exactly (same
+ * memberships).  If the bounds cannot bracket the threshold (degenerate or
+ * out-of-range inputs) PK_STATUS_NEEDS_EXACT is raised and the caller reruns
+ * without w_half / w_norm (append_index then changes nothing).
  * Token ids are written as token_base + t.  Bucket regions get
  * ceil(len*slack_frac) + slack_min spare slots for later appends;
  * ids_stride must be >= pk_build_ids_capacity(...).  */
@@ -209,7 +214,7 @@ int64_t pk_build_ids_capacity(int64_t N, int F, int key_mean, float slack_frac, 
 size_t pk_build_workspace_bytes(int U, int64_t N, int F, int key_mean, int64_t boundary_capacity);
 int pk_build_index(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride,
                    uint64_t center, float key_scale, uint64_t w_enc, uint64_t b_enc,
-                   uint64_t w_bf16, uint64_t w_norm,
+                   uint64_t w_half, uint64_t w_norm,
                    int U, int64_t N, int d, int F, int key_mean, int64_t token_base,
                    float slack_frac, int slack_min,
                    uint64_t offsets, uint64_t lens, uint64_t ids, int64_t ids_stride,
@@ -231,7 +236,7 @@ int pk_summarize(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stri
 size_t pk_append_workspace_bytes(int U, int64_t n_new, int d, int F, int key_mean, int64_t boundary_capacity);
 int pk_append_index(uint64_t new_keys, int dtype, int64_t unit_stride, int64_t row_stride, int64_t n_new,
                     uint64_t center, float key_scale, uint64_t w_enc, uint64_t b_enc,
-                    uint64_t w_bf16, uint64_t w_norm,
+                    uint64_t w_half, uint64_t w_norm,
                     int U, int d, int F, int key_mean, int64_t history,
                     uint64_t offsets, uint64_t lens, uint64_t ids, int64_t ids_stride,
                     uint64_t mean, uint64_t var,

@@ -12,6 +12,8 @@
 // then ties at that value by ascending flat index, positives only.  The dot
 // products run as one sequential FMA chain over d, the order the reference's
 // F.linear takes for a many-row block, so memberships are bit-identical.
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "mma.cuh"
 
@@ -380,20 +382,25 @@ __global__ void __launch_bounds__(1024)
 sort_buckets_big_kernel(int* __restrict__ ids, int64_t ids_stride, const int* __restrict__ offsets,
                         const int* __restrict__ start, const int* __restrict__ cnt, int F, int* __restrict__ status) {
     extern __shared__ int big[];
-    const int u = blockIdx.y, f = blockIdx.x;
-    const int L = cnt[(int64_t)u * F + f];
-    if (L <= kSortWarpCap) return;
-    if (L > kSortBigCap) {
-        if (threadIdx.x == 0) atomicOr(status, PK_STATUS_BUCKET_TOO_BIG);
-        return;
+    const int u = blockIdx.y;
+    // Grid-stride over the unit's buckets: only the few above the warp
+    // kernel's capacity do any work.
+    for (int f = blockIdx.x; f < F; f += gridDim.x) {
+        const int L = cnt[(int64_t)u * F + f];
+        if (L <= kSortWarpCap) continue;
+        if (L > kSortBigCap) {
+            if (threadIdx.x == 0) atomicOr(status, PK_STATUS_BUCKET_TOO_BIG);
+            continue;
+        }
+        int* src = ids + (int64_t)u * ids_stride + offsets[(int64_t)u * (F + 1) + f] +
+                   (start ? start[(int64_t)u * F + f] : 0);
+        const int n = next_pow2(L);
+        for (int i = threadIdx.x; i < n; i += blockDim.x) big[i] = i < L ? src[i] : INT32_MAX;
+        __syncthreads();
+        bitonic_sort_shared(big, n, threadIdx.x, blockDim.x, false);
+        for (int i = threadIdx.x; i < L; i += blockDim.x) src[i] = big[i];
+        __syncthreads();
     }
-    int* src = ids + (int64_t)u * ids_stride + offsets[(int64_t)u * (F + 1) + f] +
-               (start ? start[(int64_t)u * F + f] : 0);
-    const int n = next_pow2(L);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) big[i] = i < L ? src[i] : INT32_MAX;
-    __syncthreads();
-    bitonic_sort_shared(big, n, threadIdx.x, blockDim.x, false);
-    for (int i = threadIdx.x; i < L; i += blockDim.x) src[i] = big[i];
 }
 
 // Moments of the ORIGINAL keys per bucket (core.py:84-88) in torch's order:
@@ -565,43 +572,56 @@ int run_encode_select(const T* keys, int64_t unit_stride, int64_t row_stride, in
 // per-entry error bound, global thresholds that bracket the exact budget
 // threshold, exact recomputation of only the entries the bounds cannot decide.
 //
-// Each CTA holds 128 tokens of one unit (x = (k - c) / s, rounded to bf16)
+// Operands are fp16 (unit roundoff 2^-11; x and W_f stay far inside its
+// range, which is checked): with fp32 accumulation of exact products,
+//   |v - exact| <= e = 2^-9 |x| |W_f| + 2^-21 (|x| + |W_f|) + 2^-20 |v|
+// (2^-10 relative from the two roundings and the accumulation, doubled; the
+// second term covers fp16 subnormals, the third the reference order's own
+// rounding).  Rows with |x_i| >= 60000 or features with |W_f| >= 60000 raise
+// PK_STATUS_NEEDS_EXACT (the caller reruns the exact path).
+//
+// Each CTA holds 128 tokens of one unit (x = (k - c) / s, rounded to fp16)
 // and streams every 128-feature tile of W through a double buffer, so a
 // token block's histogram or members are gathered once per CTA.
-//   MODE 0 (sample): histogram of the positive upper bounds of a strided
+//   MODE 0 (sample): histogram of the positive lower bounds of a strided
 //     sample of token blocks and feature tiles, all 8192 bins; it places a
 //     floor well below the budget threshold.
 //   MODE 1: histograms of the lower and upper bounds at or above the floor
 //     (a 1024-bin window; the top bin collects everything above) and the
 //     counts of positive bounds.
-//   MODE 2: L above the upper bounds' cut -> member; U below the lower
-//     bounds' cut -> not a member; otherwise recompute exactly.
+//     Entries whose upper bound reaches the floor are kept, with their
+//     bounds, for build_classify_kernel (one tensor-core pass in all).
 // ---------------------------------------------------------------------------
 
 constexpr int kFBins = 8192;          // bins of the bounds' float bits >> 18
 constexpr int kFShift = 18;
 constexpr int kFWin = 1024;           // histogram window above the floor (32 octaves)
 constexpr int kFThreads = 256;        // 8 warps x 16 tokens, 128 features a tile
-constexpr int kFSampleMargin = 8;     // floor: 8x the sample's share of the budget
+constexpr int kFSampleMargin = 2;     // floor: 2x the sample's share of the budget
 
 struct FastWs {
     int* histL;                 // [U, kFWin] lower bounds from floor_bin up
     int* histU;                 // [U, kFWin] upper bounds from floor_bin up
-    int* histS;                 // [U, kFBins] sampled positive upper bounds
+    int* histS;                 // [U, kFBins] sampled positive lower bounds
     int* floor_bin;             // [U]
     unsigned long long* pos;    // [U, 2] positive upper / lower bounds
     int* cutL;                  // [U] bin of the count-th largest lower bound (-1: fewer positives)
     int* cutU;                  // [U] same for the upper bound
     int* n_amb;                 // [U]
+    int* n_cand;                // [U]
     long long* amb;             // [U, acap] flat indices to recompute exactly
+    float2* cand_hl;            // [U, acap] (U, L) bounds of the entries at or above the floor
+    long long* cand_flat;       // [U, acap] their flat indices
     int64_t acap;
 };
 
 size_t fast_counters_bytes(int U) {
     return 2 * align256((size_t)U * kFWin * 4) + align256((size_t)U * kFBins * 4) + align256((size_t)U * 4) +
-           align256((size_t)U * 16) + 3 * align256((size_t)U * 4);
+           align256((size_t)U * 16) + 4 * align256((size_t)U * 4);
 }
-size_t fast_bytes(int U, int64_t acap) { return fast_counters_bytes(U) + align256((size_t)U * acap * 8); }
+size_t fast_bytes(int U, int64_t acap) {
+    return fast_counters_bytes(U) + 2 * align256((size_t)U * acap * 8) + align256((size_t)U * acap * 8);
+}
 
 FastWs carve_fast(void* base, int U, int64_t acap) {
     FastWs w;
@@ -614,7 +634,10 @@ FastWs carve_fast(void* base, int U, int64_t acap) {
     w.cutL = (int*)p; p += align256((size_t)U * 4);
     w.cutU = (int*)p; p += align256((size_t)U * 4);
     w.n_amb = (int*)p; p += align256((size_t)U * 4);
-    w.amb = (long long*)p;
+    w.n_cand = (int*)p; p += align256((size_t)U * 4);
+    w.amb = (long long*)p; p += align256((size_t)U * acap * 8);
+    w.cand_hl = (float2*)p; p += align256((size_t)U * acap * 8);
+    w.cand_flat = (long long*)p;
     w.acap = acap;
     return w;
 }
@@ -633,13 +656,13 @@ struct TileSample {
 // Shared memory bytes per mode.
 __host__ __device__ constexpr int tile_smem(int mode) {
     return 128 * 256 + 2 * 128 * 256 + 2 * 2 * 128 * 4 + 128 * 4 + 32 * 4 +
-           (mode == 0 ? kFBins * 4 : mode == 1 ? 2 * kFWin * 4 : 0);
+           (mode == 0 ? kFBins * 4 : 2 * kFWin * 4);
 }
 
 template <int MODE, typename T>
 __global__ void __launch_bounds__(kFThreads, 2)
 build_tile_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride, int64_t N,
-                  const float* __restrict__ center, float key_scale, const __nv_bfloat16* __restrict__ Wb,
+                  const float* __restrict__ center, float key_scale, const __half* __restrict__ Wh,
                   const float* __restrict__ bias, const float* __restrict__ wn, int F, BuildWs ws, FastWs fw,
                   TileSample smp, int* __restrict__ lens, int* __restrict__ status) {
     extern __shared__ __align__(128) uint8_t fsm[];
@@ -665,11 +688,12 @@ build_tile_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_s
             const int row = c >> 4, ch = c & 15;
             const int f = f0 + row;
             const bool valid = f < F;
-            cp_async_16(smem_addr(dst) + swz(row, ch), Wb + (int64_t)(valid ? f : 0) * kBD + ch * 8, valid);
+            cp_async_16(smem_addr(dst) + swz(row, ch), Wh + (int64_t)(valid ? f : 0) * kBD + ch * 8, valid);
         }
         if (tid < 128) {
             const int f = f0 + tid;
             const float w = f < F ? wn[f] : 0.f;
+            if (w >= 60000.f) atomicOr(status, PK_STATUS_NEEDS_EXACT);
             wnt[buf * 128 + tid] = w;
             bt[buf * 128 + tid] = f < F ? bias[f] : 0.f;
             const float m = warp_max(w);
@@ -683,7 +707,7 @@ build_tile_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_s
         for (int i = tid; i < kFBins; i += kFThreads) hA[i] = 0;
     if (MODE == 1)
         for (int i = tid; i < 2 * kFWin; i += kFThreads) hA[i] = 0;
-    // x = (k - center) / key_scale in fp32 (core.py:99), rounded to bf16 for
+    // x = (k - center) / key_scale in fp32 (core.py:99), rounded to fp16 for
     // the tensor cores; the row norm bound uses the fp32 values.
     const bool unit_scale = key_scale == 1.0f;
     for (int rr = 0; rr < 16; ++rr) {
@@ -701,15 +725,18 @@ build_tile_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_s
         }
         float ss = fmaf(x[0], x[0], fmaf(x[1], x[1], fmaf(x[2], x[2], x[3] * x[3])));
         ss = warp_sum(ss);
-        if (lane == 0) xn[row] = sqrtf(ss) * (1.0f + 1.0f / 4096.0f);
-        __nv_bfloat162 p0 = __floats2bfloat162_rn(x[0], x[1]), p1 = __floats2bfloat162_rn(x[2], x[3]);
+        const float amax = warp_max(fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3]))));
+        if (lane == 0) {
+            xn[row] = sqrtf(ss) * (1.0f + 1.0f / 4096.0f);
+            if (!(amax < 60000.f)) atomicOr(status, PK_STATUS_NEEDS_EXACT);
+        }
+        __half2 p0 = __floats2half2_rn(x[0], x[1]), p1 = __floats2half2_rn(x[2], x[3]);
         uint2 pk2;
         pk2.x = *reinterpret_cast<uint32_t*>(&p0);
         pk2.y = *reinterpret_cast<uint32_t*>(&p1);
         *reinterpret_cast<uint2*>(Xs + swz(row, lane >> 1) + (lane & 1) * 8) = pk2;
     }
     const int floor_bin = MODE == 1 ? fw.floor_bin[u] : 0;
-    const int cutL = MODE == 2 ? fw.cutL[u] : 0, cutU = MODE == 2 ? fw.cutU[u] : 0;
     unsigned long long posU = 0, posL = 0;
     const int mi = lane >> 3, r8 = lane & 7;
 
@@ -734,8 +761,8 @@ build_tile_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_s
             for (int np = 0; np < 8; ++np) {
                 uint32_t b[4];
                 ldsm_x4(smem_addr(W) + swz(np * 16 + (mi >> 1) * 8 + r8, 2 * kk + (mi & 1)), b);
-                mma_16816(acc[2 * np], a, b[0], b[1]);
-                mma_16816(acc[2 * np + 1], a, b[2], b[3]);
+                mma_16816_f16(acc[2 * np], a, b[0], b[1]);
+                mma_16816_f16(acc[2 * np + 1], a, b[2], b[3]);
             }
         }
         const int f0 = ft * 128;
@@ -745,11 +772,12 @@ build_tile_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_s
             const int row = warp * 16 + (lane >> 2) + half * 8;
             const int64_t t = t0 + row;
             const bool trow = t < N;
-            const float cx = 0.015625f * xn[row];
+            const float cx = 0.001953125f * xn[row];
+            const float cs = 4.76837158203125e-07f * (xn[row] + wm);
             // |err| <= E + 2^-20 |v| for every feature of the tile; the row
             // tests below use E with the relative term folded in.
-            const float E = cx * wm * (1.0f + 1.0f / 65536.0f);
-            auto err_of = [&](int col, float v) { return fmaf(cx, wnb[col], 9.5367431640625e-07f * fabsf(v)); };
+            const float E = cx * wm * (1.0f + 1.0f / 65536.0f) + cs;
+            auto err_of = [&](int col, float v) { return fmaf(cx, wnb[col], cs + 9.5367431640625e-07f * fabsf(v)); };
             if (MODE == 0) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
@@ -757,17 +785,21 @@ build_tile_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_s
                     for (int e = 0; e < 2; ++e) {
                         const int col = 8 * j + 2 * (lane & 3) + e;
                         const float v = acc[j][2 * half + e] + bb[col];
-                        if (!trow || f0 + col >= F || !(v > -2.f * E)) continue;
-                        const float hi = v + err_of(col, v);
-                        if (hi > 0.f) atomicAdd(&hA[fbin(hi)], 1);
+                        if (!trow || f0 + col >= F || !(v > 0.f)) continue;
+                        const float lo = v - err_of(col, v);
+                        if (lo > 0.f) atomicAdd(&hA[fbin(lo)], 1);
                     }
             } else if (MODE == 1) {
-                // Bounds at or above the floor value are binned; positives
-                // are counted, exactly only where |v| is within the error.
+                // Bounds at or above the floor value are binned and the
+                // entry, with its bounds, is kept as a candidate (an entry
+                // whose U is below the floor cannot reach the threshold);
+                // positives are counted, exactly only where |v| is within
+                // the error.
                 // v below vfloor => U below the floor value: U <= v + E +
                 // 2^-20|v|, and |v| <= 4(fval + E) there or U is negative.
                 const float fval = __uint_as_float((uint32_t)floor_bin << kFShift);
                 const float vfloor = fval - 1.001f * E - 3.814697265625e-06f * (fval + E);
+                int nk = 0;
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
 #pragma unroll
@@ -783,79 +815,47 @@ build_tile_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_s
                             posU += (v + err > 0.f) ? 1 : 0;
                             posL += (v - err > 0.f) ? 1 : 0;
                         }
-                        if (v >= vfloor) {
-                            const float err = err_of(col, v);
-                            const float lo = v - err, hi = v + err;
-                            if (hi > 0.f) {
-                                const int bh = fbin(hi) - floor_bin;
-                                if (bh >= 0) atomicAdd(&hB[min(bh, kFWin - 1)], 1);
-                            }
-                            if (lo > 0.f) {
-                                const int bl = fbin(lo) - floor_bin;
-                                if (bl >= 0) atomicAdd(&hA[min(bl, kFWin - 1)], 1);
-                            }
-                        }
+                        nk += v >= vfloor ? 1 : 0;
                     }
-            } else {
-                // Entries that can reach the lower bounds' cut (or be positive
-                // when there is none); the warp skips the tile-half when none.
-                if (cutL == INT32_MAX) continue;   // this unit takes the exact path
-                const float cval = cutL >= 0 ? __uint_as_float((uint32_t)cutL << kFShift) : 0.f;
-                const float vcut = cutL >= 0 ? cval - 1.001f * E - 3.814697265625e-06f * (cval + E) : -2.f * E;
-                bool any = false;
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const int col = 8 * j + 2 * (lane & 3) + e;
-                        any |= trow && f0 + col < F && acc[j][2 * half + e] + bb[col] >= vcut;
-                    }
-                if (!__any_sync(0xffffffffu, any)) continue;
+                // Slots for every entry past the row test, reserved with one
+                // atomic per warp; entries whose exact U misses the floor are
+                // written with U = -1, which classification drops.
+                const int inc = warp_inclusive_scan(nk);
+                const int wtot = __shfl_sync(0xffffffffu, inc, 31);
+                if (wtot == 0) continue;
+                int base = 0;
+                if (lane == 31) base = atomicAdd(&fw.n_cand[u], wtot);
+                base = __shfl_sync(0xffffffffu, base, 31) + inc - nk;
+                if (nk == 0) continue;
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                         const int col = 8 * j + 2 * (lane & 3) + e;
                         const int f = f0 + col;
-                        const bool valid = trow && f < F;
                         const float v = acc[j][2 * half + e] + bb[col];
+                        if (!trow || f >= F || !(v >= vfloor)) continue;
                         const float err = err_of(col, v);
                         const float lo = v - err, hi = v + err;
-                        // Surely not a member: U not positive or below the
-                        // lower bounds' cut.  Surely a member: L above the
-                        // upper bounds' cut.  Appends are aggregated per warp.
-                        const bool out = !valid || !(hi > 0.f) || fbin(hi) < cutL;
-                        const bool mem = !out && lo > 0.f && fbin(lo) > cutU;
-                        const bool amb = !out && !mem;
-                        const long long flat = t * F + f;
-                        const unsigned mm = __ballot_sync(0xffffffffu, mem);
-                        if (mm) {
-                            const int lead = __ffs(mm) - 1;
-                            int base = 0;
-                            if (lane == lead) base = atomicAdd(&ws.n_members[u], __popc(mm));
-                            base = __shfl_sync(0xffffffffu, base, lead);
-                            if (mem) {
-                                const int at = base + __popc(mm & lane_below());
-                                if (at < ws.mcap) {
-                                    ws.members[(int64_t)u * ws.mcap + at] = flat;
-                                    atomicAdd(&lens[(int64_t)u * F + f], 1);
-                                } else {
-                                    atomicOr(status, PK_STATUS_MEMBERS_FULL);
-                                }
+                        bool keep = false;
+                        if (hi > 0.f) {
+                            const int bh = fbin(hi) - floor_bin;
+                            if (bh >= 0) {
+                                atomicAdd(&hB[min(bh, kFWin - 1)], 1);
+                                keep = true;
                             }
                         }
-                        const unsigned am = __ballot_sync(0xffffffffu, amb);
-                        if (am) {
-                            const int lead = __ffs(am) - 1;
-                            int base = 0;
-                            if (lane == lead) base = atomicAdd(&fw.n_amb[u], __popc(am));
-                            base = __shfl_sync(0xffffffffu, base, lead);
-                            if (amb) {
-                                const int at = base + __popc(am & lane_below());
-                                if (at < fw.acap) fw.amb[(int64_t)u * fw.acap + at] = flat;
-                                else atomicOr(status, PK_STATUS_BOUNDARY_FULL);
-                            }
+                        if (lo > 0.f) {
+                            const int bl = fbin(lo) - floor_bin;
+                            if (bl >= 0) atomicAdd(&hA[min(bl, kFWin - 1)], 1);
                         }
+                        if (base < fw.acap) {
+                            fw.cand_hl[(int64_t)u * fw.acap + base] = make_float2(keep ? hi : -1.f, lo);
+                            fw.cand_flat[(int64_t)u * fw.acap + base] = t * F + f;
+                        } else {
+                            atomicOr(status, PK_STATUS_BOUNDARY_FULL);
+                        }
+                        ++base;
                     }
             }
         }
@@ -934,6 +934,60 @@ __global__ void build_fast_cut_kernel(FastWs fw, long long count, int* __restric
         atomicOr(status, PK_STATUS_NEEDS_EXACT);
         fw.cutL[u] = INT32_MAX;
         fw.cutU[u] = INT32_MAX;
+    }
+}
+
+// Classification of the candidates kept by the histogram pass (every entry
+// whose upper bound reaches the floor): not a member if U is below the lower
+// bounds' cut; a member if L is above the upper bounds' cut; otherwise the
+// exact value decides.  Appends are aggregated per warp.
+__global__ void __launch_bounds__(256)
+build_classify_kernel(int F, BuildWs ws, FastWs fw, int* __restrict__ lens, int* __restrict__ status) {
+    const int u = blockIdx.y, lane = threadIdx.x & 31;
+    const int n = (int)min((int64_t)fw.n_cand[u], fw.acap);
+    const int cutL = fw.cutL[u], cutU = fw.cutU[u];
+    if (cutL == INT32_MAX) return;  // the exact path runs instead
+    const int stride = gridDim.x * blockDim.x;
+    for (int base0 = blockIdx.x * blockDim.x; base0 < n; base0 += stride) {
+        const int i = base0 + threadIdx.x;
+        bool mem = false, amb = false;
+        long long flat = 0;
+        if (i < n) {
+            const float2 hl = fw.cand_hl[(int64_t)u * fw.acap + i];
+            flat = fw.cand_flat[(int64_t)u * fw.acap + i];
+            const float hi = hl.x, lo = hl.y;
+            const bool out = !(hi > 0.f) || fbin(hi) < cutL;
+            mem = !out && lo > 0.f && fbin(lo) > cutU;
+            amb = !out && !mem;
+        }
+        const unsigned mm = __ballot_sync(0xffffffffu, mem);
+        if (mm) {
+            const int lead = __ffs(mm) - 1;
+            int base = 0;
+            if (lane == lead) base = atomicAdd(&ws.n_members[u], __popc(mm));
+            base = __shfl_sync(0xffffffffu, base, lead);
+            if (mem) {
+                const int at = base + __popc(mm & lane_below());
+                if (at < ws.mcap) {
+                    ws.members[(int64_t)u * ws.mcap + at] = flat;
+                    atomicAdd(&lens[(int64_t)u * F + (int)(flat % F)], 1);
+                } else {
+                    atomicOr(status, PK_STATUS_MEMBERS_FULL);
+                }
+            }
+        }
+        const unsigned am = __ballot_sync(0xffffffffu, amb);
+        if (am) {
+            const int lead = __ffs(am) - 1;
+            int base = 0;
+            if (lane == lead) base = atomicAdd(&fw.n_amb[u], __popc(am));
+            base = __shfl_sync(0xffffffffu, base, lead);
+            if (amb) {
+                const int at = base + __popc(am & lane_below());
+                if (at < fw.acap) fw.amb[(int64_t)u * fw.acap + at] = flat;
+                else atomicOr(status, PK_STATUS_BOUNDARY_FULL);
+            }
+        }
     }
 }
 
@@ -1115,7 +1169,7 @@ build_fast_resolve_kernel(BuildWs ws, int F, int* __restrict__ lens, int* __rest
 
 template <typename T>
 int run_encode_select_fast(const T* keys, int64_t unit_stride, int64_t row_stride, int64_t N, const float* center,
-                           float key_scale, const float* W, const __nv_bfloat16* Wb, const float* wn,
+                           float key_scale, const float* W, const __half* Wh, const float* wn,
                            const float* b, int U, int F, long long count, BuildWs ws, FastWs fw, int* lens,
                            int* status, cudaStream_t st) {
     const int nblocks = (int)((N + 127) / 128);
@@ -1129,19 +1183,17 @@ int run_encode_select_fast(const T* keys, int64_t unit_stride, int64_t row_strid
     const TileSample none = {1, 1};
     cudaFuncSetAttribute(build_tile_kernel<0, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tile_smem(0));
     cudaFuncSetAttribute(build_tile_kernel<1, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tile_smem(1));
-    cudaFuncSetAttribute(build_tile_kernel<2, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tile_smem(2));
     build_tile_kernel<0, T><<<dim3(nsample, U), kFThreads, tile_smem(0), st>>>(
-        keys, unit_stride, row_stride, N, center, key_scale, Wb, b, wn, F, ws, fw, smp, lens, status);
+        keys, unit_stride, row_stride, N, center, key_scale, Wh, b, wn, F, ws, fw, smp, lens, status);
     PK_CHECK_LAUNCH();
     build_floor_kernel<<<U, 32, 0, st>>>(fw, count, frac);
     PK_CHECK_LAUNCH();
     build_tile_kernel<1, T><<<dim3(nblocks, U), kFThreads, tile_smem(1), st>>>(
-        keys, unit_stride, row_stride, N, center, key_scale, Wb, b, wn, F, ws, fw, none, lens, status);
+        keys, unit_stride, row_stride, N, center, key_scale, Wh, b, wn, F, ws, fw, none, lens, status);
     PK_CHECK_LAUNCH();
     build_fast_cut_kernel<<<U, 32, 0, st>>>(fw, count, status);
     PK_CHECK_LAUNCH();
-    build_tile_kernel<2, T><<<dim3(nblocks, U), kFThreads, tile_smem(2), st>>>(
-        keys, unit_stride, row_stride, N, center, key_scale, Wb, b, wn, F, ws, fw, none, lens, status);
+    build_classify_kernel<<<dim3(256, U), 256, 0, st>>>(F, ws, fw, lens, status);
     PK_CHECK_LAUNCH();
     const size_t esz = sizeof(T);
     const int vec = ((uint64_t)keys % 16 == 0 && (unit_stride * (int64_t)esz) % 16 == 0 &&
@@ -1162,7 +1214,8 @@ int sort_buckets(int* ids, int64_t ids_stride, const int* offsets, const int* st
     PK_CHECK_LAUNCH();
     const int smem = kSortBigCap * (int)sizeof(int);
     cudaFuncSetAttribute(sort_buckets_big_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    sort_buckets_big_kernel<<<dim3(F, U), 1024, smem, st>>>(ids, ids_stride, offsets, start, cnt, F, status);
+    sort_buckets_big_kernel<<<dim3(F < 64 ? F : 64, U), 1024, smem, st>>>(ids, ids_stride, offsets, start, cnt, F,
+                                                                          status);
     PK_CHECK_LAUNCH();
     return PK_OK;
 }
@@ -1209,7 +1262,7 @@ extern "C" size_t pk_build_workspace_bytes(int U, int64_t N, int F, int key_mean
 }
 
 extern "C" int pk_build_index(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride, uint64_t center,
-                              float key_scale, uint64_t w_enc, uint64_t b_enc, uint64_t w_bf16, uint64_t w_norm,
+                              float key_scale, uint64_t w_enc, uint64_t b_enc, uint64_t w_half, uint64_t w_norm,
                               int U, int64_t N, int d, int F,
                               int key_mean, int64_t token_base, float slack_frac, int slack_min, uint64_t offsets,
                               uint64_t lens, uint64_t ids, int64_t ids_stride, int64_t boundary_capacity,
@@ -1233,15 +1286,15 @@ extern "C" int pk_build_index(uint64_t keys, int dtype, int64_t unit_stride, int
     cudaMemsetAsync((void*)lens, 0, (size_t)U * F * sizeof(int), st);
     const long long count = (long long)N * key_mean;
     int rc;
-    const bool fast = w_bf16 && w_norm;
+    const bool fast = w_half && w_norm;
     if (fast && dtype == PK_BF16)
         rc = run_encode_select_fast((const __nv_bfloat16*)keys, unit_stride, row_stride, N, (const float*)center,
-                                    key_scale, (const float*)w_enc, (const __nv_bfloat16*)w_bf16,
+                                    key_scale, (const float*)w_enc, (const __half*)w_half,
                                     (const float*)w_norm, (const float*)b_enc, U, F, count, ws, fw, (int*)lens,
                                     (int*)status, st);
     else if (fast && dtype == PK_F32)
         rc = run_encode_select_fast((const float*)keys, unit_stride, row_stride, N, (const float*)center, key_scale,
-                                    (const float*)w_enc, (const __nv_bfloat16*)w_bf16, (const float*)w_norm,
+                                    (const float*)w_enc, (const __half*)w_half, (const float*)w_norm,
                                     (const float*)b_enc, U, F, count, ws, fw, (int*)lens, (int*)status, st);
     else if (dtype == PK_BF16)
         rc = run_encode_select((const __nv_bfloat16*)keys, unit_stride, row_stride, N, (const float*)center, key_scale,
@@ -1293,7 +1346,7 @@ extern "C" size_t pk_append_workspace_bytes(int U, int64_t n_new, int d, int F, 
 }
 
 extern "C" int pk_append_index(uint64_t new_keys, int dtype, int64_t unit_stride, int64_t row_stride, int64_t n_new,
-                               uint64_t center, float key_scale, uint64_t w_enc, uint64_t b_enc, uint64_t w_bf16,
+                               uint64_t center, float key_scale, uint64_t w_enc, uint64_t b_enc, uint64_t w_half,
                                uint64_t w_norm, int U, int d, int F,
                                int key_mean, int64_t history, uint64_t offsets, uint64_t lens, uint64_t ids,
                                int64_t ids_stride, uint64_t mean, uint64_t var, int64_t boundary_capacity,
@@ -1321,15 +1374,15 @@ extern "C" int pk_append_index(uint64_t new_keys, int dtype, int64_t unit_stride
     cudaMemsetAsync(fbase, 0, fast_counters_bytes(U), st);
     const long long count = (long long)n_new * key_mean;
     int rc;
-    const bool fast = w_bf16 && w_norm;
+    const bool fast = w_half && w_norm;
     if (fast && dtype == PK_BF16)
         rc = run_encode_select_fast((const __nv_bfloat16*)new_keys, unit_stride, row_stride, n_new,
                                     (const float*)center, key_scale, (const float*)w_enc,
-                                    (const __nv_bfloat16*)w_bf16, (const float*)w_norm, (const float*)b_enc, U, F,
+                                    (const __half*)w_half, (const float*)w_norm, (const float*)b_enc, U, F,
                                     count, ws, fw, cnt_new, (int*)status, st);
     else if (fast && dtype == PK_F32)
         rc = run_encode_select_fast((const float*)new_keys, unit_stride, row_stride, n_new, (const float*)center,
-                                    key_scale, (const float*)w_enc, (const __nv_bfloat16*)w_bf16,
+                                    key_scale, (const float*)w_enc, (const __half*)w_half,
                                     (const float*)w_norm, (const float*)b_enc, U, F, count, ws, fw, cnt_new,
                                     (int*)status, st);
     else if (dtype == PK_BF16)

@@ -6,6 +6,8 @@
 // query block (G in 2..5: sixteen interleaved FMA chains folded pairwise;
 // G >= 6: one sequential chain), so the activations -- and with them the
 // routed bucket ids -- are bit-identical to the reference's.
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "topk.cuh"
 #include "mma.cuh"
@@ -911,6 +913,22 @@ extern "C" int pk_sae_prepare(uint64_t w_enc, int F, int d, uint64_t w_bf16, uin
     if (d != kEncD) return PK_ERR_UNSUPPORTED;
     sae_prepare_kernel<<<(F + 7) / 8, 256, 0, (cudaStream_t)stream>>>((const float*)w_enc, F, (__nv_bfloat16*)w_bf16,
                                                                       (float*)w_norm);
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}
+
+// W_enc rounded to fp16 (round to nearest) for the build's tensor-core bounds.
+__global__ void sae_half_kernel(const float* __restrict__ W, int64_t n, __half* __restrict__ Wh) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        Wh[i] = __float2half_rn(W[i]);
+}
+
+extern "C" int pk_sae_prepare_half(uint64_t w_enc, int F, int d, uint64_t w_half, uint64_t stream) {
+    if (F < 1 || !w_enc || !w_half) return PK_ERR_ARG;
+    if (d != kEncD) return PK_ERR_UNSUPPORTED;
+    const int64_t n = (int64_t)F * d;
+    sae_half_kernel<<<(unsigned)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096), 256, 0, (cudaStream_t)stream>>>(
+        (const float*)w_enc, n, (__half*)w_half);
     PK_CHECK_LAUNCH();
     return PK_OK;
 }

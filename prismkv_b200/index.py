@@ -56,6 +56,16 @@ class SAEParams:
             cached = self._prep = (wb, wn)
         return cached
 
+    def prepared_half(self):
+        """(W_half[F, d], w_norm[F]) for the bound-filtered build and append:
+        W_enc rounded to fp16 on the device (pk_sae_prepare_half)."""
+        cached = getattr(self, "_prep_half", None)
+        if cached is None or cached[0].device != self.W_enc.device:
+            wh = torch.empty(self.W_enc.shape, dtype=torch.float16, device=self.W_enc.device)
+            nv.call("pk_sae_prepare_half", self.W_enc, self.features, self.head_dim, wh)
+            cached = self._prep_half = (wh, self.prepared()[1])
+        return cached
+
     @classmethod
     def of(cls, sae, device=None) -> "SAEParams":
         """Accepts an SAEParams or any object with the reference SharedSAE's
@@ -134,7 +144,7 @@ class DeviceIndex:
         ws = workspace or nv.Workspace(keys.device)
         status = torch.zeros(1, dtype=torch.int32, device=keys.device)
         bcap = boundary_capacity or (4 * N * sae.key_mean + 65536)
-        wb, wn = (None, None) if exact else sae.prepared()
+        wb, wn = (None, None) if exact else sae.prepared_half()
         for _ in range(6):
             nbytes = nv.query("pk_build_workspace_bytes", U, N, F, sae.key_mean, bcap)
             buf = ws.get(("build", U, N, F, bcap), nbytes)
@@ -168,7 +178,7 @@ class DeviceIndex:
         status = torch.zeros(1, dtype=torch.int32, device=new_keys.device)
         bcap = 4 * n * sae.key_mean + 65536
         dt = nv.dtype_code(new_keys)
-        wb, wn = sae.prepared()
+        wb, wn = sae.prepared_half()
         for _ in range(8):
             nbytes = nv.query("pk_append_workspace_bytes", U, n, d, self.F, sae.key_mean, bcap)
             buf = ws.get(("append", U, n, self.F, bcap), nbytes)

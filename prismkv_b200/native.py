@@ -38,6 +38,7 @@ SIGNATURES = {
     "pk_route_qact_workspace_bytes": ("iiii", ctypes.c_size_t),
     "pk_route_qact": ("PiPiPPPPfPiiiiiPPPPiPPP", ctypes.c_int),
     "pk_sae_prepare": ("PiiPPP", ctypes.c_int),
+    "pk_sae_prepare_half": ("PiiPP", ctypes.c_int),
     "pk_route_moments_workspace_bytes": ("iii", ctypes.c_size_t),
     "pk_route_moments": ("PiPPPiiiiiiPPPPPiP", ctypes.c_int),
     "pk_union": ("PPPlPPiPPiiiPlPPPPPP", ctypes.c_int),

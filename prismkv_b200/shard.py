@@ -75,10 +75,14 @@ def shard_index(index: DeviceIndex, lo: int, hi: int) -> DeviceIndex:
 
 def gather_partials(part: torch.Tensor, out: torch.Tensor, group=None) -> torch.Tensor:
     """All-gather of every rank's [U*G, d+2] partial into out[P, U*G, d+2]
-    (rank order).  NCCL gathers into the flat buffer; gloo (CPU) by list."""
-    P = dist.get_world_size(group)
+    (rank order).  NCCL gathers into the flat buffer; gloo (CPU) by list.
+    Without a process group there is one shard and nothing to exchange."""
+    P = dist.get_world_size(group) if dist.is_initialized() else 1
     if out.shape[0] != P or out.shape[1:] != part.shape:
         raise ValueError("out must be [world, *part.shape]")
+    if P == 1:
+        out[0].copy_(part)
+        return out
     if dist.get_backend(group) == "nccl":
         dist.all_gather_into_tensor(out, part, group=group)
     else:
@@ -102,8 +106,9 @@ class ShardedDecode:
                  splits: int | None = None, max_history: int | None = None,
                  workspace: nv.Workspace | None = None):
         self.group = group
-        self.P = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        init = dist.is_initialized()
+        self.P = dist.get_world_size(group) if init else 1
+        self.rank = dist.get_rank(group) if init else 0
         self.budget = budget
         self.op = SparseDecode(local_index, sae, heads_per_unit=heads_per_unit, router="q_activation",
                                query_scale=query_scale, query_topk=query_topk,
