@@ -389,7 +389,7 @@ def run_ours(a):
             traffic = round(tj["dram_bytes_per_algorithmic_byte"] * mean_bytes)
         except (OSError, ValueError, KeyError):
             traffic = None
-    launches_per_step = L * 4  # encode + select + union + attention per layer
+    launches_per_step = L * 4  # approximate encode + select + union + attention per layer
     line = {
         "metric": METRIC,
         "value": round(value, 2),

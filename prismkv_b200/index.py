@@ -237,6 +237,20 @@ class DeviceIndex:
             setattr(c, name, None if t is None else t.clone())
         return c
 
+    def units(self, u0: int, u1: int) -> "DeviceIndex":
+        """Units [u0, u1) as an index over views of this one's tensors (no
+        copy): operators on disjoint unit ranges can run concurrently, for
+        example one per CUDA stream.  Appends must go through the full index."""
+        if not 0 <= u0 < u1 <= self.U:
+            raise ValueError("unit range must lie within [0, U)")
+        c = DeviceIndex.__new__(DeviceIndex)
+        c.__dict__.update(self.__dict__)
+        c.U = u1 - u0
+        for name in ("offsets", "lens", "ids", "center", "mean", "var"):
+            t = getattr(self, name)
+            setattr(c, name, None if t is None else t[u0:u1])
+        return c
+
     def lists(self, u: int = 0) -> list:
         """The reference's FeatureIndex.lists for unit u (int64 tensors)."""
         off = self.offsets[u].long().cpu()

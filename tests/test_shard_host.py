@@ -166,3 +166,17 @@ def test_shard_budget():
     assert shard_budget(None, 4) is None
     assert shard_budget(8192, 8) == 1024
     assert shard_budget(10, 3) == 3
+
+
+def test_unit_views_share_storage():
+    from prismkv_b200.index import from_lists
+    rs = np.random.RandomState(1)
+    lists = random_lists(rs, 4, 16, 300, 6)
+    idx = from_lists(lists, 300, 8, "cpu")
+    sub = idx.units(1, 3)
+    assert sub.U == 2 and sub.history == idx.history
+    assert sub.ids.data_ptr() == idx.ids[1].data_ptr()
+    for u in range(2):
+        assert all(torch.equal(a, b) for a, b in zip(sub.lists(u), idx.lists(u + 1)))
+    with pytest.raises(ValueError):
+        idx.units(2, 2)
