@@ -41,8 +41,9 @@ def parse():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", type=int, choices=[3, 4], default=3,
-                   help="3: Llama-3-8B-shaped 32-layer decode (default); 4: 1M-token sequence-sharded decode")
+    p.add_argument("--config", type=int, choices=[3, 4, 5], default=3,
+                   help="3: Llama-3-8B-shaped 32-layer decode (default); 4: 1M-token sequence-sharded decode; "
+                        "5: prefill bucket build + decode budget sweep")
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--batch", type=int, default=4)
     p.add_argument("--kv-heads", type=int, default=8)
@@ -659,10 +660,110 @@ def run_seqshard(a):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# config 5: prefill bucket build of a 32-layer x 8-KV-head cache, budget sweep
+# ---------------------------------------------------------------------------
+
+def run_build_sweep(a):
+    """Config 5: every layer's keys (B = 8 sequences x 8 KV heads = 64 units,
+    context 65536, bf16) are SAE-encoded (F = 16384, a 128 x 16384 product
+    per key) and bucketed with the global top-8 per key; then one layer
+    decodes with union budgets 512..8192 and its sparse attention is timed
+    per budget.  Build throughput is reported as keys/s and as the tensor
+    work of the encode (2*N*F*d FLOP per unit) per second."""
+    import torch
+    import prismkv_b200 as pk
+    from prismkv_b200 import native as nv
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    L, B, Hkv, G, d = a.layers, 8, 8, 4, 128
+    U = B * Hkv
+    N, F, k, C = 65536, 16384, 32, a.clusters
+    g = torch.Generator(device=dev)
+    ws = nv.Workspace(dev)
+    build_ms = []
+    K = V = centers = idx = sae = None
+    for l in range(L):
+        g.manual_seed(a.seed * 1_000_003 + 500 + l)
+        centers, K, V = gen_layer(torch, dev, g, U, N + 16, d, C)
+        W = torch.randn(F, d, device=dev, generator=g) / math.sqrt(d)
+        sae = pk.SAEParams(W, torch.zeros(F, device=dev), key_mean=8, query_topk=k)
+        sae.prepared_half()
+        if l == 0:   # allocate the build workspace untimed
+            pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=False, workspace=ws)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        idx = pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=False, workspace=ws)
+        e1.record()
+        torch.cuda.synchronize()
+        build_ms.append(e0.elapsed_time(e1))
+        if idx.encode_path != "bounds":
+            raise SystemExit("build fell back to the exact path")
+    total_ms = sum(build_ms)
+    flop = 2.0 * U * N * F * d * L
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    # Decode budget sweep on the last layer.
+    q = gen_queries(torch, dev, g, centers, 1, G)[0].contiguous()
+    sweep = []
+    for budget in (512, 1024, 2048, 4096, 8192):
+        op = pk.SparseDecode(idx, sae, heads_per_unit=G, budget=budget, workspace=nv.Workspace(dev))
+        op.route(q)
+        op.attention(q, K, V)
+        torch.cuda.synchronize()
+        op.check()
+        graph = torch.cuda.CUDAGraph()
+        s_cap = torch.cuda.Stream()
+        s_cap.wait_stream(torch.cuda.current_stream())
+        reps = 20
+        with torch.cuda.stream(s_cap):
+            with torch.cuda.graph(graph, stream=s_cap):
+                for _ in range(reps):
+                    op.attention(q, K, V)
+        torch.cuda.current_stream().wait_stream(s_cap)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        cnt = int(op.count.long().sum().item())
+        byts = (cnt + U * 16) * d * 2 * 2 + 4 * cnt + 2 * U * G * d * 2
+        sweep.append({"budget": budget, "attention_us": round(us, 2), "rows": cnt + U * 16,
+                      "GB_s": round(byts / us / 1e3, 1),
+                      "frac_of_measured_hbm": round(byts / us / 1e3 / peaks.get("hbm_gbs", 6650.0), 4)})
+        del graph
+    line = {
+        "metric": "config5 prefill bucket build keys/s; decode sparse-AV GB/s per budget",
+        "value": round(U * N * L / (total_ms / 1e3), 1), "unit": "keys/s", "n_gpus": 1, "steps": L,
+        "warmup": 1, "ms_per_step": round(total_ms / L, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded clustered keys, iid values, random-init SAE)",
+        "config": {"workload": "config5: 32 layers x 64 units x 65536 keys, F=16384, top-8 per key; budget sweep",
+                   "layers": L, "units_per_layer": U, "context": N, "features": F, "key_mean": 8,
+                   "build_ms_per_layer": [round(x, 2) for x in build_ms[:4]],
+                   "encode_tflops": round(flop / (total_ms / 1e3) / 1e12, 1),
+                   "encode_frac_of_measured_bf16": round(flop / (total_ms / 1e3) / 1e12 /
+                                                         (peaks.get("bf16_tflops", 1590.0)), 4),
+                   "decode_sweep": sweep},
+        "gpu_launches": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
 if __name__ == "__main__":
     args = parse()
     if args.impl == "ours" and args.config == 4:
         run_seqshard(args)
+        sys.exit(0)
+    if args.impl == "ours" and args.config == 5:
+        run_build_sweep(args)
         sys.exit(0)
     if args.impl == "reference":
         run_reference(args)

@@ -16,6 +16,7 @@
 
 #include "common.cuh"
 #include "mma.cuh"
+#include "tc.cuh"
 
 namespace pk {
 
@@ -581,22 +582,21 @@ int run_encode_select(const T* keys, int64_t unit_stride, int64_t row_stride, in
 // PK_STATUS_NEEDS_EXACT (the caller reruns the exact path).
 //
 // Each CTA holds 128 tokens of one unit (x = (k - c) / s, rounded to fp16)
-// and streams every 128-feature tile of W through a double buffer, so a
-// token block's histogram or members are gathered once per CTA.
+// and streams every 256-feature tile of W through a double buffer on the
+// tcgen05 tensor cores (build_tile_tc_kernel), so a token block's histogram
+// and candidates are gathered once per CTA.
 //   MODE 0 (sample): histogram of the positive lower bounds of a strided
 //     sample of token blocks and feature tiles, all 8192 bins; it places a
 //     floor well below the budget threshold.
 //   MODE 1: histograms of the lower and upper bounds at or above the floor
-//     (a 1024-bin window; the top bin collects everything above) and the
-//     counts of positive bounds.
-//     Entries whose upper bound reaches the floor are kept, with their
-//     bounds, for build_classify_kernel (one tensor-core pass in all).
+//     (a 1024-bin window; the top bin collects everything above); entries
+//     whose upper bound reaches the floor are kept, with their bounds, for
+//     build_classify_kernel (one tensor-core pass in all).
 // ---------------------------------------------------------------------------
 
 constexpr int kFBins = 8192;          // bins of the bounds' float bits >> 18
 constexpr int kFShift = 18;
 constexpr int kFWin = 1024;           // histogram window above the floor (32 octaves)
-constexpr int kFThreads = 256;        // 8 warps x 16 tokens, 128 features a tile
 constexpr int kFSampleMargin = 2;     // floor: 2x the sample's share of the budget
 
 struct FastWs {
@@ -604,7 +604,6 @@ struct FastWs {
     int* histU;                 // [U, kFWin] upper bounds from floor_bin up
     int* histS;                 // [U, kFBins] sampled positive lower bounds
     int* floor_bin;             // [U]
-    unsigned long long* pos;    // [U, 2] positive upper / lower bounds
     int* cutL;                  // [U] bin of the count-th largest lower bound (-1: fewer positives)
     int* cutU;                  // [U] same for the upper bound
     int* n_amb;                 // [U]
@@ -612,32 +611,34 @@ struct FastWs {
     long long* amb;             // [U, acap] flat indices to recompute exactly
     float2* cand_hl;            // [U, acap] (U, L) bounds of the entries at or above the floor
     long long* cand_flat;       // [U, acap] their flat indices
+    float2* wstats;             // [ceil(F/256) * 2] (max |W_f|, max b_f) per 128 features
     int64_t acap;
 };
 
 size_t fast_counters_bytes(int U) {
     return 2 * align256((size_t)U * kFWin * 4) + align256((size_t)U * kFBins * 4) + align256((size_t)U * 4) +
-           align256((size_t)U * 16) + 4 * align256((size_t)U * 4);
+           4 * align256((size_t)U * 4);
 }
-size_t fast_bytes(int U, int64_t acap) {
-    return fast_counters_bytes(U) + 2 * align256((size_t)U * acap * 8) + align256((size_t)U * acap * 8);
+size_t fast_bytes(int U, int64_t acap, int F) {
+    return fast_counters_bytes(U) + 2 * align256((size_t)U * acap * 8) + align256((size_t)U * acap * 8) +
+           align256((size_t)((F + 255) / 256) * 2 * sizeof(float2));
 }
 
-FastWs carve_fast(void* base, int U, int64_t acap) {
+FastWs carve_fast(void* base, int U, int64_t acap, int F) {
     FastWs w;
     char* p = (char*)base;
     w.histL = (int*)p; p += align256((size_t)U * kFWin * 4);
     w.histU = (int*)p; p += align256((size_t)U * kFWin * 4);
     w.histS = (int*)p; p += align256((size_t)U * kFBins * 4);
     w.floor_bin = (int*)p; p += align256((size_t)U * 4);
-    w.pos = (unsigned long long*)p; p += align256((size_t)U * 16);
     w.cutL = (int*)p; p += align256((size_t)U * 4);
     w.cutU = (int*)p; p += align256((size_t)U * 4);
     w.n_amb = (int*)p; p += align256((size_t)U * 4);
     w.n_cand = (int*)p; p += align256((size_t)U * 4);
     w.amb = (long long*)p; p += align256((size_t)U * acap * 8);
     w.cand_hl = (float2*)p; p += align256((size_t)U * acap * 8);
-    w.cand_flat = (long long*)p;
+    w.cand_flat = (long long*)p; p += align256((size_t)U * acap * 8);
+    w.wstats = (float2*)p;
     w.acap = acap;
     return w;
 }
@@ -653,63 +654,120 @@ struct TileSample {
     int tb_stride, ft_stride;   // MODE 0: token blocks and feature tiles sampled
 };
 
-// Shared memory bytes per mode.
-__host__ __device__ constexpr int tile_smem(int mode) {
-    return 128 * 256 + 2 * 128 * 256 + 2 * 2 * 128 * 4 + 128 * 4 + 32 * 4 +
-           (mode == 0 ? kFBins * 4 : 2 * kFWin * 4);
+// Per 128 features: the largest |W_f| and b_f, for the epilogue's row
+// tests; W rows out of fp16 range raise PK_STATUS_NEEDS_EXACT.
+__global__ void build_wstats_kernel(const float* __restrict__ wn, const float* __restrict__ bias, int F,
+                                    float2* __restrict__ stats, int* __restrict__ status) {
+    const int blk = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ float sw[4], sb[4];
+    const int f = blk * 128 + tid;
+    const float w = f < F ? wn[f] : 0.f, b = f < F ? bias[f] : -INFINITY;
+    if (w >= 60000.f) atomicOr(status, PK_STATUS_NEEDS_EXACT);
+    const float mw = warp_max(w), mb = warp_max(b);
+    if (lane == 0) { sw[warp] = mw; sb[warp] = mb; }
+    __syncthreads();
+    if (tid == 0) {
+        float a = sw[0], c = sb[0];
+        for (int i = 1; i < 4; ++i) { a = fmaxf(a, sw[i]); c = fmaxf(c, sb[i]); }
+        stats[blk] = make_float2(a, c == -INFINITY ? 0.f : c);
+    }
+}
+
+// The passes run on the 5th-generation tensor cores: one CTA per
+// 128-token block of a unit (one CTA per SM), 256-feature tiles of W_half
+// double-buffered in shared memory (128-byte swizzle, K-major), accumulators
+// double-buffered in TMEM (2 x 256 columns).  Iteration i waits for the MMA
+// of tile i-1, starts the copy of tile i+1 into the buffer that MMA freed,
+// issues the eight K=16 MMAs of tile i from one thread, and runs the epilogue
+// of tile i-1 from TMEM while they execute.  Each thread's epilogue covers
+// one token row and 128 features.
+constexpr int kTcTokens = 128, kTcFeat = 256, kTcThreads = 256;
+constexpr int kTcXBytes = kTcTokens * 256;          // 2 K-atoms x 128 rows x 128 B
+constexpr int kTcWBytes = kTcFeat * 256;            // 2 K-atoms x 256 rows x 128 B
+constexpr uint64_t kTcWaitNs = 200000000ull;        // 0.2 s: an MMA never takes this long
+
+__host__ __device__ constexpr int tc_smem(int mode) {
+    return 1024 /* alignment slack */ + kTcXBytes + 2 * kTcWBytes + 3 * 2 * kTcFeat * 4 + 6 * 8 + kTcTokens * 4 +
+           (mode == 0 ? kFBins * 4 : 2 * kFWin * 4) + 64;
 }
 
 template <int MODE, typename T>
-__global__ void __launch_bounds__(kFThreads, 2)
-build_tile_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride, int64_t N,
-                  const float* __restrict__ center, float key_scale, const __half* __restrict__ Wh,
-                  const float* __restrict__ bias, const float* __restrict__ wn, int F, BuildWs ws, FastWs fw,
-                  TileSample smp, int* __restrict__ lens, int* __restrict__ status) {
-    extern __shared__ __align__(128) uint8_t fsm[];
-    uint8_t* Xs = fsm;                                            // [128 rows][256 B] swizzled
-    uint8_t* Wt = fsm + 128 * 256;                                // [2][128 rows][256 B] swizzled
-    float* wnt = reinterpret_cast<float*>(fsm + 3 * 128 * 256);   // [2][128]
-    float* bt = wnt + 2 * 128;                                    // [2][128]
-    float* xn = bt + 2 * 128;                                     // [128]
-    float* wmax = xn + 128;                                       // [2] per tile max of |W_f|
-    int* hA = reinterpret_cast<int*>(wmax + 32);                  // MODE 0: [kFBins]; MODE 1: L [kFWin]
-    int* hB = hA + kFWin;                                         // MODE 1: U [kFWin]
+__global__ void __launch_bounds__(kTcThreads, 1)
+build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride, int64_t N,
+                     const float* __restrict__ center, float key_scale, const __half* __restrict__ Wh,
+                     const float* __restrict__ bias, const float* __restrict__ wn, int F, FastWs fw, TileSample smp,
+                     int* __restrict__ status) {
+    extern __shared__ uint8_t tc_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* Xs = base;
+    uint8_t* Wt = base + kTcXBytes;                                           // [2][kTcWBytes]
+    float* wnt = reinterpret_cast<float*>(Wt + 2 * kTcWBytes);               // [3][256]
+    float* bt = wnt + 3 * kTcFeat;                                           // [3][256]
+    float2* wst = reinterpret_cast<float2*>(bt + 3 * kTcFeat);              // [3][2] (max |W_f|, max b_f) per half
+    float* xn = reinterpret_cast<float*>(wst + 6);                           // [128]
+    int* hA = reinterpret_cast<int*>(xn + kTcTokens);                        // MODE 0: [kFBins]; MODE 1: L [kFWin]
+    int* hB = hA + kFWin;                                                    // MODE 1: U [kFWin]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(hA + (MODE == 0 ? kFBins : 2 * kFWin));   // [2]
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int u = blockIdx.y;
-    const int64_t t0 = (int64_t)blockIdx.x * (MODE == 0 ? smp.tb_stride : 1) * 128;
+    const int64_t t0 = (int64_t)blockIdx.x * (MODE == 0 ? smp.tb_stride : 1) * kTcTokens;
     const float* cu = center + (int64_t)u * kBD;
-    const int nft = (F + 127) / 128;
+    const int ntf = (F + kTcFeat - 1) / kTcFeat;
     const int fstep = MODE == 0 ? smp.ft_stride : 1;
+    const int ft_first = MODE == 0 ? (int)(blockIdx.x % fstep) : 0;
+    const int ntiles = ft_first < ntf ? (ntf - ft_first + fstep - 1) / fstep : 0;
 
-    auto load_w = [&](int ft, int buf) {
-        const int f0 = ft * 128;
-        uint8_t* dst = Wt + buf * 128 * 256;
-        for (int c = tid; c < 128 * 16; c += kFThreads) {
+    if (warp == 0) tmem_alloc(smem_addr(tslot), 512);
+    if (tid == 0) {
+        mbar_init(smem_addr(&bars[0]), 1);
+        mbar_init(smem_addr(&bars[1]), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // Tile j of this CTA: W rows into buffer j & 1, norms and biases into j % 3.
+    auto load_w = [&](int j) {
+        const int f0 = (ft_first + j * fstep) * kTcFeat;
+        uint8_t* dst = Wt + (j & 1) * kTcWBytes;
+        for (int c = tid; c < kTcFeat * 16; c += kTcThreads) {
             const int row = c >> 4, ch = c & 15;
             const int f = f0 + row;
             const bool valid = f < F;
-            cp_async_16(smem_addr(dst) + swz(row, ch), Wh + (int64_t)(valid ? f : 0) * kBD + ch * 8, valid);
+            cp_async_16(smem_addr(dst) + (ch >> 3) * (kTcFeat * 128) + sw128_off(row, ch & 7),
+                        Wh + (int64_t)(valid ? f : 0) * kBD + ch * 8, valid);
         }
+        // Norms and biases (16-byte chunks of 4 features, zero past F) and
+        // the two halves' maxima, all asynchronous.
         if (tid < 128) {
-            const int f = f0 + tid;
-            const float w = f < F ? wn[f] : 0.f;
-            if (w >= 60000.f) atomicOr(status, PK_STATUS_NEEDS_EXACT);
-            wnt[buf * 128 + tid] = w;
-            bt[buf * 128 + tid] = f < F ? bias[f] : 0.f;
-            const float m = warp_max(w);
-            if (lane == 0) wmax[buf * 16 + warp] = m;
+            const bool isb = tid >= 64;
+            const int q = tid & 63, f = f0 + 4 * q;
+            const int nbytes = f >= F ? 0 : (F - f >= 4 ? 16 : 4 * (F - f));
+            const float* src = (isb ? bias : wn) + (nbytes ? f : 0);
+            float* dsts = (isb ? bt : wnt) + (j % 3) * kTcFeat + 4 * q;
+            cp_async_16n(smem_addr(dsts), src, nbytes);
+        } else if (tid == 128) {
+            cp_async_16n(smem_addr(wst + (j % 3) * 2), fw.wstats + f0 / 128, 16);
         }
     };
-    const int ft_first = MODE == 0 ? (int)(blockIdx.x % fstep) : 0;
-    load_w(ft_first, 0);
+    if (ntiles > 0) load_w(0);
     cp_async_commit_group();
     if (MODE == 0)
-        for (int i = tid; i < kFBins; i += kFThreads) hA[i] = 0;
-    if (MODE == 1)
-        for (int i = tid; i < 2 * kFWin; i += kFThreads) hA[i] = 0;
-    // x = (k - center) / key_scale in fp32 (core.py:99), rounded to fp16 for
-    // the tensor cores; the row norm bound uses the fp32 values.
+        for (int i = tid; i < kFBins; i += kTcThreads) hA[i] = 0;
+    else
+        for (int i = tid; i < 2 * kFWin; i += kTcThreads) hA[i] = 0;
+    // x = (k - center) / key_scale in fp32 (core.py:99), rounded to fp16.
     const bool unit_scale = key_scale == 1.0f;
+    // This warp's 16 key rows, every load issued before any is used.
+    float kr[16][4];
+#pragma unroll
+    for (int rr = 0; rr < 16; ++rr) {
+        const int64_t t = t0 + warp * 16 + rr;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) kr[rr][e] = t < N ? key_at(keys, unit_stride, row_stride, u, t, 4 * lane + e) : 0.f;
+    }
+    float cl[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) cl[e] = cu[4 * lane + e];
+#pragma unroll
     for (int rr = 0; rr < 16; ++rr) {
         const int row = warp * 16 + rr;
         const int64_t t = t0 + row;
@@ -717,9 +775,7 @@ build_tile_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_s
         if (t < N) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const int c = 4 * lane + e;
-                const float k = key_at(keys, unit_stride, row_stride, u, t, c);
-                const float dlt = __fsub_rn(k, cu[c]);
+                const float dlt = __fsub_rn(kr[rr][e], cl[e]);
                 x[e] = unit_scale ? dlt : __fdiv_rn(dlt, key_scale);
             }
         }
@@ -734,109 +790,104 @@ build_tile_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_s
         uint2 pk2;
         pk2.x = *reinterpret_cast<uint32_t*>(&p0);
         pk2.y = *reinterpret_cast<uint32_t*>(&p1);
-        *reinterpret_cast<uint2*>(Xs + swz(row, lane >> 1) + (lane & 1) * 8) = pk2;
+        const int chunk = lane >> 1;   // 16-byte chunk of the 256-byte row
+        *reinterpret_cast<uint2*>(Xs + (chunk >> 3) * (kTcTokens * 128) + sw128_off(row, chunk & 7) + (lane & 1) * 8) =
+            pk2;
     }
+    cp_async_wait_group<0>();
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
     const int floor_bin = MODE == 1 ? fw.floor_bin[u] : 0;
-    unsigned long long posU = 0, posL = 0;
-    const int mi = lane >> 3, r8 = lane & 7;
+    const uint32_t idesc = f16_idesc(128, kTcFeat, 0);
+    const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+    const int64_t trow_t = t0 + row;
+    const bool trow = trow_t < N;
+    bool ok = true;
 
-    int buf = 0;
-    for (int ft = ft_first; ft < nft; ft += fstep, buf ^= 1) {
-        const int ftn = ft + fstep;
-        if (ftn < nft) load_w(ftn, buf ^ 1);
-        cp_async_commit_group();
-        cp_async_wait_group<1>();
-        __syncthreads();
-        const uint8_t* W = Wt + buf * 128 * 256;
-        const float* wnb = wnt + buf * 128;
-        const float* bb = bt + buf * 128;
-        float acc[16][4];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-            uint32_t a[4];
-            ldsm_x4(smem_addr(Xs) + swz(warp * 16 + (mi & 1) * 8 + r8, 2 * kk + (mi >> 1)), a);
-#pragma unroll
-            for (int np = 0; np < 8; ++np) {
-                uint32_t b[4];
-                ldsm_x4(smem_addr(W) + swz(np * 16 + (mi >> 1) * 8 + r8, 2 * kk + (mi & 1)), b);
-                mma_16816_f16(acc[2 * np], a, b[0], b[1]);
-                mma_16816_f16(acc[2 * np + 1], a, b[2], b[3]);
+    for (int i = 0; i <= ntiles; ++i) {
+        if (i >= 1) {
+            const bool done = mbar_wait(smem_addr(&bars[(i - 1) & 1]), ((i - 1) >> 1) & 1, kTcWaitNs);
+            if (__syncthreads_or(!done)) {
+                ok = false;
+                break;
             }
+            tc_fence_after();
         }
-        const int f0 = ft * 128;
-        const float wm = fmaxf(fmaxf(wmax[buf * 16 + 0], wmax[buf * 16 + 1]), fmaxf(wmax[buf * 16 + 2], wmax[buf * 16 + 3]));
+        if (i < ntiles && tid == 0) {
+            tc_fence_after();
+            const uint32_t xa = smem_addr(Xs), wa = smem_addr(Wt + (i & 1) * kTcWBytes);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-            const int row = warp * 16 + (lane >> 2) + half * 8;
-            const int64_t t = t0 + row;
-            const bool trow = t < N;
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t koff = (uint32_t)((kk & 3) * 32);   // K=16 step inside the 128-byte atom
+                umma_f16(tmem + (i & 1) * kTcFeat, sw128_desc(xa + (kk >> 2) * (kTcTokens * 128) + koff),
+                         sw128_desc(wa + (kk >> 2) * (kTcFeat * 128) + koff), idesc, kk > 0 ? 1u : 0u);
+            }
+            umma_commit(smem_addr(&bars[i & 1]));
+        }
+        if (i + 1 < ntiles) load_w(i + 1);
+        cp_async_commit_group();
+        if (i >= 1) {
+            // Epilogue of tile i-1: this thread's token row, 128 features.
+            const int j = i - 1;
+            const int f0 = (ft_first + j * fstep) * kTcFeat + half * 128;
+            const float* wnb = wnt + (j % 3) * kTcFeat + half * 128;
+            const float* bb = bt + (j % 3) * kTcFeat + half * 128;
+            const float2 st2 = wst[(j % 3) * 2 + half];
+            const float wm = st2.x, bm = st2.y;
             const float cx = 0.001953125f * xn[row];
             const float cs = 4.76837158203125e-07f * (xn[row] + wm);
-            // |err| <= E + 2^-20 |v| for every feature of the tile; the row
-            // tests below use E with the relative term folded in.
             const float E = cx * wm * (1.0f + 1.0f / 65536.0f) + cs;
             auto err_of = [&](int col, float v) { return fmaf(cx, wnb[col], cs + 9.5367431640625e-07f * fabsf(v)); };
-            if (MODE == 0) {
+            const float fval = __uint_as_float((uint32_t)floor_bin << kFShift);
+            // MODE 1 keeps v = acc + b_f >= vfloor (U can reach the floor);
+            // MODE 0 bins positive v.  Either needs acc >= tau: one compare
+            // per entry, the full bound work only for the entries it keeps.
+            const float vfloor = fval - 1.001f * E - 3.814697265625e-06f * (fval + E);
+            const float tau = (MODE == 0 ? 0.f : vfloor) - bm;
+            const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((j & 1) * kTcFeat + half * 128);
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                float v[32];
+                tmem_ld32(taddr + c * 32, v);
+                tmem_wait_ld();
+                uint32_t m = 0;
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
+                for (int q = 0; q < 32; ++q) m |= (v[q] >= tau ? 1u : 0u) << q;
+                const int cols_left = F - (f0 + c * 32);
+                if (!trow || cols_left <= 0) m = 0;
+                else if (cols_left < 32) m &= (1u << cols_left) - 1u;
+                if (MODE == 0) {
+                    if (!__any_sync(0xffffffffu, m != 0)) continue;
 #pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const int col = 8 * j + 2 * (lane & 3) + e;
-                        const float v = acc[j][2 * half + e] + bb[col];
-                        if (!trow || f0 + col >= F || !(v > 0.f)) continue;
-                        const float lo = v - err_of(col, v);
+                    for (int q = 0; q < 32; ++q) {
+                        if (!(m & (1u << q))) continue;
+                        const int col = c * 32 + q;
+                        const float vv = v[q] + bb[col];
+                        if (!(vv > 0.f)) continue;
+                        const float lo = vv - err_of(col, vv);
                         if (lo > 0.f) atomicAdd(&hA[fbin(lo)], 1);
                     }
-            } else if (MODE == 1) {
-                // Bounds at or above the floor value are binned and the
-                // entry, with its bounds, is kept as a candidate (an entry
-                // whose U is below the floor cannot reach the threshold);
-                // positives are counted, exactly only where |v| is within
-                // the error.
-                // v below vfloor => U below the floor value: U <= v + E +
-                // 2^-20|v|, and |v| <= 4(fval + E) there or U is negative.
-                const float fval = __uint_as_float((uint32_t)floor_bin << kFShift);
-                const float vfloor = fval - 1.001f * E - 3.814697265625e-06f * (fval + E);
-                int nk = 0;
+                } else {
+                    // Slots for every kept entry, one atomic per warp;
+                    // entries whose exact U misses the floor get U = -1.
+                    const int nk = __popc(m);
+                    const int inc = warp_inclusive_scan(nk);
+                    const int wtot = __shfl_sync(0xffffffffu, inc, 31);
+                    if (wtot == 0) continue;
+                    int cbase = 0;
+                    if (lane == 31) cbase = atomicAdd(&fw.n_cand[u], wtot);
+                    cbase = __shfl_sync(0xffffffffu, cbase, 31) + inc - nk;
+                    if (nk == 0) continue;
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const int col = 8 * j + 2 * (lane & 3) + e;
-                        const float v = acc[j][2 * half + e] + bb[col];
-                        if (!trow || f0 + col >= F) continue;
-                        if (v > 2.f * E) {
-                            ++posU;
-                            ++posL;
-                        } else if (v >= -2.f * E) {
-                            const float err = err_of(col, v);
-                            posU += (v + err > 0.f) ? 1 : 0;
-                            posL += (v - err > 0.f) ? 1 : 0;
-                        }
-                        nk += v >= vfloor ? 1 : 0;
-                    }
-                // Slots for every entry past the row test, reserved with one
-                // atomic per warp; entries whose exact U misses the floor are
-                // written with U = -1, which classification drops.
-                const int inc = warp_inclusive_scan(nk);
-                const int wtot = __shfl_sync(0xffffffffu, inc, 31);
-                if (wtot == 0) continue;
-                int base = 0;
-                if (lane == 31) base = atomicAdd(&fw.n_cand[u], wtot);
-                base = __shfl_sync(0xffffffffu, base, 31) + inc - nk;
-                if (nk == 0) continue;
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const int col = 8 * j + 2 * (lane & 3) + e;
-                        const int f = f0 + col;
-                        const float v = acc[j][2 * half + e] + bb[col];
-                        if (!trow || f >= F || !(v >= vfloor)) continue;
-                        const float err = err_of(col, v);
-                        const float lo = v - err, hi = v + err;
+                    for (int q = 0; q < 32; ++q) {
+                        if (!(m & (1u << q))) continue;
+                        const int col = c * 32 + q;
+                        const float vv = v[q] + bb[col];
+                        const float err = err_of(col, vv);
+                        const float lo = vv - err, hi = vv + err;
                         bool keep = false;
                         if (hi > 0.f) {
                             const int bh = fbin(hi) - floor_bin;
@@ -849,34 +900,37 @@ build_tile_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_s
                             const int bl = fbin(lo) - floor_bin;
                             if (bl >= 0) atomicAdd(&hA[min(bl, kFWin - 1)], 1);
                         }
-                        if (base < fw.acap) {
-                            fw.cand_hl[(int64_t)u * fw.acap + base] = make_float2(keep ? hi : -1.f, lo);
-                            fw.cand_flat[(int64_t)u * fw.acap + base] = t * F + f;
+                        if (cbase < fw.acap) {
+                            fw.cand_hl[(int64_t)u * fw.acap + cbase] = make_float2(keep ? hi : -1.f, lo);
+                            fw.cand_flat[(int64_t)u * fw.acap + cbase] = trow_t * F + f0 + col;
                         } else {
                             atomicOr(status, PK_STATUS_BOUNDARY_FULL);
                         }
-                        ++base;
+                        ++cbase;
                     }
+                }
             }
         }
-        __syncthreads();   // the buffer is refilled two tiles on
+        tc_fence_before();
+        cp_async_wait_group<0>();
+        fence_async_smem();
+        __syncthreads();
     }
+    // An MMA that did not complete in time: the caller reruns the exact path.
+    if (!ok && tid == 0) atomicOr(status, PK_STATUS_NEEDS_EXACT);
     cp_async_wait_group<0>();
     if (MODE == 0) {
-        for (int i = tid; i < kFBins; i += kFThreads)
+        for (int i = tid; i < kFBins; i += kTcThreads)
             if (hA[i]) atomicAdd(&fw.histS[(int64_t)u * kFBins + i], hA[i]);
-    } else if (MODE == 1) {
-        posU = warp_sum(posU);
-        posL = warp_sum(posL);
-        if (lane == 0) {
-            atomicAdd(&fw.pos[2 * u], posU);
-            atomicAdd(&fw.pos[2 * u + 1], posL);
-        }
-        for (int i = tid; i < kFWin; i += kFThreads) {
+    } else {
+        for (int i = tid; i < kFWin; i += kTcThreads) {
             if (hA[i]) atomicAdd(&fw.histL[(int64_t)u * kFWin + i], hA[i]);
             if (hB[i]) atomicAdd(&fw.histU[(int64_t)u * kFWin + i], hB[i]);
         }
     }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
 // Per unit: the floor bin.  Scanning the sample's upper-bound histogram from
@@ -901,10 +955,11 @@ __global__ void build_floor_kernel(FastWs fw, long long count, double sample_fra
 }
 
 // Per unit: the bins holding the count-th largest lower / upper bound,
-// inside the window above the floor.  When fewer than `count` bounds reach
-// the floor: if fewer are positive at all, every positive counts (cut -1);
-// otherwise the floor was too high and the exact path is needed.  A cut in
-// the window's top bin (which merges everything above) is unusable too.
+// inside the window above the floor.  Fewer than `count` bounds at or above
+// the floor (a floor placed too high, or fewer positive activations than the
+// budget -- core.py:23's all-positives case), or a cut in the window's top
+// bin (which merges everything above), leave the threshold unbracketed: the
+// exact path runs instead.
 __global__ void build_fast_cut_kernel(FastWs fw, long long count, int* __restrict__ status) {
     const int u = blockIdx.x;
     if (threadIdx.x != 0) return;
@@ -912,25 +967,16 @@ __global__ void build_fast_cut_kernel(FastWs fw, long long count, int* __restric
     bool bad = false;
     for (int which = 0; which < 2; ++which) {
         const int* h = (which ? fw.histU : fw.histL) + (int64_t)u * kFWin;
-        const unsigned long long npos = fw.pos[2 * u + (which ? 0 : 1)];
         long long above = 0;
         int b = kFWin - 1;
         for (; b >= 0; --b) {
             if (above + h[b] >= count) break;
             above += h[b];
         }
-        int cut;
-        if (b >= 0) {
-            cut = fb + b;
-            if (b == kFWin - 1) bad = true;
-        } else {
-            cut = -1;
-            if ((long long)npos >= count) bad = true;
-        }
-        (which ? fw.cutU : fw.cutL)[u] = cut;
+        if (b < 0 || b == kFWin - 1) bad = true;
+        (which ? fw.cutU : fw.cutL)[u] = fb + b;
     }
-    if (bad || (fw.cutL[u] < 0 && fw.cutU[u] >= 0)) {
-        // The exact path runs instead: classify nothing.
+    if (bad) {
         atomicOr(status, PK_STATUS_NEEDS_EXACT);
         fw.cutL[u] = INT32_MAX;
         fw.cutU[u] = INT32_MAX;
@@ -1173,7 +1219,7 @@ int run_encode_select_fast(const T* keys, int64_t unit_stride, int64_t row_strid
                            const float* b, int U, int F, long long count, BuildWs ws, FastWs fw, int* lens,
                            int* status, cudaStream_t st) {
     const int nblocks = (int)((N + 127) / 128);
-    const int nft = (F + 127) / 128;
+    const int nft = (F + kTcFeat - 1) / kTcFeat;
     // Floor sample: about 64 token blocks, a quarter of the feature tiles.
     TileSample smp;
     smp.tb_stride = nblocks > 64 ? nblocks / 64 : 1;
@@ -1181,15 +1227,17 @@ int run_encode_select_fast(const T* keys, int64_t unit_stride, int64_t row_strid
     const int nsample = (nblocks + smp.tb_stride - 1) / smp.tb_stride;
     const double frac = fmin(1.0, (double)nsample * 128.0 / (double)N) / (double)smp.ft_stride;
     const TileSample none = {1, 1};
-    cudaFuncSetAttribute(build_tile_kernel<0, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tile_smem(0));
-    cudaFuncSetAttribute(build_tile_kernel<1, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tile_smem(1));
-    build_tile_kernel<0, T><<<dim3(nsample, U), kFThreads, tile_smem(0), st>>>(
-        keys, unit_stride, row_stride, N, center, key_scale, Wh, b, wn, F, ws, fw, smp, lens, status);
+    build_wstats_kernel<<<(F + 255) / 256 * 2, 128, 0, st>>>(wn, b, F, fw.wstats, status);
+    PK_CHECK_LAUNCH();
+    cudaFuncSetAttribute(build_tile_tc_kernel<0, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(0));
+    cudaFuncSetAttribute(build_tile_tc_kernel<1, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(1));
+    build_tile_tc_kernel<0, T><<<dim3(nsample, U), kTcThreads, tc_smem(0), st>>>(
+        keys, unit_stride, row_stride, N, center, key_scale, Wh, b, wn, F, fw, smp, status);
     PK_CHECK_LAUNCH();
     build_floor_kernel<<<U, 32, 0, st>>>(fw, count, frac);
     PK_CHECK_LAUNCH();
-    build_tile_kernel<1, T><<<dim3(nblocks, U), kFThreads, tile_smem(1), st>>>(
-        keys, unit_stride, row_stride, N, center, key_scale, Wh, b, wn, F, ws, fw, none, lens, status);
+    build_tile_tc_kernel<1, T><<<dim3(nblocks, U), kTcThreads, tc_smem(1), st>>>(
+        keys, unit_stride, row_stride, N, center, key_scale, Wh, b, wn, F, fw, none, status);
     PK_CHECK_LAUNCH();
     build_fast_cut_kernel<<<U, 32, 0, st>>>(fw, count, status);
     PK_CHECK_LAUNCH();
@@ -1258,7 +1306,7 @@ extern "C" int64_t pk_build_ids_capacity(int64_t N, int F, int key_mean, float s
 extern "C" size_t pk_build_workspace_bytes(int U, int64_t N, int F, int key_mean, int64_t boundary_capacity) {
     const int64_t mcap = N * (int64_t)key_mean;
     const int64_t bcap = boundary_capacity > 0 ? boundary_capacity : 1;
-    return carve_bytes(U, F, mcap > 0 ? mcap : 1, bcap) + fast_bytes(U, bcap);
+    return carve_bytes(U, F, mcap > 0 ? mcap : 1, bcap) + fast_bytes(U, bcap, F);
 }
 
 extern "C" int pk_build_index(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride, uint64_t center,
@@ -1280,13 +1328,14 @@ extern "C" int pk_build_index(uint64_t keys, int dtype, int64_t unit_stride, int
     const int64_t mcap = N * (int64_t)key_mean;
     BuildWs ws = carve((void*)workspace, U, F, mcap, boundary_capacity);
     void* fbase = (char*)workspace + carve_bytes(U, F, mcap, boundary_capacity);
-    FastWs fw = carve_fast(fbase, U, boundary_capacity);
+    FastWs fw = carve_fast(fbase, U, boundary_capacity, F);
     cudaMemsetAsync((void*)workspace, 0, counters_bytes(U, F), st);
     cudaMemsetAsync(fbase, 0, fast_counters_bytes(U), st);
     cudaMemsetAsync((void*)lens, 0, (size_t)U * F * sizeof(int), st);
     const long long count = (long long)N * key_mean;
     int rc;
     const bool fast = w_half && w_norm;
+    if (fast && ((w_norm | b_enc | w_half) % 16)) return PK_ERR_ARG;   // 16-byte tile copies
     if (fast && dtype == PK_BF16)
         rc = run_encode_select_fast((const __nv_bfloat16*)keys, unit_stride, row_stride, N, (const float*)center,
                                     key_scale, (const float*)w_enc, (const __half*)w_half,
@@ -1340,7 +1389,7 @@ extern "C" size_t pk_append_workspace_bytes(int U, int64_t n_new, int d, int F, 
                                             int64_t boundary_capacity) {
     const int64_t mcap = n_new * (int64_t)key_mean;
     const int64_t bcap = boundary_capacity > 0 ? boundary_capacity : 1;
-    const size_t base = carve_bytes(U, F, mcap > 0 ? mcap : 1, bcap) + fast_bytes(U, bcap);
+    const size_t base = carve_bytes(U, F, mcap > 0 ? mcap : 1, bcap) + fast_bytes(U, bcap, F);
     // + new-block counts [U, F] + new-block moments [2, U, F, d]
     return base + align256((size_t)U * F * 4) + 2 * align256((size_t)U * F * d * 4);
 }
@@ -1364,8 +1413,8 @@ extern "C" int pk_append_index(uint64_t new_keys, int dtype, int64_t unit_stride
     const int64_t mcap = n_new * (int64_t)key_mean;
     BuildWs ws = carve((void*)workspace, U, F, mcap, boundary_capacity);
     void* fbase = (char*)workspace + carve_bytes(U, F, mcap, boundary_capacity);
-    FastWs fw = carve_fast(fbase, U, boundary_capacity);
-    char* extra = (char*)fbase + fast_bytes(U, boundary_capacity);
+    FastWs fw = carve_fast(fbase, U, boundary_capacity, F);
+    char* extra = (char*)fbase + fast_bytes(U, boundary_capacity, F);
     int* cnt_new = (int*)extra;
     float* mean_new = (float*)(extra + align256((size_t)U * F * 4));
     float* var_new = (float*)(extra + align256((size_t)U * F * 4) + align256((size_t)U * F * d * 4));
@@ -1375,6 +1424,7 @@ extern "C" int pk_append_index(uint64_t new_keys, int dtype, int64_t unit_stride
     const long long count = (long long)n_new * key_mean;
     int rc;
     const bool fast = w_half && w_norm;
+    if (fast && ((w_norm | b_enc | w_half) % 16)) return PK_ERR_ARG;   // 16-byte tile copies
     if (fast && dtype == PK_BF16)
         rc = run_encode_select_fast((const __nv_bfloat16*)new_keys, unit_stride, row_stride, n_new,
                                     (const float*)center, key_scale, (const float*)w_enc,

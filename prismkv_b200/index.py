@@ -106,6 +106,7 @@ class DeviceIndex:
         self.history = 0
         self.slack_frac = 0.0
         self.slack_min = 0
+        self.encode_path = None   # "bounds" (tensor-core bounds) or "exact", set by build
 
     # ------------------------------------------------------------------ build
     @classmethod
@@ -161,6 +162,7 @@ class DeviceIndex:
                 wb, wn = None, None
                 continue
             nv.check_status(status, "build_index")
+            self.encode_path = "bounds" if wb is not None else "exact"
             return
         nv.check_status(status, "build_index")
 

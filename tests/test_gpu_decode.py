@@ -311,6 +311,8 @@ def test_bound_filtered_build_equals_exact_build(pk, dtype):
     sae = pk.SAEParams(W, b, key_mean=8, query_topk=16)
     fast = pk.DeviceIndex.build(keys, sae, 1.3, moments=False)
     exact = pk.DeviceIndex.build(keys, sae, 1.3, moments=False, exact=True)
+    # The tensor-core bounds decided (no fallback to the exact path).
+    assert fast.encode_path == "bounds" and exact.encode_path == "exact"
     assert torch.equal(fast.center, exact.center)
     for u in range(U):
         cf, idf = fast.csr(u)
