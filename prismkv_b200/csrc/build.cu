@@ -611,7 +611,8 @@ struct FastWs {
     long long* amb;             // [U, acap] flat indices to recompute exactly
     float2* cand_hl;            // [U, acap] (U, L) bounds of the entries at or above the floor
     long long* cand_flat;       // [U, acap] their flat indices
-    float2* wstats;             // [ceil(F/256) * 2] (max |W_f|, max b_f) per 128 features
+    uint8_t* tiles;             // [ceil(F/256)] W_half tile images (64 KB each)
+    uint8_t* sides;             // [ceil(F/256)] side records (norms, biases, maxima)
     int64_t acap;
 };
 
@@ -620,8 +621,9 @@ size_t fast_counters_bytes(int U) {
            4 * align256((size_t)U * 4);
 }
 size_t fast_bytes(int U, int64_t acap, int F) {
+    const size_t ntf = (size_t)((F + 255) / 256);
     return fast_counters_bytes(U) + 2 * align256((size_t)U * acap * 8) + align256((size_t)U * acap * 8) +
-           align256((size_t)((F + 255) / 256) * 2 * sizeof(float2));
+           align256(ntf * 256 * 256) + align256(ntf * (2 * 256 * 4 + 16));
 }
 
 FastWs carve_fast(void* base, int U, int64_t acap, int F) {
@@ -638,7 +640,9 @@ FastWs carve_fast(void* base, int U, int64_t acap, int F) {
     w.amb = (long long*)p; p += align256((size_t)U * acap * 8);
     w.cand_hl = (float2*)p; p += align256((size_t)U * acap * 8);
     w.cand_flat = (long long*)p; p += align256((size_t)U * acap * 8);
-    w.wstats = (float2*)p;
+    const size_t ntf = (size_t)((F + 255) / 256);
+    w.tiles = (uint8_t*)p; p += align256(ntf * 256 * 256);
+    w.sides = (uint8_t*)p;
     w.acap = acap;
     return w;
 }
@@ -650,65 +654,122 @@ __device__ __forceinline__ unsigned lane_below() {
     return m;
 }
 
+// v[base + q] for a run-time q in [0, 32): a select tree over the bits of q,
+// so that the array stays in registers (no local-memory indexing).
+template <int N>
+__device__ __forceinline__ float pick32(const float (&v)[N], int base, int q) {
+    float a[16], b[8], c[4], e[2];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) a[i] = (q & 1) ? v[base + 2 * i + 1] : v[base + 2 * i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b[i] = (q & 2) ? a[2 * i + 1] : a[2 * i];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) c[i] = (q & 4) ? b[2 * i + 1] : b[2 * i];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) e[i] = (q & 8) ? c[2 * i + 1] : c[2 * i];
+    return (q & 16) ? e[1] : e[0];
+}
+
 struct TileSample {
     int tb_stride, ft_stride;   // MODE 0: token blocks and feature tiles sampled
 };
 
-// Per 128 features: the largest |W_f| and b_f, for the epilogue's row
-// tests; W rows out of fp16 range raise PK_STATUS_NEEDS_EXACT.
-__global__ void build_wstats_kernel(const float* __restrict__ wn, const float* __restrict__ bias, int F,
-                                    float2* __restrict__ stats, int* __restrict__ status) {
-    const int blk = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    __shared__ float sw[4], sb[4];
-    const int f = blk * 128 + tid;
-    const float w = f < F ? wn[f] : 0.f, b = f < F ? bias[f] : -INFINITY;
+// The tile images the passes stream through shared memory, built once per
+// call: per 256-feature tile, W_half's rows in the tensor core's shared
+// memory layout (two 128-byte-swizzled K-atoms of 256 rows) and a side record
+// of the tile's norms, biases (zero past F) and, per 128 features, the
+// largest |W_f| and b_f for the epilogue's row tests.  W rows out of fp16
+// range raise PK_STATUS_NEEDS_EXACT.
+constexpr int kTcFeat = 256;
+constexpr int kTcWBytes = kTcFeat * 256;            // 2 K-atoms x 256 rows x 128 B
+constexpr int kTcSideBytes = 2 * kTcFeat * 4 + 16;  // norms, biases, 2 x (max |W_f|, max b_f)
+
+__global__ void __launch_bounds__(256)
+build_tiles_kernel(const __half* __restrict__ Wh, const float* __restrict__ wn, const float* __restrict__ bias,
+                   int F, uint8_t* __restrict__ tiles, uint8_t* __restrict__ sides, int* __restrict__ status) {
+    const int t = blockIdx.x, row = threadIdx.x, lane = row & 31, warp = row >> 5;
+    const int f = t * kTcFeat + row;
+    const bool valid = f < F;
+    uint8_t* img = tiles + (int64_t)t * kTcWBytes;
+    const uint4* src = reinterpret_cast<const uint4*>(Wh + (int64_t)(valid ? f : 0) * kBD);
+#pragma unroll
+    for (int ch = 0; ch < 16; ++ch) {
+        const uint4 val = valid ? src[ch] : make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(img + (ch >> 3) * (kTcFeat * 128) + sw128_off(row, ch & 7)) = val;
+    }
+    float* sw = reinterpret_cast<float*>(sides + (int64_t)t * kTcSideBytes);
+    const float w = valid ? wn[f] : 0.f, b = valid ? bias[f] : -INFINITY;
+    sw[row] = w;
+    sw[kTcFeat + row] = valid ? b : 0.f;
     if (w >= 60000.f) atomicOr(status, PK_STATUS_NEEDS_EXACT);
-    const float mw = warp_max(w), mb = warp_max(b);
-    if (lane == 0) { sw[warp] = mw; sb[warp] = mb; }
+    __shared__ float mw[8], mb[8];
+    const float a = warp_max(w), c = warp_max(b);
+    if (lane == 0) {
+        mw[warp] = a;
+        mb[warp] = c;
+    }
     __syncthreads();
-    if (tid == 0) {
-        float a = sw[0], c = sb[0];
-        for (int i = 1; i < 4; ++i) { a = fmaxf(a, sw[i]); c = fmaxf(c, sb[i]); }
-        stats[blk] = make_float2(a, c == -INFINITY ? 0.f : c);
+    if (row < 2) {
+        float x = mw[4 * row], y = mb[4 * row];
+        for (int i = 1; i < 4; ++i) {
+            x = fmaxf(x, mw[4 * row + i]);
+            y = fmaxf(y, mb[4 * row + i]);
+        }
+        reinterpret_cast<float2*>(sw + 2 * kTcFeat)[row] = make_float2(x, y == -INFINITY ? 0.f : y);
     }
 }
 
-// The passes run on the 5th-generation tensor cores: one CTA per
-// 128-token block of a unit (one CTA per SM), 256-feature tiles of W_half
-// double-buffered in shared memory (128-byte swizzle, K-major), accumulators
-// double-buffered in TMEM (2 x 256 columns).  Iteration i waits for the MMA
-// of tile i-1, starts the copy of tile i+1 into the buffer that MMA freed,
-// issues the eight K=16 MMAs of tile i from one thread, and runs the epilogue
-// of tile i-1 from TMEM while they execute.  Each thread's epilogue covers
-// one token row and 128 features.
-constexpr int kTcTokens = 128, kTcFeat = 256, kTcThreads = 256;
+// The passes run on the 5th-generation tensor cores, one CTA per 128-token
+// block of a unit (one CTA per SM), warp-specialised:
+//   warp 8 (one thread): streams tile j's image and side record into
+//     shared-memory buffer j & 1 with two bulk copies, and issues the eight
+//     K=16 MMAs of tile j into TMEM accumulator j & 1 once the copy has
+//     landed and the epilogue of tile j-2 has drained that accumulator;
+//   warps 0-7: the epilogue of tile j from TMEM -- one token row and 128
+//     features per thread -- then release the accumulator.
+// The stages meet on mbarriers only (full, MMA done, TMEM empty per buffer);
+// every wait is bounded, and a wait that runs out aborts the CTA with
+// PK_STATUS_NEEDS_EXACT after the copies and MMAs in flight have landed.
+//   MODE 0: histogram of sampled lower bounds (one per 32 columns) to place
+//     the floor well below the budget threshold.
+//   MODE 1: histograms of the lower and upper bounds at or above the floor
+//     (a 1024-bin window; the top bin collects everything above); entries
+//     whose upper bound reaches the floor are kept, with their bounds, for
+//     build_classify_kernel (one tensor-core pass in all).
+constexpr int kTcTokens = 128, kTcEpiWarps = 8, kTcThreads = 32 * (kTcEpiWarps + 1);
 constexpr int kTcXBytes = kTcTokens * 256;          // 2 K-atoms x 128 rows x 128 B
-constexpr int kTcWBytes = kTcFeat * 256;            // 2 K-atoms x 256 rows x 128 B
-constexpr uint64_t kTcWaitNs = 200000000ull;        // 0.2 s: an MMA never takes this long
+constexpr int kTcSideSlots = 4;                     // side records: tile j in slot j % 4
+constexpr uint64_t kTcWaitNs = 200000000ull;        // 0.2 s: no copy or MMA takes this long
+constexpr int kTcStage = 2048;                      // MODE 1: staged candidates per CTA
+constexpr int kWarpStage = kTcStage / kTcEpiWarps;  // ... per epilogue warp
 
 __host__ __device__ constexpr int tc_smem(int mode) {
-    return 1024 /* alignment slack */ + kTcXBytes + 2 * kTcWBytes + 3 * 2 * kTcFeat * 4 + 6 * 8 + kTcTokens * 4 +
-           (mode == 0 ? kFBins * 4 : 2 * kFWin * 4) + 64;
+    return 1024 /* alignment slack */ + kTcXBytes + 2 * kTcWBytes + kTcSideSlots * kTcSideBytes + kTcTokens * 4 +
+           (mode == 0 ? kFBins * 4 : 2 * kFWin * 4) + 10 * 8 + 16 + (mode == 1 ? kTcStage * 16 : 0);
 }
 
 template <int MODE, typename T>
 __global__ void __launch_bounds__(kTcThreads, 1)
 build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride, int64_t N,
-                     const float* __restrict__ center, float key_scale, const __half* __restrict__ Wh,
-                     const float* __restrict__ bias, const float* __restrict__ wn, int F, FastWs fw, TileSample smp,
+                     const float* __restrict__ center, float key_scale, int F, FastWs fw, TileSample smp,
                      int* __restrict__ status) {
     extern __shared__ uint8_t tc_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* Xs = base;
     uint8_t* Wt = base + kTcXBytes;                                           // [2][kTcWBytes]
-    float* wnt = reinterpret_cast<float*>(Wt + 2 * kTcWBytes);               // [3][256]
-    float* bt = wnt + 3 * kTcFeat;                                           // [3][256]
-    float2* wst = reinterpret_cast<float2*>(bt + 3 * kTcFeat);              // [3][2] (max |W_f|, max b_f) per half
-    float* xn = reinterpret_cast<float*>(wst + 6);                           // [128]
+    uint8_t* side = Wt + 2 * kTcWBytes;                                       // [4][kTcSideBytes]
+    float* xn = reinterpret_cast<float*>(side + kTcSideSlots * kTcSideBytes); // [128]
     int* hA = reinterpret_cast<int*>(xn + kTcTokens);                        // MODE 0: [kFBins]; MODE 1: L [kFWin]
     int* hB = hA + kFWin;                                                    // MODE 1: U [kFWin]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(hA + (MODE == 0 ? kFBins : 2 * kFWin));   // [2]
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(hA + (MODE == 0 ? kFBins : 2 * kFWin));
+    uint64_t* full = bars;          // [2] tile image landed
+    uint64_t* mma_done = bars + 2;  // [2] MMAs of the tile complete
+    uint64_t* tmem_empty = bars + 4; // [2] epilogue drained the accumulator
+    uint64_t* side_full = bars + 6;  // [4] side record landed (slot j % 4)
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 10);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+    float2* stg_hl = reinterpret_cast<float2*>(tslot + 4);                    // MODE 1: [kTcStage]
+    long long* stg_flat = reinterpret_cast<long long*>(stg_hl + kTcStage);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int u = blockIdx.y;
     const int64_t t0 = (int64_t)blockIdx.x * (MODE == 0 ? smp.tb_stride : 1) * kTcTokens;
@@ -717,175 +778,240 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
     const int fstep = MODE == 0 ? smp.ft_stride : 1;
     const int ft_first = MODE == 0 ? (int)(blockIdx.x % fstep) : 0;
     const int ntiles = ft_first < ntf ? (ntf - ft_first + fstep - 1) / fstep : 0;
-
-    if (warp == 0) tmem_alloc(smem_addr(tslot), 512);
-    if (tid == 0) {
-        mbar_init(smem_addr(&bars[0]), 1);
-        mbar_init(smem_addr(&bars[1]), 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    // Tile j of this CTA: W rows into buffer j & 1, norms and biases into j % 3.
-    auto load_w = [&](int j) {
-        const int f0 = (ft_first + j * fstep) * kTcFeat;
-        uint8_t* dst = Wt + (j & 1) * kTcWBytes;
-        for (int c = tid; c < kTcFeat * 16; c += kTcThreads) {
-            const int row = c >> 4, ch = c & 15;
-            const int f = f0 + row;
-            const bool valid = f < F;
-            cp_async_16(smem_addr(dst) + (ch >> 3) * (kTcFeat * 128) + sw128_off(row, ch & 7),
-                        Wh + (int64_t)(valid ? f : 0) * kBD + ch * 8, valid);
-        }
-        // Norms and biases (16-byte chunks of 4 features, zero past F) and
-        // the two halves' maxima, all asynchronous.
-        if (tid < 128) {
-            const bool isb = tid >= 64;
-            const int q = tid & 63, f = f0 + 4 * q;
-            const int nbytes = f >= F ? 0 : (F - f >= 4 ? 16 : 4 * (F - f));
-            const float* src = (isb ? bias : wn) + (nbytes ? f : 0);
-            float* dsts = (isb ? bt : wnt) + (j % 3) * kTcFeat + 4 * q;
-            cp_async_16n(smem_addr(dsts), src, nbytes);
-        } else if (tid == 128) {
-            cp_async_16n(smem_addr(wst + (j % 3) * 2), fw.wstats + f0 / 128, 16);
-        }
+    const bool producer = warp == kTcEpiWarps && lane == 0;
+    // Each barrier phase is waited for before the barrier can complete
+    // again (a parity wait tells only the current phase from the last):
+    // copy j + 2 into W buffer j & 1 follows MMA j, and copy j + 4 into side
+    // slot j % 4 follows MMA j + 2, which follows epilogue j.
+    auto load_tile = [&](int j) {
+        const int t = ft_first + j * fstep;
+        const uint32_t wbar = smem_addr(&full[j & 1]), sbar = smem_addr(&side_full[j % kTcSideSlots]);
+        mbar_expect_tx(wbar, kTcWBytes);
+        bulk_g2s(smem_addr(Wt + (j & 1) * kTcWBytes), fw.tiles + (int64_t)t * kTcWBytes, kTcWBytes, wbar);
+        mbar_expect_tx(sbar, kTcSideBytes);
+        bulk_g2s(smem_addr(side + (j % kTcSideSlots) * kTcSideBytes), fw.sides + (int64_t)t * kTcSideBytes,
+                 kTcSideBytes, sbar);
     };
-    if (ntiles > 0) load_w(0);
-    cp_async_commit_group();
+
+    if (warp == kTcEpiWarps) tmem_alloc(smem_addr(tslot), 512);
+    int n_loaded = 0;
+    if (producer) {
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_addr(&full[b]), 1);
+            mbar_init(smem_addr(&mma_done[b]), 1);
+            mbar_init(smem_addr(&tmem_empty[b]), kTcEpiWarps);
+        }
+        for (int k = 0; k < kTcSideSlots; ++k) mbar_init(smem_addr(&side_full[k]), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (; n_loaded < 2 && n_loaded < ntiles; ++n_loaded) load_tile(n_loaded);
+    }
     if (MODE == 0)
         for (int i = tid; i < kFBins; i += kTcThreads) hA[i] = 0;
     else
         for (int i = tid; i < 2 * kFWin; i += kTcThreads) hA[i] = 0;
-    // x = (k - center) / key_scale in fp32 (core.py:99), rounded to fp16.
-    const bool unit_scale = key_scale == 1.0f;
-    // This warp's 16 key rows, every load issued before any is used.
-    float kr[16][4];
+    if (warp < kTcEpiWarps) {
+        // x = (k - center) / key_scale in fp32 (core.py:99), rounded to fp16;
+        // this warp's 16 key rows, every load issued before any is used.
+        const bool unit_scale = key_scale == 1.0f;
+        float kr[16][4];
 #pragma unroll
-    for (int rr = 0; rr < 16; ++rr) {
-        const int64_t t = t0 + warp * 16 + rr;
+        for (int rr = 0; rr < 16; ++rr) {
+            const int64_t t = t0 + warp * 16 + rr;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) kr[rr][e] = t < N ? key_at(keys, unit_stride, row_stride, u, t, 4 * lane + e) : 0.f;
-    }
-    float cl[4];
+            for (int e = 0; e < 4; ++e)
+                kr[rr][e] = t < N ? key_at(keys, unit_stride, row_stride, u, t, 4 * lane + e) : 0.f;
+        }
+        float cl[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) cl[e] = cu[4 * lane + e];
+        for (int e = 0; e < 4; ++e) cl[e] = cu[4 * lane + e];
 #pragma unroll
-    for (int rr = 0; rr < 16; ++rr) {
-        const int row = warp * 16 + rr;
-        const int64_t t = t0 + row;
-        float x[4] = {0.f, 0.f, 0.f, 0.f};
-        if (t < N) {
+        for (int rr = 0; rr < 16; ++rr) {
+            const int row = warp * 16 + rr;
+            const int64_t t = t0 + row;
+            float x[4] = {0.f, 0.f, 0.f, 0.f};
+            if (t < N) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float dlt = __fsub_rn(kr[rr][e], cl[e]);
-                x[e] = unit_scale ? dlt : __fdiv_rn(dlt, key_scale);
+                for (int e = 0; e < 4; ++e) {
+                    const float dlt = __fsub_rn(kr[rr][e], cl[e]);
+                    x[e] = unit_scale ? dlt : __fdiv_rn(dlt, key_scale);
+                }
             }
+            float ss = fmaf(x[0], x[0], fmaf(x[1], x[1], fmaf(x[2], x[2], x[3] * x[3])));
+            ss = warp_sum(ss);
+            const float amax = warp_max(fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3]))));
+            if (lane == 0) {
+                xn[row] = sqrtf(ss) * (1.0f + 1.0f / 4096.0f);
+                if (!(amax < 60000.f)) atomicOr(status, PK_STATUS_NEEDS_EXACT);
+            }
+            __half2 p0 = __floats2half2_rn(x[0], x[1]), p1 = __floats2half2_rn(x[2], x[3]);
+            uint2 pk2;
+            pk2.x = *reinterpret_cast<uint32_t*>(&p0);
+            pk2.y = *reinterpret_cast<uint32_t*>(&p1);
+            const int chunk = lane >> 1;   // 16-byte chunk of the 256-byte row
+            *reinterpret_cast<uint2*>(Xs + (chunk >> 3) * (kTcTokens * 128) + sw128_off(row, chunk & 7) +
+                                      (lane & 1) * 8) = pk2;
         }
-        float ss = fmaf(x[0], x[0], fmaf(x[1], x[1], fmaf(x[2], x[2], x[3] * x[3])));
-        ss = warp_sum(ss);
-        const float amax = warp_max(fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3]))));
-        if (lane == 0) {
-            xn[row] = sqrtf(ss) * (1.0f + 1.0f / 4096.0f);
-            if (!(amax < 60000.f)) atomicOr(status, PK_STATUS_NEEDS_EXACT);
-        }
-        __half2 p0 = __floats2half2_rn(x[0], x[1]), p1 = __floats2half2_rn(x[2], x[3]);
-        uint2 pk2;
-        pk2.x = *reinterpret_cast<uint32_t*>(&p0);
-        pk2.y = *reinterpret_cast<uint32_t*>(&p1);
-        const int chunk = lane >> 1;   // 16-byte chunk of the 256-byte row
-        *reinterpret_cast<uint2*>(Xs + (chunk >> 3) * (kTcTokens * 128) + sw128_off(row, chunk & 7) + (lane & 1) * 8) =
-            pk2;
     }
-    cp_async_wait_group<0>();
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
-    const int floor_bin = MODE == 1 ? fw.floor_bin[u] : 0;
-    const uint32_t idesc = f16_idesc(128, kTcFeat, 0);
-    const int row = 32 * (warp & 3) + lane, half = warp >> 2;
-    const int64_t trow_t = t0 + row;
-    const bool trow = trow_t < N;
-    bool ok = true;
 
-    for (int i = 0; i <= ntiles; ++i) {
-        if (i >= 1) {
-            const bool done = mbar_wait(smem_addr(&bars[(i - 1) & 1]), ((i - 1) >> 1) & 1, kTcWaitNs);
-            if (__syncthreads_or(!done)) {
-                ok = false;
+    if (producer) {
+        // ------------------------------------------------ copies and MMAs
+        const uint32_t idesc = f16_idesc(128, kTcFeat, 0);
+        const uint32_t xa = smem_addr(Xs);
+        int n_mma = 0;
+        for (int j = 0; j < ntiles && !*abort_flag; ++j) {
+            const int b = j & 1;
+            bool ok = mbar_wait(smem_addr(&full[b]), (j >> 1) & 1, kTcWaitNs);
+            if (ok && j >= 2) ok = mbar_wait(smem_addr(&tmem_empty[b]), ((j - 2) >> 1) & 1, kTcWaitNs);
+            if (!ok) {
+                *abort_flag = 1;
                 break;
             }
             tc_fence_after();
-        }
-        if (i < ntiles && tid == 0) {
-            tc_fence_after();
-            const uint32_t xa = smem_addr(Xs), wa = smem_addr(Wt + (i & 1) * kTcWBytes);
+            const uint32_t wa = smem_addr(Wt + b * kTcWBytes);
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
                 const uint32_t koff = (uint32_t)((kk & 3) * 32);   // K=16 step inside the 128-byte atom
-                umma_f16(tmem + (i & 1) * kTcFeat, sw128_desc(xa + (kk >> 2) * (kTcTokens * 128) + koff),
+                umma_f16(tmem + b * kTcFeat, sw128_desc(xa + (kk >> 2) * (kTcTokens * 128) + koff),
                          sw128_desc(wa + (kk >> 2) * (kTcFeat * 128) + koff), idesc, kk > 0 ? 1u : 0u);
             }
-            umma_commit(smem_addr(&bars[i & 1]));
+            umma_commit(smem_addr(&mma_done[b]));
+            n_mma = j + 1;
+            if (j + 2 < ntiles) {
+                // Buffer b is free once MMA j has read it; side slot
+                // (j + 2) % 4 held tile j - 2, drained before MMA j.
+                if (!mbar_wait(smem_addr(&mma_done[b]), (j >> 1) & 1, kTcWaitNs)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                load_tile(j + 2);
+                n_loaded = j + 3;
+            }
         }
-        if (i + 1 < ntiles) load_w(i + 1);
-        cp_async_commit_group();
-        if (i >= 1) {
-            // Epilogue of tile i-1: this thread's token row, 128 features.
-            const int j = i - 1;
+        if (*abort_flag) {
+            // Let every copy and MMA in flight land before the CTA exits
+            // (the last copies into each buffer and slot, the last MMAs).
+            for (int j = n_loaded > 2 ? n_loaded - 2 : 0; j < n_loaded; ++j)
+                mbar_wait(smem_addr(&full[j & 1]), (j >> 1) & 1, kTcWaitNs);
+            for (int j = n_loaded > kTcSideSlots ? n_loaded - kTcSideSlots : 0; j < n_loaded; ++j)
+                mbar_wait(smem_addr(&side_full[j % kTcSideSlots]), (j / kTcSideSlots) & 1, kTcWaitNs);
+            if (n_mma > 0) mbar_wait(smem_addr(&mma_done[(n_mma - 1) & 1]), ((n_mma - 1) >> 1) & 1, kTcWaitNs);
+        }
+    } else if (warp < kTcEpiWarps) {
+        // ------------------------------------------------------- epilogue
+        const int floor_bin = MODE == 1 ? fw.floor_bin[u] : 0;
+        const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+        const int64_t trow_t = t0 + row;
+        const bool trow = trow_t < N;
+        const float xr = xn[row];
+        const float cx = 0.001953125f * xr;
+        const float fval = __uint_as_float((uint32_t)floor_bin << kFShift);
+        float2* whl = stg_hl + warp * kWarpStage;
+        long long* wflat = stg_flat + warp * kWarpStage;
+        int wcnt = 0;   // this warp's staged candidates (warp-uniform)
+        auto warp_flush = [&]() {
+            __syncwarp();
+            int g = 0;
+            if (lane == 0) g = atomicAdd(&fw.n_cand[u], wcnt);
+            g = __shfl_sync(0xffffffffu, g, 0);
+            for (int e = lane; e < wcnt; e += 32) {
+                const int64_t at = (int64_t)g + e;
+                if (at < fw.acap) {
+                    fw.cand_hl[(int64_t)u * fw.acap + at] = whl[e];
+                    fw.cand_flat[(int64_t)u * fw.acap + at] = wflat[e];
+                } else if (at == fw.acap) {
+                    atomicOr(status, PK_STATUS_BOUNDARY_FULL);
+                }
+            }
+            __syncwarp();
+            wcnt = 0;
+        };
+        for (int j = 0; j < ntiles; ++j) {
+            const int b = j & 1;
+            bool done = mbar_wait(smem_addr(&mma_done[b]), (j >> 1) & 1, kTcWaitNs);
+            if (done)
+                done = mbar_wait(smem_addr(&side_full[j % kTcSideSlots]), (j / kTcSideSlots) & 1, kTcWaitNs);
+            if (__any_sync(0xffffffffu, !done || *abort_flag)) {   // warp-uniform exit
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
             const int f0 = (ft_first + j * fstep) * kTcFeat + half * 128;
-            const float* wnb = wnt + (j % 3) * kTcFeat + half * 128;
-            const float* bb = bt + (j % 3) * kTcFeat + half * 128;
-            const float2 st2 = wst[(j % 3) * 2 + half];
+            const float* sd = reinterpret_cast<const float*>(side + (j % kTcSideSlots) * kTcSideBytes);
+            const float* wnb = sd + half * 128;
+            const float* bb = sd + kTcFeat + half * 128;
+            const float2 st2 = reinterpret_cast<const float2*>(sd + 2 * kTcFeat)[half];
             const float wm = st2.x, bm = st2.y;
-            const float cx = 0.001953125f * xn[row];
-            const float cs = 4.76837158203125e-07f * (xn[row] + wm);
+            const float cs = 4.76837158203125e-07f * (xr + wm);
             const float E = cx * wm * (1.0f + 1.0f / 65536.0f) + cs;
             auto err_of = [&](int col, float v) { return fmaf(cx, wnb[col], cs + 9.5367431640625e-07f * fabsf(v)); };
-            const float fval = __uint_as_float((uint32_t)floor_bin << kFShift);
             // MODE 1 keeps v = acc + b_f >= vfloor (U can reach the floor);
             // MODE 0 bins positive v.  Either needs acc >= tau: one compare
             // per entry, the full bound work only for the entries it keeps.
             const float vfloor = fval - 1.001f * E - 3.814697265625e-06f * (fval + E);
-            const float tau = (MODE == 0 ? 0.f : vfloor) - bm;
-            const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)((j & 1) * kTcFeat + half * 128);
+            const float tau = vfloor - bm;
+            const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(b * kTcFeat + half * 128);
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                float v[32];
-                tmem_ld32(taddr + c * 32, v);
-                tmem_wait_ld();
-                uint32_t m = 0;
+            for (int c2 = 0; c2 < 2; ++c2) {
+                float v[64];
+                __syncwarp();
+                tmem_ld64_wait(taddr + c2 * 64, v);
 #pragma unroll
-                for (int q = 0; q < 32; ++q) m |= (v[q] >= tau ? 1u : 0u) << q;
-                const int cols_left = F - (f0 + c * 32);
-                if (!trow || cols_left <= 0) m = 0;
-                else if (cols_left < 32) m &= (1u << cols_left) - 1u;
-                if (MODE == 0) {
-                    if (!__any_sync(0xffffffffu, m != 0)) continue;
+                for (int h = 0; h < 2; ++h) {
+                    const int c = 2 * c2 + h;
+                    const int cols_left = F - (f0 + c * 32);
+                    if (MODE == 0) {
+                        // The sample bins one lower bound per 32 columns, below
+                        // the largest of theirs (E bounds every column's error).
+                        // Counts above any bin then fall short of the entries'
+                        // -- the floor comes out lower, never unsafe.  Columns
+                        // past F hold v = 0, which bins nothing.
+                        if (!trow) continue;
+                        float mx = -INFINITY;
 #pragma unroll
-                    for (int q = 0; q < 32; ++q) {
-                        if (!(m & (1u << q))) continue;
-                        const int col = c * 32 + q;
-                        const float vv = v[q] + bb[col];
-                        if (!(vv > 0.f)) continue;
-                        const float lo = vv - err_of(col, vv);
-                        if (lo > 0.f) atomicAdd(&hA[fbin(lo)], 1);
+                        for (int q = 0; q < 32; ++q) mx = fmaxf(mx, v[32 * h + q] + bb[c * 32 + q]);
+                        if (mx > 0.f) {
+                            const float lo = mx - (E + 9.5367431640625e-07f * mx);
+                            if (lo > 0.f) atomicAdd(&hA[fbin(lo)], 1);
+                        }
+                        continue;
                     }
-                } else {
-                    // Slots for every kept entry, one atomic per warp;
-                    // entries whose exact U misses the floor get U = -1.
+                    uint32_t m = 0;
+#pragma unroll
+                    for (int q = 0; q < 32; ++q) m |= (v[32 * h + q] >= tau ? 1u : 0u) << q;
+                    if (!trow || cols_left <= 0) m = 0;
+                    else if (cols_left < 32) m &= (1u << cols_left) - 1u;
+                    // Slots for every kept entry in this warp's staging
+                    // buffer (flushed to the unit's list with one global
+                    // reservation when full; a chunk larger than the buffer
+                    // reserves its own); entries whose exact U misses the
+                    // floor get U = -1.  Kept entries are rare: a loop over
+                    // the set bits (a branch per entry, not a predicated
+                    // body per column).
                     const int nk = __popc(m);
                     const int inc = warp_inclusive_scan(nk);
                     const int wtot = __shfl_sync(0xffffffffu, inc, 31);
                     if (wtot == 0) continue;
-                    int cbase = 0;
-                    if (lane == 31) cbase = atomicAdd(&fw.n_cand[u], wtot);
-                    cbase = __shfl_sync(0xffffffffu, cbase, 31) + inc - nk;
-                    if (nk == 0) continue;
-#pragma unroll
-                    for (int q = 0; q < 32; ++q) {
-                        if (!(m & (1u << q))) continue;
+                    if (wcnt + wtot > kWarpStage && wcnt > 0) warp_flush();
+                    const bool direct = wtot > kWarpStage;
+                    int slot;
+                    if (direct) {
+                        int g = 0;
+                        if (lane == 31) g = atomicAdd(&fw.n_cand[u], wtot);
+                        slot = __shfl_sync(0xffffffffu, g, 31) + inc - nk;
+                    } else {
+                        slot = wcnt + inc - nk;
+                        wcnt += wtot;
+                    }
+                    for (uint32_t mm = m; mm; mm &= mm - 1) {
+                        const int q = __ffs(mm) - 1;
                         const int col = c * 32 + q;
-                        const float vv = v[q] + bb[col];
+                        const float vv = pick32(v, 32 * h, q) + bb[col];
                         const float err = err_of(col, vv);
                         const float lo = vv - err, hi = vv + err;
                         bool keep = false;
@@ -900,25 +1026,30 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
                             const int bl = fbin(lo) - floor_bin;
                             if (bl >= 0) atomicAdd(&hA[min(bl, kFWin - 1)], 1);
                         }
-                        if (cbase < fw.acap) {
-                            fw.cand_hl[(int64_t)u * fw.acap + cbase] = make_float2(keep ? hi : -1.f, lo);
-                            fw.cand_flat[(int64_t)u * fw.acap + cbase] = trow_t * F + f0 + col;
+                        const float2 hl = make_float2(keep ? hi : -1.f, lo);
+                        const long long flat = trow_t * F + f0 + col;
+                        if (!direct) {
+                            whl[slot] = hl;
+                            wflat[slot] = flat;
+                        } else if (slot < fw.acap) {
+                            fw.cand_hl[(int64_t)u * fw.acap + slot] = hl;
+                            fw.cand_flat[(int64_t)u * fw.acap + slot] = flat;
                         } else {
                             atomicOr(status, PK_STATUS_BOUNDARY_FULL);
                         }
-                        ++cbase;
+                        ++slot;
                     }
                 }
             }
+            // Accumulator b drained: MMA j + 2 may overwrite it.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_addr(&tmem_empty[b]));
         }
-        tc_fence_before();
-        cp_async_wait_group<0>();
-        fence_async_smem();
-        __syncthreads();
+        if (MODE == 1 && wcnt > 0) warp_flush();
     }
-    // An MMA that did not complete in time: the caller reruns the exact path.
-    if (!ok && tid == 0) atomicOr(status, PK_STATUS_NEEDS_EXACT);
-    cp_async_wait_group<0>();
+    __syncthreads();
+    if (tid == 0 && *abort_flag) atomicOr(status, PK_STATUS_NEEDS_EXACT);
     if (MODE == 0) {
         for (int i = tid; i < kFBins; i += kTcThreads)
             if (hA[i]) atomicAdd(&fw.histS[(int64_t)u * kFBins + i], hA[i]);
@@ -930,7 +1061,8 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, 512);
+    tc_fence_after();
+    if (warp == kTcEpiWarps) tmem_dealloc(tmem, 512);
 }
 
 // Per unit: the floor bin.  Scanning the sample's upper-bound histogram from
@@ -1220,24 +1352,28 @@ int run_encode_select_fast(const T* keys, int64_t unit_stride, int64_t row_strid
                            int* status, cudaStream_t st) {
     const int nblocks = (int)((N + 127) / 128);
     const int nft = (F + kTcFeat - 1) / kTcFeat;
-    // Floor sample: about 64 token blocks, a quarter of the feature tiles.
+    // Floor sample: about 64 token blocks and every ft_stride-th feature
+    // tile, the stride chosen so that the sample expects about 8192 entries
+    // above the floor (relative noise ~1%, against the floor's 2x margin).
     TileSample smp;
     smp.tb_stride = nblocks > 64 ? nblocks / 64 : 1;
-    smp.ft_stride = nft >= 4 ? 4 : 1;
     const int nsample = (nblocks + smp.tb_stride - 1) / smp.tb_stride;
-    const double frac = fmin(1.0, (double)nsample * 128.0 / (double)N) / (double)smp.ft_stride;
+    const double tok_frac = fmin(1.0, (double)nsample * 128.0 / (double)N);
+    const double want = kFSampleMargin * (double)count * tok_frac / 8192.0;
+    smp.ft_stride = want >= (double)nft ? nft : (want >= 1.0 ? (int)want : 1);
+    const double frac = tok_frac / (double)smp.ft_stride;
     const TileSample none = {1, 1};
-    build_wstats_kernel<<<(F + 255) / 256 * 2, 128, 0, st>>>(wn, b, F, fw.wstats, status);
+    build_tiles_kernel<<<nft, 256, 0, st>>>(Wh, wn, b, F, fw.tiles, fw.sides, status);
     PK_CHECK_LAUNCH();
     cudaFuncSetAttribute(build_tile_tc_kernel<0, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(0));
     cudaFuncSetAttribute(build_tile_tc_kernel<1, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(1));
     build_tile_tc_kernel<0, T><<<dim3(nsample, U), kTcThreads, tc_smem(0), st>>>(
-        keys, unit_stride, row_stride, N, center, key_scale, Wh, b, wn, F, fw, smp, status);
+        keys, unit_stride, row_stride, N, center, key_scale, F, fw, smp, status);
     PK_CHECK_LAUNCH();
     build_floor_kernel<<<U, 32, 0, st>>>(fw, count, frac);
     PK_CHECK_LAUNCH();
     build_tile_tc_kernel<1, T><<<dim3(nblocks, U), kTcThreads, tc_smem(1), st>>>(
-        keys, unit_stride, row_stride, N, center, key_scale, Wh, b, wn, F, fw, none, status);
+        keys, unit_stride, row_stride, N, center, key_scale, F, fw, none, status);
     PK_CHECK_LAUNCH();
     build_fast_cut_kernel<<<U, 32, 0, st>>>(fw, count, status);
     PK_CHECK_LAUNCH();
@@ -1335,7 +1471,7 @@ extern "C" int pk_build_index(uint64_t keys, int dtype, int64_t unit_stride, int
     const long long count = (long long)N * key_mean;
     int rc;
     const bool fast = w_half && w_norm;
-    if (fast && ((w_norm | b_enc | w_half) % 16)) return PK_ERR_ARG;   // 16-byte tile copies
+    if (fast && (w_half % 16)) return PK_ERR_ARG;   // 16-byte row loads
     if (fast && dtype == PK_BF16)
         rc = run_encode_select_fast((const __nv_bfloat16*)keys, unit_stride, row_stride, N, (const float*)center,
                                     key_scale, (const float*)w_enc, (const __half*)w_half,
@@ -1424,7 +1560,7 @@ extern "C" int pk_append_index(uint64_t new_keys, int dtype, int64_t unit_stride
     const long long count = (long long)n_new * key_mean;
     int rc;
     const bool fast = w_half && w_norm;
-    if (fast && ((w_norm | b_enc | w_half) % 16)) return PK_ERR_ARG;   // 16-byte tile copies
+    if (fast && (w_half % 16)) return PK_ERR_ARG;   // 16-byte row loads
     if (fast && dtype == PK_BF16)
         rc = run_encode_select_fast((const __nv_bfloat16*)new_keys, unit_stride, row_stride, n_new,
                                     (const float*)center, key_scale, (const float*)w_enc,
