@@ -956,47 +956,50 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
             const float vfloor = fval - 1.001f * E - 3.814697265625e-06f * (fval + E);
             const float tau = vfloor - bm;
             const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(b * kTcFeat + half * 128);
-#pragma unroll 1
-            for (int c2 = 0; c2 < 2; ++c2) {
-                float v[64];
-                __syncwarp();
-                tmem_ld64_wait(taddr + c2 * 64, v);
+            // The row's 128 accumulators in one TMEM round trip.
+            float v[128];
+            __syncwarp();
+            tmem_ld128_wait(taddr, v);
+            if (MODE == 0) {
+                // The sample bins one lower bound per 32 columns, below the
+                // largest of theirs (E bounds every column's error).  Counts
+                // above any bin then fall short of the entries' -- the floor
+                // comes out lower, never unsafe.  Columns past F hold v = 0,
+                // which bins nothing.
+                if (trow) {
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int c = 2 * c2 + h;
-                    const int cols_left = F - (f0 + c * 32);
-                    if (MODE == 0) {
-                        // The sample bins one lower bound per 32 columns, below
-                        // the largest of theirs (E bounds every column's error).
-                        // Counts above any bin then fall short of the entries'
-                        // -- the floor comes out lower, never unsafe.  Columns
-                        // past F hold v = 0, which bins nothing.
-                        if (!trow) continue;
+                    for (int c = 0; c < 4; ++c) {
                         float mx = -INFINITY;
 #pragma unroll
-                        for (int q = 0; q < 32; ++q) mx = fmaxf(mx, v[32 * h + q] + bb[c * 32 + q]);
+                        for (int q = 0; q < 32; ++q) mx = fmaxf(mx, v[32 * c + q] + bb[32 * c + q]);
                         if (mx > 0.f) {
                             const float lo = mx - (E + 9.5367431640625e-07f * mx);
                             if (lo > 0.f) atomicAdd(&hA[fbin(lo)], 1);
                         }
-                        continue;
                     }
-                    uint32_t m = 0;
+                }
+            } else {
+                uint32_t m[4];
 #pragma unroll
-                    for (int q = 0; q < 32; ++q) m |= (v[32 * h + q] >= tau ? 1u : 0u) << q;
-                    if (!trow || cols_left <= 0) m = 0;
-                    else if (cols_left < 32) m &= (1u << cols_left) - 1u;
-                    // Slots for every kept entry in this warp's staging
-                    // buffer (flushed to the unit's list with one global
-                    // reservation when full; a chunk larger than the buffer
-                    // reserves its own); entries whose exact U misses the
-                    // floor get U = -1.  Kept entries are rare: a loop over
-                    // the set bits (a branch per entry, not a predicated
-                    // body per column).
-                    const int nk = __popc(m);
-                    const int inc = warp_inclusive_scan(nk);
-                    const int wtot = __shfl_sync(0xffffffffu, inc, 31);
-                    if (wtot == 0) continue;
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t mc = 0;
+#pragma unroll
+                    for (int q = 0; q < 32; ++q) mc |= (v[32 * c + q] >= tau ? 1u : 0u) << q;
+                    const int cols_left = F - (f0 + c * 32);
+                    if (!trow || cols_left <= 0) mc = 0;
+                    else if (cols_left < 32) mc &= (1u << cols_left) - 1u;
+                    m[c] = mc;
+                }
+                // Slots for every kept entry in this warp's staging buffer
+                // (flushed to the unit's list with one global reservation
+                // when full; a tile larger than the buffer reserves its own),
+                // one scan per tile; entries whose exact U misses the floor
+                // get U = -1.  Kept entries are rare: loops over the set bits
+                // (a branch per entry, not a predicated body per column).
+                const int nk = __popc(m[0]) + __popc(m[1]) + __popc(m[2]) + __popc(m[3]);
+                const int inc = warp_inclusive_scan(nk);
+                const int wtot = __shfl_sync(0xffffffffu, inc, 31);
+                if (wtot > 0) {
                     if (wcnt + wtot > kWarpStage && wcnt > 0) warp_flush();
                     const bool direct = wtot > kWarpStage;
                     int slot;
@@ -1008,36 +1011,39 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
                         slot = wcnt + inc - nk;
                         wcnt += wtot;
                     }
-                    for (uint32_t mm = m; mm; mm &= mm - 1) {
-                        const int q = __ffs(mm) - 1;
-                        const int col = c * 32 + q;
-                        const float vv = pick32(v, 32 * h, q) + bb[col];
-                        const float err = err_of(col, vv);
-                        const float lo = vv - err, hi = vv + err;
-                        bool keep = false;
-                        if (hi > 0.f) {
-                            const int bh = fbin(hi) - floor_bin;
-                            if (bh >= 0) {
-                                atomicAdd(&hB[min(bh, kFWin - 1)], 1);
-                                keep = true;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        for (uint32_t mm = m[c]; mm; mm &= mm - 1) {
+                            const int q = __ffs(mm) - 1;
+                            const int col = c * 32 + q;
+                            const float vv = pick32(v, 32 * c, q) + bb[col];
+                            const float err = err_of(col, vv);
+                            const float lo = vv - err, hi = vv + err;
+                            bool keep = false;
+                            if (hi > 0.f) {
+                                const int bh = fbin(hi) - floor_bin;
+                                if (bh >= 0) {
+                                    atomicAdd(&hB[min(bh, kFWin - 1)], 1);
+                                    keep = true;
+                                }
                             }
+                            if (lo > 0.f) {
+                                const int bl = fbin(lo) - floor_bin;
+                                if (bl >= 0) atomicAdd(&hA[min(bl, kFWin - 1)], 1);
+                            }
+                            const float2 hl = make_float2(keep ? hi : -1.f, lo);
+                            const long long flat = trow_t * F + f0 + col;
+                            if (!direct) {
+                                whl[slot] = hl;
+                                wflat[slot] = flat;
+                            } else if (slot < fw.acap) {
+                                fw.cand_hl[(int64_t)u * fw.acap + slot] = hl;
+                                fw.cand_flat[(int64_t)u * fw.acap + slot] = flat;
+                            } else {
+                                atomicOr(status, PK_STATUS_BOUNDARY_FULL);
+                            }
+                            ++slot;
                         }
-                        if (lo > 0.f) {
-                            const int bl = fbin(lo) - floor_bin;
-                            if (bl >= 0) atomicAdd(&hA[min(bl, kFWin - 1)], 1);
-                        }
-                        const float2 hl = make_float2(keep ? hi : -1.f, lo);
-                        const long long flat = trow_t * F + f0 + col;
-                        if (!direct) {
-                            whl[slot] = hl;
-                            wflat[slot] = flat;
-                        } else if (slot < fw.acap) {
-                            fw.cand_hl[(int64_t)u * fw.acap + slot] = hl;
-                            fw.cand_flat[(int64_t)u * fw.acap + slot] = flat;
-                        } else {
-                            atomicOr(status, PK_STATUS_BOUNDARY_FULL);
-                        }
-                        ++slot;
                     }
                 }
             }
