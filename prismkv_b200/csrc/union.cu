@@ -329,7 +329,10 @@ union_kernel(const int* __restrict__ offsets, const int* __restrict__ lens, cons
             // Every warp finds the same next bucket whose exact count fits
             // (ballots over the counts), then the whole block adds its tokens
             // and, for each token it turns on, decrements the counts of the
-            // later buckets holding it.
+            // later buckets holding it.  One barrier per accepted bucket: the
+            // decrements touch only buckets after it, so a warp still
+            // scanning for it finds the same bucket and reads its count
+            // unchanged.
             long long cnt = count;
             for (int c = cpos; c < n; ++c) {
                 const long long rem = lim - cnt;
@@ -345,7 +348,6 @@ union_kernel(const int* __restrict__ offsets, const int* __restrict__ lens, cons
                 if (next >= n) break;
                 c = next;
                 const int miss = sm.newc[c];
-                __syncthreads();   // every warp has read the counts it scanned
                 cnt += miss;
                 raw_acc += sm.cand_len[c];
                 if (tid == 0) feat[nf] = sm.cand_bucket[c];
