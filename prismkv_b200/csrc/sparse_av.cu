@@ -283,9 +283,10 @@ sparse_av_bf16_kernel(AvParams p) {
     const int G = p.G;
     const int H = p.history[u], len = p.length[u], cnt = p.count[u];
     const int rows = len > 0 ? cnt + max(len - H, 0) : 0;
-    const int per = (rows + p.S - 1) / p.S;
-    const int span = (per + kAvTile - 1) / kAvTile * kAvTile;
-    const int r0 = min(rows, s * span), r1 = min(rows, r0 + span);
+    // Whole tiles split evenly: the splits differ by at most one tile.
+    const int nt_all = (rows + kAvTile - 1) / kAvTile;
+    const int r0 = min(rows, (int)((int64_t)s * nt_all / p.S) * kAvTile);
+    const int r1 = min(rows, (int)((int64_t)(s + 1) * nt_all / p.S) * kAvTile);
     const int ntiles = (r1 - r0 + kAvTile - 1) / kAvTile;
     const int64_t ubase = (int64_t)(u / p.kv_heads) * p.kv_batch_stride + (int64_t)(u % p.kv_heads) * p.kv_head_stride;
     const __nv_bfloat16* kb = (const __nv_bfloat16*)p.k + ubase;
