@@ -41,9 +41,9 @@ def parse():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", type=int, choices=[3, 4, 5], default=3,
-                   help="3: Llama-3-8B-shaped 32-layer decode (default); 4: 1M-token sequence-sharded decode; "
-                        "5: prefill bucket build + decode budget sweep")
+    p.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=3,
+                   help="3: Llama-3-8B-shaped 32-layer decode (default); 2: isolated stage times of one 128-unit "
+                        "layer; 4: 1M-token sequence-sharded decode; 5: prefill bucket build + decode budget sweep")
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--batch", type=int, default=4)
     p.add_argument("--kv-heads", type=int, default=8)
@@ -757,8 +757,121 @@ def run_build_sweep(a):
     print(json.dumps(line), flush=True)
 
 
+def run_stages(a):
+    """Config 2: one bf16 layer of B = 16 sequences x 8 KV heads (128 units),
+    context 32768, F = 8192, 8 features per key, 32 per query, budget 2048;
+    routing (q_activation encode + top-k + aggregation), union and sparse
+    attention are each timed alone (CUDA-graph replay of 20 calls), then the
+    layer's index build.  Attention is reported against the measured HBM
+    copy peak; routing as the FP32-equivalent encode rate (2*F*d FLOP per
+    query head) and its W read."""
+    import torch
+    import prismkv_b200 as pk
+    from prismkv_b200 import native as nv
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    B, Hkv, G, d = 16, 8, 4, 128
+    U = B * Hkv
+    N, F, k, Bt, C, tail = 32768, 8192, 32, 2048, 1024, 16
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed * 1_000_003 + 200)
+    centers, K, V = gen_layer(torch, dev, g, U, N + tail, d, C)
+    W = torch.randn(F, d, device=dev, generator=g) / math.sqrt(d)
+    sae = pk.SAEParams(W, torch.zeros(F, device=dev), key_mean=8, query_topk=k)
+    sae.prepared_half()
+    ws = nv.Workspace(dev)
+    pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=False, workspace=ws)   # workspace, untimed
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    idx = pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=False, workspace=ws)
+    e1.record()
+    torch.cuda.synchronize()
+    build_ms = e0.elapsed_time(e1)
+    if idx.encode_path != "bounds":
+        raise SystemExit("build fell back to the exact path")
+    q = gen_queries(torch, dev, g, centers, 1, G)[0].contiguous()
+    op = pk.SparseDecode(idx, sae, heads_per_unit=G, budget=Bt, workspace=ws)
+    lt = torch.full((U,), N + tail, dtype=torch.int32, device=dev)
+    Wb, wn = op.prep
+    nbytes = nv.query("pk_route_qact_workspace_bytes", U, G, F, k)
+    rws = ws.get(("qact", U, G, F, k), nbytes)
+
+    def route_only():
+        nv.call("pk_route_qact", q, nv.dtype_code(q), None, U, sae.W_enc, sae.b_enc, Wb, wn, 1.0, idx.lens, U, G, d,
+                F, k, rws, nbytes, op.order, op.n_order, op.width, None, None)
+
+    def union_only():
+        nv.call("pk_union", idx.offsets, idx.lens, idx.ids, idx.ids.stride(0), op.order, op.n_order, op.width,
+                op.history, op.limit, U, F, op.max_history, op.ids, op.ids.shape[1], op.count, op.features,
+                op.n_features, op.raw, op.status)
+
+    def attn_only():
+        op.attention(q, K, V, length=lt)
+
+    def timed(fn, reps=20):
+        fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        s_cap = torch.cuda.Stream()
+        s_cap.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s_cap):
+            with torch.cuda.graph(graph, stream=s_cap):
+                for _ in range(reps):
+                    fn()
+        torch.cuda.current_stream().wait_stream(s_cap)
+        graph.replay()
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(max(3, a.steps // 10)):
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1) * 1e3 / reps)
+        del graph
+        return best
+
+    route_us = timed(route_only)
+    union_us = timed(union_only)
+    attn_us = timed(attn_only)
+    layer_us = timed(lambda: (route_only(), union_only(), attn_only()))
+    op.check()
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    cnt = int(op.count.long().sum().item())
+    av_bytes = (cnt + U * tail) * d * 2 * 2 + 4 * cnt + 2 * U * G * d * 2
+    route_flop = 2.0 * F * d * U * G
+    line = {
+        "metric": "config2 isolated stage times (routing, union, sparse-AV) per layer-step",
+        "value": round(layer_us, 2), "unit": "us", "n_gpus": 1, "steps": 20, "warmup": 1,
+        "ms_per_step": round(layer_us / 1e3, 4), "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded clustered keys, iid values, random-init SAE)",
+        "config": {"workload": "config2: 128 units, context 32768, F=8192, k=32, budget 2048 (CUDA-graph replay, "
+                               "20 calls per stage)",
+                   "route_us": round(route_us, 2), "union_us": round(union_us, 2),
+                   "attention_us": round(attn_us, 2), "attention_rows": cnt + U * tail,
+                   "attention_GB_s": round(av_bytes / attn_us / 1e3, 1),
+                   "attention_frac_of_measured_hbm": round(av_bytes / attn_us / 1e3 / hbm, 4),
+                   "routing_fp32_equiv_tflops": round(route_flop / route_us / 1e6, 2),
+                   "routing_W_read_GB_s": round(F * d * 2 / route_us / 1e3, 1),
+                   "union_unique_tokens_per_unit": round(cnt / U, 1),
+                   "build_ms": round(build_ms, 2), "build_keys_per_s": round(U * N / (build_ms / 1e3), 1)},
+        "gpu_launches": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
 if __name__ == "__main__":
     args = parse()
+    if args.impl == "ours" and args.config == 2:
+        run_stages(args)
+        sys.exit(0)
     if args.impl == "ours" and args.config == 4:
         run_seqshard(args)
         sys.exit(0)
