@@ -614,8 +614,10 @@ struct FastSmem {
 // Candidates get exact fp32 activations in the reference's dot-product
 // order.  Too many candidates (near-degenerate inputs): every feature is
 // recomputed.
-template <int ORDER, typename QT>
-__global__ void __launch_bounds__(kSelThreads)
+// MINB = 2 when there are more heads than SMs: two CTAs per SM (at most 128
+// registers a thread) instead of a second wave.
+template <int ORDER, typename QT, int MINB>
+__global__ void __launch_bounds__(kSelThreads, MINB)
 qact_select_fast_kernel(const QT* __restrict__ q, const float* __restrict__ upper,
                         const uint32_t* __restrict__ gmax, int ngroups, const int* __restrict__ units, int G,
                         const float* __restrict__ W, const float* __restrict__ bias, float query_scale, int F, int k,
@@ -988,13 +990,21 @@ extern "C" int pk_route_qact(uint64_t q, int q_dtype, uint64_t units, int n_unit
         // Shared memory for the all-features fallback and the aggregation.
         size_t fsmem = (size_t)4 * F;
         if ((size_t)16 * G * k > fsmem) fsmem = (size_t)16 * G * k;
-#define PK_LAUNCH_FAST(ORD, QT)                                                                                  \
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const bool wide = n_units * G > sms;
+#define PK_LAUNCH_FAST1(ORD, QT, MINB)                                                                           \
     do {                                                                                                         \
-        cudaFuncSetAttribute(qact_select_fast_kernel<ORD, QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
+        cudaFuncSetAttribute(qact_select_fast_kernel<ORD, QT, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                              (int)fsmem);                                                                        \
-        qact_select_fast_kernel<ORD, QT><<<n_units * G, kSelThreads, fsmem, st>>>(                               \
+        qact_select_fast_kernel<ORD, QT, MINB><<<n_units * G, kSelThreads, fsmem, st>>>(                         \
             (const QT*)q, act, gmax, ngroups, ul, G, (const float*)w_enc, (const float*)b_enc, query_scale, F,   \
             k, (const int*)counts, hid, hval, done, (int*)order, (int*)n_order, order_stride, (float*)score);    \
+    } while (0)
+#define PK_LAUNCH_FAST(ORD, QT)                                                                                  \
+    do {                                                                                                         \
+        if (wide) PK_LAUNCH_FAST1(ORD, QT, 2); else PK_LAUNCH_FAST1(ORD, QT, 1);                                 \
     } while (0)
         if (q_dtype == PK_BF16) {
             if (inter) PK_LAUNCH_FAST(kInterleaved16, __nv_bfloat16); else PK_LAUNCH_FAST(kSequential, __nv_bfloat16);
@@ -1002,6 +1012,7 @@ extern "C" int pk_route_qact(uint64_t q, int q_dtype, uint64_t units, int n_unit
             if (inter) PK_LAUNCH_FAST(kInterleaved16, float); else PK_LAUNCH_FAST(kSequential, float);
         }
 #undef PK_LAUNCH_FAST
+#undef PK_LAUNCH_FAST1
         PK_CHECK_LAUNCH();
         return PK_OK;
     }
