@@ -57,6 +57,8 @@ def parse():
     p.add_argument("--max-steps", type=int, default=256, help="decode positions the KV cache holds")
     p.add_argument("--update-interval", type=int, default=4096, help="index append cadence (tokens)")
     p.add_argument("--no-graph", action="store_true", help="eager launches instead of CUDA-graph replay")
+    p.add_argument("--layout", action="store_true",
+                   help="layout diagnostic: in-place sparse attention vs explicit gather + packed attention")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--seed", type=int, default=0)
@@ -867,8 +869,122 @@ def run_stages(a):
     print(json.dumps(line), flush=True)
 
 
+def run_layout(a):
+    """Layout diagnostic at config-3 shape (single.py:24-67): per layer, route
+    once, then CUDA-graph replay over the layers of the in-place sparse
+    attention, the explicit gather of the routed rows and tail into a packed
+    copy (pk_gather_kv), attention over the packed copy, and both together.
+    Eight layers (the selected rows of a pass, ~540 MB, far exceed L2).  The
+    gather's read rate is the HBM rate of random 256-byte rows: the ceiling
+    of the in-place attention's traffic."""
+    import torch
+    import prismkv_b200 as pk
+    from prismkv_b200 import native as nv
+    from prismkv_b200.layout import layout_probe, gather_kv
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    L = min(a.layers, 8)
+    U, G, d = a.batch * a.kv_heads, a.q_per_kv, 128
+    N, F, k, tail = a.history, a.features, a.query_topk, 128
+    g = torch.Generator(device=dev)
+    ws = nv.Workspace(dev)
+    layers = []
+    for l in range(L):
+        g.manual_seed(a.seed * 1_000_003 + 700 + l)
+        centers, K, V = gen_layer(torch, dev, g, U, N + tail, d, a.clusters)
+        W = torch.randn(F, d, device=dev, generator=g) / math.sqrt(d)
+        sae = pk.SAEParams(W, torch.zeros(F, device=dev), key_mean=a.key_mean, query_topk=k)
+        idx = pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=False, workspace=ws)
+        op = pk.SparseDecode(idx, sae, heads_per_unit=G, budget=a.budget, workspace=nv.Workspace(dev))
+        q = gen_queries(torch, dev, g, centers, 1, G)[0].contiguous()
+        op.route(q)
+        layers.append((op, q, K, V))
+    torch.cuda.synchronize()
+    length = torch.full((U,), N + tail, dtype=torch.int32, device=dev)
+    checks = [layout_probe(op, q, K, V, length, reps=2) for op, q, K, V in layers]   # bit-exact check per layer
+    rows = sum(c["rows"] for c in checks)
+    P = max(c["packed_rows"] for c in checks)
+    packed = [gather_kv(K, V, op.ids, op.count, op.history, length, P) for op, q, K, V in layers]
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    S = max(1, min(8, (2 * sms) // U))
+    ident = torch.arange(P, dtype=torch.int32, device=dev).repeat(U, 1).contiguous()
+    nbytes = nv.query("pk_sparse_av_workspace_bytes", U, G, d, S)
+    out = torch.empty(U, G, d, dtype=torch.bfloat16, device=dev)
+
+    def indexed():
+        for op, q, K, V in layers:
+            op.attention(q, K, V, length=length, splits=S)
+
+    def gather():
+        for (op, q, K, V), (pk_, pv_) in zip(layers, packed):
+            nv.call("pk_gather_kv", K, V, nv.PK_BF16, 1, K.stride(0), 0, K.stride(1), op.ids, op.ids.stride(0),
+                    op.count, op.history, length, U, d, P, pk_, pv_, None)
+
+    def prepacked():
+        for (op, q, K, V), (pk_, pv_) in zip(layers, packed):
+            p_len = op.count + (length - op.history)
+            nv.call("pk_sparse_av", q, pk_, pv_, nv.PK_BF16, 1, pk_.stride(0), 0, pk_.stride(1), ident, P, op.count,
+                    op.count, p_len, U, G, d, S, op.ws.get(("av", U, G, d, S), nbytes), nbytes, out, None)
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        s_cap = torch.cuda.Stream()
+        s_cap.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s_cap):
+            with torch.cuda.graph(graph, stream=s_cap):
+                fn()
+        torch.cuda.current_stream().wait_stream(s_cap)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        best = float("inf")
+        for _ in range(max(3, a.steps // 10)):
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1) * 1e3 / L)
+        del graph
+        return best
+
+    us = {"indexed_av": timed(indexed), "prepacked_av": timed(prepacked), "explicit_gather": timed(gather),
+          "gather_and_av": timed(lambda: (gather(), prepacked()))}
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    row_bytes = rows / L * d * 2 * 2            # K + V rows per layer
+    line = {
+        "metric": "layout probe: in-place sparse attention vs explicit gather + packed attention per layer",
+        "value": round(us["indexed_av"], 2), "unit": "us", "n_gpus": 1, "steps": L, "warmup": 1,
+        "ms_per_step": round(us["indexed_av"] / 1e3, 4), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded clustered keys, iid values, random-init SAE)",
+        "config": {"workload": f"config-3 layer shape x {L} layers (U={U}, history {N}, tail {tail}, budget "
+                               f"{a.budget}); CUDA-graph replay over the layers",
+                   "us_per_layer": {k_: round(v_, 2) for k_, v_ in us.items()},
+                   "identical_outputs": all(c["identical"] for c in checks),
+                   "rows_per_layer": rows // L,
+                   "gather_read_GB_s": round(row_bytes / us["explicit_gather"] / 1e3, 1),
+                   "gather_read_plus_write_GB_s": round(2 * row_bytes / us["explicit_gather"] / 1e3, 1),
+                   "gather_read_plus_write_frac_of_measured_hbm":
+                       round(2 * row_bytes / us["explicit_gather"] / 1e3 / hbm, 4),
+                   "indexed_av_GB_s": round(row_bytes / us["indexed_av"] / 1e3, 1),
+                   "indexed_av_frac_of_gather_rate": round(us["explicit_gather"] / us["indexed_av"], 4)},
+        "gpu_launches": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
 if __name__ == "__main__":
     args = parse()
+    if args.impl == "ours" and args.layout:
+        run_layout(args)
+        sys.exit(0)
     if args.impl == "ours" and args.config == 2:
         run_stages(args)
         sys.exit(0)

@@ -158,6 +158,19 @@ int pk_sparse_av(uint64_t q, uint64_t k, uint64_t v, int dtype,
  * generalises the in-GPU split merge of av_tuned.cu:54-61. */
 int pk_lse_merge(uint64_t partial, int P, int UG, int d, uint64_t out, int dtype, uint64_t stream);
 
+/* Packs each unit's selected rows ids[u, :count[u]] and then its dense tail
+ * rows [history[u], length[u]) of K and V (layout as pk_sparse_av) into
+ * out_k/out_v [U, packed_rows, d] (unit-major, contiguous); slots past a
+ * unit's rows are not written, and a unit with more rows than packed_rows is
+ * truncated with PK_STATUS_OUT_FULL in *status (optional).  The layout-
+ * control diagnostic of the reference (kernels/cuda_sm90/native_sources/
+ * gather.cu:22-31, gather_kv), with its unit-major output.  Rows, strides and
+ * base addresses must be 16-byte aligned. */
+int pk_gather_kv(uint64_t k, uint64_t v, int dtype, int kv_heads, int64_t kv_batch_stride, int64_t kv_head_stride,
+                 int64_t kv_row_stride, uint64_t ids, int64_t ids_stride, uint64_t count, uint64_t history,
+                 uint64_t length, int U, int d, int64_t packed_rows, uint64_t out_k, uint64_t out_v,
+                 uint64_t status, uint64_t stream);
+
 /* Sparse attention for callers that cannot allocate device memory.
  * This entry point has no counterpart in the reference.  It exists for
  * embedders that cannot hand the library a workspace: a host that reserved

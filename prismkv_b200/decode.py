@@ -16,6 +16,28 @@ from . import native as nv
 from .index import DeviceIndex, SAEParams, budget_limit
 
 
+def kv_layout(k: torch.Tensor, v: torch.Tensor, U: int, d: int):
+    """(kv_heads, batch_stride, head_stride, row_stride, total) of K/V given as
+    [U, total, d] (rows of each unit contiguous) or slot-major
+    [B, total, H_kv, d] with U = B * H_kv (native8b.py:83-84,92-101 checks)."""
+    if k.shape != v.shape or k.stride() != v.stride():
+        raise ValueError("K and V must share shape and strides")
+    if k.dim() == 3:
+        if k.shape[0] != U or k.shape[2] != d:
+            raise ValueError(f"K/V[{U},total,{d}] required")
+        kv = (1, k.stride(0), 0, k.stride(1), k.shape[1])
+    elif k.dim() == 4:
+        B, total, Hkv, dd = k.shape
+        if B * Hkv != U or dd != d:
+            raise ValueError("slot-major K/V[B,total,H_kv,d] with B*H_kv == U required")
+        kv = (Hkv, k.stride(0), k.stride(2), k.stride(1), total)
+    else:
+        raise ValueError("K/V must be 3-D or 4-D")
+    if k.stride(-1) != 1:
+        raise ValueError("K/V with contiguous head dimension required")
+    return kv
+
+
 class SparseDecode:
     def __init__(self, index: DeviceIndex, sae, *, heads_per_unit: int = 4, router: str = "q_activation",
                  query_scale: float = 1.0, query_topk: int | None = None, unique_cap: float | None = None,
@@ -106,23 +128,9 @@ class SparseDecode:
         With ``partial`` ([U*G, d+2] fp32) the per-head (m, l, o) partial is
         written instead of the output (for the sequence-sharded merge)."""
         U, G, d = self.U, self.G, self.d
-        if k.shape != v.shape or k.stride() != v.stride():
-            raise ValueError("K and V must share shape and strides")
         if k.dtype != q.dtype or v.dtype != q.dtype:
             raise ValueError("Q, K and V must share a dtype")
-        if k.dim() == 3:
-            if k.shape[0] != U or k.shape[2] != d:
-                raise ValueError(f"K/V[{U},total,{d}] required")
-            kv_heads, bs, hs, rs, total = 1, k.stride(0), 0, k.stride(1), k.shape[1]
-        elif k.dim() == 4:
-            B, total, Hkv, dd = k.shape
-            if B * Hkv != U or dd != d:
-                raise ValueError("slot-major K/V[B,total,H_kv,d] with B*H_kv == U required")
-            kv_heads, bs, hs, rs = Hkv, k.stride(0), k.stride(2), k.stride(1)
-        else:
-            raise ValueError("K/V must be 3-D or 4-D")
-        if k.stride(-1) != 1:
-            raise ValueError("K/V with contiguous head dimension required")
+        kv_heads, bs, hs, rs, total = kv_layout(k, v, U, d)
         if total < self.index.history:
             raise ValueError("K/V shorter than the indexed history")
         if length is None:
