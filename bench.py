@@ -530,7 +530,8 @@ def run_seqshard(a):
     """Config 4: B=1, 32/8 heads (U = 8 units of 4 query heads), context
     1048576, F = 32768, 64 features per query, budget 8192, clustered keys
     with 4096 clusters.  Rank r of P holds tokens [r*N/P, (r+1)*N/P) of every
-    unit and its shard-local bucket index; a decode step routes (replicated),
+    unit and its shard of the bucket index (built with the whole sequence's
+    exact BatchTopK, build_sharded); a decode step routes (replicated),
     unions its shard's buckets with budget 8192/P, attends over its rows and
     merges the P log-sum-exp partials after one NCCL all-gather.  The total
     context is fixed: strong scaling."""
@@ -538,7 +539,7 @@ def run_seqshard(a):
     import torch.distributed as dist
     import prismkv_b200 as pk
     from prismkv_b200 import native as nv
-    from prismkv_b200.shard import ShardedDecode, token_ranges
+    from prismkv_b200.shard import ShardedDecode, build_sharded, token_ranges
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -587,10 +588,12 @@ def run_seqshard(a):
     ws = nv.Workspace(dev)
     torch.cuda.synchronize()
     tb = time.time()
-    idx = pk.DeviceIndex.build(K[:, :n_local], sae, 1.0, moments=False, workspace=ws)
+    # The exact global BatchTopK over all N tokens (one device's build),
+    # each rank keeping its shard: histogram all-reduces and one all-gather.
+    idx = build_sharded(K[:, :n_local], sae, 1.0, lo=lo, N_total=N, workspace=ws)
     torch.cuda.synchronize()
     build_s = time.time() - tb
-    for key in [k_ for k_ in ws.buffers if isinstance(k_, tuple) and k_[0] == "build"]:
+    for key in [k_ for k_ in ws.buffers if isinstance(k_, tuple) and k_[0] in ("build", "shard_build")]:
         del ws.buffers[key]
     torch.cuda.empty_cache()
     sd = ShardedDecode(idx, sae, heads_per_unit=G, budget=budget, max_history=n_local, workspace=ws)
@@ -648,7 +651,7 @@ def run_seqshard(a):
                    "batch": B, "kv_heads": Hkv, "q_per_kv": G, "history": N, "features": F, "query_topk": k,
                    "budget": budget, "budget_per_shard": budget // world, "clusters": C,
                    "tokens_per_shard": n_local, "build_s": round(build_s, 2),
-                   "index": "shard-local build (per-shard BatchTopK threshold)",
+                   "index_build": "exact BatchTopK over the whole sequence (build_sharded)",
                    "parallelism": f"seq{world}", "l2": "KV rows gathered per step are scattered over >> L2"},
         "e2e": {"value": round(tokens / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(U * G * d * 2), "d2h_bytes_per_step": int(U * G * d * 2)},

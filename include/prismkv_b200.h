@@ -158,6 +158,52 @@ int pk_sparse_av(uint64_t q, uint64_t k, uint64_t v, int dtype,
  * generalises the in-GPU split merge of av_tuned.cu:54-61. */
 int pk_lse_merge(uint64_t partial, int P, int UG, int d, uint64_t out, int dtype, uint64_t stream);
 
+/* Sequence-sharded build with the exact global BatchTopK (core.py:13-26 over
+ * the whole sequence, which the reference computes on one device): rank r of
+ * P holds tokens [token_base, token_base + N) of every unit and runs the
+ * phases below, the host reducing between them:
+ *   phase 0: tensor-core sample of this shard into the sampled histogram
+ *            (workspace at layout[0], int32 [U, 8192]); sample_info[0..1] =
+ *            (sampled token blocks, feature-tile stride) of this shard.
+ *            Host: SUM all-reduce of the histogram.
+ *   phase 1: floor from the summed histogram with global_count (N_total *
+ *            key_mean) and sample_frac (entries sampled / all entries, over
+ *            all shards); bound histograms above it (layout[1], [2]).
+ *            Host: SUM all-reduce of both.
+ *   phase 2: global cut, members by their bounds, exact values for the
+ *            undecided; boundary keys with flat indices in the whole sequence
+ *            (flat_base = token_base * F) at layout[5] [U, boundary_capacity],
+ *            counts at layout[4], members so far at layout[3].
+ *            Host: need[u] = global_count - SUM of members; all-gather of the
+ *            keys into all_keys [P, U, key_cap] with counts [P, U].
+ *   phase 3: every shard selects the same need[u] smallest keys and keeps
+ *            its own, then writes CSR offsets/lens/ids (ids = token_base + t).
+ * Any status bit stops the build (the host checks all ranks).  A shard can
+ * hold more than its own N * key_mean members under the global threshold:
+ * member_capacity (at most min(global_count, N * F)) sizes the member list,
+ * and ids_stride must hold the shard's members plus their slack.  Same
+ * arguments as pk_build_index otherwise; the fast (tensor-core) path only. */
+size_t pk_build_shard_workspace_bytes(int U, int64_t N, int F, int64_t member_capacity, int64_t boundary_capacity);
+int pk_build_shard_layout(int U, int64_t N, int F, int64_t member_capacity, int64_t boundary_capacity,
+                          uint64_t out_offsets);
+int pk_build_shard_phase(int phase, uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride, uint64_t center,
+                         float key_scale, uint64_t w_enc, uint64_t b_enc, uint64_t w_half, uint64_t w_norm, int U,
+                         int64_t N, int d, int F, int key_mean, int64_t member_capacity, int64_t boundary_capacity,
+                         uint64_t workspace, uint64_t workspace_bytes, long long global_count, double sample_frac,
+                         int64_t flat_base,
+                         uint64_t lens, uint64_t offsets, uint64_t ids, int64_t ids_stride, int64_t token_base,
+                         float slack_frac, int slack_min, uint64_t all_keys, uint64_t key_counts, int P,
+                         int64_t key_cap, uint64_t need, uint64_t sample_info, uint64_t status, uint64_t stream);
+
+/* The key center of a sequence split across shards (the column mean of
+ * core.py:99 in torch's cascade order): each shard, holding whole cascade
+ * chunks of pk_key_center_chunk_rows(N_total) rows, writes its chunks' sums
+ * out[U, N / chunk_rows, d]; the mean is the in-order fp32 sum of every
+ * shard's chunk sums divided by N_total (N_total a multiple of the chunk). */
+int64_t pk_key_center_chunk_rows(int64_t N_total);
+int pk_key_center_chunks(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride, int U, int64_t N, int d,
+                         int64_t N_total, uint64_t out, uint64_t stream);
+
 /* Packs each unit's selected rows ids[u, :count[u]] and then its dense tail
  * rows [history[u], length[u]) of K and V (layout as pk_sparse_av) into
  * out_k/out_v [U, packed_rows, d] (unit-major, contiguous); slots past a

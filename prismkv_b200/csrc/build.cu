@@ -1216,7 +1216,7 @@ __global__ void __launch_bounds__(256)
 build_exact_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride,
                    const float* __restrict__ center, float key_scale, const float* __restrict__ W,
                    const float* __restrict__ bias, int F, BuildWs ws, FastWs fw, int* __restrict__ lens,
-                   int* __restrict__ status, int vec_keys) {
+                   int* __restrict__ status, int vec_keys, long long flat_base) {
     __shared__ float cs[kBD];
     const int u = blockIdx.y;
     for (int c = threadIdx.x; c < kBD; c += blockDim.x) cs[c] = center[(int64_t)u * kBD + c];
@@ -1264,15 +1264,19 @@ build_exact_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_
             }
             continue;
         }
+        // Boundary keys carry the flat index in the whole sequence (flat_base:
+        // the shard's first token times F; 0 unsharded) so that ties order
+        // the same across shards.
         const uint32_t span = hi_bits - __float_as_uint(y);          // > 0: y lies below the band's top
-        if (span >= (1u << 28) || flat >= (1ll << 36)) {
+        const long long gflat = flat + flat_base;
+        if (span >= (1u << 28) || gflat >= (1ll << 36)) {
             atomicOr(status, PK_STATUS_NEEDS_EXACT);
             continue;
         }
         const int at = atomicAdd(&ws.n_boundary[u], 1);
         if (at < ws.bcap)
             ws.boundary[(int64_t)u * ws.bcap + at] =
-                (long long)(((unsigned long long)span << 36) | (unsigned long long)flat);
+                (long long)(((unsigned long long)span << 36) | (unsigned long long)gflat);
         else
             atomicOr(status, PK_STATUS_BOUNDARY_FULL);
     }
@@ -1351,6 +1355,131 @@ build_fast_resolve_kernel(BuildWs ws, int F, int* __restrict__ lens, int* __rest
     }
 }
 
+// Sequence-sharded resolve: the boundary keys of every shard, gathered as
+// keys[P, U, key_cap] with counts[P, U] (global flat indices), and the
+// unit's need = global count - members over all shards.  Every shard runs
+// the same radix select over the same keys (so every shard finds the same
+// threshold key) and keeps the keys at or below it whose flat index lies in
+// its own range [flat_lo, flat_hi).
+__global__ void __launch_bounds__(1024)
+build_shard_resolve_kernel(const long long* __restrict__ keys, const int* __restrict__ counts, int P, int64_t key_cap,
+                           const long long* __restrict__ need_in, long long flat_lo, long long flat_hi, BuildWs ws,
+                           FastWs fw, int F, int* __restrict__ lens, int* __restrict__ status) {
+    const int u = blockIdx.x, tid = threadIdx.x, nt = blockDim.x, U = gridDim.x;
+    __shared__ int hist[256];
+    __shared__ unsigned long long s_prefix;
+    __shared__ long long s_need;
+    if (fw.cutL[u] == INT32_MAX || fw.cutU[u] < 0) return;   // flagged, or all positives (nothing to resolve)
+    const long long need0 = need_in[u];
+    if (need0 <= 0) return;
+    long long total = 0;
+    for (int r = 0; r < P; ++r) total += min((int64_t)counts[(int64_t)r * U + u], key_cap);
+    if (need0 > total) {
+        if (tid == 0) atomicOr(status, PK_STATUS_NEEDS_EXACT);
+        return;
+    }
+    const int64_t nslots = (int64_t)P * key_cap;
+    auto key_of = [&](int64_t i, unsigned long long& kk) -> bool {
+        const int r = (int)(i / key_cap);
+        const int64_t j = i % key_cap;
+        if (j >= counts[(int64_t)r * U + u]) return false;
+        kk = (unsigned long long)keys[((int64_t)r * U + u) * key_cap + j];
+        return true;
+    };
+    unsigned long long prefix = ~0ull;
+    if (need0 < total) {
+        unsigned long long pre = 0, pmask = 0;
+        long long need = need0;
+        for (int pass = 0; pass < 8; ++pass) {
+            const int shift = 56 - 8 * pass;
+            for (int i = tid; i < 256; i += nt) hist[i] = 0;
+            __syncthreads();
+            for (int64_t i = tid; i < nslots; i += nt) {
+                unsigned long long kk;
+                if (key_of(i, kk) && (kk & pmask) == pre) atomicAdd(&hist[(kk >> shift) & 255ull], 1);
+            }
+            __syncthreads();
+            if (tid == 0) {
+                long long acc = 0;
+                int dgt = 0;
+                for (; dgt < 256; ++dgt) {
+                    if (acc + hist[dgt] >= need) break;
+                    acc += hist[dgt];
+                }
+                s_prefix = pre | ((unsigned long long)dgt << shift);
+                s_need = need - acc;
+            }
+            __syncthreads();
+            pre = s_prefix;
+            pmask |= 0xFFull << shift;
+            need = s_need;
+            __syncthreads();
+        }
+        prefix = pre;
+    }
+    for (int64_t i = tid; i < nslots; i += nt) {
+        unsigned long long kk;
+        if (!key_of(i, kk) || kk > prefix) continue;
+        const long long gflat = (long long)(kk & ((1ull << 36) - 1));
+        if (gflat < flat_lo || gflat >= flat_hi) continue;
+        const long long flat = gflat - flat_lo;
+        const int at = atomicAdd(&ws.n_members[u], 1);
+        if (at < ws.mcap) {
+            ws.members[(int64_t)u * ws.mcap + at] = flat;
+            atomicAdd(&lens[(int64_t)u * F + (int)(flat % F)], 1);
+        } else {
+            atomicOr(status, PK_STATUS_MEMBERS_FULL);
+        }
+    }
+}
+
+__global__ void set_ints_kernel(int* __restrict__ out, int a, int b) {
+    out[0] = a;
+    out[1] = b;
+}
+
+// Chunk sums of the key-center cascade (center_kernel) for a shard of a
+// longer sequence: lp comes from the whole sequence's length, and the shard
+// holds whole chunks; out[u, ch, c] = the cascade's sum of chunk ch.
+template <typename T>
+__global__ void __launch_bounds__(1024)
+center_chunks_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride, int64_t nchunks, int lp,
+                     int d, float* __restrict__ out) {
+    const int u = blockIdx.y, lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int c = blockIdx.x * 32 + lane;
+    const int64_t step = (int64_t)1 << lp, chunk = step * step * step;
+    if (c >= d) return;
+    for (int64_t ch = w; ch < nchunks; ch += nw) {
+        int64_t i = ch * chunk;
+        float a2 = 0.f;
+        for (int64_t g = 0; g < step; ++g) {
+            float a1 = 0.f;
+            for (int64_t b = 0; b < step; ++b) {
+                float a0 = 0.f;
+                for (int64_t s = 0; s < step; ++s, ++i) a0 = __fadd_rn(a0, key_at(keys, unit_stride, row_stride, u, i, c));
+                a1 = __fadd_rn(a1, a0);
+            }
+            a2 = __fadd_rn(a2, a1);
+        }
+        out[((int64_t)u * nchunks + ch) * d + c] = a2;
+    }
+}
+
+// The sampled floor's parameters for a shard of N keys: about 64 token
+// blocks and every ft_stride-th feature tile (see run_encode_select_fast).
+TileSample sample_plan(int64_t N, int F, long long count, int* nsample_out) {
+    const int nblocks = (int)((N + 127) / 128);
+    const int nft = (F + 255) / 256;
+    TileSample smp;
+    smp.tb_stride = nblocks > 64 ? nblocks / 64 : 1;
+    const int nsample = (nblocks + smp.tb_stride - 1) / smp.tb_stride;
+    const double tok_frac = fmin(1.0, (double)nsample * 128.0 / (double)N);
+    const double want = kFSampleMargin * (double)count * tok_frac / 8192.0;
+    smp.ft_stride = want >= (double)nft ? nft : (want >= 1.0 ? (int)want : 1);
+    *nsample_out = nsample;
+    return smp;
+}
+
 template <typename T>
 int run_encode_select_fast(const T* keys, int64_t unit_stride, int64_t row_stride, int64_t N, const float* center,
                            float key_scale, const float* W, const __half* Wh, const float* wn,
@@ -1361,13 +1490,9 @@ int run_encode_select_fast(const T* keys, int64_t unit_stride, int64_t row_strid
     // Floor sample: about 64 token blocks and every ft_stride-th feature
     // tile, the stride chosen so that the sample expects about 8192 entries
     // above the floor (relative noise ~1%, against the floor's 2x margin).
-    TileSample smp;
-    smp.tb_stride = nblocks > 64 ? nblocks / 64 : 1;
-    const int nsample = (nblocks + smp.tb_stride - 1) / smp.tb_stride;
-    const double tok_frac = fmin(1.0, (double)nsample * 128.0 / (double)N);
-    const double want = kFSampleMargin * (double)count * tok_frac / 8192.0;
-    smp.ft_stride = want >= (double)nft ? nft : (want >= 1.0 ? (int)want : 1);
-    const double frac = tok_frac / (double)smp.ft_stride;
+    int nsample = 0;
+    const TileSample smp = sample_plan(N, F, count, &nsample);
+    const double frac = fmin(1.0, (double)nsample * 128.0 / (double)N) / (double)smp.ft_stride;
     const TileSample none = {1, 1};
     build_tiles_kernel<<<nft, 256, 0, st>>>(Wh, wn, b, F, fw.tiles, fw.sides, status);
     PK_CHECK_LAUNCH();
@@ -1389,7 +1514,7 @@ int run_encode_select_fast(const T* keys, int64_t unit_stride, int64_t row_strid
     const int vec = ((uint64_t)keys % 16 == 0 && (unit_stride * (int64_t)esz) % 16 == 0 &&
                      (row_stride * (int64_t)esz) % 16 == 0) ? 1 : 0;
     build_exact_kernel<T><<<dim3(512, U), 256, 0, st>>>(keys, unit_stride, row_stride, center, key_scale, W, b, F,
-                                                        ws, fw, lens, status, vec);
+                                                        ws, fw, lens, status, vec, 0ll);
     PK_CHECK_LAUNCH();
     build_fast_need_kernel<<<U, 32, 0, st>>>(ws, fw, count);
     PK_CHECK_LAUNCH();
@@ -1621,4 +1746,176 @@ extern "C" int pk_append_index(uint64_t new_keys, int dtype, int64_t unit_stride
     append_commit_kernel<<<g2, 256, 0, st>>>(ws.flag, (int*)lens, cnt_new, F, (int*)status);
     PK_CHECK_LAUNCH();
     return PK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Sequence-sharded build with the exact global BatchTopK.
+// ---------------------------------------------------------------------------
+
+extern "C" size_t pk_build_shard_workspace_bytes(int U, int64_t N, int F, int64_t member_capacity,
+                                                  int64_t boundary_capacity) {
+    const int64_t mcap = member_capacity > 0 ? member_capacity : 1;
+    const int64_t bcap = boundary_capacity > 0 ? boundary_capacity : 1;
+    (void)N;
+    return carve_bytes(U, F, mcap, bcap) + fast_bytes(U, bcap, F);
+}
+
+extern "C" int pk_build_shard_layout(int U, int64_t N, int F, int64_t member_capacity, int64_t boundary_capacity,
+                                     uint64_t out) {
+    if (U < 1 || N < 1 || F < 1 || member_capacity < 1 || boundary_capacity < 1 || !out) return PK_ERR_ARG;
+    const int64_t mcap = member_capacity;
+    const size_t fbase = carve_bytes(U, F, mcap, boundary_capacity);
+    char* zero = nullptr;
+    BuildWs ws = carve(zero, U, F, mcap, boundary_capacity);
+    FastWs fw = carve_fast(zero + fbase, U, boundary_capacity, F);
+    int64_t* o = (int64_t*)out;
+    o[0] = (int64_t)((char*)fw.histS - zero);
+    o[1] = (int64_t)((char*)fw.histL - zero);
+    o[2] = (int64_t)((char*)fw.histU - zero);
+    o[3] = (int64_t)((char*)ws.n_members - zero);
+    o[4] = (int64_t)((char*)ws.n_boundary - zero);
+    o[5] = (int64_t)((char*)ws.boundary - zero);
+    o[6] = (int64_t)((char*)fw.cutU - zero);
+    o[7] = (int64_t)((char*)fw.cutL - zero);
+    return PK_OK;
+}
+
+template <typename T>
+int shard_phase(int phase, const T* keys, int64_t us, int64_t rs, const float* center, float key_scale,
+                const float* W, const float* b, const __half* Wh, const float* wn, int U, int64_t N, int F,
+                BuildWs ws, FastWs fw, long long local_count, long long global_count, double sample_frac,
+                long long flat_base, int* lens,
+                int* offsets, int* ids, int64_t ids_stride, long long token_base, float slack_frac, int slack_min,
+                const long long* all_keys, const int* key_counts, int P, int64_t key_cap, const long long* need,
+                int* sample_info, int* status, cudaStream_t st) {
+    const int nft = (F + kTcFeat - 1) / kTcFeat;
+    const int nblocks = (int)((N + 127) / 128);
+    if (phase == 0) {
+        // The sample is planned on this shard's own share of the budget.
+        int ns = 0;
+        const TileSample plan = sample_plan(N, F, local_count, &ns);
+        build_tiles_kernel<<<nft, 256, 0, st>>>(Wh, wn, b, F, fw.tiles, fw.sides, status);
+        PK_CHECK_LAUNCH();
+        cudaFuncSetAttribute(build_tile_tc_kernel<0, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(0));
+        build_tile_tc_kernel<0, T><<<dim3(ns, U), kTcThreads, tc_smem(0), st>>>(
+            keys, us, rs, N, center, key_scale, F, fw, plan, status);
+        PK_CHECK_LAUNCH();
+        set_ints_kernel<<<1, 1, 0, st>>>(sample_info, ns, plan.ft_stride);
+        PK_CHECK_LAUNCH();
+        return PK_OK;
+    }
+    if (phase == 1) {
+        const TileSample none = {1, 1};
+        build_floor_kernel<<<U, 32, 0, st>>>(fw, global_count, sample_frac);
+        PK_CHECK_LAUNCH();
+        cudaFuncSetAttribute(build_tile_tc_kernel<1, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(1));
+        build_tile_tc_kernel<1, T><<<dim3(nblocks, U), kTcThreads, tc_smem(1), st>>>(
+            keys, us, rs, N, center, key_scale, F, fw, none, status);
+        PK_CHECK_LAUNCH();
+        return PK_OK;
+    }
+    if (phase == 2) {
+        build_fast_cut_kernel<<<U, 32, 0, st>>>(fw, global_count, status);
+        PK_CHECK_LAUNCH();
+        build_classify_kernel<<<dim3(256, U), 256, 0, st>>>(F, ws, fw, lens, status);
+        PK_CHECK_LAUNCH();
+        const size_t esz = sizeof(T);
+        const int vec = ((uint64_t)keys % 16 == 0 && (us * (int64_t)esz) % 16 == 0 && (rs * (int64_t)esz) % 16 == 0)
+                            ? 1 : 0;
+        build_exact_kernel<T><<<dim3(512, U), 256, 0, st>>>(keys, us, rs, center, key_scale, W, b, F, ws, fw, lens,
+                                                            status, vec, flat_base);
+        PK_CHECK_LAUNCH();
+        return PK_OK;
+    }
+    // phase 3: the global resolve, then CSR.
+    build_shard_resolve_kernel<<<U, 1024, 0, st>>>(all_keys, key_counts, P, key_cap, need, flat_base,
+                                                   flat_base + (long long)N * F, ws, fw, F, lens, status);
+    PK_CHECK_LAUNCH();
+    build_offsets_kernel<<<U, 1024, 0, st>>>(lens, F, slack_frac, slack_min, offsets, ids_stride, status);
+    PK_CHECK_LAUNCH();
+    build_scatter_kernel<<<dim3(64, U), 256, 0, st>>>(ws, F, offsets, ids, ids_stride, token_base);
+    PK_CHECK_LAUNCH();
+    return sort_buckets(ids, ids_stride, offsets, nullptr, lens, U, F, status, st);
+}
+
+extern "C" int pk_build_shard_phase(int phase, uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride,
+                                    uint64_t center, float key_scale, uint64_t w_enc, uint64_t b_enc, uint64_t w_half,
+                                    uint64_t w_norm, int U, int64_t N, int d, int F, int key_mean,
+                                    int64_t member_capacity, int64_t boundary_capacity, uint64_t workspace,
+                                    uint64_t workspace_bytes,
+                                    long long global_count, double sample_frac, int64_t flat_base, uint64_t lens,
+                                    uint64_t offsets, uint64_t ids, int64_t ids_stride, int64_t token_base,
+                                    float slack_frac, int slack_min, uint64_t all_keys, uint64_t key_counts, int P,
+                                    int64_t key_cap, uint64_t need, uint64_t sample_info, uint64_t status,
+                                    uint64_t stream) {
+    if (phase < 0 || phase > 3) return PK_ERR_ARG;
+    if (U < 1 || N < 1 || F < 1 || key_mean < 1 || !(key_scale > 0.f) || slack_frac < 0.f || slack_min < 0)
+        return PK_ERR_ARG;
+    if (d != kBD) return PK_ERR_UNSUPPORTED;
+    if (!keys || !center || !w_enc || !b_enc || !w_half || !w_norm || !lens || !workspace || !status)
+        return PK_ERR_ARG;
+    if (w_half % 16 || row_stride < d || N > INT32_MAX || global_count < 1 || flat_base < 0) return PK_ERR_ARG;
+    if (flat_base + (long long)N * F >= (1ll << 36)) return PK_ERR_ARG;
+    if (boundary_capacity < 1 || member_capacity < 1) return PK_ERR_ARG;
+    if (workspace_bytes < pk_build_shard_workspace_bytes(U, N, F, member_capacity, boundary_capacity))
+        return PK_ERR_WORKSPACE;
+    if (phase == 0 && !sample_info) return PK_ERR_ARG;
+    if (phase == 3 && (!offsets || !ids || !all_keys || !key_counts || P < 1 || key_cap < 1 || !need ||
+                       ids_stride < 1 || token_base < 0 || token_base + N > INT32_MAX))
+        return PK_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int64_t mcap = member_capacity;
+    BuildWs ws = carve((void*)workspace, U, F, mcap, boundary_capacity);
+    void* fbase = (char*)workspace + carve_bytes(U, F, mcap, boundary_capacity);
+    FastWs fw = carve_fast(fbase, U, boundary_capacity, F);
+    if (phase == 0) {
+        cudaMemsetAsync((void*)workspace, 0, counters_bytes(U, F), st);
+        cudaMemsetAsync(fbase, 0, fast_counters_bytes(U), st);
+        cudaMemsetAsync((void*)lens, 0, (size_t)U * F * sizeof(int), st);
+    }
+    if (dtype == PK_BF16)
+        return shard_phase(phase, (const __nv_bfloat16*)keys, unit_stride, row_stride, (const float*)center,
+                           key_scale, (const float*)w_enc, (const float*)b_enc, (const __half*)w_half,
+                           (const float*)w_norm, U, N, F, ws, fw, (long long)N * key_mean, global_count, sample_frac,
+                           flat_base, (int*)lens,
+                           (int*)offsets, (int*)ids, ids_stride, token_base, slack_frac, slack_min,
+                           (const long long*)all_keys, (const int*)key_counts, P, key_cap, (const long long*)need,
+                           (int*)sample_info, (int*)status, st);
+    if (dtype == PK_F32)
+        return shard_phase(phase, (const float*)keys, unit_stride, row_stride, (const float*)center, key_scale,
+                           (const float*)w_enc, (const float*)b_enc, (const __half*)w_half, (const float*)w_norm, U, N,
+                           F, ws, fw, (long long)N * key_mean, global_count, sample_frac, flat_base, (int*)lens,
+                           (int*)offsets, (int*)ids,
+                           ids_stride, token_base, slack_frac, slack_min, (const long long*)all_keys,
+                           (const int*)key_counts, P, key_cap, (const long long*)need, (int*)sample_info,
+                           (int*)status, st);
+    return PK_ERR_ARG;
+}
+
+extern "C" int pk_key_center_chunks(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stride, int U,
+                                    int64_t N, int d, int64_t N_total, uint64_t out, uint64_t stream) {
+    if (U < 1 || N < 1 || d < 1 || N_total < N || !keys || !out || row_stride < d) return PK_ERR_ARG;
+    int lp = ceil_log2_i64(N_total) / 4;
+    if (lp < 4) lp = 4;
+    const int64_t chunk = (int64_t)1 << (3 * lp);
+    if (N % chunk) return PK_ERR_ARG;   // the shard holds whole chunks
+    const int64_t nchunks = N / chunk;
+    cudaStream_t st = (cudaStream_t)stream;
+    dim3 grid((d + 31) / 32, U);
+    if (dtype == PK_BF16)
+        center_chunks_kernel<__nv_bfloat16><<<grid, 1024, 0, st>>>((const __nv_bfloat16*)keys, unit_stride,
+                                                                   row_stride, nchunks, lp, d, (float*)out);
+    else if (dtype == PK_F32)
+        center_chunks_kernel<float><<<grid, 1024, 0, st>>>((const float*)keys, unit_stride, row_stride, nchunks, lp,
+                                                           d, (float*)out);
+    else
+        return PK_ERR_ARG;
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}
+
+extern "C" int64_t pk_key_center_chunk_rows(int64_t N_total) {
+    int lp = ceil_log2_i64(N_total) / 4;
+    if (lp < 4) lp = 4;
+    return (int64_t)1 << (3 * lp);
 }

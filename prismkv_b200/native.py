@@ -54,11 +54,16 @@ SIGNATURES = {
     "pk_summarize": ("PillPPPliiiPPP", ctypes.c_int),
     "pk_append_workspace_bytes": ("iliiil", ctypes.c_size_t),
     "pk_append_index": ("PilllPfPPPPiiiilPPPlPPlPPPP", ctypes.c_int),
+    "pk_build_shard_layout": ("ilillP", ctypes.c_int),
+    "pk_build_shard_workspace_bytes": ("ilill", ctypes.c_size_t),
+    "pk_build_shard_phase": ("iPillPfPPPPiliiillPPldlPPPllfiPPilPPPP", ctypes.c_int),
+    "pk_key_center_chunks": ("PillililPP", ctypes.c_int),
+    "pk_key_center_chunk_rows": ("l", ctypes.c_int64),
 }
-_CT = {"P": ctypes.c_uint64, "i": ctypes.c_int, "l": ctypes.c_int64, "f": ctypes.c_float}
+_CT = {"P": ctypes.c_uint64, "i": ctypes.c_int, "l": ctypes.c_int64, "f": ctypes.c_float, "d": ctypes.c_double}
 # Entry points that take the stream as their last argument.
 _ASYNC = {n for n, (c, r) in SIGNATURES.items() if r is ctypes.c_int and c.endswith("P") and n not in
-          ("pk_version", "pk_supported_head_dim")}
+          ("pk_version", "pk_supported_head_dim", "pk_build_shard_layout")}
 
 _lib = None
 
@@ -108,7 +113,7 @@ def call(name: str, *args) -> None:
     for a, c in zip(args, codes):
         if c == "P":
             conv.append(addr(a))
-        elif c == "f":
+        elif c in ("f", "d"):
             conv.append(float(a))
         else:
             conv.append(int(a))

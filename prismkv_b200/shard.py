@@ -19,6 +19,8 @@ There is no other collective on the path.
 """
 from __future__ import annotations
 
+import math
+
 import torch
 import torch.distributed as dist
 
@@ -136,3 +138,209 @@ class ShardedDecode:
 
     def check(self) -> None:
         self.op.check()
+
+
+# ---------------------------------------------------------------------------
+# Sequence-sharded build with the exact global BatchTopK
+# ---------------------------------------------------------------------------
+
+class ShardBuilder:
+    """This shard's side of the sequence-sharded build (pk_build_shard_phase):
+    keys [U, N, d] of tokens [lo, lo + N) of a sequence of N_total tokens,
+    with the global center.  The phases are driven by ``drive_build`` with the
+    collectives between them; the result is the shard-local index (token ids
+    relative to lo) whose memberships are exactly those of the whole
+    sequence's index cut at the shard (the reference's one-device build)."""
+
+    def __init__(self, keys: torch.Tensor, sae, key_scale: float, *, lo: int, N_total: int, center: torch.Tensor,
+                 slack_frac: float = 0.25, slack_min: int = 4, boundary_capacity: int | None = None,
+                 workspace: nv.Workspace | None = None):
+        from .index import SAEParams, _unit_view
+        keys, U, N, d, us, rs = _unit_view(keys)
+        self.keys, self.U, self.N, self.d, self.us, self.rs = keys, U, N, d, us, rs
+        self.sae = SAEParams.of(sae, keys.device)
+        self.F = self.sae.features
+        self.key_scale = float(key_scale)
+        self.lo, self.N_total = int(lo), int(N_total)
+        self.global_count = self.N_total * self.sae.key_mean
+        self.slack_frac, self.slack_min = float(slack_frac), int(slack_min)
+        self.bcap = int(boundary_capacity or (4 * N * self.sae.key_mean + 65536))
+        # Under the global threshold a shard may hold more than its own
+        # N * key_mean members: the member list is sized for all of them.
+        self.mcap = int(min(self.global_count, N * self.F))
+        self.ws = workspace or nv.Workspace(keys.device)
+        dev = keys.device
+        self.index = DeviceIndex(U, self.F, d, 1, dev, moments=False)
+        self.index.slack_frac, self.index.slack_min = self.slack_frac, self.slack_min
+        self.index.center.copy_(torch.as_tensor(center, dtype=torch.float32, device=dev).reshape(-1, d).expand(U, d))
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.sample_info = torch.zeros(2, dtype=torch.int32, device=dev)
+        self._alloc()
+
+    def _alloc(self):
+        U, N, F = self.U, self.N, self.F
+        self.nbytes = int(nv.query("pk_build_shard_workspace_bytes", U, N, F, self.mcap, self.bcap))
+        self.buf = self.ws.get(("shard_build", U, N, F, self.mcap, self.bcap), self.nbytes)
+        lay = torch.zeros(8, dtype=torch.int64)
+        rc = nv.query("pk_build_shard_layout", U, N, F, self.mcap, self.bcap, lay.data_ptr())
+        if rc:
+            raise RuntimeError(f"pk_build_shard_layout: argument error {rc}")
+        o = lay.tolist()
+
+        def view(k, n, dtype):
+            nb = n * torch.empty(0, dtype=dtype).element_size()
+            return self.buf[o[k]:o[k] + nb].view(dtype)
+
+        self.histS = view(0, U * 8192, torch.int32).view(U, 8192)
+        self.histL = view(1, U * 1024, torch.int32).view(U, 1024)
+        self.histU = view(2, U * 1024, torch.int32).view(U, 1024)
+        self.n_members = view(3, U, torch.int32)
+        self.n_boundary = view(4, U, torch.int32)
+        self.bkeys = view(5, U * self.bcap, torch.int64).view(U, self.bcap)
+
+    def _phase(self, phase, *, sample_frac=0.0, all_keys=None, key_counts=None, P=1, key_cap=1, need=None):
+        wh, wn = self.sae.prepared_half()
+        idx = self.index
+        nv.call("pk_build_shard_phase", phase, self.keys, nv.dtype_code(self.keys), self.us, self.rs, idx.center,
+                self.key_scale, self.sae.W_enc, self.sae.b_enc, wh, wn, self.U, self.N, self.d, self.F,
+                self.sae.key_mean, self.mcap, self.bcap, self.buf, self.nbytes, self.global_count, float(sample_frac),
+                self.lo * self.F, idx.lens, idx.offsets, idx.ids, idx.ids.stride(0), 0, self.slack_frac,
+                self.slack_min, all_keys, key_counts, P, key_cap, need, self.sample_info, self.status)
+
+    def sample(self) -> torch.Tensor:
+        self.status.zero_()
+        self._phase(0)
+        return self.histS
+
+    def sample_fraction(self) -> float:
+        """This shard's share of the sampled fraction of all N_total * F entries."""
+        ns, fts = self.sample_info.tolist()
+        return min(ns * 128, self.N) / self.N_total / max(1, fts)
+
+    def bounds(self, sample_frac: float):
+        self._phase(1, sample_frac=sample_frac)
+        return self.histL, self.histU
+
+    def classify(self):
+        self._phase(2)
+        return self.n_members, self.n_boundary, self.bkeys
+
+    def finish(self, all_keys: torch.Tensor, key_counts: torch.Tensor, need: torch.Tensor) -> DeviceIndex:
+        P, U, key_cap = all_keys.shape
+        # CSR room for this shard's members: those decided so far plus, at
+        # most, all of its boundary keys, each bucket with its slack.
+        ub = int((self.n_members.long() + self.n_boundary.long()).max().item())
+        cap = ub + int(math.ceil(ub * self.slack_frac)) + self.F * (self.slack_min + 1) + 64
+        self.index.ids = torch.zeros(U, max(1, cap), dtype=torch.int32, device=self.keys.device)
+        self._phase(3, all_keys=all_keys, key_counts=key_counts, P=P, key_cap=key_cap, need=need)
+        self.index.history = self.N
+        self.index.encode_path = "bounds"
+        return self.index
+
+
+def drive_build(builders, allreduce_sum, allreduce_max, allgather):
+    """Runs the phases of the local builders (one per rank, or every shard
+    when emulated in one process) with the given collectives over the lists
+    of per-builder tensors: allreduce_sum / allreduce_max in place,
+    allgather -> [P, ...] stacked in rank order."""
+    def check(what):
+        st = [b.status for b in builders]
+        allreduce_max(st)
+        v = int(st[0].item())
+        if v:
+            msgs = [m for bit, m in nv.STATUS_BITS.items() if v & bit]
+            raise RuntimeError(f"sharded build ({what}): " + "; ".join(msgs))
+
+    allreduce_sum([b.sample() for b in builders])
+    fr = [torch.tensor([b.sample_fraction()], dtype=torch.float64, device=b.keys.device) for b in builders]
+    allreduce_sum(fr)
+    check("sample")
+    hs = [b.bounds(float(fr[0].item())) for b in builders]
+    allreduce_sum([h[0] for h in hs])
+    allreduce_sum([h[1] for h in hs])
+    check("bounds")
+    cl = [b.classify() for b in builders]
+    check("classify")
+    members = [c[0].long().clone() for c in cl]
+    allreduce_sum(members)
+    caps = [c[1].max().long().reshape(1).clone() for c in cl]
+    allreduce_max(caps)
+    key_cap = max(1, min(int(caps[0].item()), min(b.bcap for b in builders)))
+    all_keys = allgather([c[2][:, :key_cap].contiguous() for c in cl])
+    counts = allgather([c[1].clone() for c in cl])
+    out = []
+    for b, m in zip(builders, members):
+        need = (b.global_count - m).contiguous()
+        out.append(b.finish(all_keys, counts, need))
+    check("finish")
+    return out
+
+
+def global_center(keys_shards, N_total: int, gather=None) -> torch.Tensor:
+    """Key center [U, d] of a sequence split into shards of whole cascade
+    chunks (pk_key_center_chunks): the in-order fp32 sum of all chunk sums
+    over N_total, bit-identical to the one-device torch-order mean.
+    ``keys_shards``: this rank's keys [U, N, d] (with ``gather`` an
+    all-gather over ranks) or the list of every shard's keys in order."""
+    from .index import _unit_view
+    local = keys_shards if isinstance(keys_shards, (list, tuple)) else [keys_shards]
+    rows = int(nv.query("pk_key_center_chunk_rows", int(N_total)))
+    if N_total % rows:
+        raise ValueError(f"the sequence length must be a multiple of the cascade chunk ({rows} rows)")
+    parts = []
+    for k in local:
+        k, U, N, d, us, rs = _unit_view(k)
+        if N % rows:
+            raise ValueError(f"every shard must hold whole cascade chunks of {rows} rows")
+        out = torch.empty(U, N // rows, d, dtype=torch.float32, device=k.device)
+        nv.call("pk_key_center_chunks", k, nv.dtype_code(k), us, rs, U, N, d, int(N_total), out)
+        parts.append(out)
+    chunks = torch.cat(parts, 1) if gather is None else torch.cat(list(gather(parts[0]).unbind(0)), 1)
+    acc = torch.zeros_like(chunks[:, 0])
+    for c in range(chunks.shape[1]):
+        acc = acc + chunks[:, c]
+    return acc / float(N_total)
+
+
+def build_sharded(keys: torch.Tensor, sae, key_scale: float, *, lo: int, N_total: int, group=None, center=None,
+                  slack_frac: float = 0.25, slack_min: int = 4, workspace: nv.Workspace | None = None) -> DeviceIndex:
+    """This rank's index of tokens [lo, lo + N) under the whole sequence's
+    exact BatchTopK (one SUM all-reduce of the sampled histogram, of the
+    bound histograms and of the member counts, one MAX all-reduce of the
+    status and key counts, one all-gather of the boundary keys).  The center
+    defaults to the global key mean (global_center, all-gathered chunk sums).
+    Without an initialised process group the shard is the whole sequence."""
+    init = dist.is_initialized()
+    P = dist.get_world_size(group) if init else 1
+
+    def gather(t):
+        out = torch.empty((P,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        return _gather(t, out, group)
+
+    if center is None:
+        center = global_center(keys, N_total, gather if P > 1 else None)
+    b = ShardBuilder(keys, sae, key_scale, lo=lo, N_total=N_total, center=center, slack_frac=slack_frac,
+                     slack_min=slack_min, workspace=workspace)
+
+    def red(ts, op):
+        if P > 1:
+            dist.all_reduce(ts[0], op=op, group=group)
+
+    def allgather(ts):
+        t = ts[0]
+        out = torch.empty((P,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        return _gather(t, out, group)
+
+    return drive_build([b], lambda ts: red(ts, dist.ReduceOp.SUM), lambda ts: red(ts, dist.ReduceOp.MAX),
+                       allgather)[0]
+
+
+def _gather(t: torch.Tensor, out: torch.Tensor, group=None) -> torch.Tensor:
+    P = out.shape[0]
+    if P == 1:
+        out[0].copy_(t)
+    elif dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, t.contiguous(), group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), t.contiguous(), group=group)
+    return out
