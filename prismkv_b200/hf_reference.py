@@ -68,6 +68,8 @@ class _Batch:
         self.index: DeviceIndex | None = None
         self.op: SparseDecode | None = None
         self.dense_ids = None
+        self.len_dev = None   # rows per unit (history + tail), read by the attention on the device
+        self.kv = None        # the layer's K/V cache tensors of the last decode step
 
     def rows(self, t: torch.Tensor) -> torch.Tensor:
         """t[0, groups] ([B, H_kv, T, d] -> [U, T, d]); a view for a run of groups."""
@@ -141,6 +143,7 @@ class HFReference:
     # ----------------------------------------------------------- lifecycle
     def begin_request(self):
         self.prefix_lengths, self.layers, self._records = {}, {}, []
+        self._graph_total = None
 
     @contextmanager
     def prefill(self):
@@ -211,14 +214,25 @@ class HFReference:
             raise NotImplementedError("sliding-window/soft-capped attention is outside this adapter")
         if kwargs.get("dropout", 0) != 0:
             raise ValueError("inference only: disable dropout")
-        layer, total, steps = module.layer_idx, k.shape[-2], q.shape[-2]
-        if attention_mask is not None:
-            if attention_mask.ndim != 4:
-                raise NotImplementedError("padding/arbitrary attention masks are unsupported")
-            last = attention_mask[..., -1, :total]
-            invalid = ~last if last.dtype == torch.bool else last != 0
-            if bool(invalid.any()):
-                raise NotImplementedError("padding/arbitrary attention masks are unsupported")
+        layer, steps = module.layer_idx, q.shape[-2]
+        graph = self._graph_total is not None
+        if graph:
+            # Replayed decode (GraphDecoder): the length comes from the host,
+            # nothing is read back from the device while capturing.
+            total = self._graph_total
+        else:
+            total = k.shape[-2]
+            if attention_mask is not None:
+                if attention_mask.ndim != 4:
+                    raise NotImplementedError("padding/arbitrary attention masks are unsupported")
+                # The last row must see a prefix of the cache: all of it (a
+                # growing cache) or its first `total` slots (a static cache).
+                last = attention_mask[..., -1, :total].reshape(-1, total)[0]
+                visible = last if last.dtype == torch.bool else last == 0
+                n = int(visible.sum().item())
+                if n == 0 or not bool(visible[:n].all()):
+                    raise NotImplementedError("padding/arbitrary attention masks are unsupported")
+                total = n
         is_prefill = self.force_prefill or layer not in self.prefix_lengths or steps > 1
         if is_prefill:
             self.prefix_lengths[layer] = total
@@ -245,19 +259,25 @@ class HFReference:
         for batch in self._batches(layer, groups):
             Qb = (qh[batch.span] if batch.span is not None else qh[batch.groups]).contiguous()
             Kb, Vb = batch.rows(k), batch.rows(v)
+            batch.kv = (k, v)
             if self.mode == "all_read":
                 history = self.prefix_lengths[layer]
                 out, count, raw, nfeat = self._dense(batch, Qb, Kb, Vb, history, total, ws)
             else:
-                history = self._advance(batch, layer, per_group, Kb, total, ws)
+                if not graph:
+                    history = self._advance(batch, layer, per_group, Kb, total, ws)
+                    batch.len_dev.fill_(total)
+                else:
+                    history = batch.index.history
                 op = batch.op
                 op.route(Qb)
-                out = op.attention(Qb, Kb, Vb, length=total)
+                out = op.attention(Qb, Kb, Vb, length=batch.len_dev)
                 count, raw, nfeat = op.count, op.raw, op.n_features
             for i, g in enumerate(batch.groups):
                 answer[0, 0, g * per_group:(g + 1) * per_group] = out[i]
-            self._records.append((layer, tuple(batch.groups), history, total - history, count.clone(), raw.clone(),
-                                  nfeat.clone()))
+            if not graph:
+                self._records.append((layer, tuple(batch.groups), history, total - history, count.clone(),
+                                      raw.clone(), nfeat.clone()))
         return answer, None
 
     def _advance(self, batch: _Batch, layer: int, per_group: int, Kb: torch.Tensor, total: int,
@@ -284,6 +304,7 @@ class HFReference:
                                     query_scale=float(enc.query_scale), query_topk=self.selected_buckets,
                                     unique_cap=self.unique_cap, max_history=index.history + 8 * self.update_interval,
                                     workspace=ws)
+            batch.len_dev = torch.zeros(len(batch.groups), dtype=torch.int32, device=Kb.device)
         elif grew:
             op.sync_history()
         return index.history
@@ -306,3 +327,85 @@ class HFReference:
                 count, hist, length, U, G, d, S, ws.get(("av", U, G, d, S), nbytes), nbytes, out, None)
         zeros = torch.zeros(U, dtype=torch.int64, device=Qb.device)
         return out, count, torch.full((U,), history, dtype=torch.int64, device=Qb.device), zeros
+
+
+class GraphDecoder:
+    """One-token decode of a model over a transformers StaticCache, replayed
+    as one CUDA graph per step (the reference's serving loop,
+    kernels/cuda_sm90/serving.py:71-125: a captured decode step whose inputs
+    are refreshed before each replay).
+
+    The first call runs eagerly (building every layer's index from the
+    prefix) and then captures the step.  Before each replay the host writes
+    the token and its position, indexes complete ``update_interval`` blocks
+    (appends run outside the graph; the index and operator update in place),
+    and refreshes the per-unit lengths.  If an append had to reallocate an
+    index, the step is captured again.  Records are not kept for replayed
+    steps.  mode='sparse' only."""
+
+    def __init__(self, session: "HFReference", model, cache):
+        if session.mode != "sparse":
+            raise ValueError("graph decode needs mode='sparse'")
+        self.s, self.model, self.cache = session, model, cache
+        dev = next(model.parameters()).device
+        self.tok = torch.zeros(1, 1, dtype=torch.long, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.long, device=dev)
+        self.graph = None
+        self.logits = None
+        self._ptrs = None
+        self.captures = 0
+        self.replays = 0
+
+    def _buffers(self):
+        return [(b.index.ids.data_ptr(), b.index.offsets.data_ptr(), b.index.lens.data_ptr(),
+                 b.op.ids.data_ptr()) for st in self.s.layers.values() for b in st]
+
+    @torch.no_grad()
+    def step(self, token: int, position: int) -> torch.Tensor:
+        """Logits of the next token after ``token`` at cache slot
+        ``position`` (the positions continue the prefilled cache)."""
+        s = self.s
+        total = position + 1
+        if self.graph is not None:
+            ws = None
+            for layer, st in s.layers.items():
+                for b in st:
+                    k, _ = b.kv
+                    ws = ws or s._workspace(k.device)
+                    s._advance(b, layer, b.op.G, b.rows(k), total, ws)
+                    b.len_dev.fill_(total)
+            if self._buffers() != self._ptrs:
+                self.graph = None    # an index was reallocated: capture again
+        if self.graph is None:
+            self.tok.fill_(token)
+            self.pos.fill_(position)
+            out = self.model(input_ids=self.tok, past_key_values=self.cache, cache_position=self.pos, use_cache=True)
+            eager = out.logits[:, -1].clone()
+            self._capture(total + 1)
+            return eager
+        self.tok.fill_(token)
+        self.pos.fill_(position)
+        s._graph_total = total
+        try:
+            self.graph.replay()
+        finally:
+            s._graph_total = None
+        self.replays += 1
+        return self.logits[:, -1]
+
+    def _capture(self, total_next: int):
+        s = self.s
+        self.graph = torch.cuda.CUDAGraph()
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        s._graph_total = total_next
+        try:
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(self.graph, stream=stream):
+                    self.logits = self.model(input_ids=self.tok, past_key_values=self.cache,
+                                             cache_position=self.pos, use_cache=True).logits
+        finally:
+            s._graph_total = None
+        torch.cuda.current_stream().wait_stream(stream)
+        self._ptrs = self._buffers()
+        self.captures += 1

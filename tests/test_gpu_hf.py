@@ -148,3 +148,60 @@ def test_sparse_decode_matches_oracle(pk, oracle, router, shared, kind):
             ref = orc.attend(Q, K, V, want, idx.history)
             assert rel_l2(out[g * per_group:(g + 1) * per_group], ref) < TOL_F32
     assert appended
+
+
+def _run_static(model, encs, prompt, steps, ui, graph):
+    """Greedy decode over a StaticCache, eager or replayed (GraphDecoder)."""
+    from transformers import StaticCache
+    from prismkv_b200.hf_reference import GraphDecoder, HFReference
+    s = HFReference(model, encs, router="q_activation", selected_buckets=8, update_interval=ui)
+    cache = StaticCache(config=model.config, max_cache_len=256)
+    n = prompt.shape[1]
+    logits = []
+    try:
+        with torch.no_grad():
+            out = model(input_ids=prompt, past_key_values=cache, cache_position=torch.arange(n, device="cuda"),
+                        use_cache=True)
+            tok = int(out.logits[0, -1].argmax())
+            gd = GraphDecoder(s, model, cache) if graph else None
+            for i in range(steps):
+                pos = n + i
+                if graph:
+                    lg = gd.step(tok, pos).clone()
+                else:
+                    o = model(input_ids=torch.tensor([[tok]], device="cuda"), past_key_values=cache,
+                              cache_position=torch.tensor([pos], device="cuda"), use_cache=True)
+                    lg = o.logits[:, -1].clone()
+                logits.append(lg.float().cpu())
+                tok = int(lg.argmax())
+            appended = any(b.index.history > n for st in s.layers.values() for b in st)
+            if graph:
+                # Steps replay one captured graph (a new capture only when an
+                # append reallocated an index).
+                assert gd.captures <= 3 and gd.replays >= steps - 3, (gd.captures, gd.replays)
+    finally:
+        s.close()
+    return logits, appended
+
+
+def test_static_cache_and_graph_decode(pk):
+    """A static cache (full-length K/V, the length from the mask) decodes as
+    the growing cache does, and the replayed CUDA-graph step (appends between
+    replays) reproduces the eager static-cache steps."""
+    model = tiny_model("qwen3")
+    encs = make_encoders(2, 2, 256, shared=False)
+    prompt = torch.randint(0, 96, (1, 150), generator=torch.Generator().manual_seed(9)).cuda()
+    steps, ui = 30, 16
+    from prismkv_b200.hf_reference import HFReference
+    s = HFReference(model, encs, router="q_activation", selected_buckets=8, update_interval=ui)
+    try:
+        dynamic = decode(model, prompt, steps)
+    finally:
+        s.close()
+    eager, app_e = _run_static(model, encs, prompt, steps, ui, graph=False)
+    graphed, app_g = _run_static(model, encs, prompt, steps, ui, graph=True)
+    assert app_e and app_g
+    for a, b in zip(eager, dynamic):
+        assert rel_l2(a.numpy(), b.numpy()) < 1e-5
+    for a, b in zip(graphed, eager):
+        assert rel_l2(a.numpy(), b.numpy()) < 1e-6
