@@ -3,14 +3,17 @@
 // (src/prismkv/core.py:170-183), split across CTAs along the row list with an
 // exact log-sum-exp merge (the split-KV scheme of kernels/ppu_8b/av_tuned.cu).
 //
-// bf16 path: the CTA gathers 64 K rows and 64 V rows per pipeline stage with
-// 16-byte cp.async (rows addressed through the id list), three stages deep;
-// each warp runs QK^T and PV for 16 rows with mma.sync m16n8k16 (the G heads
-// fill the M=16 rows), keeps an fp32 online softmax, and feeds P to the PV
-// product in bf16.  The S split CTAs of a unit form a thread-block cluster
-// and merge their states through distributed shared memory (S <= 16); for
-// more splits, the last CTA of a unit to finish merges partials from global
-// memory.
+// bf16 path: a CTA of four warps streams its split's rows in tiles of 64 K
+// rows and 64 V rows, three stages deep.  Each warp gathers its own 16 rows of
+// every tile with 16-byte cp.async (rows addressed through the id list) and
+// computes on them alone, so the warps pipeline independently (no CTA barrier
+// per tile).  For G <= 8 heads the warp's 16 key rows fill the M = 16 of
+// mma.sync m16n8k16 and the heads its N = 8 (S^T = K Q^T, then O^T += V^T P^T
+// with P^T formed by movmatrix); for 9..16 heads the heads fill M instead.
+// Softmax is online in fp32 and P enters the PV product in bf16.  The S split
+// CTAs of a unit form a thread-block cluster and merge their states through
+// distributed shared memory; above 8 splits the last CTA of a unit to finish
+// merges partials from global memory.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -81,6 +84,12 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&t);
+}
+// Transpose of an 8x8 16-bit matrix held as the warp's mma fragment.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
+    return y;
 }
 
 // Byte offset of (row, 16-byte chunk) inside a 64-row x 256-byte tile, the
@@ -274,9 +283,259 @@ __device__ void av_finish_cluster(const AvParams& p, int u, int s, const float* 
     cluster.sync();
 }
 
+
+// Push merge (used with the cluster launch of sparse_av_bf16_kernel): output
+// element e = h*D + d of the unit belongs to CTA e / per of the cluster.
+// Each CTA combines its warps' states, stores its (o) of every element and
+// its (m, l) of every head into the owning CTA's receive buffer (pbuf:
+// o_in[S][per], then ml_in[S][G][2]), and after one cluster barrier merges
+// the S states of its own elements from its own shared memory, in split
+// order: the arithmetic of av_finish_cluster, with one barrier fewer and
+// remote stores instead of remote loads.  The caller arrived on the cluster
+// barrier at kernel start; the wait here, before the first remote store,
+// makes sure every CTA of the cluster is running.
+template <typename OT>
+__device__ void av_finish_push(const AvParams& p, int u, int s, const float* red, int nwarps, float* ml_loc,
+                               float* pbuf) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int G = p.G, S = p.S, tid = threadIdx.x;
+    const int GD = G * kAvD, per = (GD + S - 1) / S;
+    float* o_in = pbuf;
+    float* ml_in = pbuf + S * per;
+    const float* rm = red;
+    const float* rl = red + nwarps * kAvMaxG;
+    const float* ro = red + 2 * nwarps * kAvMaxG;
+    asm volatile("barrier.cluster.wait;\n" ::: "memory");
+    const int dim = tid;  // kAvThreads == kAvD
+    for (int h = 0; h < G; ++h) {
+        float M = -INFINITY;
+        for (int w = 0; w < nwarps; ++w) M = fmaxf(M, rm[w * kAvMaxG + h]);
+        float L = 0.f, O = 0.f;
+        for (int w = 0; w < nwarps; ++w) {
+            const float mw = rm[w * kAvMaxG + h];
+            const float sc = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+            L = fmaf(sc, rl[w * kAvMaxG + h], L);
+            O = fmaf(sc, ro[(w * kAvMaxG + h) * kAvD + dim], O);
+        }
+        if (dim == 0) { ml_loc[2 * h] = M; ml_loc[2 * h + 1] = L; }
+        const int e = h * kAvD + dim, owner = e / per;
+        float* dst = cluster.map_shared_rank(o_in, owner);
+        dst[s * per + (e - owner * per)] = O;
+    }
+    __syncthreads();
+    for (int i = tid; i < 2 * G * S; i += kAvThreads) {
+        const int r = i / (2 * G), j = i % (2 * G);
+        float* dst = cluster.map_shared_rank(ml_in, r);
+        dst[s * 2 * G + j] = ml_loc[j];
+    }
+    cluster.sync();
+    for (int jj = tid; jj < per && s * per + jj < GD; jj += kAvThreads) {
+        const int e = s * per + jj, h = e / kAvD, d = e % kAvD;
+        float M = -INFINITY;
+        for (int j = 0; j < S; ++j) M = fmaxf(M, ml_in[(j * G + h) * 2]);
+        float L = 0.f, O = 0.f;
+        for (int j = 0; j < S; ++j) {
+            const float mj = ml_in[(j * G + h) * 2];
+            const float sc = (mj == -INFINITY) ? 0.f : exp2f(mj - M);
+            L = fmaf(sc, ml_in[(j * G + h) * 2 + 1], L);
+            O = fmaf(sc, o_in[j * per + jj], O);
+        }
+        const int64_t uh = (int64_t)u * G + h;
+        if (p.xpart) {
+            float* xp = p.xpart + uh * (kAvD + 2);
+            if (d == 0) { xp[0] = M == -INFINITY ? -INFINITY : M / kLog2e; xp[1] = L; }
+            xp[2 + d] = O;
+        } else {
+            OT* o = (OT*)p.out + uh * kAvD;
+            o[d] = to_out<OT>(L > 0.f ? O / L : 0.f);
+        }
+    }
+}
+
+// Receive buffer of av_finish_push, in floats.
+__host__ __device__ constexpr int av_push_floats(int G, int S) { return S * ((G * kAvD + S - 1) / S) + 2 * G * S; }
+
+// G <= 8 heads.  Warp w owns rows [16w, 16w + 16) of every tile: it copies
+// them in and computes on them, so each warp's stages are its own.
+template <bool kCluster>
+__global__ void __launch_bounds__(kAvThreads, 2)
+sparse_av_bf16_kernel(AvParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int s = blockIdx.x, u = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = p.G;
+    if constexpr (kCluster) asm volatile("barrier.cluster.arrive.relaxed;\n" ::: "memory");
+    const int H = p.history[u], len = p.length[u], cnt = p.count[u];
+    const int rows = len > 0 ? cnt + max(len - H, 0) : 0;
+    // Whole tiles split evenly: the splits differ by at most one tile.
+    const int nt_all = (rows + kAvTile - 1) / kAvTile;
+    const int r0 = min(rows, (int)((int64_t)s * nt_all / p.S) * kAvTile);
+    const int r1 = min(rows, (int)((int64_t)(s + 1) * nt_all / p.S) * kAvTile);
+    const int ntiles = (r1 - r0 + kAvTile - 1) / kAvTile;
+    const int64_t ubase = (int64_t)(u / p.kv_heads) * p.kv_batch_stride + (int64_t)(u % p.kv_heads) * p.kv_head_stride;
+    const __nv_bfloat16* kb = (const __nv_bfloat16*)p.k + ubase;
+    const __nv_bfloat16* vb = (const __nv_bfloat16*)p.v + ubase;
+    const int* idp = p.ids + (int64_t)u * p.ids_stride;
+    const __nv_bfloat16* qp = (const __nv_bfloat16*)p.q + (int64_t)u * G * kAvD;
+    const int g = lane >> 2, q4 = lane & 3;
+
+    // Q^T as the MMA B operand: n = head g, k = dims.
+    uint32_t qb[8][2];
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+            qb[kk][r] = g < G ? *reinterpret_cast<const uint32_t*>(qp + g * kAvD + kk * 16 + r * 8 + 2 * q4) : 0u;
+
+    // The split's row ids, staged once in shared memory (all copies in flight
+    // together) so that issuing a tile's copies never waits on a global load.
+    int* sids = reinterpret_cast<int*>(smem + kAvStages * kAvStageBytes);
+    const int n_staged = min(max(0, min(r1, cnt) - r0), kAvIdsCap);
+    for (int i = tid; i < n_staged; i += kAvThreads) cp_async4(smem_u32(sids + i), idp + r0 + i);
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    auto pos_of = [&](int r) -> int {
+        if (r >= r1) return -1;
+        if (r >= cnt) return H + (r - cnt);
+        return r - r0 < kAvIdsCap ? sids[r - r0] : idp[r];
+    };
+    // Loader: the warp's 16 rows, two 256-byte rows per instruction (16
+    // lanes x 16 bytes per row: fully coalesced); rows past the split end
+    // are zero-filled.
+    const int ld_sub = lane >> 4, ld_ch = lane & 15;
+    auto issue = [&](int t) {
+        uint8_t* st = smem + (t % kAvStages) * kAvStageBytes;
+        const uint32_t kd = smem_u32(st), vd = smem_u32(st + kAvTile * kAvRowBytes);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int row = warp * 16 + 2 * i + ld_sub;
+            const int pos = pos_of(r0 + t * kAvTile + row);
+            const bool valid = pos >= 0;
+            const int64_t off = valid ? (int64_t)pos * p.kv_row_stride : 0;
+            cp_async16(kd + tile_off(row, ld_ch), kb + off + ld_ch * 8, valid);
+            cp_async16(vd + tile_off(row, ld_ch), vb + off + ld_ch * 8, valid);
+        }
+    };
+    if (0 < ntiles) issue(0);
+    cp_async_commit();
+    if (1 < ntiles) issue(1);
+    cp_async_commit();
+
+    // Online softmax state of heads 2*q4 and 2*q4 + 1 (lanes with the same
+    // q4 agree); O^T accumulators oc[mt] hold dims mt*16 + g (+8) of them.
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float oc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) oc[j][0] = oc[j][1] = oc[j][2] = oc[j][3] = 0.f;
+    const float scale = kLog2e / sqrtf((float)kAvD);
+    const int mi = lane >> 3, r8 = lane & 7;
+    const int wrow = warp * 16;
+    for (int t = 0; t < ntiles; ++t) {
+        const int tn = t + kAvStages - 1;
+        if (tn < ntiles) issue(tn);
+        cp_async_commit();
+        cp_async_wait<kAvStages - 1>();
+        __syncwarp();   // the warp's own copies of tile t are visible to all its lanes
+        const uint8_t* st = smem + (t % kAvStages) * kAvStageBytes;
+        const uint32_t kbase = smem_u32(st), vbase = smem_u32(st + kAvTile * kAvRowBytes);
+        // S^T = K Q^T, A = the warp's 16 key rows; two accumulation chains.
+        float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            uint32_t a[4];
+            ldmatrix_x4(kbase + tile_off(wrow + (mi & 1) * 8 + r8, 2 * kk + (mi >> 1)), a);
+            if (kk & 1) mma_bf16(sb, a, qb[kk][0], qb[kk][1]);
+            else mma_bf16(sa, a, qb[kk][0], qb[kk][1]);
+        }
+        // Scale, mask rows past the split end (c0/c1: key g, heads 2q4 and
+        // 2q4+1; c2/c3: key g+8), online softmax per head.
+        const int base_r = r0 + t * kAvTile + wrow;
+        const bool ok0 = base_r + g < r1, ok1 = base_r + g + 8 < r1;
+        const float s0 = ok0 ? (sa[0] + sb[0]) * scale : -INFINITY;
+        const float s1 = ok0 ? (sa[1] + sb[1]) * scale : -INFINITY;
+        const float s2 = ok1 ? (sa[2] + sb[2]) * scale : -INFINITY;
+        const float s3 = ok1 ? (sa[3] + sb[3]) * scale : -INFINITY;
+        float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+        }
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float al0 = mn0 == -INFINITY ? 1.f : exp2f(m0 - mn0);
+        const float al1 = mn1 == -INFINITY ? 1.f : exp2f(m1 - mn1);
+        const float p0 = mn0 == -INFINITY ? 0.f : exp2f(s0 - mn0);
+        const float p2 = mn0 == -INFINITY ? 0.f : exp2f(s2 - mn0);
+        const float p1 = mn1 == -INFINITY ? 0.f : exp2f(s1 - mn1);
+        const float p3 = mn1 == -INFINITY ? 0.f : exp2f(s3 - mn1);
+        float ps0 = p0 + p2, ps1 = p1 + p3;
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            ps0 += __shfl_xor_sync(0xffffffffu, ps0, o);
+            ps1 += __shfl_xor_sync(0xffffffffu, ps1, o);
+        }
+        l0 = fmaf(l0, al0, ps0);
+        l1 = fmaf(l1, al1, ps1);
+        m0 = mn0;
+        m1 = mn1;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            oc[j][0] *= al0; oc[j][1] *= al1;
+            oc[j][2] *= al0; oc[j][3] *= al1;
+        }
+        // P^T as the B operand (k = keys, n = heads), rounded to bf16
+        // (relative error 2^-9 per weight, the output's own rounding); l
+        // above sums the unrounded fp32 weights.
+        const uint32_t pb0 = movmatrix_trans(pack_bf16(p0, p1));
+        const uint32_t pb1 = movmatrix_trans(pack_bf16(p2, p3));
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            uint32_t a[4];
+            ldmatrix_x4_trans(vbase + tile_off(wrow + (mi >> 1) * 8 + r8, 2 * mt + (mi & 1)), a);
+            mma_bf16(oc[mt], a, pb0, pb1);
+        }
+        __syncwarp();   // every lane has read the stage before it is refilled
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // Per-warp states to shared memory (reusing the stage buffers).
+    float* red = reinterpret_cast<float*>(smem);
+    float* rm = red;
+    float* rl = red + 4 * kAvMaxG;
+    float* ro = red + 2 * 4 * kAvMaxG;
+    const int h0 = 2 * q4, h1 = h0 + 1;
+    if (g == 0) {
+        if (h0 < G) { rm[warp * kAvMaxG + h0] = m0; rl[warp * kAvMaxG + h0] = l0; }
+        if (h1 < G) { rm[warp * kAvMaxG + h1] = m1; rl[warp * kAvMaxG + h1] = l1; }
+    }
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+        const int da = mt * 16 + g, db = da + 8;
+        if (h0 < G) {
+            ro[(warp * kAvMaxG + h0) * kAvD + da] = oc[mt][0];
+            ro[(warp * kAvMaxG + h0) * kAvD + db] = oc[mt][2];
+        }
+        if (h1 < G) {
+            ro[(warp * kAvMaxG + h1) * kAvD + da] = oc[mt][1];
+            ro[(warp * kAvMaxG + h1) * kAvD + db] = oc[mt][3];
+        }
+    }
+    __syncthreads();
+    if constexpr (kCluster) {
+        float* pbuf = reinterpret_cast<float*>(smem + kAvStages * kAvStageBytes + kAvIdsCap * sizeof(int));
+        av_finish_push<__nv_bfloat16>(p, u, s, red, 4, red + 2 * 4 * kAvMaxG + 4 * kAvMaxG * kAvD, pbuf);
+    } else {
+        av_finish<__nv_bfloat16>(p, u, s, red, 4);
+    }
+}
+
+// 9..16 heads: the heads fill the MMA's M = 16 rows.
 template <bool kCluster>
 __global__ void __launch_bounds__(kAvThreads)
-sparse_av_bf16_kernel(AvParams p) {
+sparse_av_bf16_g16_kernel(AvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int s = blockIdx.x, u = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -542,13 +801,18 @@ __global__ void lse_merge_kernel(const float* __restrict__ part, int P, int UG, 
     else out_b[(int64_t)uh * kAvD + dim] = __float2bfloat16_rn(r);
 }
 
-// Whether a cluster of S split CTAs (S <= 16; above 8 the non-portable
-// cluster sizes) can be resident; answered once per S and kept.
-bool cluster_fits(int S, int smem) {
-    static int known[kAvMaxCluster + 1] = {};   // 0 unknown, 1 yes, 2 no
+// Whether a cluster of S split CTAs of kernel `which` (0: up to 8 heads,
+// 1: 9..16 heads; S <= 16, above 8 the non-portable cluster sizes) with
+// `smem` bytes each can be resident; answered once per (kernel, S, smem)
+// and kept.
+bool cluster_fits(int which, int S, int smem) {
+    static int known[2][kAvMaxCluster + 1] = {};   // 0 unknown, 1 yes, 2 no
+    static int known_smem[2][kAvMaxCluster + 1] = {};
     if (S < 2 || S > kAvMaxCluster) return false;
-    if (!known[S]) {
-        auto fn = sparse_av_bf16_kernel<true>;
+    if (known_smem[which][S] != smem) known[which][S] = 0;
+    if (!known[which][S]) {
+        known_smem[which][S] = smem;
+        auto fn = which == 0 ? sparse_av_bf16_kernel<true> : sparse_av_bf16_g16_kernel<true>;
         bool ok = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess;
         if (ok && S > 8) ok = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
         int clusters = 0;
@@ -567,9 +831,9 @@ bool cluster_fits(int S, int smem) {
             ok = cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) == cudaSuccess && clusters > 0;
         }
         cudaGetLastError();   // a refused query leaves no sticky error
-        known[S] = ok ? 1 : 2;
+        known[which][S] = ok ? 1 : 2;
     }
-    return known[S] == 1;
+    return known[which][S] == 1;
 }
 
 int default_splits(int U) {
@@ -626,12 +890,15 @@ extern "C" int pk_sparse_av(uint64_t q, uint64_t k, uint64_t v, int dtype, int k
     dim3 grid(splits, U);
     if (dtype == PK_BF16) {
         if (kv_row_stride % 8 || kv_batch_stride % 8 || kv_head_stride % 8 || (k | v) % 16) return PK_ERR_ARG;
-        const int smem = kAvStages * kAvStageBytes + kAvIdsCap * (int)sizeof(int);
-        if (splits >= 2 && cluster_fits(splits, smem)) {
+        const int which = G <= 8 ? 0 : 1;
+        const int base_smem = kAvStages * kAvStageBytes + kAvIdsCap * (int)sizeof(int);
+        // The cluster form of the G <= 8 kernel adds the push-merge receive buffer.
+        const int csmem = base_smem + (which == 0 ? av_push_floats(G, splits) * (int)sizeof(float) : 0);
+        if (splits >= 2 && cluster_fits(which, splits, csmem)) {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = grid;
             cfg.blockDim = dim3(kAvThreads);
-            cfg.dynamicSmemBytes = smem;
+            cfg.dynamicSmemBytes = csmem;
             cfg.stream = st;
             cudaLaunchAttribute attr[1];
             attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -640,11 +907,13 @@ extern "C" int pk_sparse_av(uint64_t q, uint64_t k, uint64_t v, int dtype, int k
             attr[0].val.clusterDim.z = 1;
             cfg.attrs = attr;
             cfg.numAttrs = 1;
-            const cudaError_t e = cudaLaunchKernelEx(&cfg, sparse_av_bf16_kernel<true>, p);
+            const cudaError_t e = cudaLaunchKernelEx(
+                &cfg, which == 0 ? sparse_av_bf16_kernel<true> : sparse_av_bf16_g16_kernel<true>, p);
             if (e != cudaSuccess) return (int)e;
         } else {
-            cudaFuncSetAttribute(sparse_av_bf16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            sparse_av_bf16_kernel<false><<<grid, kAvThreads, smem, st>>>(p);
+            auto fn = which == 0 ? sparse_av_bf16_kernel<false> : sparse_av_bf16_g16_kernel<false>;
+            cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, base_smem);
+            fn<<<grid, kAvThreads, base_smem, st>>>(p);
         }
     } else if (dtype == PK_F32) {
         if (kv_row_stride % 4 || kv_batch_stride % 4 || kv_head_stride % 4 || (k | v | q) % 16) return PK_ERR_ARG;

@@ -319,3 +319,44 @@ def test_bound_filtered_build_equals_exact_build(pk, dtype):
         ce, ide = exact.csr(u)
         assert np.array_equal(cf, ce), u
         assert np.array_equal(idf, ide), u
+
+
+@pytest.mark.parametrize("G", [1, 3, 8, 12, 16])
+def test_attention_head_counts_and_split_forms_match_oracle(pk, oracle, G):
+    """Both bf16 attention kernels -- heads in the MMA's N for G <= 8, in its
+    M for 9..16 -- with one split, a cluster of splits merged on chip, and
+    more than 8 splits merged through global memory, against the oracle's
+    attend (core.py:170-183) on the same bf16 inputs."""
+    from prismkv_b200 import native as nv
+    rs = np.random.RandomState(11 + G)
+    U, N, tail, d = 3, 2048, 5, 128
+    keys = bf16_round(rs.standard_normal((U, N + tail, d)).astype(np.float32))
+    vals = bf16_round(rs.standard_normal((U, N + tail, d)).astype(np.float32))
+    q = bf16_round(rs.standard_normal((U, G, d)).astype(np.float32))
+    counts = [700, 0, 1531]
+    width = 1536
+    ids = np.zeros((U, width), np.int32)
+    sel = []
+    for u, c in enumerate(counts):
+        s = np.sort(rs.choice(N, c, replace=False)).astype(np.int32)
+        ids[u, :c] = s
+        sel.append(s)
+    dev = torch.device("cuda")
+    K = torch.from_numpy(keys).to(dev).to(torch.bfloat16)
+    V = torch.from_numpy(vals).to(dev).to(torch.bfloat16)
+    Q = torch.from_numpy(q).to(dev).to(torch.bfloat16).contiguous()
+    tid = torch.from_numpy(ids).to(dev)
+    count = torch.tensor(counts, dtype=torch.int32, device=dev)
+    hist = torch.full((U,), N, dtype=torch.int32, device=dev)
+    length = torch.full((U,), N + tail, dtype=torch.int32, device=dev)
+    refs = [oracle.attend(q[u], keys[u], vals[u], sel[u], N) for u in range(U)]
+    for splits in (1, 4, 8, 13):
+        nbytes = nv.query("pk_sparse_av_workspace_bytes", U, G, d, splits)
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        out = torch.full((U, G, d), float("nan"), dtype=torch.bfloat16, device=dev)
+        nv.call("pk_sparse_av", Q, K, V, nv.PK_BF16, 1, K.stride(0), 0, K.stride(1), tid, width, count, hist, length,
+                U, G, d, splits, ws, nbytes, out, None)
+        torch.cuda.synchronize()
+        got = out.float().cpu().numpy()
+        for u in range(U):
+            assert rel_l2(got[u], refs[u]) < TOL_BF16, (G, splits, u)
