@@ -201,6 +201,11 @@ def run_ours(a):
     torch.cuda.empty_cache()
     # Per-step lengths: history + the tokens generated so far (dense tail).
     lens = torch.stack([torch.full((U,), N + s + 1, dtype=torch.int32, device=dev) for s in range(total_steps)])
+    # Each step appends its token's K/V rows at position N + s of every layer's
+    # cache (the reference's decode append, model.py:109-115); the rows are the
+    # generated cache rows themselves, so the attention sees the same data.
+    kv_steps = torch.stack([torch.stack([torch.stack([lay["K"][:, N + s], lay["V"][:, N + s]]) for lay in layers])
+                            for s in range(total_steps)]).contiguous()   # [steps, L, 2, U, d]
     setup_s = time.time() - t_setup
 
     # Static inputs for graph replay.
@@ -209,6 +214,7 @@ def run_ours(a):
     for lay in layers:
         del lay["Q"]
     q_static = q_steps[0].clone()   # [L, U, G, d]
+    kv_static = kv_steps[0].clone()  # [L, 2, U, d]
     len_static = lens[0].clone()
     outs = torch.empty(L, U, G, d, dtype=torch.bfloat16, device=dev)
 
@@ -218,13 +224,17 @@ def run_ours(a):
             lay["op"].route(q)
             if av_events is not None:
                 av_events[l][0].record()
-            o = lay["op"].attention(q, lay["K"], lay["V"], length=len_static)
+            # The token's KV append fused into the attention launch: its rows
+            # are attended as the newest tail row and written into the cache.
+            o = lay["op"].attention(q, lay["K"], lay["V"], length=len_static,
+                                    append=(kv_static[l, 0], kv_static[l, 1]))
             if av_events is not None:
                 av_events[l][1].record()
             outs[l].copy_(o)
 
     def load_step(s):
         q_static.copy_(q_steps[s])
+        kv_static.copy_(kv_steps[s])
         len_static.copy_(lens[s])
 
     # Warm up eagerly once (creates every workspace), then capture.
@@ -318,12 +328,14 @@ def run_ours(a):
     # End to end through the public API with host buffers: pinned host
     # queries -> device, full step, outputs -> pinned host, every step.
     h_q = q_steps.cpu().pin_memory()
+    h_kv = kv_steps.cpu().pin_memory()
     h_out = torch.empty(L, U, G, d, dtype=torch.bfloat16).pin_memory()
     ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     ee0.record()
     for s in range(a.warmup, total_steps):
         q_static.copy_(h_q[s], non_blocking=True)
+        kv_static.copy_(h_kv[s], non_blocking=True)
         len_static.copy_(lens[s])
         if graph is not None:
             graph.replay()
@@ -392,7 +404,7 @@ def run_ours(a):
             traffic = round(tj["dram_bytes_per_algorithmic_byte"] * mean_bytes)
         except (OSError, ValueError, KeyError):
             traffic = None
-    launches_per_step = L * 4  # approximate encode + select + union + attention per layer
+    launches_per_step = L * 4  # approximate encode + select + union + attention (with the KV append) per layer
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -415,8 +427,9 @@ def run_ours(a):
                    "decode_ms_per_step": round(decode_ms / a.steps, 4),
                    "append_ms_per_block": round(append_block_ms, 3),
                    "append_ms_per_step": round(append_ms_per_step, 5),
-                   "step": "32 x (route + union + sparse attention) per token, plus the amortised append of an "
-                           "update_interval block per layer every update_interval tokens"},
+                   "step": "32 x (route + union + sparse attention with the token's KV append) per token, plus "
+                           "the amortised index append of an update_interval block per layer every "
+                           "update_interval tokens"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": "sparse_av_bf16_kernel", "avg_launch_us": round(mean_av_ms * 1e3, 2),
@@ -424,7 +437,7 @@ def run_ours(a):
                      "share_of_step": round(av_ms / a.steps / (ms / a.steps), 3),
                      "peak_source": "measured" if "hbm_gbs" in peaks else "fallback"},
         "e2e": {"value": round(e2e, 2), "unit": "tokens/s",
-                "h2d_bytes_per_step": int(L * U * G * d * 2 + U * 4),
+                "h2d_bytes_per_step": int(L * U * G * d * 2 + L * 2 * U * d * 2),
                 "d2h_bytes_per_step": int(L * U * G * d * 2)},
         "gpu_launches": launches_per_step * a.steps,
         "clocks": clk,

@@ -153,6 +153,21 @@ int pk_sparse_av(uint64_t q, uint64_t k, uint64_t v, int dtype,
                  uint64_t workspace, uint64_t workspace_bytes,
                  uint64_t out, uint64_t partial, uint64_t stream);
 
+/* pk_sparse_av fused with the decode KV append: unit u's new rows
+ * k_new/v_new[u, d] (contiguous, dtype, 16-byte aligned; u = slot * kv_heads
+ * + head) take the place of row length[u] - 1 -- the newest tail row, when
+ * length[u] > history[u] -- in the attention, and are written into K and V
+ * at that row.  One launch instead of batch_append followed by the attention
+ * (kernels/cuda_sm90/model.py:109-137); the same fusion as
+ * flash_attn_with_kvcache's k/v arguments.  No counterpart entry point in
+ * the reference. */
+int pk_sparse_av_append(uint64_t q, uint64_t k, uint64_t v, int dtype,
+                        int kv_heads, int64_t kv_batch_stride, int64_t kv_head_stride, int64_t kv_row_stride,
+                        uint64_t ids, int64_t ids_stride, uint64_t count, uint64_t history, uint64_t length,
+                        int U, int G, int d, int splits,
+                        uint64_t workspace, uint64_t workspace_bytes,
+                        uint64_t out, uint64_t partial, uint64_t k_new, uint64_t v_new, uint64_t stream);
+
 /* Log-sum-exp merge of P partial states partial[P, UG, d+2] (m, l, o[d]) into
  * out[UG, d] (dtype).  The cross-GPU step of the sequence-sharded decode;
  * generalises the in-GPU split merge of av_tuned.cu:54-61. */
@@ -216,6 +231,19 @@ int pk_gather_kv(uint64_t k, uint64_t v, int dtype, int kv_heads, int64_t kv_bat
                  int64_t kv_row_stride, uint64_t ids, int64_t ids_stride, uint64_t count, uint64_t history,
                  uint64_t length, int U, int d, int64_t packed_rows, uint64_t out_k, uint64_t out_v,
                  uint64_t status, uint64_t stream);
+
+/* Decode KV append: slot s's new rows k_new/v_new[s, kv_heads, d]
+ * (contiguous, dtype) are written at row positions[s] of the caches, row(p)
+ * of head h of slot s at s * kv_batch_stride + h * kv_head_stride +
+ * p * kv_row_stride (elements): the slot-major [slot, capacity, H_kv, d]
+ * cache of the reference, or [U, capacity, d] with kv_heads = 1.  A position
+ * outside [0, capacity) leaves the slot untouched (inactive slot).  Replaces
+ * batch_append (kernels/cuda_sm90/native_sources/av.cu:70-90, bound at
+ * kernels/cuda_sm90/native.py:23, called by model.py:109-115).  Rows,
+ * strides and base addresses must be 16-byte aligned. */
+int pk_kv_append(uint64_t k_new, uint64_t v_new, uint64_t k_cache, uint64_t v_cache, int dtype,
+                 int kv_heads, int64_t kv_batch_stride, int64_t kv_head_stride, int64_t kv_row_stride,
+                 uint64_t positions, int slots, int capacity, int d, uint64_t stream);
 
 /* Sparse attention for callers that cannot allocate device memory.
  * This entry point has no counterpart in the reference.  It exists for

@@ -9,8 +9,8 @@ every operation raises -- there is no CPU path.
 """
 from .core import (FeatureIndex, SharedSAE, append_index, attend, bucket_scores, build_index, select_buckets,
                    summarize)
-from .decode import SparseDecode
+from .decode import SparseDecode, kv_append
 from .index import DeviceIndex, SAEParams
 
 __all__ = ["FeatureIndex", "SharedSAE", "build_index", "select_buckets", "attend", "append_index",
-           "bucket_scores", "summarize", "SparseDecode", "DeviceIndex", "SAEParams"]
+           "bucket_scores", "summarize", "SparseDecode", "kv_append", "DeviceIndex", "SAEParams"]

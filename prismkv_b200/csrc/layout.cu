@@ -59,6 +59,27 @@ gather_kv_kernel(const uint4* __restrict__ k, const uint4* __restrict__ v, int k
     }
 }
 
+// Decode append: slot s's new K and V rows (kv_heads rows of d each,
+// contiguous in k_new/v_new) written at row positions[s] of the cache.  One
+// CTA per slot, 16-byte vectors; a position outside [0, capacity) leaves the
+// slot untouched (an inactive slot), as the reference's append_slots does.
+__global__ void __launch_bounds__(128)
+kv_append_kernel(const uint4* __restrict__ k_new, const uint4* __restrict__ v_new, uint4* __restrict__ k_cache,
+                 uint4* __restrict__ v_cache, int kv_heads, int64_t bs, int64_t hs, int64_t rs,
+                 const int* __restrict__ positions, int capacity, int row_vecs) {
+    const int slot = blockIdx.x;
+    const int pos = positions[slot];
+    if (pos < 0 || pos >= capacity) return;
+    const int n = kv_heads * row_vecs;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int h = i / row_vecs, j = i % row_vecs;
+        const int64_t dst = (int64_t)slot * bs + (int64_t)h * hs + (int64_t)pos * rs + j;
+        const int64_t src = ((int64_t)slot * kv_heads + h) * row_vecs + j;
+        k_cache[dst] = k_new[src];
+        v_cache[dst] = v_new[src];
+    }
+}
+
 }  // namespace pk
 
 using namespace pk;
@@ -90,6 +111,26 @@ extern "C" int pk_gather_kv(uint64_t k, uint64_t v, int dtype, int kv_heads, int
         (const uint4*)k, (const uint4*)v, kv_heads, kv_batch_stride / per, kv_head_stride / per, kv_row_stride / per,
         (const int*)ids, ids_stride, (const int*)count, (const int*)history, (const int*)length, U, row_vecs,
         packed_rows, (uint4*)out_k, (uint4*)out_v, (int*)status);
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}
+
+extern "C" int pk_kv_append(uint64_t k_new, uint64_t v_new, uint64_t k_cache, uint64_t v_cache, int dtype,
+                            int kv_heads, int64_t kv_batch_stride, int64_t kv_head_stride, int64_t kv_row_stride,
+                            uint64_t positions, int slots, int capacity, int d, uint64_t stream) {
+    if (slots < 0 || kv_heads < 1 || d < 1 || capacity < 0) return PK_ERR_ARG;
+    if (slots == 0) return PK_OK;
+    if (!k_new || !v_new || !k_cache || !v_cache || !positions) return PK_ERR_ARG;
+    const int esz = dtype == PK_BF16 ? 2 : dtype == PK_F32 ? 4 : 0;
+    if (!esz) return PK_ERR_ARG;
+    // 16-byte vectors: rows, strides and bases 16-byte aligned.
+    if ((d * esz) % 16 || (k_new | v_new | k_cache | v_cache) % 16 || (kv_batch_stride * esz) % 16 ||
+        (kv_head_stride * esz) % 16 || (kv_row_stride * esz) % 16)
+        return PK_ERR_ARG;
+    const int per = 16 / esz;
+    kv_append_kernel<<<slots, 128, 0, (cudaStream_t)stream>>>(
+        (const uint4*)k_new, (const uint4*)v_new, (uint4*)k_cache, (uint4*)v_cache, kv_heads, kv_batch_stride / per,
+        kv_head_stride / per, kv_row_stride / per, (const int*)positions, capacity, d * esz / 16);
     PK_CHECK_LAUNCH();
     return PK_OK;
 }

@@ -47,7 +47,33 @@ struct AvParams {
     int* done;      // [U] arrival counters
     void* out;      // [U, G, D] (dtype of q)
     float* xpart;   // [U*G, D+2] exported partial (natural-log m), or null
+    // Fused decode append, or null: unit u's new K/V rows k_new/v_new[u, D]
+    // are attended in place of cache row length[u] - 1 (the newest tail row)
+    // and written there by the unit's first split CTA.
+    const void* k_new;
+    const void* v_new;
 };
+
+// The row position the fused append fills (-1: none).
+__device__ __forceinline__ int fresh_row(const AvParams& p, int H, int len) {
+    return p.k_new && len > H ? len - 1 : -1;
+}
+
+// The unit's first split CTA writes its new K/V rows into the cache at the
+// fresh position with 16-byte vectors (nothing in this launch reads that
+// cache row: the loaders take it from k_new/v_new).
+template <typename T>
+__device__ __forceinline__ void append_fresh_row(const AvParams& p, int u, int64_t ubase, int fresh) {
+    if (fresh < 0 || blockIdx.x != 0) return;
+    constexpr int kVecs = kAvD * (int)sizeof(T) / 16;
+    const int tid = threadIdx.x;
+    if (tid >= 2 * kVecs) return;
+    const bool isv = tid >= kVecs;
+    const int j = isv ? tid - kVecs : tid;
+    const uint4* src = reinterpret_cast<const uint4*>((const T*)(isv ? p.v_new : p.k_new) + (int64_t)u * kAvD);
+    uint4* dst = reinterpret_cast<uint4*>((T*)(isv ? p.v : p.k) + ubase + (int64_t)fresh * p.kv_row_stride);
+    dst[j] = src[j];
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -378,6 +404,10 @@ sparse_av_bf16_kernel(AvParams p) {
     const __nv_bfloat16* vb = (const __nv_bfloat16*)p.v + ubase;
     const int* idp = p.ids + (int64_t)u * p.ids_stride;
     const __nv_bfloat16* qp = (const __nv_bfloat16*)p.q + (int64_t)u * G * kAvD;
+    const int fresh = fresh_row(p, H, len);
+    const __nv_bfloat16* knew = fresh >= 0 ? (const __nv_bfloat16*)p.k_new + (int64_t)u * kAvD : kb;
+    const __nv_bfloat16* vnew = fresh >= 0 ? (const __nv_bfloat16*)p.v_new + (int64_t)u * kAvD : vb;
+    append_fresh_row<__nv_bfloat16>(p, u, ubase, fresh);
     const int g = lane >> 2, q4 = lane & 3;
 
     // Q^T as the MMA B operand: n = head g, k = dims.
@@ -412,10 +442,10 @@ sparse_av_bf16_kernel(AvParams p) {
         for (int i = 0; i < 8; ++i) {
             const int row = warp * 16 + 2 * i + ld_sub;
             const int pos = pos_of(r0 + t * kAvTile + row);
-            const bool valid = pos >= 0;
-            const int64_t off = valid ? (int64_t)pos * p.kv_row_stride : 0;
-            cp_async16(kd + tile_off(row, ld_ch), kb + off + ld_ch * 8, valid);
-            cp_async16(vd + tile_off(row, ld_ch), vb + off + ld_ch * 8, valid);
+            const bool valid = pos >= 0, nw = valid && pos == fresh;
+            const int64_t off = valid && !nw ? (int64_t)pos * p.kv_row_stride : 0;
+            cp_async16(kd + tile_off(row, ld_ch), (nw ? knew : kb) + off + ld_ch * 8, valid);
+            cp_async16(vd + tile_off(row, ld_ch), (nw ? vnew : vb) + off + ld_ch * 8, valid);
         }
     };
     if (0 < ntiles) issue(0);
@@ -552,6 +582,10 @@ sparse_av_bf16_g16_kernel(AvParams p) {
     const __nv_bfloat16* vb = (const __nv_bfloat16*)p.v + ubase;
     const int* idp = p.ids + (int64_t)u * p.ids_stride;
     const __nv_bfloat16* qp = (const __nv_bfloat16*)p.q + (int64_t)u * G * kAvD;
+    const int fresh = fresh_row(p, H, len);
+    const __nv_bfloat16* knew = fresh >= 0 ? (const __nv_bfloat16*)p.k_new + (int64_t)u * kAvD : kb;
+    const __nv_bfloat16* vnew = fresh >= 0 ? (const __nv_bfloat16*)p.v_new + (int64_t)u * kAvD : vb;
+    append_fresh_row<__nv_bfloat16>(p, u, ubase, fresh);
 
     // Q as the MMA A operand: rows = heads, columns = dims.
     uint32_t qa[8][4];
@@ -587,10 +621,10 @@ sparse_av_bf16_g16_kernel(AvParams p) {
         for (int i = 0; i < 8; ++i) {
             const int row = warp * 16 + 2 * i + ld_sub;
             const int pos = pos_of(r0 + t * kAvTile + row);
-            const bool valid = pos >= 0;
-            const int64_t off = valid ? (int64_t)pos * p.kv_row_stride : 0;
-            cp_async16(kd + tile_off(row, ld_ch), kb + off + ld_ch * 8, valid);
-            cp_async16(vd + tile_off(row, ld_ch), vb + off + ld_ch * 8, valid);
+            const bool valid = pos >= 0, nw = valid && pos == fresh;
+            const int64_t off = valid && !nw ? (int64_t)pos * p.kv_row_stride : 0;
+            cp_async16(kd + tile_off(row, ld_ch), (nw ? knew : kb) + off + ld_ch * 8, valid);
+            cp_async16(vd + tile_off(row, ld_ch), (nw ? vnew : vb) + off + ld_ch * 8, valid);
         }
     };
 
@@ -737,6 +771,8 @@ sparse_av_f32_kernel(AvParams p) {
     const float* vb = (const float*)p.v + ubase;
     const int* idp = p.ids + (int64_t)u * p.ids_stride;
     const float* qp = (const float*)p.q + (int64_t)u * G * kAvD;
+    const int fresh = fresh_row(p, H, len);
+    append_fresh_row<float>(p, u, ubase, fresh);
     float* red = reinterpret_cast<float*>(smem);
     float* rm = red;
     float* rl = red + 4 * kAvMaxG;
@@ -756,8 +792,11 @@ sparse_av_f32_kernel(AvParams p) {
         }
         for (int r = r0 + warp; r < r1; r += 4) {
             const int pos = r < cnt ? idp[r] : H + (r - cnt);
-            const float4 kv = reinterpret_cast<const float4*>(kb + (int64_t)pos * p.kv_row_stride)[lane];
-            const float4 vv = reinterpret_cast<const float4*>(vb + (int64_t)pos * p.kv_row_stride)[lane];
+            const bool nw = pos == fresh;
+            const float* kr = nw ? (const float*)p.k_new + (int64_t)u * kAvD : kb + (int64_t)pos * p.kv_row_stride;
+            const float* vr = nw ? (const float*)p.v_new + (int64_t)u * kAvD : vb + (int64_t)pos * p.kv_row_stride;
+            const float4 kv = reinterpret_cast<const float4*>(kr)[lane];
+            const float4 vv = reinterpret_cast<const float4*>(vr)[lane];
 #pragma unroll
             for (int a = 0; a < 4; ++a) {
                 float d = qv[a].x * kv.x + qv[a].y * kv.y + qv[a].z * kv.z + qv[a].w * kv.w;
@@ -862,12 +901,13 @@ extern "C" size_t pk_sparse_av_workspace_bytes(int U, int G, int d, int splits) 
     return (part + 255) / 256 * 256 + ((size_t)U * sizeof(int) + 255) / 256 * 256;
 }
 
-extern "C" int pk_sparse_av(uint64_t q, uint64_t k, uint64_t v, int dtype, int kv_heads, int64_t kv_batch_stride,
+static int sparse_av_launch(uint64_t q, uint64_t k, uint64_t v, int dtype, int kv_heads, int64_t kv_batch_stride,
                             int64_t kv_head_stride, int64_t kv_row_stride, uint64_t ids, int64_t ids_stride,
                             uint64_t count, uint64_t history, uint64_t length, int U, int G, int d, int splits,
                             uint64_t workspace, uint64_t workspace_bytes, uint64_t out, uint64_t partial,
-                            uint64_t stream) {
+                            uint64_t k_new, uint64_t v_new, uint64_t stream) {
     if (U < 1 || G < 1 || G > kAvMaxG || kv_heads < 1 || kv_row_stride < d) return PK_ERR_ARG;
+    if ((k_new == 0) != (v_new == 0) || (k_new | v_new) % 16) return PK_ERR_ARG;
     if (d != kAvD) return PK_ERR_UNSUPPORTED;
     if (!q || !k || !v || !ids || !count || !history || !length || (!out && !partial)) return PK_ERR_ARG;
     if (splits <= 0) splits = default_splits(U);
@@ -886,6 +926,8 @@ extern "C" int pk_sparse_av(uint64_t q, uint64_t k, uint64_t v, int dtype, int k
     p.done = workspace ? (int*)((char*)workspace + (part_bytes + 255) / 256 * 256) : nullptr;
     p.out = (void*)out;
     p.xpart = (float*)partial;
+    p.k_new = (const void*)k_new;
+    p.v_new = (const void*)v_new;
     cudaStream_t st = (cudaStream_t)stream;
     dim3 grid(splits, U);
     if (dtype == PK_BF16) {
@@ -925,6 +967,28 @@ extern "C" int pk_sparse_av(uint64_t q, uint64_t k, uint64_t v, int dtype, int k
     }
     PK_CHECK_LAUNCH();
     return PK_OK;
+}
+
+extern "C" int pk_sparse_av(uint64_t q, uint64_t k, uint64_t v, int dtype, int kv_heads, int64_t kv_batch_stride,
+                            int64_t kv_head_stride, int64_t kv_row_stride, uint64_t ids, int64_t ids_stride,
+                            uint64_t count, uint64_t history, uint64_t length, int U, int G, int d, int splits,
+                            uint64_t workspace, uint64_t workspace_bytes, uint64_t out, uint64_t partial,
+                            uint64_t stream) {
+    return sparse_av_launch(q, k, v, dtype, kv_heads, kv_batch_stride, kv_head_stride, kv_row_stride, ids, ids_stride,
+                            count, history, length, U, G, d, splits, workspace, workspace_bytes, out, partial, 0, 0,
+                            stream);
+}
+
+extern "C" int pk_sparse_av_append(uint64_t q, uint64_t k, uint64_t v, int dtype, int kv_heads,
+                                   int64_t kv_batch_stride, int64_t kv_head_stride, int64_t kv_row_stride,
+                                   uint64_t ids, int64_t ids_stride, uint64_t count, uint64_t history,
+                                   uint64_t length, int U, int G, int d, int splits, uint64_t workspace,
+                                   uint64_t workspace_bytes, uint64_t out, uint64_t partial, uint64_t k_new,
+                                   uint64_t v_new, uint64_t stream) {
+    if (!k_new || !v_new) return PK_ERR_ARG;
+    return sparse_av_launch(q, k, v, dtype, kv_heads, kv_batch_stride, kv_head_stride, kv_row_stride, ids, ids_stride,
+                            count, history, length, U, G, d, splits, workspace, workspace_bytes, out, partial, k_new,
+                            v_new, stream);
 }
 
 extern "C" int pk_lse_merge(uint64_t partial, int P, int UG, int d, uint64_t out, int dtype, uint64_t stream) {

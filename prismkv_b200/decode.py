@@ -38,6 +38,35 @@ def kv_layout(k: torch.Tensor, v: torch.Tensor, U: int, d: int):
     return kv
 
 
+def kv_append(k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+              positions: torch.Tensor) -> None:
+    """Decode KV append (the reference's ``batch_append``,
+    kernels/cuda_sm90/native_sources/av.cu:70-90, called from
+    kernels/cuda_sm90/model.py:109-115): slot s's new rows
+    k_new/v_new[s] ([H_kv, d], or [d] for a unit-major cache) are written at
+    row positions[s] of the caches, given as slot-major [slots, capacity,
+    H_kv, d] or unit-major [slots, capacity, d].  positions: int32 [slots] on
+    the device; a position outside [0, capacity) leaves its slot untouched.
+    Asynchronous on the current stream; graph-capturable."""
+    if k_cache.dim() == 4:
+        slots, capacity, kv_heads, d = k_cache.shape
+    elif k_cache.dim() == 3:
+        slots, capacity, d = k_cache.shape
+        kv_heads = 1
+    else:
+        raise ValueError("caches must be [slots, capacity, H_kv, d] or [slots, capacity, d]")
+    _, bs, hs, rs, _ = kv_layout(k_cache, v_cache, slots * kv_heads, d)
+    for t in (k_new, v_new):
+        if t.dtype != k_cache.dtype or v_cache.dtype != k_cache.dtype:
+            raise ValueError("new rows and caches must share a dtype")
+        if t.numel() != slots * kv_heads * d or not t.is_contiguous():
+            raise ValueError(f"new rows must be contiguous [{slots}, {kv_heads}, {d}]")
+    if positions.dtype != torch.int32 or tuple(positions.shape) != (slots,) or not positions.is_cuda:
+        raise ValueError(f"positions must be a device int32 tensor [{slots}]")
+    nv.call("pk_kv_append", k_new, v_new, k_cache, v_cache, nv.dtype_code(k_cache), kv_heads, bs, hs, rs, positions,
+            slots, capacity, d)
+
+
 class SparseDecode:
     def __init__(self, index: DeviceIndex, sae, *, heads_per_unit: int = 4, router: str = "q_activation",
                  query_scale: float = 1.0, query_topk: int | None = None, unique_cap: float | None = None,
@@ -119,14 +148,18 @@ class SparseDecode:
 
     # ------------------------------------------------------------ attention
     def attention(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, length=None, splits=None,
-                  partial: torch.Tensor | None = None) -> torch.Tensor:
+                  partial: torch.Tensor | None = None, append=None) -> torch.Tensor:
         """Sparse attention over the routed ids plus the dense tail.
 
         k, v: [U, total, d] (rows of each unit contiguous) or slot-major
         [B, total, H_kv, d] with U = B * H_kv.  length: rows per unit
         (history + tail), an int or an int32 tensor [U]; default all rows.
         With ``partial`` ([U*G, d+2] fp32) the per-head (m, l, o) partial is
-        written instead of the output (for the sequence-sharded merge)."""
+        written instead of the output (for the sequence-sharded merge).
+        ``append=(k_new, v_new)`` (contiguous, U*d elements each, unit u =
+        slot * H_kv + head) fuses the decode KV append: each unit's new rows
+        are attended as row length[u] - 1, the newest tail row, and written
+        into k and v there (one launch; as kv_append then attention)."""
         U, G, d = self.U, self.G, self.d
         if k.dtype != q.dtype or v.dtype != q.dtype:
             raise ValueError("Q, K and V must share a dtype")
@@ -156,9 +189,16 @@ class SparseDecode:
             if self.out is None or self.out.dtype != q.dtype:
                 self.out = torch.empty(U, G, d, dtype=q.dtype, device=q.device)
             out = self.out
-        nv.call("pk_sparse_av", q, k, v, nv.dtype_code(q), kv_heads, bs, hs, rs, self.ids, self.ids.shape[1],
-                self.count, self.history, lt, U, G, d, S, self.ws.get(("av", U, G, d, S), nbytes), nbytes, out,
-                partial)
+        args = (q, k, v, nv.dtype_code(q), kv_heads, bs, hs, rs, self.ids, self.ids.shape[1], self.count,
+                self.history, lt, U, G, d, S, self.ws.get(("av", U, G, d, S), nbytes), nbytes, out, partial)
+        if append is None:
+            nv.call("pk_sparse_av", *args)
+        else:
+            k_new, v_new = append
+            for t in (k_new, v_new):
+                if t.dtype != q.dtype or t.numel() != U * d or not t.is_contiguous() or not t.is_cuda:
+                    raise ValueError(f"append rows must be contiguous device tensors of {U}x{d} {q.dtype}")
+            nv.call("pk_sparse_av_append", *args, k_new, v_new)
         return out if partial is None else partial
 
     def _length_buf(self, n: int) -> torch.Tensor:

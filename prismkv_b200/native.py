@@ -44,8 +44,10 @@ SIGNATURES = {
     "pk_union": ("PPPlPPiPPiiiPlPPPPPP", ctypes.c_int),
     "pk_sparse_av_workspace_bytes": ("iiii", ctypes.c_size_t),
     "pk_sparse_av": ("PPPiilllPlPPPiiiiPPPPP", ctypes.c_int),
+    "pk_sparse_av_append": ("PPPiilllPlPPPiiiiPPPPPPP", ctypes.c_int),
     "pk_lse_merge": ("PiiiPiP", ctypes.c_int),
     "pk_gather_kv": ("PPiilllPlPPPiilPPPP", ctypes.c_int),
+    "pk_kv_append": ("PPPPiilllPiiiP", ctypes.c_int),
     "pk_sparse_av_noalloc": ("PPPiilllPlPPPiiiiPP", ctypes.c_int),
     "pk_key_center": ("PilliliPP", ctypes.c_int),
     "pk_build_ids_capacity": ("liifi", ctypes.c_int64),

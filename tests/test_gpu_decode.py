@@ -360,3 +360,79 @@ def test_attention_head_counts_and_split_forms_match_oracle(pk, oracle, G):
         got = out.float().cpu().numpy()
         for u in range(U):
             assert rel_l2(got[u], refs[u]) < TOL_BF16, (G, splits, u)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_kv_append_matches_indexed_assignment(pk, dtype):
+    """The decode KV append (batch_append, kernels/cuda_sm90/native_sources/
+    av.cu:70-90) into a slot-major and a unit-major cache equals indexed
+    assignment; positions outside [0, capacity) leave their slot untouched."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(3)
+    S, cap, Hkv, d = 5, 40, 4, 128
+    pos = torch.tensor([0, 17, cap - 1, -1, cap], dtype=torch.int32, device=dev)
+    for shape, new_shape in (((S, cap, Hkv, d), (S, Hkv, d)), ((S, cap, d), (S, d))):
+        Kc = torch.randn(*shape, device=dev, generator=g).to(dtype)
+        Vc = torch.randn(*shape, device=dev, generator=g).to(dtype)
+        kn = torch.randn(*new_shape, device=dev, generator=g).to(dtype)
+        vn = torch.randn(*new_shape, device=dev, generator=g).to(dtype)
+        refK, refV = Kc.clone(), Vc.clone()
+        for s in range(S):
+            p = int(pos[s])
+            if 0 <= p < cap:
+                refK[s, p] = kn[s]
+                refV[s, p] = vn[s]
+        pk.kv_append(kn, vn, Kc, Vc, pos)
+        torch.cuda.synchronize()
+        assert torch.equal(Kc, refK) and torch.equal(Vc, refV)
+    with pytest.raises(ValueError):
+        pk.kv_append(kn, vn, Kc, Vc, pos.long())
+
+
+@pytest.mark.parametrize("G,dtype", [(4, torch.bfloat16), (12, torch.bfloat16), (4, torch.float32)])
+def test_fused_append_equals_append_then_attention(pk, G, dtype):
+    """pk_sparse_av_append (the KV append fused into the attention launch)
+    gives the output and caches of writing the new rows first and attending
+    after (batch_append then batch_av, kernels/cuda_sm90/model.py:109-137),
+    bit for bit: both attention kernels and the fp32 one, with one split, a
+    cluster of splits and more than 8 splits; an inactive unit and a unit
+    without a tail row are left alone."""
+    from prismkv_b200 import native as nv
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(21 + G)
+    U, N, tail, d = 6, 1024, 9, 128
+    total = N + tail + 4
+    K = torch.randn(U, total, d, device=dev, generator=g).to(dtype)
+    V = torch.randn(U, total, d, device=dev, generator=g).to(dtype)
+    Q = torch.randn(U, G, d, device=dev, generator=g).to(dtype).contiguous()
+    kn = torch.randn(U, d, device=dev, generator=g).to(dtype)
+    vn = torch.randn(U, d, device=dev, generator=g).to(dtype)
+    width = 320
+    ids = torch.zeros(U, width, dtype=torch.int32, device=dev)
+    count = torch.full((U,), 300, dtype=torch.int32, device=dev)
+    count[2] = 0
+    for u in range(U):
+        ids[u, :300] = torch.randperm(N, device=dev, generator=g)[:300].sort().values.int()
+    hist = torch.full((U,), N, dtype=torch.int32, device=dev)
+    length = torch.full((U,), N + tail, dtype=torch.int32, device=dev)
+    length[4] = 0          # inactive unit
+    length[5] = N          # no tail row: nothing appended
+    for splits in (1, 8, 12):
+        nbytes = nv.query("pk_sparse_av_workspace_bytes", U, G, d, splits)
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        K1, V1 = K.clone(), V.clone()
+        for u in range(U):
+            if int(length[u]) > N:
+                K1[u, int(length[u]) - 1] = kn[u]
+                V1[u, int(length[u]) - 1] = vn[u]
+        out1 = torch.empty(U, G, d, dtype=dtype, device=dev)
+        code = nv.dtype_code(Q)
+        nv.call("pk_sparse_av", Q, K1, V1, code, 1, K1.stride(0), 0, K1.stride(1), ids, width, count, hist, length,
+                U, G, d, splits, ws, nbytes, out1, None)
+        K2, V2 = K.clone(), V.clone()
+        out2 = torch.empty(U, G, d, dtype=dtype, device=dev)
+        nv.call("pk_sparse_av_append", Q, K2, V2, code, 1, K2.stride(0), 0, K2.stride(1), ids, width, count, hist,
+                length, U, G, d, splits, ws, nbytes, out2, None, kn, vn)
+        torch.cuda.synchronize()
+        assert torch.equal(out1, out2), splits
+        assert torch.equal(K1, K2) and torch.equal(V1, V2), splits
