@@ -613,16 +613,40 @@ def run_seqshard(a):
     q_static = Q[0].clone()
     len_static = torch.full((U,), n_local + (1 if tail else 0), dtype=torch.int32, device=dev)
 
+    out_static = [None]
+
+    def body():
+        out_static[0] = sd(q_static, K, V, length=len_static)
+
+    # The step (route, union, attention, the all-gather of partials, the
+    # merge) replayed as one CUDA graph, captured after eager warm-up steps
+    # (which also set up the NCCL communicator).
+    graph = [None]
+
     def step(s):
         q_static.copy_(Q[s])
         len_static.fill_(n_local + (s + 1 if tail else 0))
-        return sd(q_static, K, V, length=len_static)
+        if graph[0] is not None:
+            graph[0].replay()
+        else:
+            body()
+        return out_static[0]
 
     for s_ in range(a.warmup):
         step(s_)
     torch.cuda.synchronize()
     sd.check()
     barrier()
+    if not a.no_graph:
+        graph[0] = torch.cuda.CUDAGraph()
+        s_cap = torch.cuda.Stream()
+        s_cap.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s_cap):
+            with torch.cuda.graph(graph[0], stream=s_cap):
+                body()
+        torch.cuda.current_stream().wait_stream(s_cap)
+        torch.cuda.synchronize()
+        barrier()
     clocks = Clocks(local)
     clocks.start()
     time.sleep(0.2)
@@ -647,8 +671,11 @@ def run_seqshard(a):
     for s_ in range(a.warmup, steps_total):
         q_static.copy_(h_q[s_], non_blocking=True)
         len_static.fill_(n_local + (s_ + 1 if tail else 0))
-        o = sd(q_static, K, V, length=len_static)
-        h_out.copy_(o, non_blocking=True)
+        if graph[0] is not None:
+            graph[0].replay()
+        else:
+            body()
+        h_out.copy_(out_static[0], non_blocking=True)
     ee1.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(ee0.elapsed_time(ee1))
@@ -665,7 +692,8 @@ def run_seqshard(a):
                    "budget": budget, "budget_per_shard": budget // world, "clusters": C,
                    "tokens_per_shard": n_local, "build_s": round(build_s, 2),
                    "index_build": "exact BatchTopK over the whole sequence (build_sharded)",
-                   "parallelism": f"seq{world}", "l2": "KV rows gathered per step are scattered over >> L2"},
+                   "parallelism": f"seq{world}", "graph": graph[0] is not None,
+                   "l2": "KV rows gathered per step are scattered over >> L2"},
         "e2e": {"value": round(tokens / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(U * G * d * 2), "d2h_bytes_per_step": int(U * G * d * 2)},
         "gpu_launches": 5 * a.steps,
@@ -673,6 +701,8 @@ def run_seqshard(a):
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    graph[0] = None   # a graph holding NCCL calls is released before the group
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
