@@ -8,6 +8,8 @@
 // routed bucket ids -- are bit-identical to the reference's.
 #include <cuda_fp16.h>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "topk.cuh"
 #include "mma.cuh"
@@ -180,13 +182,11 @@ struct QactSmem {
     int is_last;
 };
 
-// Given this head's m positive picks in rank order (sm.sel = feature ids,
-// sm.selkey = value bits), write the normalised contributions and, in the
-// unit's last CTA, aggregate.  `agg` is shared scratch of >= 16*G*k bytes.
-__device__ void head_finish(int u, int g, int G, int F, int k, int m, QactSmem& sm, void* agg,
-                            const int* __restrict__ counts, int* __restrict__ head_ids, float* __restrict__ head_val,
-                            int* __restrict__ unit_done, int* __restrict__ order, int* __restrict__ n_order,
-                            int order_stride, float* __restrict__ score) {
+// This head's m positive picks in rank order (sm.sel = feature ids,
+// sm.selkey = value bits), normalised by their sum (floored at 1e-20) and
+// divided by G, stored in feature order into hid[k] / hv[k], unused slots
+// INT_MAX / 0 (the layout the aggregation's binary searches expect).
+__device__ void head_picks(int G, int k, int m, QactSmem& sm, int* hid, float* hv) {
     const int tid = threadIdx.x, nt = blockDim.x;
     for (int r = tid; r < k; r += nt) sm.val[r] = r < m ? __uint_as_float(sm.selkey[r]) : 0.f;
     __syncthreads();
@@ -197,10 +197,6 @@ __device__ void head_finish(int u, int g, int G, int F, int k, int m, QactSmem& 
     }
     __syncthreads();
     const float s = sm.norm;
-    // Stored in feature order, unused slots INT_MAX, for the binary
-    // searches of the aggregation below.
-    int* hid = head_ids + ((int64_t)u * G + g) * k;
-    float* hv = head_val + ((int64_t)u * G + g) * k;
     for (int r = tid; r < k; r += nt) {
         if (r < m) {
             const int f = sm.sel[r];
@@ -216,23 +212,19 @@ __device__ void head_finish(int u, int g, int G, int F, int k, int m, QactSmem& 
             hv[r] = 0.f;
         }
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) sm.is_last = atomicAdd(&unit_done[u], 1) == G - 1;
-    __syncthreads();
-    if (!sm.is_last) return;
-    __threadfence();
+}
 
-    const int E = G * k;  // <= 256
-    int* eid = reinterpret_cast<int*>(agg);            // [E]
-    float* ev = reinterpret_cast<float*>(agg) + E;     // [E]
-    float* sc = ev + E;                                // [E]
-    int* cand = reinterpret_cast<int*>(sc + E);        // [E]
-    for (int e = tid; e < E; e += nt) {
-        eid[e] = __ldcg(head_ids + (int64_t)u * E + e);
-        ev[e] = __ldcg(head_val + (int64_t)u * E + e);
-    }
-    __syncthreads();
+// Scores of the unit's G*k pick entries (eid/ev: G segments of k sorted
+// entries in shared memory): score[f] = 0 + v_h1 + v_h2 + ... over the heads
+// that picked f, in head order (scatter_add_ of core.py:137), kept at f's
+// first entry; cand[e] = f for a first entry with score > 0 and a live
+// bucket (live[e], or counts[f] > 0 read here when live is null), else -1.
+// One entry per thread; every thread must call it.
+__device__ void unit_scores(int u, int G, int F, int k, const int* eid, const float* ev, const int* live,
+                            const int* __restrict__ counts, float* sc, int* cand, int e_lo, int e_hi,
+                            float* __restrict__ score) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const int E = G * k;
     // Position of feature f in head hh's sorted picks, or -1.
     auto find = [&](int hh, int f) -> int {
         const int* seg = eid + hh * k;
@@ -244,8 +236,6 @@ __device__ void head_finish(int u, int g, int G, int F, int k, int m, QactSmem& 
         }
         return lo < k && seg[lo] == f ? lo : -1;
     };
-    // score[f] = 0 + v_h1 + v_h2 + ... over the heads that picked f, in head
-    // order (scatter_add_ of core.py:137), kept at f's first entry.
     for (int e = tid; e < E; e += nt) {
         const int f = eid[e];
         const int h = e / k;
@@ -259,21 +249,29 @@ __device__ void head_finish(int u, int g, int G, int F, int k, int m, QactSmem& 
                 if (i >= 0) acc = __fadd_rn(acc, ev[hh * k + i]);
             }
         }
-        const bool keep = first && acc > 0.f && counts[(int64_t)u * F + f] > 0;
+        const bool keep = first && acc > 0.f && (live ? live[e] != 0 : counts[(int64_t)u * F + f] > 0);
         sc[e] = acc;
         cand[e] = keep ? f : -1;
-        if (score && first) score[(int64_t)u * F + f] = acc;
+        if (score && first && e >= e_lo && e < e_hi) score[(int64_t)u * F + f] = acc;
     }
     __syncthreads();
-    // Rank the kept candidates by (score desc, feature asc); P threads
-    // (a power of two within a warp) share each entry's comparisons.
+}
+
+// order[u, r] = f for the kept entries e in [e_lo, e_hi), r = the rank of
+// (score desc, feature asc) among all kept entries; P threads (a power of
+// two within a warp) share each entry's comparisons.  Returns the number of
+// kept entries (every thread).  Every thread must call it.
+__device__ int unit_rank(int u, int E, const float* sc, const int* cand, int e_lo, int e_hi, int* scan,
+                         int* __restrict__ order, int order_stride) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const int n_own = e_hi - e_lo;
     int P = 1;
-    while (P < 32 && 2 * P * E <= nt) P *= 2;
-    {
-        const int e = tid / P, part = tid % P;
+    while (P < 32 && 2 * P * n_own <= nt) P *= 2;
+    for (int base = 0; base < n_own * P; base += nt) {
+        const int e = e_lo + (base + tid) / P, part = (base + tid) % P;
         int f = -1;
         float v = 0.f;
-        if (e < E) {
+        if (e < e_hi) {
             f = cand[e];
             v = sc[e];
         }
@@ -292,7 +290,38 @@ __device__ void head_finish(int u, int g, int G, int F, int k, int m, QactSmem& 
     int mine = 0;
     for (int e = tid; e < E; e += nt) mine += cand[e] >= 0;
     int tot;
-    block_exclusive_scan(mine, sm.tk.scan, &tot);
+    block_exclusive_scan(mine, scan, &tot);
+    return tot;
+}
+
+// Given this head's m positive picks in rank order, write the normalised
+// contributions to global memory and, in the unit's last CTA (an arrival
+// counter), aggregate.  `agg` is shared scratch of >= 16*G*k bytes.
+__device__ void head_finish(int u, int g, int G, int F, int k, int m, QactSmem& sm, void* agg,
+                            const int* __restrict__ counts, int* __restrict__ head_ids, float* __restrict__ head_val,
+                            int* __restrict__ unit_done, int* __restrict__ order, int* __restrict__ n_order,
+                            int order_stride, float* __restrict__ score) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    head_picks(G, k, m, sm, head_ids + ((int64_t)u * G + g) * k, head_val + ((int64_t)u * G + g) * k);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) sm.is_last = atomicAdd(&unit_done[u], 1) == G - 1;
+    __syncthreads();
+    if (!sm.is_last) return;
+    __threadfence();
+
+    const int E = G * k;  // <= 256
+    int* eid = reinterpret_cast<int*>(agg);            // [E]
+    float* ev = reinterpret_cast<float*>(agg) + E;     // [E]
+    float* sc = ev + E;                                // [E]
+    int* cand = reinterpret_cast<int*>(sc + E);        // [E]
+    for (int e = tid; e < E; e += nt) {
+        eid[e] = __ldcg(head_ids + (int64_t)u * E + e);
+        ev[e] = __ldcg(head_val + (int64_t)u * E + e);
+    }
+    __syncthreads();
+    unit_scores(u, G, F, k, eid, ev, nullptr, counts, sc, cand, 0, E, score);
+    const int tot = unit_rank(u, E, sc, cand, 0, E, sm.tk.scan, order, order_stride);
     if (tid == 0) {
         n_order[u] = tot;
         unit_done[u] = 0;
@@ -604,6 +633,14 @@ struct FastSmem {
     uint32_t gkey[kMaxGroups];
     int wc[32];
     float lam;
+    // Cluster form: this head's sorted picks and their live flags, and a
+    // copy of every head's of the unit.
+    int hid[256];
+    float hv[256];
+    int hlive[256];
+    int all_id[256];
+    float all_v[256];
+    int all_live[256];
 };
 
 // Per (unit, head), the exact top-k of the activations from the bounds of
@@ -620,7 +657,13 @@ struct FastSmem {
 // recomputed.
 // MINB = 2 when there are more heads than SMs: two CTAs per SM (at most 128
 // registers a thread) instead of a second wave.
-template <int ORDER, typename QT, int MINB>
+// kCluster: the G head CTAs of a unit form a thread-block cluster (G <= 8);
+// each copies every head's picks from the others' shared memory, computes
+// all entries' scores (the same arithmetic as the single-CTA aggregation)
+// and ranks and writes the order slots of its own head's entries.
+// Otherwise the picks go through global memory and the unit's last CTA to
+// arrive builds the whole order.
+template <int ORDER, typename QT, int MINB, bool kCluster>
 __global__ void __launch_bounds__(kSelThreads, MINB)
 qact_select_fast_kernel(const QT* __restrict__ q, const float* __restrict__ upper,
                         const uint32_t* __restrict__ gmax, int ngroups, const int* __restrict__ units, int G,
@@ -665,22 +708,28 @@ qact_select_fast_kernel(const QT* __restrict__ q, const float* __restrict__ uppe
     const int s0 = min(F, warp * seg), s1 = min(F, s0 + seg);
     int* wslot = sm.cand + warp * kWarpCand;
     int mine = 0;
+    // Slots in feature order (lane-major, then the lane's four features):
+    // the candidates before this lane come from four ballots, no scan.
+    const unsigned lt_mask = (1u << lane) - 1u;
     auto take = [&](int base, const float (&v)[4]) {
         unsigned m = 0;
 #pragma unroll
         for (int c = 0; c < 4; ++c)
             if (base + 4 * lane + c < s1 && is_cand(v[c])) m |= 1u << c;
-        const int cnt = __popc(m);
-        if (__ballot_sync(0xffffffffu, cnt != 0)) {
-            const int inc = warp_inclusive_scan(cnt);
-            int at = mine + inc - cnt;
+        unsigned b[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) b[c] = __ballot_sync(0xffffffffu, (m >> c) & 1u);
+        const unsigned any = b[0] | b[1] | b[2] | b[3];
+        if (any) {
+            int at = mine + __popc(b[0] & lt_mask) + __popc(b[1] & lt_mask) + __popc(b[2] & lt_mask) +
+                     __popc(b[3] & lt_mask);
 #pragma unroll
             for (int c = 0; c < 4; ++c)
                 if (m & (1u << c)) {
                     if (at < kWarpCand) wslot[at] = base + 4 * lane + c;
                     ++at;
                 }
-            mine += __shfl_sync(0xffffffffu, inc, 31);
+            mine += __popc(b[0]) + __popc(b[1]) + __popc(b[2]) + __popc(b[3]);
         }
     };
     if (vec) {
@@ -787,8 +836,33 @@ qact_select_fast_kernel(const QT* __restrict__ q, const float* __restrict__ uppe
             sm.q.selkey, sm.q.tk);
     }
     __syncthreads();
-    head_finish(u, g, G, F, k, m, sm.q, sA, counts, head_ids, head_val, unit_done, order, n_order, order_stride,
-                score);
+    if constexpr (kCluster) {
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        head_picks(G, k, m, sm.q, sm.hid, sm.hv);
+        __syncthreads();
+        for (int r = tid; r < k; r += nt) {
+            const int f = sm.hid[r];
+            sm.hlive[r] = f != INT32_MAX && counts[(int64_t)u * F + f] > 0;
+        }
+        cluster.sync();   // every head's picks are in its CTA's shared memory
+        const int E = G * k;
+        for (int e = tid; e < E; e += nt) {
+            const int h = e / k, r = e - h * k;
+            sm.all_id[e] = cluster.map_shared_rank(sm.hid, h)[r];
+            sm.all_v[e] = cluster.map_shared_rank(sm.hv, h)[r];
+            sm.all_live[e] = cluster.map_shared_rank(sm.hlive, h)[r];
+        }
+        cluster.sync();   // no CTA exits while another still reads its picks
+        float* sc = reinterpret_cast<float*>(sA);
+        int* cand = reinterpret_cast<int*>(sA) + E;
+        unit_scores(u, G, F, k, sm.all_id, sm.all_v, sm.all_live, counts, sc, cand, g * k, (g + 1) * k, score);
+        const int tot = unit_rank(u, E, sc, cand, g * k, (g + 1) * k, sm.q.tk.scan, order, order_stride);
+        if (g == 0 && tid == 0) n_order[u] = tot;
+    } else {
+        head_finish(u, g, G, F, k, m, sm.q, sA, counts, head_ids, head_val, unit_done, order, n_order, order_stride,
+                    score);
+    }
 }
 
 __global__ void zero_rows_kernel(float* __restrict__ score, const int* __restrict__ units, int F) {
@@ -1012,13 +1086,38 @@ extern "C" int pk_route_qact(uint64_t q, int q_dtype, uint64_t units, int n_unit
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         const bool wide = n_units * G > sms;
+        // The G head CTAs of a unit as one cluster (G <= 8, portable sizes).
+        const bool clustered = G <= 8;
 #define PK_LAUNCH_FAST1(ORD, QT, MINB)                                                                           \
     do {                                                                                                         \
-        cudaFuncSetAttribute(qact_select_fast_kernel<ORD, QT, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                             (int)fsmem);                                                                        \
-        qact_select_fast_kernel<ORD, QT, MINB><<<n_units * G, kSelThreads, fsmem, st>>>(                         \
-            (const QT*)q, act, gmax, ngroups, ul, G, (const float*)w_enc, (const float*)b_enc, query_scale, F,   \
-            k, (const int*)counts, hid, hval, done, (int*)order, (int*)n_order, order_stride, (float*)score);    \
+        if (clustered) {                                                                                         \
+            auto fn = qact_select_fast_kernel<ORD, QT, MINB, true>;                                              \
+            cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem);                   \
+            cudaLaunchConfig_t cfg = {};                                                                         \
+            cfg.gridDim = dim3(n_units * G);                                                                     \
+            cfg.blockDim = dim3(kSelThreads);                                                                    \
+            cfg.dynamicSmemBytes = fsmem;                                                                        \
+            cfg.stream = st;                                                                                     \
+            cudaLaunchAttribute attr[1];                                                                         \
+            attr[0].id = cudaLaunchAttributeClusterDimension;                                                    \
+            attr[0].val.clusterDim.x = G;                                                                        \
+            attr[0].val.clusterDim.y = 1;                                                                        \
+            attr[0].val.clusterDim.z = 1;                                                                        \
+            cfg.attrs = attr;                                                                                    \
+            cfg.numAttrs = 1;                                                                                    \
+            const cudaError_t e_ = cudaLaunchKernelEx(                                                           \
+                &cfg, fn, (const QT*)q, (const float*)act, (const uint32_t*)gmax, ngroups, ul, G,                \
+                (const float*)w_enc, (const float*)b_enc, query_scale, F, k, (const int*)counts, hid, hval,      \
+                done, (int*)order, (int*)n_order, order_stride, (float*)score);                                  \
+            if (e_ != cudaSuccess) return (int)e_;                                                               \
+        } else {                                                                                                 \
+            auto fn = qact_select_fast_kernel<ORD, QT, MINB, false>;                                             \
+            cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem);                   \
+            fn<<<n_units * G, kSelThreads, fsmem, st>>>(                                                         \
+                (const QT*)q, act, gmax, ngroups, ul, G, (const float*)w_enc, (const float*)b_enc, query_scale,  \
+                F, k, (const int*)counts, hid, hval, done, (int*)order, (int*)n_order, order_stride,             \
+                (float*)score);                                                                                  \
+        }                                                                                                        \
     } while (0)
 #define PK_LAUNCH_FAST(ORD, QT)                                                                                  \
     do {                                                                                                         \
