@@ -436,3 +436,25 @@ def test_fused_append_equals_append_then_attention(pk, G, dtype):
         torch.cuda.synchronize()
         assert torch.equal(out1, out2), splits
         assert torch.equal(K1, K2) and torch.equal(V1, V2), splits
+
+
+@pytest.mark.parametrize("G", [3, 8, 12])
+def test_routing_head_counts_match_oracle(pk, oracle, batch, G):
+    """q_activation routing (core.py:131-139) for G heads per unit, bit-exact
+    against the oracle: G <= 8 builds the unit's order in a cluster of its
+    head CTAs, G = 12 in the unit's last CTA; G = 3 takes the interleaved dot
+    order of F.linear, G >= 6 the sequential one."""
+    B = batch
+    U, d, k = B["U"], B["d"], B["k"]
+    rs = np.random.RandomState(40 + G)
+    q = bf16_round(rs.standard_normal((U, G, d)).astype(np.float32))
+    Q = torch.from_numpy(q).cuda().to(torch.bfloat16).contiguous()
+    op = pk.SparseDecode(B["idx"], B["sae"], heads_per_unit=G, unique_cap=512 / B["N"])
+    op.route(Q)
+    torch.cuda.synchronize()
+    for u in range(U):
+        _, ref = oracle.bucket_scores(q[u], B["oidx"][u], router="q_activation", sae=B["osae"], query_scale=1.0,
+                                      query_topk=k)
+        n = int(op.n_order[u])
+        assert n == len(ref), (G, u)
+        assert np.array_equal(op.order[u, :n].cpu().numpy(), ref), (G, u)
