@@ -725,8 +725,10 @@ build_tiles_kernel(const __half* __restrict__ Wh, const float* __restrict__ wn, 
 //     shared-memory buffer j & 1 with two bulk copies, and issues the eight
 //     K=16 MMAs of tile j into TMEM accumulator j & 1 once the copy has
 //     landed and the epilogue of tile j-2 has drained that accumulator;
-//   warps 0-7: the epilogue of tile j from TMEM -- one token row and 128
-//     features per thread -- then release the accumulator.
+//   warps 0-15: the epilogue of tile j from TMEM -- one token row and 64
+//     features per thread (warp w: rows of lane quarter w % 4, features of
+//     quarter w / 4) -- then release the accumulator; warps 0-7 also stage
+//     the CTA's 128 key rows first.
 // The stages meet on mbarriers only (full, MMA done, TMEM empty per buffer);
 // every wait is bounded, and a wait that runs out aborts the CTA with
 // PK_STATUS_NEEDS_EXACT after the copies and MMAs in flight have landed.
@@ -736,7 +738,11 @@ build_tiles_kernel(const __half* __restrict__ Wh, const float* __restrict__ wn, 
 //     (a 1024-bin window; the top bin collects everything above); entries
 //     whose upper bound reaches the floor are kept, with their bounds, for
 //     build_classify_kernel (one tensor-core pass in all).
-constexpr int kTcTokens = 128, kTcEpiWarps = 8, kTcThreads = 32 * (kTcEpiWarps + 1);
+constexpr int kTcTokens = 128, kTcEpiWarps = 16, kTcThreads = 32 * (kTcEpiWarps + 1);
+constexpr int kTcStageWarps = 8;                                  // warps that stage the key rows (16 each)
+constexpr int kTcCols = kTcFeat * 4 / kTcEpiWarps;                // features per epilogue thread
+constexpr int kTcChunks = kTcCols / 32;
+static_assert(kTcCols == 64, "the epilogue loads its 64 columns with one tmem_ld64_wait");
 constexpr int kTcXBytes = kTcTokens * 256;          // 2 K-atoms x 128 rows x 128 B
 constexpr int kTcSideSlots = 4;                     // side records: tile j in slot j % 4
 constexpr uint64_t kTcWaitNs = 200000000ull;        // 0.2 s: no copy or MMA takes this long
@@ -810,7 +816,7 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
         for (int i = tid; i < kFBins; i += kTcThreads) hA[i] = 0;
     else
         for (int i = tid; i < 2 * kFWin; i += kTcThreads) hA[i] = 0;
-    if (warp < kTcEpiWarps) {
+    if (warp < kTcStageWarps) {
         // x = (k - center) / key_scale in fp32 (core.py:99), rounded to fp16;
         // this warp's 16 key rows, every load issued before any is used.
         const bool unit_scale = key_scale == 1.0f;
@@ -905,7 +911,7 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
     } else if (warp < kTcEpiWarps) {
         // ------------------------------------------------------- epilogue
         const int floor_bin = MODE == 1 ? fw.floor_bin[u] : 0;
-        const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+        const int row = 32 * (warp & 3) + lane, part = warp >> 2, half = part * kTcCols / 128;
         const int64_t trow_t = t0 + row;
         const bool trow = trow_t < N;
         const float xr = xn[row];
@@ -941,10 +947,12 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
                 break;
             }
             tc_fence_after();
-            const int f0 = (ft_first + j * fstep) * kTcFeat + half * 128;
+            const int f0 = (ft_first + j * fstep) * kTcFeat + part * kTcCols;
             const float* sd = reinterpret_cast<const float*>(side + (j % kTcSideSlots) * kTcSideBytes);
-            const float* wnb = sd + half * 128;
-            const float* bb = sd + kTcFeat + half * 128;
+            const float* wnb = sd + part * kTcCols;
+            const float* bb = sd + kTcFeat + part * kTcCols;
+            // The side record's maxima cover 128-feature halves (bounds for
+            // any quarter inside).
             const float2 st2 = reinterpret_cast<const float2*>(sd + 2 * kTcFeat)[half];
             const float wm = st2.x, bm = st2.y;
             const float cs = 4.76837158203125e-07f * (xr + wm);
@@ -955,11 +963,11 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
             // per entry, the full bound work only for the entries it keeps.
             const float vfloor = fval - 1.001f * E - 3.814697265625e-06f * (fval + E);
             const float tau = vfloor - bm;
-            const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(b * kTcFeat + half * 128);
-            // The row's 128 accumulators in one TMEM round trip.
-            float v[128];
+            const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(b * kTcFeat + part * kTcCols);
+            // The row's kTcCols accumulators in one TMEM round trip.
+            float v[kTcCols];
             __syncwarp();
-            tmem_ld128_wait(taddr, v);
+            tmem_ld64_wait(taddr, v);
             if (MODE == 0) {
                 // The sample bins one lower bound per 32 columns, below the
                 // largest of theirs (E bounds every column's error).  Counts
@@ -968,7 +976,7 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
                 // which bins nothing.
                 if (trow) {
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
+                    for (int c = 0; c < kTcChunks; ++c) {
                         float mx = -INFINITY;
 #pragma unroll
                         for (int q = 0; q < 32; ++q) mx = fmaxf(mx, v[32 * c + q] + bb[32 * c + q]);
@@ -979,9 +987,9 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
                     }
                 }
             } else {
-                uint32_t m[4];
+                uint32_t m[kTcChunks];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < kTcChunks; ++c) {
                     uint32_t mc = 0;
 #pragma unroll
                     for (int q = 0; q < 32; ++q) mc |= (v[32 * c + q] >= tau ? 1u : 0u) << q;
@@ -996,7 +1004,9 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
                 // one scan per tile; entries whose exact U misses the floor
                 // get U = -1.  Kept entries are rare: loops over the set bits
                 // (a branch per entry, not a predicated body per column).
-                const int nk = __popc(m[0]) + __popc(m[1]) + __popc(m[2]) + __popc(m[3]);
+                int nk = 0;
+#pragma unroll
+                for (int c = 0; c < kTcChunks; ++c) nk += __popc(m[c]);
                 const int inc = warp_inclusive_scan(nk);
                 const int wtot = __shfl_sync(0xffffffffu, inc, 31);
                 if (wtot > 0) {
@@ -1012,7 +1022,7 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
                         wcnt += wtot;
                     }
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
+                    for (int c = 0; c < kTcChunks; ++c) {
                         for (uint32_t mm = m[c]; mm; mm &= mm - 1) {
                             const int q = __ffs(mm) - 1;
                             const int col = c * 32 + q;
