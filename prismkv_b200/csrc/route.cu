@@ -458,10 +458,6 @@ qact_approx_kernel(const QT* __restrict__ q, const int* __restrict__ units, int 
         cp_async_16(smem_addr(Wt) + swz(row, ch), Wb + (int64_t)(valid ? f : 0) * kEncD + ch * 8, valid);
     }
     cp_async_commit_group();
-    // Everything above reads only the SAE (static); when this launch is a
-    // programmatic dependent of the previous kernel, the queries are read
-    // only after that kernel has completed.
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     // The 64 query rows, 16-byte chunks of 8 values (all loads of a thread
     // issued before any is used), scaled, rounded to bf16, and their norms.
     constexpr int kChunks = kApxHeads * 16 / kApxThreads;
@@ -1049,31 +1045,17 @@ extern "C" int pk_route_qact(uint64_t q, int q_dtype, uint64_t units, int n_unit
         if (q % 16 || w_bf16 % 16) return PK_ERR_ARG;   // 16-byte row loads
         dim3 ag((F + kApxFeat - 1) / kApxFeat, (n_units * G + kApxHeads - 1) / kApxHeads);
         const int asmem = (kApxHeads + kApxFeat) * 256;
-        // Launched as a programmatic dependent of the stream's previous
-        // kernel: its SAE tile loads overlap that kernel's tail.
-        cudaLaunchConfig_t acfg = {};
-        acfg.gridDim = ag;
-        acfg.blockDim = dim3(kApxThreads);
-        acfg.dynamicSmemBytes = asmem;
-        acfg.stream = st;
-        cudaLaunchAttribute aattr[1];
-        aattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        aattr[0].val.programmaticStreamSerializationAllowed = 1;
-        acfg.attrs = aattr;
-        acfg.numAttrs = 1;
-        cudaError_t ae;
         if (q_dtype == PK_BF16) {
             cudaFuncSetAttribute(qact_approx_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, asmem);
-            ae = cudaLaunchKernelEx(&acfg, qact_approx_kernel<__nv_bfloat16>, (const __nv_bfloat16*)q, ul, n_units, G,
-                                    (const __nv_bfloat16*)w_bf16, (const float*)b_enc, (const float*)w_norm,
-                                    query_scale, F, gs, ngroups, act, gmax);
+            qact_approx_kernel<__nv_bfloat16><<<ag, kApxThreads, asmem, st>>>(
+                (const __nv_bfloat16*)q, ul, n_units, G, (const __nv_bfloat16*)w_bf16, (const float*)b_enc,
+                (const float*)w_norm, query_scale, F, gs, ngroups, act, gmax);
         } else {
             cudaFuncSetAttribute(qact_approx_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, asmem);
-            ae = cudaLaunchKernelEx(&acfg, qact_approx_kernel<float>, (const float*)q, ul, n_units, G,
-                                    (const __nv_bfloat16*)w_bf16, (const float*)b_enc, (const float*)w_norm,
-                                    query_scale, F, gs, ngroups, act, gmax);
+            qact_approx_kernel<float><<<ag, kApxThreads, asmem, st>>>(
+                (const float*)q, ul, n_units, G, (const __nv_bfloat16*)w_bf16, (const float*)b_enc,
+                (const float*)w_norm, query_scale, F, gs, ngroups, act, gmax);
         }
-        if (ae != cudaSuccess) return (int)ae;
         PK_CHECK_LAUNCH();
         if (score) {
             zero_rows_kernel<<<n_units, 256, 0, st>>>((float*)score, ul, F);

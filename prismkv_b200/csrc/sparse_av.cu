@@ -528,10 +528,6 @@ sparse_av_bf16_kernel(AvParams p) {
         }
         __syncwarp();   // every lane has read the stage before it is refilled
     }
-    // The rows are in: a programmatic dependent of this launch (the next
-    // layer's routing, which reads its SAE before it waits for this grid)
-    // may start.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     cp_async_wait<0>();
     __syncthreads();
 
