@@ -5,15 +5,18 @@
 //
 // bf16 path: a CTA of four warps streams its split's rows in tiles of 64 K
 // rows and 64 V rows, three stages deep.  Each warp gathers its own 16 rows of
-// every tile with 16-byte cp.async (rows addressed through the id list) and
-// computes on them alone, so the warps pipeline independently (no CTA barrier
-// per tile).  For G <= 8 heads the warp's 16 key rows fill the M = 16 of
-// mma.sync m16n8k16 and the heads its N = 8 (S^T = K Q^T, then O^T += V^T P^T
-// with P^T formed by movmatrix); for 9..16 heads the heads fill M instead.
-// Softmax is online in fp32 and P enters the PV product in bf16.  The S split
-// CTAs of a unit form a thread-block cluster and merge their states through
-// distributed shared memory; above 8 splits the last CTA of a unit to finish
-// merges partials from global memory.
+// every tile with 16-byte cp.async (rows addressed through the id list).  For
+// G <= 8 heads the warp also computes on those rows alone, so the warps
+// pipeline independently (no CTA barrier per tile): its 16 key rows fill the
+// M = 16 of mma.sync m16n8k16 and the heads its N = 8 (S^T = K Q^T, then
+// O^T += V^T P^T with P^T formed by movmatrix).  For 9..16 heads the heads
+// fill M, with a CTA barrier per tile.  Softmax is online in fp32 and P
+// enters the PV product in bf16.  The S split CTAs of a unit form a
+// thread-block cluster and merge their states through distributed shared
+// memory; above 8 splits the last CTA of a unit to finish merges partials
+// from global memory.  The _append entry point fuses the decode KV append:
+// the unit's new rows are attended in place of its newest tail row and
+// written into the cache by its first split CTA.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
