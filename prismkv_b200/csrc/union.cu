@@ -25,7 +25,7 @@
 
 namespace pk {
 
-constexpr int kUnionThreads = 512;
+constexpr int kUnionThreads = 1024;
 constexpr int kMaxCand = 256;     // candidates per unit (G * k)
 constexpr uint32_t kFlipFlag = 0x80000000u;
 
