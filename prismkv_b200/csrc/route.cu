@@ -390,7 +390,7 @@ __global__ void sae_prepare_kernel(const float* __restrict__ W, int F, __nv_bflo
     if (lane == 0) wn[f] = sqrtf(ss) * (1.0f + 1.0f / 4096.0f);
 }
 
-constexpr int kApxHeads = 64, kApxFeat = 128, kApxThreads = 128;
+constexpr int kApxHeads = 64, kApxFeat = 128, kApxThreads = 256;
 constexpr int kMaxGroups = 512;
 
 __device__ __forceinline__ uint32_t fkey(float x) {
@@ -429,7 +429,7 @@ __device__ __forceinline__ void load8(const float* p, float (&x)[8]) {
 
 // Tensor-core approximation of the query activations with rigorous bounds.
 // v[u, g, f] = (q/scale) . W_f + b_f with bf16 operands on mma.sync and fp32
-// accumulation (a 64-head x 128-feature tile per CTA, 16 heads per warp)
+// accumulation (a 64-head x 128-feature tile per CTA, 16 x 64 per warp)
 // differs from the exact fp32 activation by at most
 //     e_f = 2^-6 |x| |W_f| + 2^-20 |v|
 // (bf16 rounding of both operands, 2^-8 relative each, fp32 accumulation and
@@ -500,36 +500,46 @@ qact_approx_kernel(const QT* __restrict__ q, const int* __restrict__ units, int 
     cp_async_wait_group<0>();
     __syncthreads();
 
-    float acc[16][4];
+    // Warp w multiplies head rows 16(w&3).. by feature half fh = w>>2
+    // (64 features): eight warps keep twice the loads and stores in flight
+    // of a 16 x 128 warp tile at the same register count.
+    const int rb = warp & 3, fh = warp >> 2;
+    float acc[8][4];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
     const int mi = lane >> 3, r = lane & 7;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
         uint32_t a[4];
-        ldsm_x4(smem_addr(Xs) + swz(warp * 16 + (mi & 1) * 8 + r, 2 * kk + (mi >> 1)), a);
+        ldsm_x4(smem_addr(Xs) + swz(rb * 16 + (mi & 1) * 8 + r, 2 * kk + (mi >> 1)), a);
 #pragma unroll
-        for (int np = 0; np < 8; ++np) {
+        for (int np = 0; np < 4; ++np) {
             uint32_t b[4];
-            ldsm_x4(smem_addr(Wt) + swz(np * 16 + (mi >> 1) * 8 + r, 2 * kk + (mi & 1)), b);
+            ldsm_x4(smem_addr(Wt) + swz(fh * 64 + np * 16 + (mi >> 1) * 8 + r, 2 * kk + (mi & 1)), b);
             mma_16816(acc[2 * np], a, b[0], b[1]);
             mma_16816(acc[2 * np + 1], a, b[2], b[3]);
         }
     }
-    // acc[j][2*half + e] is feature f0 + 8j + 2(lane&3) + e of local row
-    // warp*16 + (lane>>2) + 8*half.
-    float bv[16][2], wv[16][2];
+    // acc[j][2*half + e] is feature fb + 8j + 2(lane&3) + e of local row
+    // rb*16 + (lane>>2) + 8*half, fb = f0 + 64 fh.
+    const int fb = f0 + fh * 64;
+    float bv[8][2], wv[8][2];
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
+    for (int j = 0; j < 8; ++j)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-            const int f = f0 + 8 * j + 2 * (lane & 3) + e;
+            const int f = fb + 8 * j + 2 * (lane & 3) + e;
             bv[j][e] = f < F ? bias[f] : 0.f;
             wv[j][e] = f < F ? wn[f] : 0.f;
         }
+    // 8-feature blocks per group; a group of 128 spans both feature halves
+    // and is finished through shared memory below.
+    const int per = gs >> 3, g0 = gs ? f0 / gs : 0;
+    const bool split = per == 16;
+    uint32_t part[2] = {0u, 0u};
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
-        const int lrow = warp * 16 + (lane >> 2) + half * 8;
+        const int lrow = rb * 16 + (lane >> 2) + half * 8;
         const int h = h0 + lrow;
         const bool hv = h < n_heads;
         int u = 0, g = 0;
@@ -540,13 +550,12 @@ qact_approx_kernel(const QT* __restrict__ q, const int* __restrict__ units, int 
         }
         const float xn = sxn[lrow];
         float* out = upper + ((int64_t)u * G + g) * F;
-        const int per = gs >> 3, g0 = gs ? f0 / gs : 0;   // 8-feature blocks per group
         uint32_t* gm = gmax + ((int64_t)u * G + g) * ngroups;
         const bool writer = gs && hv && (lane & 3) == 0;
         uint32_t run = 0u;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const int f = f0 + 8 * j + 2 * (lane & 3);
+        for (int j = 0; j < 8; ++j) {
+            const int f = fb + 8 * j + 2 * (lane & 3);
             float up[2];
             uint32_t lk = 0u;
 #pragma unroll
@@ -567,12 +576,38 @@ qact_approx_kernel(const QT* __restrict__ q, const int* __restrict__ units, int 
             // At a group's last 8-feature block, reduce over the quad
             // (the four lanes holding the row's features of each block).
             run = max(run, lk);
-            if (gs && ((j + 1) & (per - 1)) == 0) {
+            if (gs && !split && ((fh * 8 + j + 1) & (per - 1)) == 0) {
                 run = max(run, __shfl_xor_sync(0xffffffffu, run, 1));
                 run = max(run, __shfl_xor_sync(0xffffffffu, run, 2));
-                const int gi = g0 + (j + 1) / per - 1;
+                const int gi = g0 + (fh * 8 + j + 1) / per - 1;
                 if (writer && gi < ngroups) gm[gi] = run;
                 run = 0u;
+            }
+        }
+        if (split) {
+            run = max(run, __shfl_xor_sync(0xffffffffu, run, 1));
+            part[half] = max(run, __shfl_xor_sync(0xffffffffu, run, 2));
+        }
+    }
+    if (split) {
+        // Half 0 leaves its row maxima in shared memory; half 1 adds its own
+        // and writes the group (g0 < ngroups: the tile starts inside F).
+        __shared__ uint32_t sgrp[kApxHeads];
+        if (fh == 0 && (lane & 3) == 0) {
+            sgrp[rb * 16 + (lane >> 2)] = part[0];
+            sgrp[rb * 16 + (lane >> 2) + 8] = part[1];
+        }
+        __syncthreads();
+        if (fh == 1 && (lane & 3) == 0) {
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int lrow = rb * 16 + (lane >> 2) + half * 8;
+                const int h = h0 + lrow;
+                if (h < n_heads) {
+                    const int ui = h / G, g = h % G;
+                    const int u = units ? units[ui] : ui;
+                    gmax[((int64_t)u * G + g) * ngroups + g0] = max(part[half], sgrp[lrow]);
+                }
             }
         }
     }
