@@ -456,35 +456,29 @@ def run_ours(a):
 # CPU: the reference path restated by the oracle, on a bounded sample
 # ---------------------------------------------------------------------------
 
-def cpu_rate(a, seconds: float = 10.0) -> dict:
-    """Times the oracle's route + select + attend for a sample of config-3
-    units on the host cores (one unit per thread) and scales to a full
-    decode step (all units x layers).  The sample's bucket index is a
-    synthetic CSR with key_mean memberships per token (its build is not
-    timed)."""
+def _oracle_decode_time(N, F, d, G, k, C, key_mean, budget, tail, n_units, seconds, seed=1234):
+    """Seconds per batch of n_units units for the oracle's route + select +
+    attend (q_activation), one unit per host thread.  Each unit's bucket
+    index is a synthetic CSR with key_mean memberships per token (its build
+    is not timed).  Returns (seconds per batch, reps)."""
     import numpy as np
     from concurrent.futures import ThreadPoolExecutor
     sys.path.insert(0, str(ROOT / "tests" / "golden"))
     import oracle
     from gen import bf16_round
 
-    cores = os.cpu_count() or 1
-    n_units = max(1, min(cores, a.batch * a.kv_heads))
-    N, F, d, G, k = a.history, a.features, 128, a.q_per_kv, a.query_topk
-    tail = 128
-    rs = np.random.RandomState(1234)
+    rs = np.random.RandomState(seed)
     W = (rs.standard_normal((F, d)) / np.sqrt(d)).astype(np.float32)
-    sae = oracle.SAE(W, np.zeros(F, np.float32), key_mean=a.key_mean, query_topk=k)
+    sae = oracle.SAE(W, np.zeros(F, np.float32), key_mean=key_mean, query_topk=k)
     units = []
     for u in range(n_units):
-        C = a.clusters
         centers = rs.standard_normal((C, d)).astype(np.float32)
         cid = rs.randint(0, C, N + tail)
         keys = bf16_round(centers[cid] + np.float32(0.3) * rs.standard_normal((N + tail, d)).astype(np.float32))
         vals = bf16_round(rs.standard_normal((N + tail, d)).astype(np.float32))
         q = bf16_round(centers[rs.randint(0, C, G)] + np.float32(0.3) * rs.standard_normal((G, d)).astype(np.float32))
-        feats = rs.randint(0, F, size=(N, a.key_mean))
-        tok = np.repeat(np.arange(N), a.key_mean)
+        feats = rs.randint(0, F, size=(N, key_mean))
+        tok = np.repeat(np.arange(N), key_mean)
         order = np.lexsort((tok, feats.reshape(-1)))
         fs, ts = feats.reshape(-1)[order], tok[order]
         keep = np.ones(len(fs), bool)
@@ -495,7 +489,7 @@ def cpu_rate(a, seconds: float = 10.0) -> dict:
         np.cumsum(counts, out=offsets[1:])
         idx = oracle.FeatureIndex(N, np.zeros(d, np.float32), counts, None, None, offsets, ts.astype(np.int64))
         units.append((q, keys, vals, idx))
-    cap = a.budget / N
+    cap = budget / N
 
     def one(unit):
         q, keys, vals, idx = unit
@@ -511,13 +505,58 @@ def cpu_rate(a, seconds: float = 10.0) -> dict:
             list(ex.map(one, units))
             t_total += time.perf_counter() - t0
             reps += 1
-    per_batch = t_total / reps                       # n_units units in parallel
+    return t_total / reps, reps
+
+
+def cpu_rate(a, seconds: float = 10.0) -> dict:
+    """Times the oracle's route + select + attend for a sample of config-3
+    units on the host cores (one unit per thread) and scales to a full
+    decode step (all units x layers).  The sample's bucket index is a
+    synthetic CSR with key_mean memberships per token (its build is not
+    timed)."""
+    cores = os.cpu_count() or 1
+    n_units = max(1, min(cores, a.batch * a.kv_heads))
+    N, F, d, G, k = a.history, a.features, 128, a.q_per_kv, a.query_topk
+    tail = 128
+    per_batch, reps = _oracle_decode_time(N, F, d, G, k, a.clusters, a.key_mean, a.budget, tail, n_units, seconds)
     U_total = a.batch * a.kv_heads * a.layers
     step_s = per_batch * U_total / n_units
     return {"value": round(a.batch / step_s, 4), "unit": "tokens/s", "cores": n_units, "kind": "port",
             "sample": f"{n_units} config-3 units (history {N}, F {F}, k {k}, budget {a.budget}, tail {tail}) "
                       f"x {reps} reps, one unit per thread, scaled to {U_total} units per step; synthetic CSR "
                       f"index, build not timed"}
+
+
+def cpu_stage_rate(seconds: float = 10.0, build_keys: int = 4096) -> dict:
+    """Config 2 on the host cores through the oracle port: one decode
+    layer-step (route + select + attend of all 128 units, timed on a sample
+    of units, one unit per thread, scaled to 128) and the index build of one
+    unit on a sample of build_keys keys (the C restatement's own threads),
+    reported as keys/s."""
+    import numpy as np
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    import oracle
+
+    cores = os.cpu_count() or 1
+    U, N, F, d, G, k, Bt, C, tail = 128, 32768, 8192, 128, 4, 32, 2048, 1024, 16
+    n_units = max(1, min(cores, U))
+    per_batch, reps = _oracle_decode_time(N, F, d, G, k, C, 8, Bt, tail, n_units, seconds)
+    layer_us = per_batch * U / n_units * 1e6
+    rs = np.random.RandomState(4321)
+    W = (rs.standard_normal((F, d)) / np.sqrt(d)).astype(np.float32)
+    sae = oracle.SAE(W, np.zeros(F, np.float32), key_mean=8, query_topk=k)
+    centers = rs.standard_normal((C, d)).astype(np.float32)
+    keys = centers[rs.randint(0, C, build_keys)] + np.float32(0.3) * rs.standard_normal((build_keys, d)).astype(
+        np.float32)
+    t0 = time.perf_counter()
+    oracle.build_index(keys, sae, 1.0, moments=False)
+    build_s = time.perf_counter() - t0
+    return {"value": round(layer_us, 1), "unit": "us", "cores": n_units, "kind": "port",
+            "build_keys_per_s": round(build_keys / build_s, 1), "build_threads": oracle.num_threads(),
+            "sample": f"decode: {n_units} config-2 units (history {N}, F {F}, k {k}, budget {Bt}, tail {tail}) x "
+                      f"{reps} reps, one unit per thread, scaled to {U} units per layer-step, synthetic CSR index; "
+                      f"build: one unit of {build_keys} clustered keys, F {F}, key_mean 8, "
+                      f"{oracle.num_threads()} threads"}
 
 
 def run_reference(a):
@@ -912,6 +951,8 @@ def run_stages(a):
                    "build_ms": round(build_ms, 2), "build_keys_per_s": round(U * N / (build_ms / 1e3), 1)},
         "gpu_launches": None,
     }
+    if not a.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_stage_rate(seconds=a.cpu_seconds)
     print(json.dumps(line), flush=True)
 
 
