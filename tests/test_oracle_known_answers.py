@@ -97,3 +97,40 @@ def test_query_feature_shared_weighted_route(oracle):  # test_core.py:88-96
                                         query_scale=1, query_topk=1)
     np.testing.assert_allclose(score, [.5, .5, 0., 0.])
     assert order.tolist() == [0, 1]
+
+
+def test_tied_witness_routes_by_feature_id(oracle):  # kernels/cuda_sm90/validate.py:21-37
+    """The seeded decode witness's expectation: with every bucket mean and
+    variance zero, all live buckets tie and the route takes the first
+    min(16, count) by feature id; the union is their sorted unique tokens."""
+    F, d, H = 3000, 128, 257
+    q = np.random.RandomState(0).standard_normal((6, d)).astype(np.float32)
+    for count in (17, 9, 1, 0):
+        lists = [[0, f + 1, H // 2, H - 1] if f < count else [] for f in range(F)]
+        idx = oracle.index_from_lists(H, np.zeros(d, np.float32), lists, mean=np.zeros((F, d), np.float32),
+                                      variance=np.zeros((F, d), np.float32))
+        ids, meta = oracle.select_buckets(q, idx, router="moments", query_topk=16)
+        n = min(16, count)
+        assert meta["features"] == list(range(n))
+        want = sorted({t for f in range(n) for t in (0, f + 1, H // 2, H - 1)})
+        assert ids.tolist() == want
+
+
+@pytest.mark.parametrize("kind", ["random", "rounded", "sparse", "zeros"])
+def test_positive_topk_witness(oracle, kind):  # kernels/cuda_sm90/validate.py:64-74
+    """The positive global top-k witness: the kept coordinates are the
+    largest positive values (as many as the count allows), none twice."""
+    rs = np.random.RandomState(5)
+    a = rs.random_sample((93, 3000)).astype(np.float32)
+    if kind == "rounded":
+        a = np.round(a * 8).astype(np.float32)
+    elif kind == "sparse":
+        a = np.zeros_like(a)
+        a.reshape(-1)[:11] = 1.0
+    elif kind == "zeros":
+        a = np.zeros_like(a)
+    ids = oracle.positive_global_topk(a, 744)
+    assert len(np.unique(ids)) == len(ids)
+    flat = a.reshape(-1)
+    target = np.sort(flat)[::-1][:744]
+    np.testing.assert_array_equal(np.sort(flat[ids])[::-1], target[target > 0])
