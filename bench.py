@@ -60,6 +60,8 @@ def parse():
     p.add_argument("--layout", action="store_true",
                    help="layout diagnostic: in-place sparse attention vs explicit gather + packed attention")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--parity-units", type=int, default=1,
+                   help="units of layer 0 recomputed by the CPU oracle after timing (0: none)")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
@@ -130,6 +132,37 @@ class Clocks:
 # ---------------------------------------------------------------------------
 # workload
 # ---------------------------------------------------------------------------
+
+def graph_kernel_launches(graph):
+    """Kernel nodes of this library (C++ namespace pk) in a captured CUDA
+    graph, or None when the graph cannot be inspected."""
+    try:
+        from cuda.bindings import runtime as rt
+        raw = graph.raw_cuda_graph()
+        handle = raw if isinstance(raw, rt.cudaGraph_t) else rt.cudaGraph_t(init_value=int(raw))
+        err, _, n = rt.cudaGraphGetNodes(handle, 0)
+        if err != rt.cudaError_t.cudaSuccess:
+            return None
+        err, nodes, n = rt.cudaGraphGetNodes(handle, n)
+        if err != rt.cudaError_t.cudaSuccess:
+            return None
+        count = 0
+        for node in nodes[:n]:
+            err, kind = rt.cudaGraphNodeGetType(node)
+            if err != rt.cudaError_t.cudaSuccess or kind != rt.cudaGraphNodeType.cudaGraphNodeTypeKernel:
+                continue
+            err, params = rt.cudaGraphKernelNodeGetParams(node)
+            if err != rt.cudaError_t.cudaSuccess:
+                return None
+            err, name = rt.cudaFuncGetName(params.func)
+            if err != rt.cudaError_t.cudaSuccess:
+                return None
+            name = name.decode() if isinstance(name, bytes) else str(name)
+            count += name.startswith("_ZN2pk")
+        return count
+    except Exception:  # noqa: BLE001 -- an inspection aid, never fatal
+        return None
+
 
 def gen_layer(torch, dev, g, U, T, d, C):
     """Clustered keys (centers ~ N(0,1), noise sigma 0.3) and iid values, bf16."""
@@ -226,11 +259,10 @@ def run_ours(a):
                 av_events[l][0].record()
             # The token's KV append fused into the attention launch: its rows
             # are attended as the newest tail row and written into the cache.
-            o = lay["op"].attention(q, lay["K"], lay["V"], length=len_static,
-                                    append=(kv_static[l, 0], kv_static[l, 1]))
+            lay["op"].attention(q, lay["K"], lay["V"], length=len_static,
+                                append=(kv_static[l, 0], kv_static[l, 1]), out=outs[l])
             if av_events is not None:
                 av_events[l][1].record()
-            outs[l].copy_(o)
 
     def load_step(s):
         q_static.copy_(q_steps[s])
@@ -244,15 +276,18 @@ def run_ours(a):
     for lay in layers:
         lay["op"].check()
     graph = None
+    graph_launches = None
     if not a.no_graph:
-        graph = torch.cuda.CUDAGraph()
+        graph = torch.cuda.CUDAGraph(keep_graph=True)
         s_cap = torch.cuda.Stream()
         s_cap.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s_cap):
             with torch.cuda.graph(graph, stream=s_cap):
                 step_body()
         torch.cuda.current_stream().wait_stream(s_cap)
+        graph.instantiate()
         torch.cuda.synchronize()
+        graph_launches = graph_kernel_launches(graph)
 
     def run_step(s):
         load_step(s)
@@ -378,6 +413,19 @@ def run_ours(a):
         append_ms_per_step = float(t.item())
     clocks.stop()
     clk = clocks.summary(t0, t1)
+    encode_paths = sorted({lay["idx"].encode_path for lay in layers})
+    parity = None
+    if rank == 0 and a.parity_units > 0:
+        # Outside every timed region: one decode step of sampled units of
+        # layer 0, recomputed by the CPU oracle on this run's own inputs.
+        s_last = total_steps - 1
+        load_step(s_last)
+        lay = layers[0]
+        lay["op"].route(q_static[0])
+        o = lay["op"].attention(q_static[0], lay["K"], lay["V"], length=len_static)
+        torch.cuda.synchronize()
+        units = sorted({0, U - 1})[:a.parity_units]
+        parity = sample_parity(lay, q_static[0], o, int(lens[s_last][0].item()), units, N, F, k, a)
 
     tokens = world * B * a.steps
     decode_ms = ms
@@ -404,7 +452,10 @@ def run_ours(a):
             traffic = round(tj["dram_bytes_per_algorithmic_byte"] * mean_bytes)
         except (OSError, ValueError, KeyError):
             traffic = None
-    launches_per_step = L * 4  # approximate encode + select + union + attention (with the KV append) per layer
+    # This library's kernels per step, counted in the captured step graph
+    # (kernel nodes whose function lives in namespace pk); eager runs fall
+    # back to the four launches per layer the step issues.
+    launches_per_step = graph_launches if graph_launches is not None else L * 4
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -440,7 +491,10 @@ def run_ours(a):
                 "h2d_bytes_per_step": int(L * U * G * d * 2 + L * 2 * U * d * 2),
                 "d2h_bytes_per_step": int(L * U * G * d * 2)},
         "gpu_launches": launches_per_step * a.steps,
+        "gpu_launches_source": "graph kernel nodes" if graph_launches is not None else "per-layer launch count",
         "clocks": clk,
+        "encode_path": encode_paths[0] if len(encode_paths) == 1 else encode_paths,
+        "parity": parity,
     }
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         line["cpu_baseline"] = cpu_rate(a, seconds=a.cpu_seconds)
@@ -450,6 +504,53 @@ def run_ours(a):
         del graph
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# sampled-unit parity against the CPU oracle (outside the timed region)
+# ---------------------------------------------------------------------------
+
+def sample_parity(lay, q, out, length, units, N, F, k, a) -> dict:
+    """Recomputes one decode step of `units` of one layer with the CPU
+    oracle on the bench's own inputs: the unit's index from its keys (the
+    whole-history global BatchTopK, core.py:92-103), the q_activation order
+    (core.py:131-139), the budgeted union (core.py:142-167) and the attention
+    over the union and the dense tail (core.py:170-183).  Memberships, order,
+    union ids and accepted buckets must be bit-exact; the attention within
+    2e-2 relative L2 (bf16)."""
+    import numpy as np
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    import oracle
+
+    op, idx = lay["op"], lay["idx"]
+    t0 = time.time()
+    sae = oracle.SAE(op.sae.W_enc.float().cpu().numpy(), op.sae.b_enc.float().cpu().numpy(), key_mean=a.key_mean,
+                     query_topk=k)
+    res = {"units": list(units), "layer": 0, "memberships": True, "order": True, "ids": True, "features": True,
+           "attn_rel_l2": 0.0}
+    for u in units:
+        keys = lay["K"][u, :length].float().cpu().numpy()
+        vals = lay["V"][u, :length].float().cpu().numpy()
+        qu = q[u].float().cpu().numpy()
+        oidx = oracle.build_index(keys[:N], sae, 1.0, moments=False)
+        counts, mem = idx.csr(u)
+        res["memberships"] &= bool(np.array_equal(counts, oidx.counts) and np.array_equal(mem, oidx.ids))
+        _, order = oracle.bucket_scores(qu, oidx, router="q_activation", sae=sae, query_scale=1.0, query_topk=k)
+        n_order = int(op.n_order[u].item())
+        res["order"] &= bool(np.array_equal(op.order[u, :n_order].long().cpu().numpy(), order))
+        ids, feats, _ = oracle.select_from_order(order, oidx, int(op.limit[u].item()))
+        c = int(op.count[u].item())
+        res["ids"] &= bool(np.array_equal(op.ids[u, :c].long().cpu().numpy(), ids))
+        nf = int(op.n_features[u].item())
+        res["features"] &= op.features[u, :nf].long().cpu().tolist() == feats
+        ref = oracle.attend(qu, keys, vals, ids, N)
+        got = out[u].float().cpu().numpy().astype(np.float64)
+        err = float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
+        res["attn_rel_l2"] = max(res["attn_rel_l2"], round(err, 6))
+    res["ok"] = bool(res["memberships"] and res["order"] and res["ids"] and res["features"]
+                     and res["attn_rel_l2"] < 2e-2)
+    res["oracle_s"] = round(time.time() - t0, 1)
+    return res
 
 
 # ---------------------------------------------------------------------------

@@ -65,6 +65,8 @@ def lib():
         L.orc_summarize.argtypes = [P, I, P, P, I, P, P]
         L.orc_build_index.argtypes = [P, I64, I, P, F32, P, P, I, I, P, P, P, P, I64, P, P]
         L.orc_build_index.restype = I64
+        L.orc_build_index_stream.argtypes = L.orc_build_index.argtypes
+        L.orc_build_index_stream.restype = I64
         L.orc_merge_moments.argtypes = [P, P, P, P, P, P, I, I, P, P]
         L.orc_route_qact.argtypes = [P, I, I, P, P, I, F32, I, P, P, P, P]
         L.orc_route_qact.restype = I
@@ -198,7 +200,15 @@ def summarize(keys, lists, center=None) -> FeatureIndex:
     return idx
 
 
-def build_index(keys, sae: SAE, key_scale: float, *, center=None, moments: bool = True) -> FeatureIndex:
+# Above this many activations (n * F) build_index evaluates them in token
+# blocks (orc_build_index_stream) instead of holding the [n, F] matrix.
+STREAM_ACTIVATIONS = 1 << 25
+
+
+def build_index(keys, sae: SAE, key_scale: float, *, center=None, moments: bool = True,
+                stream: bool | None = None) -> FeatureIndex:
+    """core.py:92-103.  ``stream`` picks the blocked evaluation (same result);
+    by default it is used above STREAM_ACTIVATIONS activations."""
     keys = _f32(keys)
     if keys.ndim != 2 or len(keys) == 0 or key_scale <= 0:
         raise ValueError("nonempty [history,head_dim] keys and positive scale required")
@@ -214,7 +224,10 @@ def build_index(keys, sae: SAE, key_scale: float, *, center=None, moments: bool 
     mean = np.empty((F, d), np.float32) if moments else None
     var = np.empty((F, d), np.float32) if moments else None
     c_in = _f32(center) if center is not None else None
-    m = lib().orc_build_index(_p(keys), n, d, _p(c_in), float(key_scale), _p(sae.W_enc), _p(sae.b_enc),
+    if stream is None:
+        stream = n * F > STREAM_ACTIVATIONS
+    fn = lib().orc_build_index_stream if stream else lib().orc_build_index
+    m = fn(_p(keys), n, d, _p(c_in), float(key_scale), _p(sae.W_enc), _p(sae.b_enc),
                               F, sae.key_mean, _p(center_out), _p(counts), _p(offsets), _p(ids), cap,
                               _p(mean), _p(var))
     if m < 0:

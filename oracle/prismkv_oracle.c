@@ -43,6 +43,10 @@
 #include <omp.h>
 #endif
 
+#if defined(__x86_64__)
+#include <immintrin.h>
+#endif
+
 /* ------------------------------------------------------------------------- */
 /* Reduction orders                                                          */
 /* ------------------------------------------------------------------------- */
@@ -324,6 +328,280 @@ int64_t orc_build_index(const float *keys, int64_t n, int d, const float *center
             if (member[t * F + f]) lists[fill[f]++] = t;
     free(fill);
     free(member);
+    if (mean && var) orc_summarize(keys, d, offsets, lists, F, mean, var);
+    return m;
+}
+
+/* ------------------------------------------------------------------------- */
+/* core.py:92-103 at scale -- build_index without the [n, F] matrix          */
+/* ------------------------------------------------------------------------- */
+
+/* The same index as orc_build_index for n >= 6 rows (the sequential-chain
+ * regime of F.linear), computed in token blocks so that memory stays O(n*d +
+ * members) instead of n*F floats.  Activations are evaluated twice: pass 1
+ * histograms the upper 16 bits of every positive activation to find the bin
+ * that holds the count-th largest; pass 2 recomputes them and keeps the
+ * entries in or above that bin, from which the exact threshold, the strict
+ * members and the first ties in flat order follow as in core.py:13-26.  Each
+ * activation is the same fp32 chain as dot_sequential (lane j of a vector
+ * accumulator runs feature f+j's chain over k), so the result is bit-identical
+ * to orc_build_index. */
+
+#define STREAM_TB 32   /* token rows per block */
+#define STREAM_FC 512  /* features per chunk (W^T chunk 256 KB) */
+
+#if defined(__x86_64__)
+/* out[r * nf + j] = relu(chain(x[r], W[f0 + j]) + b[f0 + j]) for r < rows,
+ * j < nf; WT = W transposed, [d][F]. */
+__attribute__((target("avx2,fma")))
+static void dense_chunk_avx2(const float *x, int rows, int d, const float *WT, const float *b, int F,
+                             int f0, int nf, float *out) {
+    int j = 0;
+    const __m256 zero = _mm256_setzero_ps();
+    for (; j + 16 <= nf; j += 16) {
+        const float *wt = WT + f0 + j;
+        const __m256 b0 = _mm256_loadu_ps(b + f0 + j), b1 = _mm256_loadu_ps(b + f0 + j + 8);
+        int r = 0;
+        for (; r + 4 <= rows; r += 4) {
+            __m256 a00 = zero, a01 = zero, a10 = zero, a11 = zero;
+            __m256 a20 = zero, a21 = zero, a30 = zero, a31 = zero;
+            const float *x0 = x + (int64_t)r * d;
+            for (int k = 0; k < d; ++k) {
+                const __m256 w0 = _mm256_loadu_ps(wt + (int64_t)k * F);
+                const __m256 w1 = _mm256_loadu_ps(wt + (int64_t)k * F + 8);
+                __m256 xb = _mm256_set1_ps(x0[k]);
+                a00 = _mm256_fmadd_ps(xb, w0, a00); a01 = _mm256_fmadd_ps(xb, w1, a01);
+                xb = _mm256_set1_ps(x0[d + k]);
+                a10 = _mm256_fmadd_ps(xb, w0, a10); a11 = _mm256_fmadd_ps(xb, w1, a11);
+                xb = _mm256_set1_ps(x0[2 * d + k]);
+                a20 = _mm256_fmadd_ps(xb, w0, a20); a21 = _mm256_fmadd_ps(xb, w1, a21);
+                xb = _mm256_set1_ps(x0[3 * d + k]);
+                a30 = _mm256_fmadd_ps(xb, w0, a30); a31 = _mm256_fmadd_ps(xb, w1, a31);
+            }
+            __m256 acc[8] = {a00, a01, a10, a11, a20, a21, a30, a31};
+            for (int t = 0; t < 8; ++t) {
+                __m256 v = _mm256_add_ps(acc[t], (t & 1) ? b1 : b0);
+                v = _mm256_and_ps(v, _mm256_cmp_ps(v, zero, _CMP_GT_OQ));
+                _mm256_storeu_ps(out + (int64_t)(r + (t >> 1)) * nf + j + 8 * (t & 1), v);
+            }
+        }
+        for (; r < rows; ++r) {
+            __m256 a0 = zero, a1 = zero;
+            const float *x0 = x + (int64_t)r * d;
+            for (int k = 0; k < d; ++k) {
+                const __m256 xb = _mm256_set1_ps(x0[k]);
+                a0 = _mm256_fmadd_ps(xb, _mm256_loadu_ps(wt + (int64_t)k * F), a0);
+                a1 = _mm256_fmadd_ps(xb, _mm256_loadu_ps(wt + (int64_t)k * F + 8), a1);
+            }
+            __m256 v0 = _mm256_add_ps(a0, b0), v1 = _mm256_add_ps(a1, b1);
+            v0 = _mm256_and_ps(v0, _mm256_cmp_ps(v0, zero, _CMP_GT_OQ));
+            v1 = _mm256_and_ps(v1, _mm256_cmp_ps(v1, zero, _CMP_GT_OQ));
+            _mm256_storeu_ps(out + (int64_t)r * nf + j, v0);
+            _mm256_storeu_ps(out + (int64_t)r * nf + j + 8, v1);
+        }
+    }
+    for (; j < nf; ++j)
+        for (int r = 0; r < rows; ++r) {
+            float c = 0.f;
+            for (int k = 0; k < d; ++k) c = fmaf(x[(int64_t)r * d + k], WT[(int64_t)k * F + f0 + j], c);
+            c = c + b[f0 + j];
+            out[(int64_t)r * nf + j] = c > 0.f ? c : 0.f;
+        }
+}
+#endif
+
+static void dense_chunk_scalar(const float *x, int rows, int d, const float *WT, const float *b, int F,
+                               int f0, int nf, float *out) {
+    for (int r = 0; r < rows; ++r)
+        for (int j = 0; j < nf; ++j) {
+            float c = 0.f;
+            for (int k = 0; k < d; ++k) c = fmaf(x[(int64_t)r * d + k], WT[(int64_t)k * F + f0 + j], c);
+            c = c + b[f0 + j];
+            out[(int64_t)r * nf + j] = c > 0.f ? c : 0.f;
+        }
+}
+
+static void dense_chunk(const float *x, int rows, int d, const float *WT, const float *b, int F, int f0,
+                        int nf, float *out) {
+#if defined(__x86_64__)
+    if (__builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma")) {
+        dense_chunk_avx2(x, rows, d, WT, b, F, f0, nf, out);
+        return;
+    }
+#endif
+    dense_chunk_scalar(x, rows, d, WT, b, F, f0, nf, out);
+}
+
+typedef struct { int64_t flat; float v; } fv_t;
+
+static int cmp_i64(const void *a, const void *b) {
+    int64_t x = *(const int64_t *)a, y = *(const int64_t *)b;
+    return (x > y) - (x < y);
+}
+
+static int cmp_f32_desc(const void *a, const void *b) {
+    float x = *(const float *)a, y = *(const float *)b;
+    return (x < y) - (x > y);
+}
+
+static inline uint32_t f32_bits(float v) {
+    uint32_t u;
+    memcpy(&u, &v, 4);
+    return u;
+}
+
+/* Arguments and return value as orc_build_index. */
+int64_t orc_build_index_stream(const float *keys, int64_t n, int d, const float *center_in, float key_scale,
+                               const float *W, const float *b, int F, int key_mean,
+                               float *center_out, int64_t *counts, int64_t *offsets, int64_t *lists, int64_t cap,
+                               float *mean, float *var) {
+    if (n <= 0 || d <= 0 || F <= 0 || !(key_scale > 0.f)) return -2;
+    if (n < 6)
+        return orc_build_index(keys, n, d, center_in, key_scale, W, b, F, key_mean, center_out, counts, offsets,
+                               lists, cap, mean, var);
+    if (center_in) memcpy(center_out, center_in, d * sizeof(float));
+    else orc_colmean(keys, n, d, center_out);
+    float *x = (float *)malloc((size_t)n * d * sizeof(float));
+    for (int64_t r = 0; r < n; ++r)
+        for (int c = 0; c < d; ++c) x[r * d + c] = (keys[r * d + c] - center_out[c]) / key_scale;
+    float *WT = (float *)malloc((size_t)F * d * sizeof(float));
+    for (int f = 0; f < F; ++f)
+        for (int k = 0; k < d; ++k) WT[(int64_t)k * F + f] = W[(int64_t)f * d + k];
+    const int64_t total = n * (int64_t)F;
+    const int64_t budget = n * (int64_t)key_mean;
+    const int64_t count = budget < total ? budget : total;
+    const int64_t nblocks = (n + STREAM_TB - 1) / STREAM_TB;
+
+    /* Pass 1: histogram of the upper 16 bits of the positive activations. */
+    uint64_t *hist = (uint64_t *)calloc(65536, sizeof(uint64_t));
+    #pragma omp parallel
+    {
+        uint64_t *h = (uint64_t *)calloc(65536, sizeof(uint64_t));
+        float *act = (float *)malloc((size_t)STREAM_TB * STREAM_FC * sizeof(float));
+        #pragma omp for schedule(dynamic, 4)
+        for (int64_t blk = 0; blk < nblocks; ++blk) {
+            const int64_t t0 = blk * STREAM_TB;
+            const int rows = (int)(n - t0 < STREAM_TB ? n - t0 : STREAM_TB);
+            for (int f0 = 0; f0 < F; f0 += STREAM_FC) {
+                const int nf = F - f0 < STREAM_FC ? F - f0 : STREAM_FC;
+                dense_chunk(x + t0 * d, rows, d, WT, b, F, f0, nf, act);
+                for (int64_t i = 0; i < (int64_t)rows * nf; ++i)
+                    if (act[i] > 0.f) h[f32_bits(act[i]) >> 16]++;
+            }
+        }
+        #pragma omp critical
+        for (int i = 0; i < 65536; ++i) hist[i] += h[i];
+        free(h);
+        free(act);
+    }
+    uint64_t positives = 0;
+    for (int i = 0; i < 65536; ++i) positives += hist[i];
+    /* Positive floats order like their bit patterns.  With fewer positives
+     * than `count` the threshold is zero and every positive is a member. */
+    const int all_pos = (int64_t)positives <= count;
+    int bin = 0;
+    int64_t above = 0;
+    if (!all_pos) {
+        for (bin = 65535; bin > 0; --bin) {
+            if (above + (int64_t)hist[bin] >= count) break;
+            above += hist[bin];
+        }
+    }
+    free(hist);
+
+    /* Pass 2: keep every positive entry in or above the threshold's bin. */
+    int nthreads = 1;
+#ifdef _OPENMP
+    nthreads = omp_get_max_threads();
+#endif
+    fv_t **kept = (fv_t **)calloc(nthreads, sizeof(fv_t *));
+    int64_t *nkept = (int64_t *)calloc(nthreads, sizeof(int64_t));
+    #pragma omp parallel
+    {
+        int tid = 0;
+#ifdef _OPENMP
+        tid = omp_get_thread_num();
+#endif
+        int64_t capk = 1 << 16, m = 0;
+        fv_t *buf = (fv_t *)malloc(capk * sizeof(fv_t));
+        float *act = (float *)malloc((size_t)STREAM_TB * STREAM_FC * sizeof(float));
+        #pragma omp for schedule(dynamic, 4)
+        for (int64_t blk = 0; blk < nblocks; ++blk) {
+            const int64_t t0 = blk * STREAM_TB;
+            const int rows = (int)(n - t0 < STREAM_TB ? n - t0 : STREAM_TB);
+            for (int f0 = 0; f0 < F; f0 += STREAM_FC) {
+                const int nf = F - f0 < STREAM_FC ? F - f0 : STREAM_FC;
+                dense_chunk(x + t0 * d, rows, d, WT, b, F, f0, nf, act);
+                for (int r = 0; r < rows; ++r)
+                    for (int j = 0; j < nf; ++j) {
+                        const float v = act[(int64_t)r * nf + j];
+                        if (!(v > 0.f) || (int)(f32_bits(v) >> 16) < bin) continue;
+                        if (m == capk) { capk *= 2; buf = (fv_t *)realloc(buf, capk * sizeof(fv_t)); }
+                        buf[m].flat = (t0 + r) * (int64_t)F + f0 + j;
+                        buf[m].v = v;
+                        ++m;
+                    }
+            }
+        }
+        kept[tid] = buf;
+        nkept[tid] = m;
+        free(act);
+    }
+    free(x);
+    free(WT);
+    int64_t nk = 0;
+    for (int t = 0; t < nthreads; ++t) nk += nkept[t];
+    fv_t *all = (fv_t *)malloc((nk > 0 ? nk : 1) * sizeof(fv_t));
+    {
+        int64_t o = 0;
+        for (int t = 0; t < nthreads; ++t) {
+            memcpy(all + o, kept[t], nkept[t] * sizeof(fv_t));
+            o += nkept[t];
+            free(kept[t]);
+        }
+    }
+    free(kept);
+    free(nkept);
+
+    /* Exact threshold: the (count - above)-th largest value in the bin. */
+    float thr = 0.f;
+    if (!all_pos) {
+        int64_t inbin = 0;
+        for (int64_t i = 0; i < nk; ++i) inbin += (int)(f32_bits(all[i].v) >> 16) == bin;
+        float *vals = (float *)malloc((inbin > 0 ? inbin : 1) * sizeof(float));
+        int64_t q = 0;
+        for (int64_t i = 0; i < nk; ++i)
+            if ((int)(f32_bits(all[i].v) >> 16) == bin) vals[q++] = all[i].v;
+        qsort(vals, inbin, sizeof(float), cmp_f32_desc);
+        thr = vals[count - above - 1];
+        free(vals);
+    }
+    /* Members: strict entries above the threshold, then ties in flat order. */
+    int64_t *flat = (int64_t *)malloc((nk > 0 ? nk : 1) * sizeof(int64_t));
+    int64_t m = 0, ntie = 0;
+    int64_t *tie = (int64_t *)malloc((nk > 0 ? nk : 1) * sizeof(int64_t));
+    for (int64_t i = 0; i < nk; ++i) {
+        if (all_pos || all[i].v > thr) flat[m++] = all[i].flat;
+        else if (all[i].v == thr) tie[ntie++] = all[i].flat;
+    }
+    free(all);
+    if (!all_pos) {
+        qsort(tie, ntie, sizeof(int64_t), cmp_i64);
+        int64_t want = count - m;
+        for (int64_t i = 0; i < ntie && i < want; ++i) flat[m++] = tie[i];
+    }
+    free(tie);
+    if (m > cap) { free(flat); return -1; }
+    qsort(flat, m, sizeof(int64_t), cmp_i64);
+    for (int f = 0; f < F; ++f) counts[f] = 0;
+    for (int64_t i = 0; i < m; ++i) counts[flat[i] % F]++;
+    offsets[0] = 0;
+    for (int f = 0; f < F; ++f) offsets[f + 1] = offsets[f] + counts[f];
+    int64_t *fill = (int64_t *)malloc(F * sizeof(int64_t));
+    for (int f = 0; f < F; ++f) fill[f] = offsets[f];
+    for (int64_t i = 0; i < m; ++i) lists[fill[flat[i] % F]++] = flat[i] / F;
+    free(fill);
+    free(flat);
     if (mean && var) orc_summarize(keys, d, offsets, lists, F, mean, var);
     return m;
 }

@@ -148,7 +148,7 @@ class SparseDecode:
 
     # ------------------------------------------------------------ attention
     def attention(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, length=None, splits=None,
-                  partial: torch.Tensor | None = None, append=None) -> torch.Tensor:
+                  partial: torch.Tensor | None = None, append=None, out: torch.Tensor | None = None) -> torch.Tensor:
         """Sparse attention over the routed ids plus the dense tail.
 
         k, v: [U, total, d] (rows of each unit contiguous) or slot-major
@@ -159,7 +159,9 @@ class SparseDecode:
         ``append=(k_new, v_new)`` (contiguous, U*d elements each, unit u =
         slot * H_kv + head) fuses the decode KV append: each unit's new rows
         are attended as row length[u] - 1, the newest tail row, and written
-        into k and v there (one launch; as kv_append then attention)."""
+        into k and v there (one launch; as kv_append then attention).
+        ``out`` (contiguous [U, G, d] of Q's dtype) receives the output
+        instead of the operator's own buffer."""
         U, G, d = self.U, self.G, self.d
         if k.dtype != q.dtype or v.dtype != q.dtype:
             raise ValueError("Q, K and V must share a dtype")
@@ -184,8 +186,12 @@ class SparseDecode:
             sms = torch.cuda.get_device_properties(q.device).multi_processor_count
             S = max(1, min(8, (2 * sms) // U))
         nbytes = nv.query("pk_sparse_av_workspace_bytes", U, G, d, S)
-        out = None
-        if partial is None:
+        if partial is not None:
+            out = None
+        elif out is not None:
+            if tuple(out.shape) != (U, G, d) or out.dtype != q.dtype or not out.is_contiguous():
+                raise ValueError(f"out must be a contiguous [{U},{G},{d}] {q.dtype} tensor")
+        else:
             if self.out is None or self.out.dtype != q.dtype:
                 self.out = torch.empty(U, G, d, dtype=q.dtype, device=q.device)
             out = self.out

@@ -65,6 +65,18 @@ CASES = [
     ("cfg1", 18, 8192, 128, 256, 2048, 4, 16, 0, False, (0.125,), 256, 8),
 ]
 
+# Units at the GPU configurations' shapes.  cfg2: one unit of config 2
+# (N 32768, 1024 clusters, F 8192, k 32, budget 2048 tokens); cfg3u: one unit
+# of config 3 (N 131072, F 16384, k 32, budget 4096, a 64-token tail); cfg4c:
+# a 65536-token cut of a config-4 unit (F 32768, k 64, 4096 clusters, budget
+# 8192 tokens).  They take minutes of reference CPU time each, so they are
+# generated only when named on the command line.
+LARGE = [
+    ("cfg2", 19, 32768, 128, 1024, 8192, 4, 32, 0, True, (2048 / 32768, None), 128, 8),
+    ("cfg3u", 20, 131072, 128, 1024, 16384, 4, 32, 64, True, (4096 / 131072,), 64, 8),
+    ("cfg4c", 21, 65536, 128, 4096, 32768, 4, 64, 0, True, (8192 / 65536,), 32, 8),
+]
+
 
 def run_case(name, seed, n, d, clusters, F, G, k, tail, bf16, caps, append_n, key_mean):
     c = unit_case(seed, n, d, clusters, F, G, tail=tail + append_n, bf16=bf16, key_mean=key_mean)
@@ -147,6 +159,11 @@ def run_edge():
 
 if __name__ == "__main__":
     torch.set_num_threads(os.cpu_count())
-    for case in CASES:
-        run_case(*case)
-    run_edge()
+    names = sys.argv[1:]
+    if not names:
+        for case in CASES:
+            run_case(*case)
+        run_edge()
+    for case in CASES + LARGE:
+        if case[0] in names:
+            run_case(*case)

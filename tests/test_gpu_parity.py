@@ -21,7 +21,10 @@ from gen import unit_case
 pytestmark = pytest.mark.gpu
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-CASES = sorted(p.stem for p in GOLDEN.glob("u*.npz")) + ["cfg1"]
+# Units at the GPU configurations' shapes (reference-generated like the rest):
+# config 2, a config-3 unit and a 65536-token cut of a config-4 unit.
+LARGE = ["cfg2", "cfg3u", "cfg4c"]
+CASES = sorted(p.stem for p in GOLDEN.glob("u*.npz")) + ["cfg1"] + [c for c in LARGE if (GOLDEN / f"{c}.npz").exists()]
 TOL_F32, TOL_BF16 = 1e-3, 2e-2
 
 
@@ -65,6 +68,10 @@ def case(request, pk, oracle):
 
 def test_build_index_matches_reference(case):
     z, idx = case["z"], case["idx"]
+    if case["m"]["name"] in LARGE:
+        # At the configurations' sizes the index must come from the
+        # bound-filtered tensor-core build, the path the bench times.
+        assert idx.dev.encode_path == "bounds"
     center = idx.center.cpu().numpy()
     assert np.array_equal(center.view(np.uint32), z["center"].view(np.uint32))
     counts, ids = idx.dev.csr(0)

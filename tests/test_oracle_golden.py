@@ -16,7 +16,10 @@ import pytest
 from gen import unit_case
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-CASES = sorted(p.stem for p in GOLDEN.glob("u*.npz")) + ["cfg1"]
+# Units at the GPU configurations' shapes (reference-generated like the rest):
+# config 2, a config-3 unit and a 65536-token cut of a config-4 unit.
+LARGE = ["cfg2", "cfg3u", "cfg4c"]
+CASES = sorted(p.stem for p in GOLDEN.glob("u*.npz")) + ["cfg1"] + [c for c in LARGE if (GOLDEN / f"{c}.npz").exists()]
 
 
 def digest(a):
