@@ -257,8 +257,10 @@ int pk_kv_append(uint64_t k_new, uint64_t v_new, uint64_t k_cache, uint64_t v_ca
  * library holds until exit.  A shape whose scratch
  * (pk_sparse_av_workspace_bytes) exceeds that returns
  * PK_ERR_SCRATCH_LIMIT; pass fewer splits (splits == 1 needs none).
- * The first call on each device looks the array up with the device current;
- * make that first call before any stream capture.  All calls share the one
+ * Outside a stream capture each call looks the array's device address up
+ * with the device current (a device reset moves it); a call inside a capture
+ * uses the address found by the device's last uncaptured call, so make the
+ * first call on each device before any stream capture.  All calls share the one
  * array, so calls that overlap on the GPU (other streams, other threads)
  * race: serialise them.  Nothing is allocated or freed. */
 #define PK_SPARSE_AV_NOALLOC_SCRATCH_BYTES (4u << 20)

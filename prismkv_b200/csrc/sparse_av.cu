@@ -19,6 +19,8 @@
 // written into the cache by its first split CTA.
 #include <cooperative_groups.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace pk {
@@ -845,15 +847,26 @@ __global__ void lse_merge_kernel(const float* __restrict__ part, int P, int UG, 
 
 // Whether a cluster of S split CTAs of kernel `which` (0: up to 8 heads,
 // 1: 9..16 heads; S <= 16, above 8 the non-portable cluster sizes) with
-// `smem` bytes each can be resident; answered once per (kernel, S, smem)
-// and kept.
+// `smem` bytes each can be resident on the current device; answered once per
+// (device, kernel, S, smem) and kept.  Host threads may launch concurrently,
+// so the caches below are guarded by one mutex.
+static std::mutex g_launch_cache_mu;
+constexpr int kMaxDevices = 64;
+
 bool cluster_fits(int which, int S, int smem) {
-    static int known[2][kAvMaxCluster + 1] = {};   // 0 unknown, 1 yes, 2 no
-    static int known_smem[2][kAvMaxCluster + 1] = {};
+    static int known[kMaxDevices][2][kAvMaxCluster + 1] = {};   // 0 unknown, 1 yes, 2 no
+    static int known_smem[kMaxDevices][2][kAvMaxCluster + 1] = {};
     if (S < 2 || S > kAvMaxCluster) return false;
-    if (known_smem[which][S] != smem) known[which][S] = 0;
-    if (!known[which][S]) {
-        known_smem[which][S] = smem;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        return false;
+    }
+    std::lock_guard<std::mutex> lock(g_launch_cache_mu);
+    int& state = known[dev][which][S];
+    if (known_smem[dev][which][S] != smem) state = 0;
+    if (!state) {
+        known_smem[dev][which][S] = smem;
         auto fn = which == 0 ? sparse_av_bf16_kernel<true> : sparse_av_bf16_g16_kernel<true>;
         bool ok = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess;
         if (ok && S > 8) ok = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
@@ -873,19 +886,25 @@ bool cluster_fits(int which, int S, int smem) {
             ok = cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) == cudaSuccess && clusters > 0;
         }
         cudaGetLastError();   // a refused query leaves no sticky error
-        known[which][S] = ok ? 1 : 2;
+        state = ok ? 1 : 2;
     }
-    return known[which][S] == 1;
+    return state == 1;
 }
 
 int default_splits(int U) {
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (sms <= 0) sms = 148;
+    // SM count of the current device, looked up once per device.
+    static int sms_of[kMaxDevices] = {};
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+        std::lock_guard<std::mutex> lock(g_launch_cache_mu);
+        if (!sms_of[dev]) {
+            int n = 0;
+            if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+            sms_of[dev] = n;
+        }
+        sms = sms_of[dev];
     }
+    cudaGetLastError();
     // About one wave of two CTAs per SM across all units, at most 8 splits
     // (portable clusters, merged on chip): each split pays a fixed prologue
     // (ids, Q, first tile), so more splits than resident slots only add
@@ -1012,24 +1031,33 @@ extern "C" int pk_lse_merge(uint64_t partial, int P, int UG, int d, uint64_t out
 // device allocator -- so the split scratch lives here, in a file-scope device
 // array every GPU that loads the library keeps until exit.
 // ---------------------------------------------------------------------------
-#include <mutex>
 
 namespace pk {
 static __device__ __align__(256) unsigned char g_av_noalloc_scratch[PK_SPARSE_AV_NOALLOC_SCRATCH_BYTES];
 
 // The array's name is only a host-side stand-in; its device address is looked
-// up once per device, with that device current.
-static void* noalloc_scratch_address(int* rc) {
+// up with the device current.  Outside stream capture every call looks it up
+// again (so a device reset, which reloads the module at a new address, is
+// followed); inside a capture the address cached by the device's last
+// uncaptured call is used, so the first call on a device must come before any
+// stream capture.
+static void* noalloc_scratch_address(cudaStream_t stream, int* rc) {
     static std::mutex mu;
-    static void* addr[128] = {};
+    static void* addr[kMaxDevices] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess || dev < 0 || dev >= 128) {
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
         *rc = e != cudaSuccess ? (int)e : PK_ERR_ARG;
         return nullptr;
     }
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(stream, &cap);
+    if (e != cudaSuccess) {
+        *rc = (int)e;
+        return nullptr;
+    }
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    if (cap == cudaStreamCaptureStatusNone) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_av_noalloc_scratch);
         if (e != cudaSuccess || !p) {
@@ -1037,6 +1065,9 @@ static void* noalloc_scratch_address(int* rc) {
             return nullptr;
         }
         addr[dev] = p;
+    } else if (!addr[dev]) {
+        *rc = PK_ERR_ARG;   // never set up on this device outside a capture
+        return nullptr;
     }
     *rc = 0;
     return addr[dev];
@@ -1054,7 +1085,7 @@ extern "C" int pk_sparse_av_noalloc(uint64_t q, uint64_t k, uint64_t v, int dtyp
     const size_t need = pk_sparse_av_workspace_bytes(U, G, d, splits);
     if (splits > 1 && need > PK_SPARSE_AV_NOALLOC_SCRATCH_BYTES) return PK_ERR_SCRATCH_LIMIT;
     int rc = 0;
-    void* scratch = noalloc_scratch_address(&rc);
+    void* scratch = noalloc_scratch_address((cudaStream_t)stream, &rc);
     if (!scratch) return rc;
     if (splits > 1) {
         // The arrival counters must start at zero; the array keeps whatever

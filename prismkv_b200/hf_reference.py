@@ -1,14 +1,22 @@
 """Hugging Face attention integration for unpadded, batch-one causal decode.
 
-The reference's adapter (src/prismkv/hf_reference.py:66-240, ``HFReference``)
-with its decode path on this library's device operator:
+The drop-in for the reference's adapter (src/prismkv/hf_reference.py:66-240,
+``HFReference``): the same constructor arguments, refusals (their exception
+types), lifecycle calls and records, with the decode path on this library's
+device operator.  Its contract, restated:
 
-* prefill runs the model's own attention backend (SDPA or eager), exactly as
-  the reference (hf_reference.py:173-185);
-* each decode token routes, unions and attends every KV group of the layer
-  at once: the groups that share an encoder form the units of one
+* every standard attention module of the model (Qwen3Attention,
+  Qwen3_5Attention; LlamaAttention here as well) must have one encoder per
+  (layer, KV group), no more and no fewer;
+* the model's attention backend is replaced by a dispatcher that sends each
+  call to the session; prefill calls (several query rows, a layer's first
+  call, or any call inside ``prefill()``) run the backend the model was
+  configured with (SDPA or eager), with a causal mask offset to the cache
+  when a chunk arrives without one; ``close()`` puts the backends back;
+* a decode call (one query row) routes, unions and attends every KV group of
+  the layer: the groups that share an encoder form the units of one
   ``DeviceIndex`` / ``SparseDecode`` (one kernel chain per layer instead of
-  one Python loop iteration per group, hf_reference.py:193-217);
+  one loop iteration per group, hf_reference.py:193-217);
 * the index of a layer is built from the prefix at its first decode token
   and grows by complete blocks of ``update_interval`` keys, the current
   token always staying in the dense tail (hf_reference.py:202-213);
@@ -16,15 +24,15 @@ with its decode path on this library's device operator:
   through the same sparse-attention kernel.
 
 Routing, union and attention run asynchronously on the current stream; the
-per-group records (history, unique, raw, buckets, tail) are kept as device
-tensors and read when ``records`` is accessed.  Supported attention modules:
-Qwen3Attention, Qwen3_5Attention (the reference's) and LlamaAttention (the
-Llama-3-8B-shaped decode loop); K/V in bf16 or fp32.
+per-group records (history, unique, raw, buckets, tail, and with
+``detailed_records`` the split between the prefix and indexed generated
+tokens) are kept as device tensors and read when ``records`` is accessed.
+K/V in bf16 or fp32.
 """
 from __future__ import annotations
 
-import importlib
 import math
+import sys
 from contextlib import contextmanager
 from dataclasses import dataclass
 
@@ -37,6 +45,7 @@ from .index import DeviceIndex, SAEParams
 SUPPORTED_MODULES = ("Qwen3Attention", "Qwen3_5Attention", "LlamaAttention")
 BACKEND = "prismkv_b200"
 BACKEND_EAGER = "prismkv_b200_eager"
+SESSION_ATTR = "_prismkv_b200_session"
 
 
 @dataclass
@@ -48,10 +57,84 @@ class Encoder:
 
 
 def _dispatch(module, q, k, v, attention_mask, **kwargs):
-    session = getattr(module, "_prismkv_b200_session", None)
+    """The registered attention function: hands the call to the module's
+    session."""
+    session = getattr(module, SESSION_ATTR, None)
     if session is None:
-        raise RuntimeError("PrismKV B200 backend selected without an attached session")
+        raise RuntimeError(f"attention backend {BACKEND!r} called on a module with no PrismKV B200 session")
     return session.forward(module, q, k, v, attention_mask, **kwargs)
+
+
+def _check_options(mode, router, selected_buckets, unique_cap, update_interval) -> None:
+    """The constructor's refusals of bad options (ValueError, as the
+    reference's adapter)."""
+    problems = []
+    if mode not in ("sparse", "all_read"):
+        problems.append(f"mode {mode!r} (expected 'sparse' or 'all_read')")
+    if router not in ("moments", "q_activation"):
+        problems.append(f"router {router!r} (expected 'moments' or 'q_activation')")
+    if not selected_buckets > 0:
+        problems.append(f"selected_buckets {selected_buckets!r} (expected a positive count)")
+    if unique_cap is not None and not 0 <= unique_cap <= 1:
+        problems.append(f"unique_cap {unique_cap!r} (expected None or a fraction in [0, 1])")
+    if not update_interval > 0:
+        problems.append(f"update_interval {update_interval!r} (expected a positive token count)")
+    if problems:
+        raise ValueError("invalid adapter options: " + "; ".join(problems))
+
+
+def _prefill_backend(module, implementation: str):
+    """The attention function the model would call for `implementation`:
+    the registry entry for SDPA, the modeling file's own eager function for
+    eager."""
+    if implementation == "eager":
+        return getattr(sys.modules[type(module).__module__], "eager_attention_forward")
+    from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
+    return ALL_ATTENTION_FUNCTIONS[implementation]
+
+
+def _causal_chunk_mask(steps: int, total: int, like: torch.Tensor) -> torch.Tensor:
+    """Additive mask [1, 1, steps, total] for the last `steps` positions of a
+    `total`-slot cache: query row i sits at position total - steps + i and
+    sees the slots up to it."""
+    mask = torch.full((steps, total), -torch.inf, dtype=like.dtype, device=like.device)
+    return torch.triu(mask, diagonal=total - steps + 1)[None, None]
+
+
+def _check_call(q, k, v, kwargs) -> int:
+    """Refusals of an attention call outside the adapter's contract
+    (unpadded batch one, standard scale, no sliding window, soft cap or
+    dropout); returns the head dimension."""
+    if q.shape[0] != 1 or k.shape[0] != 1:
+        raise NotImplementedError(f"batch {q.shape[0]}: only unpadded batch-one requests are supported")
+    d = q.shape[-1]
+    if q.shape[-2] < 1 or k.shape[-1] != d or v.shape != k.shape:
+        raise ValueError(f"attention shapes q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)} do not agree")
+    if not math.isclose(kwargs.get("scaling", d ** -0.5), d ** -0.5):
+        raise NotImplementedError(f"attention scale {kwargs['scaling']} differs from 1/sqrt({d})")
+    for name in ("sliding_window", "softcap"):
+        if kwargs.get(name) is not None:
+            raise NotImplementedError(f"{name} attention is not supported")
+    if kwargs.get("dropout", 0) != 0:
+        raise ValueError("attention dropout must be 0 (inference only)")
+    return d
+
+
+def _visible_length(mask, slots: int) -> int:
+    """Cache slots the last query row sees.  Without a mask it is every slot;
+    a 4-D mask must let the last row see a prefix of the cache (all of a
+    growing cache, the filled part of a static one) -- anything else is
+    padding or a custom mask, which the adapter refuses."""
+    if mask is None:
+        return slots
+    if mask.ndim != 4:
+        raise NotImplementedError("only 4-D causal masks are supported (no padding or custom masks)")
+    row = mask[..., -1, :slots].reshape(-1, slots)[0]
+    sees = row if row.dtype == torch.bool else row == 0
+    n = int(sees.sum().item())
+    if n == 0 or not bool(sees[:n].all()):
+        raise NotImplementedError("only 4-D causal masks are supported (no padding or custom masks)")
+    return n
 
 
 class _Batch:
@@ -70,6 +153,7 @@ class _Batch:
         self.dense_ids = None
         self.len_dev = None   # rows per unit (history + tail), read by the attention on the device
         self.kv = None        # the layer's K/V cache tensors of the last decode step
+        self.prefix_lens = None   # per-unit bucket sizes over the prefix (detailed records)
 
     def rows(self, t: torch.Tensor) -> torch.Tensor:
         """t[0, groups] ([B, H_kv, T, d] -> [U, T, d]); a view for a run of groups."""
@@ -77,96 +161,98 @@ class _Batch:
 
 
 class HFReference:
-    """A stateful, all-group adapter; one session per model, one request at a
-    time (hf_reference.py:66-128).
+    """One session per model and one request at a time (the reference's
+    hf_reference.py:66-128 interface).
 
-    mode='all_read' is the dense-equivalence control; the main method is
-    mode='sparse', router='moments', selected_buckets=16, unique_cap=None.
-    Call begin_request() when starting a new KV cache; close() restores the
-    model's attention backends."""
+    mode='all_read' is the dense-equivalence control; the reference's main
+    method is mode='sparse', router='moments', selected_buckets=16,
+    unique_cap=None.  Call begin_request() when starting a new KV cache;
+    close() gives the model its attention backends back."""
 
     def __init__(self, model, encoders, *, mode="sparse", router="moments", selected_buckets=16, unique_cap=None,
                  update_interval=4096, detailed_records=False):
-        if mode not in ("sparse", "all_read"):
-            raise ValueError("mode must be sparse or all_read")
-        if router not in ("moments", "q_activation") or selected_buckets <= 0:
-            raise ValueError("unsupported router/bucket count")
-        if unique_cap is not None and not 0 <= unique_cap <= 1:
-            raise ValueError("unique cap must be a fraction")
-        if update_interval <= 0:
-            raise ValueError("positive update interval required")
-        if detailed_records:
-            raise NotImplementedError("detailed records (per-list old/new splits) are not kept on the device path")
+        _check_options(mode, router, selected_buckets, unique_cap, update_interval)
+        # Discover the attention modules and check the encoder coverage
+        # before anything on the model changes.
+        modules, backends, configs = {}, {}, {}
+        for name, module in model.named_modules():
+            if type(module).__name__ not in SUPPORTED_MODULES:
+                continue
+            if hasattr(module, SESSION_ATTR):
+                raise ValueError(f"{name} is already attached to a PrismKV B200 session")
+            layer = module.layer_idx
+            if layer in modules:
+                raise ValueError(f"attention layer id {layer} appears twice ({name})")
+            cfg = module.config
+            implementation = cfg._attn_implementation
+            if implementation not in ("sdpa", "eager"):
+                raise ValueError(f"{name}: prefill backend {implementation!r} is not supported (sdpa or eager)")
+            modules[layer] = module
+            backends[layer] = _prefill_backend(module, implementation)
+            configs[id(cfg)] = (cfg, implementation)
+        wanted = {(layer, g) for layer, m in modules.items() for g in range(m.config.num_key_value_heads)}
+        given = set(encoders)
+        if not modules or given != wanted:
+            raise ValueError(f"encoders must cover exactly the (layer, KV group) pairs of the model's attention: "
+                             f"missing={sorted(wanted - given)}, extra={sorted(given - wanted)}")
         self.model, self.encoders = model, encoders
         self.mode, self.router = mode, router
         self.selected_buckets, self.unique_cap = selected_buckets, unique_cap
-        self.update_interval, self.force_prefill = update_interval, False
-        self.detailed_records = detailed_records
-        self.modules, self.original, self.configs = {}, {}, {}
-        expected = set()
-        for module in model.modules():
-            if type(module).__name__ not in SUPPORTED_MODULES:
-                continue
-            if hasattr(module, "_prismkv_b200_session"):
-                raise ValueError("model already has a PrismKV B200 session")
-            layer = module.layer_idx
-            if layer in self.modules:
-                raise ValueError("duplicate attention-layer IDs")
-            cfg = module.config
-            expected.update((layer, g) for g in range(cfg.num_key_value_heads))
-            self.modules[layer] = module
-            implementation = cfg._attn_implementation
-            if implementation not in ("sdpa", "eager"):
-                raise ValueError("the adapter is validated for SDPA/eager prefill only")
-            namespace = vars(importlib.import_module(type(module).__module__))
-            registry = namespace["ALL_ATTENTION_FUNCTIONS"]
-            self.original[layer] = (namespace["eager_attention_forward"] if implementation == "eager"
-                                    else registry[implementation])
-            self.configs[id(cfg)] = (cfg, implementation)
-        if not self.modules or set(encoders) != expected:
-            raise ValueError(f"provide exactly all standard-attention KV encoders; missing={expected - set(encoders)}, "
-                             f"extra={set(encoders) - expected}")
-        from transformers import AttentionInterface, AttentionMaskInterface
-        from transformers.masking_utils import eager_mask, sdpa_mask
-        AttentionInterface.register(BACKEND, _dispatch)
-        AttentionMaskInterface.register(BACKEND, sdpa_mask)
-        # Eager attention does not infer causality from a missing mask.
-        AttentionInterface.register(BACKEND_EAGER, _dispatch)
-        AttentionMaskInterface.register(BACKEND_EAGER, eager_mask)
-        for module in self.modules.values():
-            module._prismkv_b200_session = self
-        for cfg, old in self.configs.values():
-            cfg._attn_implementation = BACKEND_EAGER if old == "eager" else BACKEND
+        self.update_interval = update_interval
+        self.detailed_records = bool(detailed_records)
+        self.modules, self.original, self.configs = modules, backends, configs
+        self._prefill_depth = 0
+        self._attach()
         self.workspaces = {}
         self.begin_request()
 
     # ----------------------------------------------------------- lifecycle
+    def _attach(self) -> None:
+        from transformers import AttentionInterface, AttentionMaskInterface
+        from transformers.masking_utils import eager_mask, sdpa_mask
+        # Two registry names: an eager model keeps the eager mask builder,
+        # which always materialises the causal mask.
+        for name, mask_fn in ((BACKEND, sdpa_mask), (BACKEND_EAGER, eager_mask)):
+            AttentionInterface.register(name, _dispatch)
+            AttentionMaskInterface.register(name, mask_fn)
+        for module in self.modules.values():
+            setattr(module, SESSION_ATTR, self)
+        for cfg, implementation in self.configs.values():
+            cfg._attn_implementation = BACKEND_EAGER if implementation == "eager" else BACKEND
+
     def begin_request(self):
+        """Forget every layer's prefix and index (a new KV cache)."""
         self.prefix_lengths, self.layers, self._records = {}, {}, []
         self._graph_total = None
 
+    @property
+    def force_prefill(self) -> bool:
+        return self._prefill_depth > 0
+
     @contextmanager
     def prefill(self):
-        """Explicitly mark chunked prefill, including one-token chunks."""
-        previous = self.force_prefill
-        self.force_prefill = True
+        """Within this block every call is prefill (chunked prefill,
+        one-token chunks included)."""
+        self._prefill_depth += 1
         try:
             yield self
         finally:
-            self.force_prefill = previous
+            self._prefill_depth -= 1
 
     def close(self):
+        """Detach from the model and restore its attention backends."""
         for module in self.modules.values():
-            if getattr(module, "_prismkv_b200_session", None) is self:
-                del module._prismkv_b200_session
+            if getattr(module, SESSION_ATTR, None) is self:
+                delattr(module, SESSION_ATTR)
         for cfg, implementation in self.configs.values():
             cfg._attn_implementation = implementation
         self.layers.clear()
 
     def generate(self, *args, **kwargs):
-        """Reset for a new model.generate call/cache. Existing cache reuse is manual."""
+        """model.generate on a fresh request; continuing an existing cache is
+        done with manual model calls."""
         if kwargs.get("past_key_values") is not None:
-            raise ValueError("use manual model calls and session state for an existing cache")
+            raise ValueError("generate() starts a new request; drive an existing cache with manual model calls")
         self.begin_request()
         return self.model.generate(*args, **kwargs)
 
@@ -176,11 +262,19 @@ class HFReference:
         (read from the device here, not during decode)."""
         out = []
         for rec in self._records:
-            layer, groups, history, tail, count, raw, nfeat = rec
+            layer, groups, history, tail, count, raw, nfeat, detail = rec
             c, r, nf = count.tolist(), raw.tolist(), nfeat.tolist()
+            if detail is not None:
+                initial, old_unique, old_raw = detail
+                ou, orw = old_unique.tolist(), old_raw.tolist()
             for i, g in enumerate(groups):
-                out.append(dict(layer=layer, group=g, history=history, unique=int(c[i]), raw=int(r[i]),
-                                buckets=int(nf[i]), tail=tail, routing_policy=self.mode))
+                row = dict(layer=layer, group=g, history=history, unique=int(c[i]), raw=int(r[i]),
+                           buckets=int(nf[i]), tail=tail, routing_policy=self.mode)
+                if detail is not None:
+                    row.update(initial_history=initial, old_unique=int(ou[i]), old_raw=int(orw[i]),
+                               generated_indexed_unique=int(c[i]) - int(ou[i]),
+                               generated_indexed_raw=int(r[i]) - int(orw[i]))
+                out.append(row)
         return out
 
     # ------------------------------------------------------------- forward
@@ -203,50 +297,22 @@ class HFReference:
 
     @torch.no_grad()
     def forward(self, module, q, k, v, attention_mask, **kwargs):
-        if q.shape[0] != 1 or k.shape[0] != 1:
-            raise NotImplementedError("the adapter supports unpadded batch-one requests")
-        if q.shape[-2] < 1 or q.shape[-1] != k.shape[-1] or k.shape != v.shape:
-            raise ValueError("invalid QKV shapes")
-        d = q.shape[-1]
-        if not math.isclose(kwargs.get("scaling", 1 / math.sqrt(d)), 1 / math.sqrt(d)):
-            raise NotImplementedError("nonstandard attention scale")
-        if kwargs.get("sliding_window") is not None or kwargs.get("softcap") is not None:
-            raise NotImplementedError("sliding-window/soft-capped attention is outside this adapter")
-        if kwargs.get("dropout", 0) != 0:
-            raise ValueError("inference only: disable dropout")
+        d = _check_call(q, k, v, kwargs)
         layer, steps = module.layer_idx, q.shape[-2]
         graph = self._graph_total is not None
-        if graph:
-            # Replayed decode (GraphDecoder): the length comes from the host,
-            # nothing is read back from the device while capturing.
-            total = self._graph_total
-        else:
-            total = k.shape[-2]
-            if attention_mask is not None:
-                if attention_mask.ndim != 4:
-                    raise NotImplementedError("padding/arbitrary attention masks are unsupported")
-                # The last row must see a prefix of the cache: all of it (a
-                # growing cache) or its first `total` slots (a static cache).
-                last = attention_mask[..., -1, :total].reshape(-1, total)[0]
-                visible = last if last.dtype == torch.bool else last == 0
-                n = int(visible.sum().item())
-                if n == 0 or not bool(visible[:n].all()):
-                    raise NotImplementedError("padding/arbitrary attention masks are unsupported")
-                total = n
-        is_prefill = self.force_prefill or layer not in self.prefix_lengths or steps > 1
-        if is_prefill:
+        # Replayed decode (GraphDecoder) takes the length from the host, so
+        # nothing is read back from the device while capturing.
+        total = self._graph_total if graph else _visible_length(attention_mask, k.shape[-2])
+        if self.force_prefill or steps > 1 or layer not in self.prefix_lengths:
+            # Prefill: the model's own backend over the whole chunk; the
+            # layer's decode state starts again from this prefix.
             self.prefix_lengths[layer] = total
             self.layers.pop(layer, None)
             if attention_mask is None and 1 < steps < total:
-                positions = torch.arange(total - steps, total, device=q.device)
-                visible = torch.arange(total, device=q.device)[None] <= positions[:, None]
-                attention_mask = torch.zeros((1, 1, steps, total), device=q.device, dtype=q.dtype)
-                attention_mask.masked_fill_(~visible[None, None], -torch.inf)
+                attention_mask = _causal_chunk_mask(steps, total, q)
             return self.original[layer](module, q, k, v, attention_mask, **kwargs)
-        if steps != 1:
-            raise NotImplementedError("decode is one token per forward")
         if not q.is_cuda:
-            raise RuntimeError("the PrismKV B200 decode path needs CUDA tensors")
+            raise RuntimeError("the PrismKV B200 decode path runs on CUDA tensors only")
         groups, queries = k.shape[1], q.shape[1]
         if queries % groups:
             raise ValueError("Q heads must form equal-sized KV groups")
@@ -276,9 +342,29 @@ class HFReference:
             for i, g in enumerate(batch.groups):
                 answer[0, 0, g * per_group:(g + 1) * per_group] = out[i]
             if not graph:
+                detail = self._detail(batch, layer, count) if self.detailed_records else None
                 self._records.append((layer, tuple(batch.groups), history, total - history, count.clone(),
-                                      raw.clone(), nfeat.clone()))
+                                      raw.clone(), nfeat.clone(), detail))
         return answer, None
+
+    def _detail(self, batch: _Batch, layer: int, count: torch.Tensor):
+        """The detailed record's split (hf_reference.py:218-231) on the
+        device: of the union's ids, those inside the prefix the index was
+        built from (ids are ascending, so the ones below its length); of the
+        accepted buckets' raw entries, those from that prefix -- a bucket's
+        size at build time, since appends only add later tokens."""
+        initial = self.prefix_lengths[layer]
+        if self.mode == "all_read":
+            n = count.to(torch.int64)
+            return initial, n, n
+        op = batch.op
+        width = op.ids.shape[1]
+        slot = torch.arange(width, device=op.ids.device)
+        old_unique = ((op.ids < initial) & (slot[None] < count[:, None])).sum(1)
+        picks = torch.gather(batch.prefix_lens, 1, op.features.long())
+        taken = torch.arange(op.features.shape[1], device=op.ids.device)[None] < op.n_features[:, None]
+        old_raw = (picks * taken).sum(1)
+        return initial, old_unique, old_raw
 
     def _advance(self, batch: _Batch, layer: int, per_group: int, Kb: torch.Tensor, total: int,
                  ws: nv.Workspace) -> int:
@@ -292,6 +378,8 @@ class HFReference:
             batch.index = DeviceIndex.build(Kb[:, :h], batch.sae, float(enc.key_scale),
                                             moments=self.router == "moments", slack_frac=0.25, slack_min=4,
                                             workspace=ws)
+            if self.detailed_records:
+                batch.prefix_lens = batch.index.lens.to(torch.int64)
         index = batch.index
         grew = False
         while total - index.history > self.update_interval:

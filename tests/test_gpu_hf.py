@@ -99,7 +99,7 @@ def test_sparse_decode_matches_oracle(pk, oracle, router, shared, kind):
     layers, kv_heads, per_group, F, ui, prefix, steps = 2, 2, 2, 256, 16, 160, 24
     model = tiny_model(kind)
     encs = make_encoders(layers, kv_heads, F, shared)
-    s = HFReference(model, encs, router=router, selected_buckets=8, update_interval=ui)
+    s = HFReference(model, encs, router=router, selected_buckets=8, update_interval=ui, detailed_records=True)
     caps = []
     inner = s.forward
 
@@ -124,10 +124,12 @@ def test_sparse_decode_matches_oracle(pk, oracle, router, shared, kind):
     finally:
         s.close()
     assert len(caps) == steps * layers
+    recs = s.records
+    assert len(recs) == steps * layers * kv_heads
     oidx = {}
     saes = {key: orc.SAE(e.sae.W_enc.cpu().numpy(), e.sae.b_enc.cpu().numpy(), 8, 8) for key, e in encs.items()}
     appended = False
-    for layer, q, k, v, out, ids in caps:
+    for ci, (layer, q, k, v, out, ids) in enumerate(caps):
         total = k.shape[1]
         for g in range(kv_heads):
             sae = saes[(layer, g)]
@@ -147,6 +149,15 @@ def test_sparse_decode_matches_oracle(pk, oracle, router, shared, kind):
             assert np.array_equal(got, want), (layer, g, total)
             ref = orc.attend(Q, K, V, want, idx.history)
             assert rel_l2(out[g * per_group:(g + 1) * per_group], ref) < TOL_F32
+            # The record, detailed split included (hf_reference.py:218-231).
+            rec = next(r for r in recs[ci * kv_heads:(ci + 1) * kv_heads] if r["group"] == g)
+            assert (rec["layer"], rec["history"], rec["tail"]) == (layer, idx.history, total - idx.history)
+            assert (rec["unique"], rec["raw"], rec["buckets"]) == (len(want), meta["raw"], len(meta["features"]))
+            old_unique = int((want < prefix).sum())
+            old_raw = sum(int((idx.lists[b] < prefix).sum()) for b in meta["features"])
+            assert (rec["initial_history"], rec["old_unique"], rec["old_raw"]) == (prefix, old_unique, old_raw)
+            assert rec["generated_indexed_unique"] == len(want) - old_unique
+            assert rec["generated_indexed_raw"] == meta["raw"] - old_raw
     assert appended
 
 

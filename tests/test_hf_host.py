@@ -85,8 +85,36 @@ def test_prefill_passthrough_and_cpu_decode_refused(kind):
         s.close()
 
 
-def test_detailed_records_refused():
+def test_detailed_records_accepted():
+    """detailed_records=True is a supported option (the split is computed on
+    the device at decode time; tests/test_gpu_hf.py checks its values)."""
     m = tiny_model()
-    with pytest.raises(NotImplementedError):
-        HFReference(m, encoders(2, 1), detailed_records=True)
+    s = HFReference(m, encoders(2, 1), detailed_records=True)
+    try:
+        assert s.detailed_records and s.records == []
+    finally:
+        s.close()
     assert m.config._attn_implementation == "sdpa"
+
+
+def test_chunked_prefill_mask_and_prefill_block():
+    """A chunk that arrives without a mask gets the causal mask offset to the
+    cache (its row i sees slots up to total - steps + i); inside prefill()
+    even one-token calls are prefill."""
+    from prismkv_b200.hf_reference import _causal_chunk_mask
+    mask = _causal_chunk_mask(3, 7, torch.zeros(1))[0, 0]
+    want = torch.tensor([[0 if j <= 4 + i else float("-inf") for j in range(7)] for i in range(3)])
+    assert torch.equal(mask, want)
+    m = tiny_model()
+    s = HFReference(m, encoders(2, 1))
+    try:
+        ids = torch.randint(0, 96, (1, 9), generator=torch.Generator().manual_seed(2))
+        with torch.no_grad():
+            out = m(input_ids=ids[:, :8], use_cache=True)
+            with s.prefill():
+                assert s.force_prefill
+                m(input_ids=ids[:, 8:], past_key_values=out.past_key_values, use_cache=True)
+            assert not s.force_prefill
+        assert s.prefix_lengths == {0: 9, 1: 9}
+    finally:
+        s.close()

@@ -92,8 +92,8 @@ def test_other_refusals(tmp_path):
         load_encoders(root)
     root = fresh("contents")
     torch.save({"W_enc": torch.zeros(16, 4), "b_enc": torch.zeros(16), "extra": torch.zeros(1)}, root / "l00_g00.pt")
-    from prismkv_b200.weights import _sha
-    _rewrite(root, lambda m: m["groups"][0].update(sha256=_sha(root / "l00_g00.pt")))
+    from prismkv_b200.weights import file_digest
+    _rewrite(root, lambda m: m["groups"][0].update(sha256=file_digest(root / "l00_g00.pt")))
     with pytest.raises(ValueError, match="contents"):
         load_encoders(root)
     with pytest.raises(ValueError):
