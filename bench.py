@@ -11,10 +11,13 @@ this library's own build kernels before timing.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Multi-GPU (torchrun, one rank per GPU): every rank serves its own batch of
-B=4 sequences (batch x KV-head sharding, no collective on the path), so the
-job's tokens/s is the sum over ranks -- weak scaling.  Timing is on the
-device with CUDA events, max over ranks.
+Multi-GPU (torchrun, one rank per GPU): the config's 32 units are split over
+the ranks (2 and 4 ranks split the batch, 8 ranks split the batch 4 ways and
+the KV heads 2 ways); the job still decodes the same B=4 sequences, so this
+is strong scaling with no collective on the path.  The line's ``seqshard``
+object measures config 4 on the same ranks: the 1M-token context split
+along the sequence, with one NCCL all-gather of the attention partials per
+step.  Timing is on the device with CUDA events, max over ranks.
 """
 from __future__ import annotations
 
@@ -60,6 +63,7 @@ def parse():
     p.add_argument("--layout", action="store_true",
                    help="layout diagnostic: in-place sparse attention vs explicit gather + packed attention")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-seqshard", action="store_true", help="skip the config-4 sub-measurement")
     p.add_argument("--parity-units", type=int, default=1,
                    help="units of layer 0 recomputed by the CPU oracle after timing (0: none)")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -133,6 +137,9 @@ class Clocks:
 # workload
 # ---------------------------------------------------------------------------
 
+GRAPH_INSPECT_ERRORS: list = []
+
+
 def graph_kernel_launches(graph):
     """Kernel nodes of this library (C++ namespace pk) in a captured CUDA
     graph, or None when the graph cannot be inspected."""
@@ -160,7 +167,8 @@ def graph_kernel_launches(graph):
             name = name.decode() if isinstance(name, bytes) else str(name)
             count += name.startswith("_ZN2pk")
         return count
-    except Exception:  # noqa: BLE001 -- an inspection aid, never fatal
+    except Exception as err:  # noqa: BLE001 -- an inspection aid, never fatal
+        GRAPH_INSPECT_ERRORS.append(f"{type(err).__name__}: {err}")
         return None
 
 
@@ -186,37 +194,100 @@ def gen_queries(torch, dev, g, centers, n, G):
     return (c + 0.3 * torch.randn(n, U, G, d, device=dev, generator=g)).to(torch.bfloat16)
 
 
+class Ranks:
+    """One process per GPU (torchrun's RANK / LOCAL_RANK / WORLD_SIZE), NCCL
+    between them; device timings are reduced as the max over ranks."""
+
+    def __init__(self):
+        import torch
+        import torch.distributed as dist
+        self.torch, self.dist = torch, dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            from datetime import timedelta
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=self.dev)
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        t = self.torch.tensor([x], device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        self.torch.cuda.synchronize()
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def unit_partition(B: int, Hkv: int, world: int, rank: int):
+    """The config's U = B * Hkv units (unit id b * Hkv + h) split over the
+    ranks batch-first: 2 and 4 ranks split the batch, 8 ranks split the
+    batch 4 ways and the KV heads 2 ways.  Returns this rank's unit ids."""
+    U = B * Hkv
+    if U % world:
+        raise SystemExit(f"{U} units do not split evenly over {world} ranks")
+    per = U // world
+    return list(range(rank * per, (rank + 1) * per))
+
+
+def gen_units(torch, dev, seed, layer, units, T, d, C, steps, G):
+    """K, V [U, T, d] and every step's queries [steps, U, G, d] (bf16) of the
+    given global unit ids of one layer: clustered keys (centers ~ N(0,1),
+    noise sigma 0.3), iid values, queries a random center plus noise.  Each
+    unit has its own seed, so a unit's data does not depend on how the units
+    are spread over ranks."""
+    U = len(units)
+    K = torch.empty(U, T, d, device=dev, dtype=torch.bfloat16)
+    V = torch.empty(U, T, d, device=dev, dtype=torch.bfloat16)
+    Q = torch.empty(steps, U, G, d, device=dev, dtype=torch.bfloat16)
+    g = torch.Generator(device=dev)
+    for i, u in enumerate(units):
+        g.manual_seed(seed * 1_000_003 + layer * 4099 + u)
+        centers = torch.randn(C, d, device=dev, generator=g)
+        for lo in range(0, T, 32768):
+            hi = min(T, lo + 32768)
+            cid = torch.randint(0, C, (hi - lo,), device=dev, generator=g)
+            K[i, lo:hi] = (centers[cid] + 0.3 * torch.randn(hi - lo, d, device=dev, generator=g)).to(torch.bfloat16)
+            V[i, lo:hi] = torch.randn(hi - lo, d, device=dev, generator=g).to(torch.bfloat16)
+        qc = torch.randint(0, C, (steps, G), device=dev, generator=g)
+        Q[:, i] = (centers[qc] + 0.3 * torch.randn(steps, G, d, device=dev, generator=g)).to(torch.bfloat16)
+    return K, V, Q
+
+
 def run_ours(a):
     import torch
-    import torch.distributed as dist
     import prismkv_b200 as pk
     from prismkv_b200 import native as nv
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
-
+    ctx = Ranks()
+    world, rank, dev = ctx.world, ctx.rank, ctx.dev
     L, B, Hkv, G, d = a.layers, a.batch, a.kv_heads, a.q_per_kv, 128
-    U = B * Hkv
+    units = unit_partition(B, Hkv, world, rank)
+    U = len(units)
     N, F, k = a.history, a.features, a.query_topk
     T = N + a.max_steps
     total_steps = a.warmup + a.steps
     if total_steps > a.max_steps:
         raise SystemExit("warmup + steps exceeds the KV cache's decode positions (--max-steps)")
-    g = torch.Generator(device=dev)
     t_setup = time.time()
     layers = []
     ws = nv.Workspace(dev)
     build_s = 0.0
     for l in range(L):
-        g.manual_seed(a.seed * 1_000_003 + rank * 10_007 + l)
-        centers, K, V = gen_layer(torch, dev, g, U, T, d, a.clusters)
-        W = torch.randn(F, d, device=dev, generator=g) / math.sqrt(d)
+        K, V, Q = gen_units(torch, dev, a.seed, l, units, T, d, a.clusters, total_steps, G)
+        gw = torch.Generator(device=dev)
+        gw.manual_seed(a.seed * 1_000_003 + l * 4099 + 999_983)   # one SAE per layer, shared by its units
+        W = torch.randn(F, d, device=dev, generator=gw) / math.sqrt(d)
         sae = pk.SAEParams(W, torch.zeros(F, device=dev), key_mean=a.key_mean, query_topk=k)
         torch.cuda.synchronize()
         tb = time.time()
@@ -225,10 +296,7 @@ def run_ours(a):
         build_s += time.time() - tb
         op = pk.SparseDecode(idx, sae, heads_per_unit=G, query_scale=1.0, budget=a.budget,
                              max_history=N + a.max_steps, workspace=ws)
-        Q = gen_queries(torch, dev, g, centers, total_steps, G)
         layers.append(dict(K=K, V=V, idx=idx, op=op, Q=Q))
-        del centers
-    ws.buffers.pop(("build",), None)
     for key in [k_ for k_ in ws.buffers if isinstance(k_, tuple) and k_[0] == "build"]:
         del ws.buffers[key]
     torch.cuda.empty_cache()
@@ -251,18 +319,14 @@ def run_ours(a):
     len_static = lens[0].clone()
     outs = torch.empty(L, U, G, d, dtype=torch.bfloat16, device=dev)
 
-    def step_body(av_events=None):
+    def step_body():
         for l, lay in enumerate(layers):
             q = q_static[l]
             lay["op"].route(q)
-            if av_events is not None:
-                av_events[l][0].record()
             # The token's KV append fused into the attention launch: its rows
             # are attended as the newest tail row and written into the cache.
             lay["op"].attention(q, lay["K"], lay["V"], length=len_static,
                                 append=(kv_static[l, 0], kv_static[l, 1]), out=outs[l])
-            if av_events is not None:
-                av_events[l][1].record()
 
     def load_step(s):
         q_static.copy_(q_steps[s])
@@ -299,15 +363,13 @@ def run_ours(a):
     for s in range(a.warmup):
         run_step(s)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clocks = Clocks(local)
+    ctx.barrier()
+    clocks = Clocks(ctx.local)
     clocks.start()
     time.sleep(0.2)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    ctx.barrier()
     t0 = time.time()
     e0.record()
     for s in range(a.warmup, total_steps):
@@ -315,20 +377,15 @@ def run_ours(a):
     e1.record()
     torch.cuda.synchronize()
     t1 = time.time()
-    if world > 1:
-        dist.barrier()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ctx.barrier()
+    ms = ctx.max(e0.elapsed_time(e1))
     for lay in layers:
         lay["op"].check()
 
     # Per-launch sparse-attention timing.  After each step's routing, a CUDA
-    # graph holding only the 32 layers' attention launches is replayed
-    # between two events on the launching stream (no host gaps inside), and
-    # each launch's algorithmic bytes come from that step's routed counts.
+    # graph holding only the layers' attention launches is replayed between
+    # two events on the launching stream (no host gaps inside), and each
+    # launch's algorithmic bytes come from that step's routed counts.
     def av_body():
         for l, lay in enumerate(layers):
             lay["op"].attention(q_static[l], lay["K"], lay["V"], length=len_static)
@@ -367,6 +424,7 @@ def run_ours(a):
     h_out = torch.empty(L, U, G, d, dtype=torch.bfloat16).pin_memory()
     ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    ctx.barrier()
     ee0.record()
     for s in range(a.warmup, total_steps):
         q_static.copy_(h_q[s], non_blocking=True)
@@ -379,11 +437,7 @@ def run_ours(a):
         h_out.copy_(outs, non_blocking=True)
     ee1.record()
     torch.cuda.synchronize()
-    e2e_ms = ee0.elapsed_time(ee1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = ctx.max(ee0.elapsed_time(ee1))
     # Index append (core.py:186-201) at the reference's cadence: a block of
     # update_interval keys per layer every update_interval decode steps.  It
     # is timed on a clone of each layer's index (the decode index stays as
@@ -407,10 +461,7 @@ def run_ours(a):
             del idx_c
         torch.cuda.empty_cache()
     append_ms_per_step = append_block_ms / a.update_interval if a.update_interval > 0 else 0.0
-    if world > 1:
-        t = torch.tensor([append_ms_per_step], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        append_ms_per_step = float(t.item())
+    append_ms_per_step = ctx.max(append_ms_per_step)
     clocks.stop()
     clk = clocks.summary(t0, t1)
     encode_paths = sorted({lay["idx"].encode_path for lay in layers})
@@ -424,10 +475,11 @@ def run_ours(a):
         lay["op"].route(q_static[0])
         o = lay["op"].attention(q_static[0], lay["K"], lay["V"], length=len_static)
         torch.cuda.synchronize()
-        units = sorted({0, U - 1})[:a.parity_units]
-        parity = sample_parity(lay, q_static[0], o, int(lens[s_last][0].item()), units, N, F, k, a)
+        sample = sorted({0, U - 1})[:a.parity_units]
+        parity = sample_parity(lay, q_static[0], o, int(lens[s_last][0].item()), sample, N, F, k, a)
+        parity["units"] = [units[u] for u in sample]
 
-    tokens = world * B * a.steps
+    tokens = B * a.steps          # the job decodes the config's B sequences
     decode_ms = ms
     ms = ms + append_ms_per_step * a.steps        # amortised append included
     e2e_ms = e2e_ms + append_ms_per_step * a.steps
@@ -456,6 +508,10 @@ def run_ours(a):
     # (kernel nodes whose function lives in namespace pk); eager runs fall
     # back to the four launches per layer the step issues.
     launches_per_step = graph_launches if graph_launches is not None else L * 4
+    if world == 1:
+        partition = "all 32 units on one GPU"
+    else:
+        partition = f"{U} units per rank ({B * Hkv} units split batch-first over {world} ranks)"
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -465,22 +521,23 @@ def run_ours(a):
         "warmup": a.warmup,
         "ms_per_step": round(ms / a.steps, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded clustered keys, iid values, random-init SAE)",
         "config": {"workload": "config3: Llama-3-8B-shaped decode attention path, 32 layers",
-                   "layers": L, "batch_per_gpu": B, "kv_heads": Hkv, "q_per_kv": G, "head_dim": d,
+                   "layers": L, "batch": B, "kv_heads": Hkv, "q_per_kv": G, "head_dim": d,
                    "history": N, "features": F, "query_topk": k, "budget": a.budget, "key_mean": a.key_mean,
                    "router": "q_activation", "update_interval": a.update_interval,
                    "graph": graph is not None, "l2": "inputs larger than L2 (KV and index per step >> 126 MB)",
-                   "parallelism": f"units{world}", "setup_s": round(setup_s, 1), "build_s": round(build_s, 1),
+                   "parallelism": f"batch x kv-heads over {world} GPU(s): {partition}",
+                   "units_per_gpu": U, "setup_s": round(setup_s, 1), "build_s": round(build_s, 1),
                    "decode_ms_per_step": round(decode_ms / a.steps, 4),
                    "append_ms_per_block": round(append_block_ms, 3),
                    "append_ms_per_step": round(append_ms_per_step, 5),
-                   "step": "32 x (route + union + sparse attention with the token's KV append) per token, plus "
-                           "the amortised index append of an update_interval block per layer every "
-                           "update_interval tokens"},
+                   "step": "32 x (route + union + sparse attention with the token's KV append) per token of each "
+                           "of the B sequences, plus the amortised index append of an update_interval block per "
+                           "layer every update_interval tokens"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": "sparse_av_bf16_kernel", "avg_launch_us": round(mean_av_ms * 1e3, 2),
@@ -488,22 +545,30 @@ def run_ours(a):
                      "share_of_step": round(av_ms / a.steps / (ms / a.steps), 3),
                      "peak_source": "measured" if "hbm_gbs" in peaks else "fallback"},
         "e2e": {"value": round(e2e, 2), "unit": "tokens/s",
-                "h2d_bytes_per_step": int(L * U * G * d * 2 + L * 2 * U * d * 2),
-                "d2h_bytes_per_step": int(L * U * G * d * 2)},
+                "h2d_bytes_per_step": int(L * U * G * d * 2 + L * 2 * U * d * 2) * world,
+                "d2h_bytes_per_step": int(L * U * G * d * 2) * world},
         "gpu_launches": launches_per_step * a.steps,
-        "gpu_launches_source": "graph kernel nodes" if graph_launches is not None else "per-layer launch count",
+        "gpu_launches_source": "graph kernel nodes" if graph_launches is not None else
+                               "per-layer launch count" + (f" ({GRAPH_INSPECT_ERRORS[0]})" if GRAPH_INSPECT_ERRORS
+                                                           else ""),
         "clocks": clk,
         "encode_path": encode_paths[0] if len(encode_paths) == 1 else encode_paths,
         "parity": parity,
     }
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         line["cpu_baseline"] = cpu_rate(a, seconds=a.cpu_seconds)
+    # The config-4 sequence-sharded step on the same ranks (its NCCL
+    # all-gather is the path's one collective), after this config's memory
+    # is released.
+    del graph, av_graph, layers, kv_steps, q_steps, outs, h_q, h_kv
+    ws.buffers.clear()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    if not a.no_seqshard:
+        line["seqshard"] = seqshard_measure(a, ctx)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
-        del graph
-        dist.barrier()
-        dist.destroy_process_group()
+    ctx.close()
 
 
 # ---------------------------------------------------------------------------
@@ -666,7 +731,7 @@ def run_reference(a):
         return
     base = cpu_rate(a, seconds=max(1.0, a.cpu_seconds))
     line = {"metric": METRIC, "value": base["value"], "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps,
-            "warmup": a.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "warmup": a.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic", "impl": "reference",
             "config": {"workload": "config3: Llama-3-8B-shaped decode attention path, 32 layers",
                        "history": a.history, "features": a.features, "budget": a.budget},
@@ -679,7 +744,7 @@ def run_reference(a):
 # config 4: million-token single-layer decode, KV cache sequence-sharded
 # ---------------------------------------------------------------------------
 
-def run_seqshard(a):
+def seqshard_measure(a, ctx) -> dict:
     """Config 4: B=1, 32/8 heads (U = 8 units of 4 query heads), context
     1048576, F = 32768, 64 features per query, budget 8192, clustered keys
     with 4096 clusters.  Rank r of P holds tokens [r*N/P, (r+1)*N/P) of every
@@ -687,32 +752,14 @@ def run_seqshard(a):
     exact BatchTopK, build_sharded); a decode step routes (replicated),
     unions its shard's buckets with budget 8192/P, attends over its rows and
     merges the P log-sum-exp partials after one NCCL all-gather.  The total
-    context is fixed: strong scaling."""
+    context is fixed: strong scaling.  Returns the measurement as a dict."""
     import torch
-    import torch.distributed as dist
     import prismkv_b200 as pk
     from prismkv_b200 import native as nv
     from prismkv_b200.shard import ShardedDecode, build_sharded, token_ranges
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    from datetime import timedelta
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    world, rank, local, dev = ctx.world, ctx.rank, ctx.local, ctx.dev
+    barrier, max_over_ranks = ctx.barrier, ctx.max
     B, Hkv, G, d = 1, 8, 4, 128
     U = B * Hkv
     N, F, k, budget, C = 1 << 20, 32768, 64, 8192, 4096
@@ -777,15 +824,18 @@ def run_seqshard(a):
     torch.cuda.synchronize()
     sd.check()
     barrier()
+    launches = None
     if not a.no_graph:
-        graph[0] = torch.cuda.CUDAGraph()
+        graph[0] = torch.cuda.CUDAGraph(keep_graph=True)
         s_cap = torch.cuda.Stream()
         s_cap.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s_cap):
             with torch.cuda.graph(graph[0], stream=s_cap):
                 body()
         torch.cuda.current_stream().wait_stream(s_cap)
+        graph[0].instantiate()
         torch.cuda.synchronize()
+        launches = graph_kernel_launches(graph[0])
         barrier()
     clocks = Clocks(local)
     clocks.start()
@@ -822,30 +872,38 @@ def run_seqshard(a):
     clocks.stop()
     sd.check()
     tokens = B * a.steps
-    line = {
+    out = {
         "metric": "config4 decode tokens/s at 1M ctx (sequence-sharded)", "value": round(tokens / (ms / 1e3), 2),
         "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
-        "ms_per_step": round(ms / a.steps, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic (seeded clustered keys, iid values, random-init SAE)",
+        "ms_per_step": round(ms / a.steps, 4), "higher_is_better": True, "scaling": "strong",
         "config": {"workload": "config4: 1M-token single-layer decode, KV cache sequence-sharded",
                    "batch": B, "kv_heads": Hkv, "q_per_kv": G, "history": N, "features": F, "query_topk": k,
                    "budget": budget, "budget_per_shard": budget // world, "clusters": C,
                    "tokens_per_shard": n_local, "build_s": round(build_s, 2),
                    "index_build": "exact BatchTopK over the whole sequence (build_sharded)",
                    "parallelism": f"seq{world}", "graph": graph[0] is not None,
+                   "collective": "one NCCL all-gather of the (m, l, o) partials per step" if world > 1 else None,
                    "l2": "KV rows gathered per step are scattered over >> L2"},
         "e2e": {"value": round(tokens / (e2e_ms / 1e3), 2), "unit": "tokens/s",
-                "h2d_bytes_per_step": int(U * G * d * 2), "d2h_bytes_per_step": int(U * G * d * 2)},
-        "gpu_launches": 5 * a.steps,
+                "h2d_bytes_per_step": int(U * G * d * 2) * world, "d2h_bytes_per_step": int(U * G * d * 2) * world},
+        "gpu_launches": launches * a.steps if launches is not None else None,
         "clocks": clocks.summary(t0, t1),
     }
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     graph[0] = None   # a graph holding NCCL calls is released before the group
+    del sd, idx, K, V
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_seqshard(a):
+    """bench.py --config 4: the config-4 step alone, as its own JSON line."""
+    ctx = Ranks()
+    line = seqshard_measure(a, ctx)
+    line.update(vs_baseline=None, dtype="bf16", data="synthetic (seeded clustered keys, iid values, random-init SAE)")
+    if ctx.rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
 
 
 # ---------------------------------------------------------------------------

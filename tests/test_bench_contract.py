@@ -41,3 +41,18 @@ def test_reference_arm_other_ranks_exit_quietly():
     r = _run({"RANK": "1"})
     assert r.returncode == 0, r.stderr
     assert r.stdout.strip() == ""
+
+
+def test_unit_partition_splits_batch_then_kv_heads():
+    """bench.py --gpus N spreads config 3's 4 x 8 units batch-first: 2 and 4
+    ranks split the batch, 8 ranks split it 4 ways and the KV heads 2 ways."""
+    import bench
+    B, H = 4, 8
+    for world in (1, 2, 4, 8):
+        parts = [bench.unit_partition(B, H, world, r) for r in range(world)]
+        assert sorted(u for p in parts for u in p) == list(range(B * H))
+        assert all(len(p) == B * H // world for p in parts)
+    eight = [bench.unit_partition(B, H, 8, r) for r in range(8)]
+    for r, p in enumerate(eight):
+        assert {u // H for u in p} == {r // 2}                     # one sequence
+        assert {u % H for u in p} == set(range(4 * (r % 2), 4 * (r % 2) + 4))   # half its KV heads
