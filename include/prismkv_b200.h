@@ -62,7 +62,10 @@ extern "C" {
 #define PK_TERM_MEAN 2
 #define PK_TERM_VARIANCE 4
 
-/* Library build facts: target sm version * 100 + ABI revision; head dims. */
+/* Library build facts: target sm version * 100 + ABI revision; head dims.
+ * Every kernel is compiled for head_dim d = 128 (the reference's 8B
+ * configuration); any other d returns PK_ERR_UNSUPPORTED.  The reference's
+ * d = 256 configuration (its SM90 27B kernels) is not served. */
 int pk_version(void);
 int pk_supported_head_dim(int d);
 
@@ -129,6 +132,7 @@ int pk_union(uint64_t offsets, uint64_t lens, uint64_t ids, int64_t ids_stride,
              uint64_t out_ids, int64_t out_stride, uint64_t out_count,
              uint64_t features, uint64_t n_features, uint64_t raw,
              uint64_t status, uint64_t stream);
+
 
 /* ------------------------------------------------------------------------
  * Sparse attention over selected rows plus the dense tail (a4 + a11).

@@ -112,6 +112,7 @@ def _route(q, dev: DeviceIndex, *, router, sae, query_scale, query_topk, terms, 
     if q.ndim != 2:
         raise ValueError("q must be [heads, head_dim]")
     G, d = q.shape
+    nv.require_head_dim(d)
     F = dev.F
     device = q.device
     qc = q.contiguous()
@@ -196,6 +197,7 @@ def attend(q, keys, values, old_ids, history):
     if len(old_ids.unique()) != len(old_ids):
         raise ValueError("deduplicate history before attention")
     G, d = q.shape
+    nv.require_head_dim(d)
     device = q.device
     dt = q.dtype if q.dtype in (torch.float32, torch.bfloat16) else torch.float32
     qc = q.to(dt).contiguous()

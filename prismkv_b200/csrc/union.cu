@@ -14,12 +14,17 @@
 //      staged entry that turned a bit on carries a flag), and the range
 //      halves.  Ranges of more than one bucket run on lists staged in shared
 //      memory; a one-bucket probe counts its tokens missing from the bitmap.
-//   2. after i*, rounds: every remaining bucket's count of tokens missing
-//      from the bitmap is taken in parallel; the first bucket whose count
-//      fits is accepted (its count is exact: nothing changed since), the ones
-//      before it are skipped, and every bucket whose count exceeds the
-//      remaining budget is dropped for good (its count can shrink by at most
-//      what the budget shrinks).  Rounds = accepted tail buckets + 1.
+//   2. after i*, the tail: each remaining bucket's count of tokens missing
+//      from the bitmap is taken once, and a chained hash maps every missing
+//      token to the tail entries that hold it.  The block then walks the
+//      buckets in order: the next bucket whose exact count fits is accepted,
+//      its tokens are turned on, and each token turned on decrements the
+//      counts of the later buckets holding it (one barrier per accepted
+//      bucket).  When the tail or the hash does not fit in shared memory,
+//      rounds run instead: every remaining bucket's count is retaken from
+//      the bitmap, the first that fits is accepted, and a bucket whose count
+//      exceeds the remaining budget is dropped for good (its count can
+//      shrink by at most what the budget shrinks).
 #include "common.cuh"
 #include "mma.cuh"
 
@@ -57,16 +62,50 @@ __device__ __forceinline__ int block_sum(int v, int* red) {
     return s;
 }
 
-__global__ void __launch_bounds__(kUnionThreads)
-union_kernel(const int* __restrict__ offsets, const int* __restrict__ lens, const int* __restrict__ ids,
-             int64_t ids_stride, const int* __restrict__ order, const int* __restrict__ n_order, int order_stride,
-             const int* __restrict__ history, const long long* __restrict__ limit, int F, int max_history,
-             int stage_cap, int* __restrict__ out_ids, int64_t out_stride, int* __restrict__ out_count,
-             int* __restrict__ features, int* __restrict__ n_features, long long* __restrict__ raw,
-             int* __restrict__ status) {
-    extern __shared__ __align__(16) uint32_t dyn[];
-    __shared__ UnionSmem sm;
-    const int u = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+struct UnionArgs {
+    const int* offsets;
+    const int* lens;
+    const int* ids;
+    int64_t ids_stride;
+    const int* order;
+    const int* n_order;
+    int order_stride;
+    const int* history;
+    const long long* limit;
+    int F;
+    int max_history;
+    int stage_cap;       // staged list entries
+    int* out_ids;
+    int64_t out_stride;
+    int* out_count;
+    int* features;
+    int* n_features;
+    long long* raw;
+    int* status;
+};
+
+// One unit's union by one CTA of kUnionThreads threads; `dyn` is the
+// block's dynamic shared memory (bitmap of max_history bits, then stage_cap
+// staged entries), `sm` its static scratch.
+__device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* dyn, UnionSmem& sm) {
+    const int* __restrict__ offsets = A.offsets;
+    const int* __restrict__ lens = A.lens;
+    const int* __restrict__ ids = A.ids;
+    const int64_t ids_stride = A.ids_stride;
+    const int* __restrict__ order = A.order;
+    const int* __restrict__ n_order = A.n_order;
+    const int order_stride = A.order_stride;
+    const int* __restrict__ history = A.history;
+    const long long* __restrict__ limit = A.limit;
+    const int F = A.F, max_history = A.max_history, stage_cap = A.stage_cap;
+    int* __restrict__ out_ids = A.out_ids;
+    const int64_t out_stride = A.out_stride;
+    int* __restrict__ out_count = A.out_count;
+    int* __restrict__ features = A.features;
+    int* __restrict__ n_features = A.n_features;
+    long long* __restrict__ raw = A.raw;
+    int* __restrict__ status = A.status;
+    const int tid = threadIdx.x, nt = blockDim.x;
     const int lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
     const int H = history[u];
     if (H > max_history || H < 0) {
@@ -437,14 +476,20 @@ union_kernel(const int* __restrict__ offsets, const int* __restrict__ lens, cons
     }
 }
 
+__global__ void __launch_bounds__(kUnionThreads) union_kernel(UnionArgs A) {
+    extern __shared__ __align__(16) uint32_t dyn[];
+    __shared__ UnionSmem sm;
+    union_unit(A, blockIdx.x, dyn, sm);
+}
+
 }  // namespace pk
 
 using namespace pk;
 
-extern "C" int pk_union(uint64_t offsets, uint64_t lens, uint64_t ids, int64_t ids_stride, uint64_t order,
+static int union_launch(uint64_t offsets, uint64_t lens, uint64_t ids, int64_t ids_stride, uint64_t order,
                         uint64_t n_order, int order_stride, uint64_t history, uint64_t limit, int U, int F,
-                        int max_history, uint64_t out_ids, int64_t out_stride, uint64_t out_count,
-                        uint64_t features, uint64_t n_features, uint64_t raw, uint64_t status, uint64_t stream) {
+                        int max_history, uint64_t out_ids, int64_t out_stride, uint64_t out_count, uint64_t features,
+                        uint64_t n_features, uint64_t raw, uint64_t status, uint64_t stream) {
     if (U < 1 || F < 1 || max_history < 0 || order_stride < 1 || out_stride < 0 || ids_stride < 0) return PK_ERR_ARG;
     if (!offsets || !lens || !ids || !order || !n_order || !history || !limit || !out_ids || !out_count ||
         !features || !n_features || !raw)
@@ -455,11 +500,23 @@ extern "C" int pk_union(uint64_t offsets, uint64_t lens, uint64_t ids, int64_t i
     // The bitmap, then as many staged list entries as fit (at least 2048).
     if (bitmap + 2048 * 4 > cap) return PK_ERR_UNSUPPORTED;
     const int stage_cap = (int)((cap - bitmap) / 4);
+    UnionArgs A;
+    A.offsets = (const int*)offsets; A.lens = (const int*)lens; A.ids = (const int*)ids; A.ids_stride = ids_stride;
+    A.order = (const int*)order; A.n_order = (const int*)n_order; A.order_stride = order_stride;
+    A.history = (const int*)history; A.limit = (const long long*)limit; A.F = F; A.max_history = max_history;
+    A.stage_cap = stage_cap; A.out_ids = (int*)out_ids; A.out_stride = out_stride;
+    A.out_count = (int*)out_count; A.features = (int*)features; A.n_features = (int*)n_features;
+    A.raw = (long long*)raw; A.status = (int*)status;
     cudaFuncSetAttribute(union_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cap);
-    union_kernel<<<U, kUnionThreads, cap, (cudaStream_t)stream>>>(
-        (const int*)offsets, (const int*)lens, (const int*)ids, ids_stride, (const int*)order, (const int*)n_order,
-        order_stride, (const int*)history, (const long long*)limit, F, max_history, stage_cap, (int*)out_ids,
-        out_stride, (int*)out_count, (int*)features, (int*)n_features, (long long*)raw, (int*)status);
+    union_kernel<<<U, kUnionThreads, cap, (cudaStream_t)stream>>>(A);
     PK_CHECK_LAUNCH();
     return PK_OK;
+}
+
+extern "C" int pk_union(uint64_t offsets, uint64_t lens, uint64_t ids, int64_t ids_stride, uint64_t order,
+                        uint64_t n_order, int order_stride, uint64_t history, uint64_t limit, int U, int F,
+                        int max_history, uint64_t out_ids, int64_t out_stride, uint64_t out_count,
+                        uint64_t features, uint64_t n_features, uint64_t raw, uint64_t status, uint64_t stream) {
+    return union_launch(offsets, lens, ids, ids_stride, order, n_order, order_stride, history, limit, U, F,
+                        max_history, out_ids, out_stride, out_count, features, n_features, raw, status, stream);
 }

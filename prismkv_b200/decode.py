@@ -79,6 +79,7 @@ class SparseDecode:
             raise ValueError("give unique_cap or budget, not both")
         if unique_cap is not None and not 0 <= unique_cap <= 1:
             raise ValueError("unique_cap must be a fraction in [0,1]")
+        nv.require_head_dim(index.d)
         self.index = index
         self.sae = SAEParams.of(sae, index.device)
         self.router = router

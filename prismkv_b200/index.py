@@ -122,6 +122,7 @@ class DeviceIndex:
         sae = SAEParams.of(sae, keys.device)
         if d != sae.head_dim:
             raise ValueError("SAE and attention head dimensions differ")
+        nv.require_head_dim(d)
         F = sae.features
         cap = int(nv.query("pk_build_ids_capacity", N, F, sae.key_mean, float(slack_frac), int(slack_min)))
         idx = cls(U, F, d, cap, keys.device, moments)

@@ -74,6 +74,16 @@ class NativeError(RuntimeError):
     pass
 
 
+HEAD_DIM = 128   # the one head dimension the kernels are compiled for
+
+
+def require_head_dim(d: int) -> None:
+    """Refuse, before any launch, a head dimension the kernels do not
+    implement (the library returns PK_ERR_UNSUPPORTED for it)."""
+    if int(d) != HEAD_DIM:
+        raise ValueError(f"head_dim {int(d)} is not supported: the CUDA kernels are built for head_dim {HEAD_DIM} only")
+
+
 def lib():
     """Load the library once; raise if it is absent (no CPU fallback)."""
     global _lib

@@ -251,30 +251,30 @@ def test_bound_filtered_routing_equals_exact_encode(pk, batch):
             assert torch.equal(fast.ids[u, :c], exact.ids[u, :c])
 
 
-@pytest.mark.parametrize("seed", [0, 1, 2])
-def test_union_greedy_matches_oracle_on_large_buckets(pk, oracle, seed):
-    """Budgeted union on synthetic CSR indexes whose buckets are large and
-    overlap heavily (multi-round hash path, single-bucket rounds, accepted
-    buckets after the first skip), against the oracle's greedy."""
+def _union_case(pk, oracle, rs, U, H, F, n_cand, sizes_from, probs, hot_n, limits, hist_u=None, n_u=None):
+    """Random CSR indexes (buckets drawn from a shared hot set plus random
+    tokens, so they overlap), a random candidate order per unit; every limit
+    through pk_union against the oracle's greedy."""
     from prismkv_b200 import native as nv
-    rs = np.random.RandomState(100 + seed)
-    U, H, F, n_cand = 6, 60000, 300, 200
     dev = torch.device("cuda")
+    hist_u = hist_u or [H] * U
+    n_u = n_u if n_u is not None else [n_cand] * U
     lists_all, orders = [], []
     for u in range(U):
-        sizes = rs.choice([3, 40, 300, 2000, 9000], size=F, p=[0.2, 0.4, 0.3, 0.08, 0.02])
-        hot = rs.randint(0, H, size=3000)  # shared tokens -> overlap between buckets
+        Hu = hist_u[u]
+        sizes = rs.choice(sizes_from, size=F, p=probs)
+        hot = rs.randint(0, Hu, size=hot_n)
         lists = []
         for f in range(F):
-            pool = np.concatenate([hot, rs.randint(0, H, size=int(sizes[f]))])
+            pool = np.concatenate([hot, rs.randint(0, Hu, size=int(sizes[f]))])
             lists.append(np.unique(rs.choice(pool, size=min(len(pool), int(sizes[f])), replace=False)))
         lists_all.append(lists)
         orders.append(rs.permutation(F)[:n_cand])
     dindex = pk.index.from_lists([[torch.from_numpy(x) for x in l] for l in lists_all], H, 128, dev)
     order = torch.tensor(np.stack(orders), dtype=torch.int32, device=dev)
-    n_order = torch.full((U,), n_cand, dtype=torch.int32, device=dev)
-    hist = torch.full((U,), H, dtype=torch.int32, device=dev)
-    for lim in (0, 500, 4096, 20000, 10 ** 9):
+    n_order = torch.tensor(n_u, dtype=torch.int32, device=dev)
+    hist = torch.tensor(hist_u, dtype=torch.int32, device=dev)
+    for lim in limits:
         limit = torch.full((U,), lim, dtype=torch.int64, device=dev)
         out = torch.empty(U, H, dtype=torch.int32, device=dev)
         cnt = torch.empty(U, dtype=torch.int32, device=dev)
@@ -282,17 +282,40 @@ def test_union_greedy_matches_oracle_on_large_buckets(pk, oracle, seed):
         nf = torch.empty(U, dtype=torch.int32, device=dev)
         raw = torch.empty(U, dtype=torch.int64, device=dev)
         status = torch.zeros(1, dtype=torch.int32, device=dev)
-        nv.call("pk_union", dindex.offsets, dindex.lens, dindex.ids, dindex.ids.stride(0), order, n_order, n_cand,
-                hist, limit, U, F, H, out, H, cnt, feats, nf, raw, status)
+        nv.call("pk_union", dindex.offsets, dindex.lens, dindex.ids, dindex.ids.stride(0), order, n_order,
+                n_cand, hist, limit, U, F, H, out, H, cnt, feats, nf, raw, status)
         torch.cuda.synchronize()
         assert int(status.item()) == 0
         for u in range(U):
-            oi = oracle.index_from_lists(H, np.zeros(128, np.float32), lists_all[u])
-            ids, fts, rw = oracle.select_from_order(orders[u], oi, lim)
+            oi = oracle.index_from_lists(hist_u[u], np.zeros(128, np.float32), lists_all[u])
+            ids, fts, rw = oracle.select_from_order(orders[u][:n_u[u]], oi, lim)
             c = int(cnt[u])
             assert np.array_equal(out[u, :c].cpu().numpy().astype(np.int64), ids), (lim, u)
             assert feats[u, :int(nf[u])].cpu().tolist() == fts, (lim, u)
             assert int(raw[u]) == rw, (lim, u)
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_union_matches_oracle_on_config3_like_buckets(pk, oracle, seed):
+    """Buckets of config-3-like sizes that overlap, against the oracle: the
+    unbudgeted path, prefixes that stop at the first skip, and tail walks
+    with accepted buckets after it.  Units differ in history (the bitmap's
+    last partial word at several widths) and one unit has no candidates."""
+    rs = np.random.RandomState(200 + seed)
+    U, H, F, n_cand = 5, 70001, 400, 160
+    _union_case(pk, oracle, rs, U, H, F, n_cand, [2, 30, 120, 400], [0.2, 0.4, 0.3, 0.1], 2000,
+                (0, 300, 2500, 4096, 9000, 10 ** 9),
+                hist_u=[70001, 65536, 1000, 70001, 33], n_u=[160, 160, 160, 0, 160])
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_union_greedy_matches_oracle_on_large_buckets(pk, oracle, seed):
+    """Budgeted union on synthetic CSR indexes whose buckets are large and
+    overlap heavily (multi-round hash path, single-bucket rounds, accepted
+    buckets after the first skip), against the oracle's greedy."""
+    rs = np.random.RandomState(100 + seed)
+    _union_case(pk, oracle, rs, 6, 60000, 300, 200, [3, 40, 300, 2000, 9000], [0.2, 0.4, 0.3, 0.08, 0.02], 3000,
+                (0, 500, 4096, 20000, 10 ** 9))
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])

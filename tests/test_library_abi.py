@@ -79,3 +79,16 @@ def test_missing_library_fails_loudly(lib, monkeypatch, tmp_path):
     monkeypatch.setattr(lib, "_lib", None)
     with pytest.raises(lib.NativeError):
         lib.lib()
+
+
+def test_other_head_dims_refused_before_any_launch():
+    """Every kernel is built for head_dim 128; the Python layer refuses any
+    other head dimension with a clear error before reaching the library."""
+    import torch
+    import prismkv_b200 as pk
+    keys = torch.zeros(8, 256)
+    sae = pk.SAEParams(torch.zeros(16, 256), torch.zeros(16), key_mean=2, query_topk=2)
+    with pytest.raises(ValueError, match="head_dim 256"):
+        pk.build_index(keys, sae, 1.0)
+    with pytest.raises(ValueError, match="head_dim 256"):
+        pk.attend(torch.zeros(4, 256), torch.zeros(8, 256), torch.zeros(8, 256), torch.zeros(0, dtype=torch.long), 8)
