@@ -142,27 +142,32 @@ GRAPH_INSPECT_ERRORS: list = []
 
 def graph_kernel_launches(graph):
     """Kernel nodes of this library (C++ namespace pk) in a captured CUDA
-    graph, or None when the graph cannot be inspected."""
+    graph, through the driver API, or None when the graph cannot be
+    inspected (the reason goes to GRAPH_INSPECT_ERRORS)."""
     try:
-        from cuda.bindings import runtime as rt
-        raw = graph.raw_cuda_graph()
-        handle = raw if isinstance(raw, rt.cudaGraph_t) else rt.cudaGraph_t(init_value=int(raw))
-        err, _, n = rt.cudaGraphGetNodes(handle, 0)
-        if err != rt.cudaError_t.cudaSuccess:
+        from cuda.bindings import driver as drv
+        ok = drv.CUresult.CUDA_SUCCESS
+        handle = drv.CUgraph(int(graph.raw_cuda_graph()))
+        err, _, n = drv.cuGraphGetNodes(handle, 0)
+        if err != ok:
+            GRAPH_INSPECT_ERRORS.append(f"cuGraphGetNodes: {err}")
             return None
-        err, nodes, n = rt.cudaGraphGetNodes(handle, n)
-        if err != rt.cudaError_t.cudaSuccess:
+        err, nodes, n = drv.cuGraphGetNodes(handle, n)
+        if err != ok:
+            GRAPH_INSPECT_ERRORS.append(f"cuGraphGetNodes: {err}")
             return None
         count = 0
         for node in nodes[:n]:
-            err, kind = rt.cudaGraphNodeGetType(node)
-            if err != rt.cudaError_t.cudaSuccess or kind != rt.cudaGraphNodeType.cudaGraphNodeTypeKernel:
+            err, kind = drv.cuGraphNodeGetType(node)
+            if err != ok or kind != drv.CUgraphNodeType.CU_GRAPH_NODE_TYPE_KERNEL:
                 continue
-            err, params = rt.cudaGraphKernelNodeGetParams(node)
-            if err != rt.cudaError_t.cudaSuccess:
+            err, params = drv.cuGraphKernelNodeGetParams(node)
+            if err != ok or params is None:
+                GRAPH_INSPECT_ERRORS.append(f"cuGraphKernelNodeGetParams: {err}")
                 return None
-            err, name = rt.cudaFuncGetName(params.func)
-            if err != rt.cudaError_t.cudaSuccess:
+            err, name = drv.cuFuncGetName(params.func)
+            if err != ok:
+                GRAPH_INSPECT_ERRORS.append(f"cuFuncGetName: {err}")
                 return None
             name = name.decode() if isinstance(name, bytes) else str(name)
             count += name.startswith("_ZN2pk")

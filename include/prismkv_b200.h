@@ -319,6 +319,15 @@ int pk_summarize(uint64_t keys, int dtype, int64_t unit_stride, int64_t row_stri
                  uint64_t offsets, uint64_t lens, uint64_t ids, int64_t ids_stride,
                  int U, int d, int F, uint64_t mean, uint64_t var, uint64_t stream);
 
+/* Folds one block's bucket moments into a running state in place:
+ * mean/var[U, F, d] fp32 of the state, whose bucket sizes are counts_a[U, F]
+ * (int32), absorb mean_b/var_b of a block with sizes counts_b, by the
+ * parallel formula of append_index (src/prismkv/core.py:194-199, the same
+ * operation order).  The reference has no separate entry point for it; the
+ * sequence-sharded index folds its shards' moments in token order with it. */
+int pk_merge_moments(uint64_t counts_a, uint64_t mean, uint64_t var, uint64_t counts_b, uint64_t mean_b,
+                     uint64_t var_b, int U, int F, int d, uint64_t stream);
+
 /* Appends a block of n_new keys per unit (rows at new_keys + u*unit_stride +
  * t*row_stride) to an index built with history `history`: BatchTopK over the
  * block only with the stored centers, bucket lists extended in place (token

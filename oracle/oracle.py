@@ -253,6 +253,19 @@ def append_index(index: FeatureIndex, new_keys, sae: SAE, key_scale: float) -> F
     return out
 
 
+def merge_moments(counts_a, mean_a, var_a, counts_b, mean_b, var_b):
+    """The moments half of append_index (core.py:194-199): blocks a and b of
+    bucket sizes counts_* and moments [F, d] merged; returns (mean, var)."""
+    counts_a, counts_b = _i64(counts_a), _i64(counts_b)
+    mean_a, var_a, mean_b, var_b = _f32(mean_a), _f32(var_a), _f32(mean_b), _f32(var_b)
+    F, d = mean_a.shape
+    mean = np.empty_like(mean_a)
+    var = np.empty_like(var_a)
+    lib().orc_merge_moments(_p(counts_a), _p(mean_a), _p(var_a), _p(counts_b), _p(mean_b), _p(var_b), F, d,
+                            _p(mean), _p(var))
+    return mean, var
+
+
 def bucket_scores(q, index: FeatureIndex, *, router="moments", sae: SAE | None = None,
                   query_scale=None, query_topk=16, terms=("count", "mean", "variance")):
     q = _f32(q)

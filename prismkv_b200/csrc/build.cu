@@ -449,7 +449,7 @@ __global__ void merge_moments_kernel(const int* __restrict__ lens_old, const int
                                      float* __restrict__ mean, float* __restrict__ var,
                                      const float* __restrict__ mean_new, const float* __restrict__ var_new,
                                      const int* __restrict__ flag) {
-    if (*flag) return;
+    if (flag && *flag) return;
     const int u = blockIdx.y;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)F * kBD) return;
@@ -1658,6 +1658,22 @@ extern "C" int pk_summarize(uint64_t keys, int dtype, int64_t unit_stride, int64
                                                      (float*)mean, (float*)var);
     else
         return PK_ERR_ARG;
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}
+
+// Folds one block's bucket moments into a running state with the
+// parallel formula of core.py:194-199 (the append_index merge), in place:
+// mean/var[U, F, d] of the state (counts_a[U, F]) absorb mean_b/var_b of a
+// block with counts_b.  The sequence-sharded index folds its shards' moments
+// in token order with it.
+extern "C" int pk_merge_moments(uint64_t counts_a, uint64_t mean, uint64_t var, uint64_t counts_b, uint64_t mean_b,
+                                uint64_t var_b, int U, int F, int d, uint64_t stream) {
+    if (U < 1 || F < 1 || !counts_a || !mean || !var || !counts_b || !mean_b || !var_b) return PK_ERR_ARG;
+    if (d != kBD) return PK_ERR_UNSUPPORTED;
+    merge_moments_kernel<<<dim3((unsigned)(((int64_t)F * kBD + 255) / 256), U), 256, 0, (cudaStream_t)stream>>>(
+        (const int*)counts_a, (const int*)counts_b, F, (float*)mean, (float*)var, (const float*)mean_b,
+        (const float*)var_b, nullptr);
     PK_CHECK_LAUNCH();
     return PK_OK;
 }

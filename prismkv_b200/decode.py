@@ -72,7 +72,7 @@ class SparseDecode:
                  query_scale: float = 1.0, query_topk: int | None = None, unique_cap: float | None = None,
                  budget: int | None = None, terms=("count", "mean", "variance"), splits: int | None = None,
                  max_history: int | None = None, workspace: nv.Workspace | None = None,
-                 exact_encode: bool = False):
+                 exact_encode: bool = False, route_counts: torch.Tensor | None = None):
         if router not in ("q_activation", "moments"):
             raise ValueError("router must be 'q_activation' or 'moments'")
         if unique_cap is not None and budget is not None:
@@ -113,6 +113,12 @@ class SparseDecode:
         # Bound-filtered routing (tensor-core approximation + exact recompute
         # of the candidates) unless the all-features exact encode is asked for.
         self.prep = (None, None) if exact_encode else self.sae.prepared()
+        # Bucket sizes the moments router reads (count term and liveness):
+        # the index's own unless given (a sequence shard routes with the
+        # whole sequence's sizes).
+        if route_counts is not None and (route_counts.dtype != torch.int32 or tuple(route_counts.shape) != (U, self.F)):
+            raise ValueError(f"route_counts must be int32 [{U}, {self.F}]")
+        self.route_counts = route_counts
 
     def sync_history(self) -> None:
         """Refresh per-unit history and limits after the index grew (append)."""
@@ -140,7 +146,8 @@ class SparseDecode:
                     | (nv.PK_TERM_MEAN if "mean" in self.terms else 0)
                     | (nv.PK_TERM_VARIANCE if "variance" in self.terms else 0))
             nbytes = nv.query("pk_route_moments_workspace_bytes", U, G, F)
-            nv.call("pk_route_moments", q, nv.dtype_code(q), idx.mean, idx.var, idx.lens, bits, U, G, d, F, k,
+            counts = self.route_counts if self.route_counts is not None else idx.lens
+            nv.call("pk_route_moments", q, nv.dtype_code(q), idx.mean, idx.var, counts, bits, U, G, d, F, k,
                     self.ws.get(("moments", U, G, F), nbytes), nbytes, self.score, self.order, self.n_order,
                     self.width)
         nv.call("pk_union", idx.offsets, idx.lens, idx.ids, idx.ids.stride(0), self.order, self.n_order, self.width,

@@ -107,6 +107,7 @@ class DeviceIndex:
         self.slack_frac = 0.0
         self.slack_min = 0
         self.encode_path = None   # "bounds" (tensor-core bounds) or "exact", set by build
+        self.global_counts = None  # a sequence shard's whole-sequence bucket sizes (attach_global_moments)
 
     # ------------------------------------------------------------------ build
     @classmethod

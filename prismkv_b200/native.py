@@ -54,6 +54,7 @@ SIGNATURES = {
     "pk_build_workspace_bytes": ("iliil", ctypes.c_size_t),
     "pk_build_index": ("PillPfPPPPiliiilfiPPPllPPPP", ctypes.c_int),
     "pk_summarize": ("PillPPPliiiPPP", ctypes.c_int),
+    "pk_merge_moments": ("PPPPPPiiiP", ctypes.c_int),
     "pk_append_workspace_bytes": ("iliiil", ctypes.c_size_t),
     "pk_append_index": ("PilllPfPPPPiiiilPPPlPPlPPPP", ctypes.c_int),
     "pk_build_shard_layout": ("ilillP", ctypes.c_int),

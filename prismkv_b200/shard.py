@@ -5,7 +5,9 @@ Rank r of P owns tokens [lo_r, hi_r) of the history (``token_ranges``); the
 dense tail of generated tokens lives on the last rank.  One decode step is:
 
 1. routing, replicated on every rank (the q_activation scores depend only on
-   the query and the SAE, core.py:131-139; bucket liveness is local);
+   the query and the SAE, core.py:131-139, bucket liveness being local; the
+   moments router, core.py:117-130, reads the whole sequence's bucket moments
+   and sizes, attach_global_moments, so every rank takes the same buckets);
 2. the union of the routed buckets' shard-local lists (core.py:152-164) with
    the per-shard budget ``budget // P`` -- in the unbudgeted mode the shards'
    unions are exactly the global union cut at the shard boundaries;
@@ -41,7 +43,8 @@ def shard_index(index: DeviceIndex, lo: int, hi: int) -> DeviceIndex:
     """The part of ``index`` that covers tokens [lo, hi), with token ids made
     relative to lo.  Each bucket's entries in the range form one contiguous,
     still ascending run of its list; counts are the shard-local list sizes.
-    Moments are not carried (the sharded path routes with q_activation)."""
+    Moments are not carried: attach_global_moments gives the shard the whole
+    sequence's."""
     if not 0 <= lo <= hi <= index.history:
         raise ValueError("shard range must lie within the index history")
     U, F, dev = index.U, index.F, index.device
@@ -97,25 +100,97 @@ def shard_budget(budget, P: int):
     return None if budget is None else int(budget) // P
 
 
+# ---------------------------------------------------------------------------
+# Bucket moments of the whole sequence on every rank (the moments router)
+# ---------------------------------------------------------------------------
+
+def shard_moments(index: DeviceIndex, keys: torch.Tensor):
+    """(bucket sizes int32 [U, F], mean, var fp32 [U, F, d]) of this shard:
+    the population moments of its own keys over its own part of every
+    bucket (core.py:76-89 on the shard)."""
+    from .index import _unit_view
+    keys, U, N, d, us, rs = _unit_view(keys)
+    if (U, d) != (index.U, index.d) or N < index.history:
+        raise ValueError("keys must be the shard's [U, N, d] rows of the index")
+    F = index.F
+    mean = torch.zeros(U, F, d, dtype=torch.float32, device=keys.device)
+    var = torch.zeros_like(mean)
+    nv.call("pk_summarize", keys, nv.dtype_code(keys), us, rs, index.offsets, index.lens, index.ids,
+            index.ids.stride(0), U, d, F, mean, var)
+    return index.lens.clone(), mean, var
+
+
+def fold_moments(parts):
+    """Moments of consecutive blocks folded in order with the reference's
+    append merge (core.py:194-199, pk_merge_moments): parts is a list of
+    (sizes int32 [U, F], mean, var [U, F, d]) in token order; returns the
+    folded (sizes, mean, var)."""
+    counts, mean, var = (t.clone() for t in parts[0])
+    U, F, d = mean.shape
+    for lens, m, v in parts[1:]:
+        nv.call("pk_merge_moments", counts, mean, var, lens.contiguous(), m.contiguous(), v.contiguous(), U, F, d)
+        counts += lens
+    return counts, mean, var
+
+
+def attach_global_moments(index: DeviceIndex, keys: torch.Tensor, *, group=None,
+                          gather_bytes: int = 256 << 20) -> DeviceIndex:
+    """Gives this rank's shard index the bucket moments and sizes of the
+    whole sequence, so that the moments router (core.py:117-130) routes the
+    same on every rank: each shard's moments (shard_moments) all-gathered
+    and folded in token order with the append merge.  The result is the
+    moments the reference's append_index would hold after indexing the
+    shards one after another with these memberships.  Features are gathered
+    in chunks of at most ``gather_bytes``.  index.mean / index.var /
+    index.global_counts are set; returns the index."""
+    P = dist.get_world_size(group) if dist.is_initialized() else 1
+    lens, mean, var = shard_moments(index, keys)
+    if P == 1:
+        index.mean, index.var, index.global_counts = mean, var, lens
+        return index
+    U, F, d = mean.shape
+    all_lens = _gather(lens, torch.empty((P, U, F), dtype=lens.dtype, device=lens.device), group)
+    fc = max(1, min(F, gather_bytes // (2 * P * U * d * 4)))
+    out_mean, out_var = torch.empty_like(mean), torch.empty_like(var)
+    for f0 in range(0, F, fc):
+        f1 = min(F, f0 + fc)
+        m_all = _gather(mean[:, f0:f1].contiguous(), torch.empty((P, U, f1 - f0, d), device=mean.device), group)
+        v_all = _gather(var[:, f0:f1].contiguous(), torch.empty((P, U, f1 - f0, d), device=var.device), group)
+        _, m, v = fold_moments([(all_lens[r, :, f0:f1].contiguous(), m_all[r], v_all[r]) for r in range(P)])
+        out_mean[:, f0:f1] = m
+        out_var[:, f0:f1] = v
+    index.mean, index.var = out_mean, out_var
+    index.global_counts = all_lens.sum(0, dtype=torch.int32)
+    return index
+
+
 class ShardedDecode:
     """Decode over this rank's sequence shard of every unit, merged across
     the group.  ``local_index`` covers this rank's token range (built on the
     shard, or cut from a full index by ``shard_index``); K/V passed to the
-    call hold the shard's rows, the last rank's followed by the dense tail."""
+    call hold the shard's rows, the last rank's followed by the dense tail.
+    router="moments" needs the whole sequence's moments on the index
+    (attach_global_moments): every rank then routes with the global bucket
+    moments and sizes and takes the same buckets."""
 
     def __init__(self, local_index: DeviceIndex, sae, *, group=None, heads_per_unit: int = 4,
-                 query_scale: float = 1.0, query_topk: int | None = None, budget: int | None = None,
-                 splits: int | None = None, max_history: int | None = None,
+                 router: str = "q_activation", query_scale: float = 1.0, query_topk: int | None = None,
+                 budget: int | None = None, splits: int | None = None, max_history: int | None = None,
                  workspace: nv.Workspace | None = None):
         self.group = group
         init = dist.is_initialized()
         self.P = dist.get_world_size(group) if init else 1
         self.rank = dist.get_rank(group) if init else 0
         self.budget = budget
-        self.op = SparseDecode(local_index, sae, heads_per_unit=heads_per_unit, router="q_activation",
+        route_counts = None
+        if router == "moments":
+            route_counts = getattr(local_index, "global_counts", None)
+            if local_index.mean is None or route_counts is None:
+                raise ValueError("the sharded moments router needs attach_global_moments on the shard index")
+        self.op = SparseDecode(local_index, sae, heads_per_unit=heads_per_unit, router=router,
                                query_scale=query_scale, query_topk=query_topk,
                                budget=shard_budget(budget, self.P), splits=splits, max_history=max_history,
-                               workspace=workspace)
+                               workspace=workspace, route_counts=route_counts)
         U, G, d = self.op.U, self.op.G, self.op.d
         dev = local_index.device
         self.part = torch.empty(U * G, d + 2, dtype=torch.float32, device=dev)

@@ -140,3 +140,139 @@ def test_two_rank_nccl_sharded_decode():
     assert all(p.exitcode == 0 for p in procs)
     res = dict(q.get(timeout=5) for _ in range(2))
     assert all(e < 2e-2 for e in res.values()), res
+
+
+@pytest.mark.parametrize("P", [2, 4])
+def test_emulated_shards_moments_router(pk, oracle, P):
+    """The moments router on sequence shards: each shard's moments folded in
+    token order with the append merge (core.py:194-199) equal the oracle's
+    fold bit for bit; with them and the whole sequence's bucket sizes every
+    shard routes the buckets the oracle routes from those moments
+    (core.py:117-130), the unbudgeted shard unions are the global union cut
+    at the shard boundaries, and the merged attention matches the oracle."""
+    from prismkv_b200 import native as nv
+    from prismkv_b200.shard import fold_moments, shard_index, shard_moments, token_ranges, ShardedDecode
+    c = make_case(17)
+    U, N, G, d, F, k = c["U"], c["N"], c["G"], c["d"], c["F"], c["k"]
+    dev = torch.device("cuda")
+    K = torch.from_numpy(c["keys"]).to(dev).bfloat16()
+    V = torch.from_numpy(c["vals"]).to(dev).bfloat16()
+    Q = torch.from_numpy(c["q"]).to(dev).bfloat16().contiguous()
+    sae = pk.SAEParams(torch.from_numpy(c["W"]).to(dev), torch.zeros(F, device=dev), key_mean=8, query_topk=k)
+    idx = pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=False)
+    ranges = token_ranges(N, P)
+    shards = [shard_index(idx, lo, hi) for lo, hi in ranges]
+    parts = [shard_moments(sh, K[:, lo:hi].contiguous()) for sh, (lo, hi) in zip(shards, ranges)]
+    counts, mean, var = fold_moments(parts)
+    torch.cuda.synchronize()
+    assert torch.equal(counts, idx.lens)
+    osae = oracle.SAE(c["W"], np.zeros(F, np.float32), key_mean=8, query_topk=k)
+    fulls = [oracle.build_index(c["keys"][u, :N], osae, 1.0, moments=False) for u in range(U)]
+    for u in range(U):
+        # The oracle's fold: per shard, summarize its keys over its part of
+        # every bucket, then merge in token order.
+        om = ov = oc = None
+        for lo, hi in ranges:
+            lists = [x[(x >= lo) & (x < hi)] - lo for x in fulls[u].lists]
+            part = oracle.summarize(c["keys"][u, lo:hi], lists)
+            if om is None:
+                om, ov, oc = part.mean, part.variance, part.counts
+            else:
+                om, ov = oracle.merge_moments(oc, om, ov, part.counts, part.mean, part.variance)
+                oc = oc + part.counts
+        assert np.array_equal(mean[u].cpu().numpy().view(np.uint32), om.view(np.uint32)), u
+        assert np.array_equal(var[u].cpu().numpy().view(np.uint32), ov.view(np.uint32)), u
+    # Level 1: the order the oracle takes from the device's own scores of
+    # the folded moments and the whole sequence's sizes.
+    orders = []
+    for u in range(U):
+        s_dev = torch.empty(1, F, device=dev)
+        o1 = torch.empty(1, k, dtype=torch.int32, device=dev)
+        n1 = torch.empty(1, dtype=torch.int32, device=dev)
+        ws = torch.empty(int(nv.query("pk_route_moments_workspace_bytes", 1, G, F)), dtype=torch.uint8, device=dev)
+        nv.call("pk_route_moments", Q[u:u + 1].contiguous(), nv.PK_BF16, mean[u:u + 1].contiguous(),
+                var[u:u + 1].contiguous(), counts[u:u + 1].contiguous(), 7, 1, G, d, F, k, ws, ws.numel(), s_dev,
+                o1, n1, k)
+        orders.append(oracle.order_live(s_dev[0].cpu().numpy(), counts[u].long().cpu().numpy(), k))
+    out_parts = torch.empty(P, U * G, d + 2, device=dev)
+    for r, (sh, (lo, hi)) in enumerate(zip(shards, ranges)):
+        sh.mean, sh.var, sh.global_counts = mean, var, counts
+        sd = ShardedDecode(sh, sae, heads_per_unit=G, router="moments", query_topk=k, budget=None)
+        sd.op.route(Q)
+        torch.cuda.synchronize()
+        sd.check()
+        for u in range(U):
+            n = int(sd.op.n_order[u])
+            assert np.array_equal(sd.op.order[u, :n].long().cpu().numpy(), orders[u]), (r, u)
+            local = oracle.index_from_lists(hi - lo, np.zeros(d, np.float32),
+                                            [x[(x >= lo) & (x < hi)] - lo for x in fulls[u].lists])
+            ids, _, _ = oracle.select_from_order(orders[u], local, hi - lo)
+            cnt = int(sd.op.count[u])
+            assert np.array_equal(sd.op.ids[u, :cnt].long().cpu().numpy(), ids), (r, u)
+        rows = slice(lo, hi + c["tail"]) if r == P - 1 else slice(lo, hi)
+        sd.op.attention(Q, K[:, rows].contiguous(), V[:, rows].contiguous(), partial=out_parts[r])
+    merged = torch.empty(U * G, d, device=dev)
+    nv.call("pk_lse_merge", out_parts, P, U * G, d, merged, nv.PK_F32)
+    merged = merged.view(U, G, d).cpu().numpy()
+    for u in range(U):
+        gids, _, _ = oracle.select_from_order(orders[u], fulls[u], N)
+        ref = oracle.attend(c["q"][u], c["keys"][u], c["vals"][u], gids, N)
+        assert rel_l2(merged[u], ref) < 2e-2, u
+
+
+def _rank_main_moments(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        import prismkv_b200 as pk
+        from prismkv_b200.shard import ShardedDecode, attach_global_moments, fold_moments, shard_index, \
+            shard_moments, token_ranges
+        c = make_case(23)
+        U, N, G, d, F, k = c["U"], c["N"], c["G"], c["d"], c["F"], c["k"]
+        K = torch.from_numpy(c["keys"]).to(dev).bfloat16()
+        V = torch.from_numpy(c["vals"]).to(dev).bfloat16()
+        Q = torch.from_numpy(c["q"]).to(dev).bfloat16().contiguous()
+        sae = pk.SAEParams(torch.from_numpy(c["W"]).to(dev), torch.zeros(F, device=dev), key_mean=8, query_topk=k)
+        idx = pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=False)
+        ranges = token_ranges(N, world)
+        lo, hi = ranges[rank]
+        sh = attach_global_moments(shard_index(idx, lo, hi), K[:, lo:hi].contiguous(), gather_bytes=1 << 20)
+        # Every rank's moments equal the in-process fold of all shards.
+        _, m_ref, v_ref = fold_moments([shard_moments(shard_index(idx, a, b), K[:, a:b].contiguous())
+                                        for a, b in ranges])
+        same = torch.equal(sh.mean, m_ref) and torch.equal(sh.var, v_ref) and torch.equal(sh.global_counts, idx.lens)
+        sd = ShardedDecode(sh, sae, heads_per_unit=G, router="moments", query_topk=k, budget=None)
+        rows = slice(lo, hi + c["tail"]) if sd.is_tail_rank else slice(lo, hi)
+        out = sd(Q, K[:, rows].contiguous(), V[:, rows].contiguous()).float()
+        full = pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=False)
+        full.mean, full.var = m_ref, v_ref
+        ref = pk.SparseDecode(full, sae, heads_per_unit=G, router="moments", query_topk=k,
+                              unique_cap=None)(Q, K, V).float()
+        torch.cuda.synchronize()
+        err = float((out - ref).norm() / ref.norm())
+        q.put((rank, (same, err)))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_nccl_sharded_moments_router():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main_moments, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs)
+    res = dict(q.get(timeout=5) for _ in range(2))
+    assert all(s and e < 2e-2 for s, e in res.values()), res
