@@ -308,6 +308,13 @@ def test_union_matches_oracle_on_config3_like_buckets(pk, oracle, seed):
                 hist_u=[70001, 65536, 1000, 70001, 33], n_u=[160, 160, 160, 0, 160])
 
 
+def test_union_matches_oracle_when_tokens_are_mostly_distinct(pk, oracle):
+    """About 18,000 list entries over a 200,000-token history with almost no
+    overlap between the candidates' lists."""
+    rs = np.random.RandomState(7)
+    _union_case(pk, oracle, rs, 3, 200000, 300, 120, [150], [1.0], 10, (0, 5000, 12000, 10 ** 9))
+
+
 @pytest.mark.parametrize("seed", [0, 1, 2])
 def test_union_greedy_matches_oracle_on_large_buckets(pk, oracle, seed):
     """Budgeted union on synthetic CSR indexes whose buckets are large and
