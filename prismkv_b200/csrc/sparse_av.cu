@@ -959,6 +959,11 @@ static int sparse_av_launch(uint64_t q, uint64_t k, uint64_t v, int dtype, int k
         // The cluster form of the G <= 8 kernel adds the push-merge receive buffer.
         const int csmem = base_smem + (which == 0 ? av_push_floats(G, splits) * (int)sizeof(float) : 0);
         if (splits >= 2 && cluster_fits(which, splits, csmem)) {
+            // The shared-memory limit is one attribute per kernel, shared by
+            // every split count: set it for this launch's size.
+            auto cfn = which == 0 ? sparse_av_bf16_kernel<true> : sparse_av_bf16_g16_kernel<true>;
+            if (cudaFuncSetAttribute(cfn, cudaFuncAttributeMaxDynamicSharedMemorySize, csmem) != cudaSuccess)
+                return (int)cudaGetLastError();
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = grid;
             cfg.blockDim = dim3(kAvThreads);

@@ -91,6 +91,19 @@ def test_splits_agree(pk, batch):
         assert rel_l2(o.cpu().numpy(), outs[0].cpu().numpy()) < 5e-3
 
 
+def test_split_counts_in_any_order(pk, batch):
+    """Cluster launches of different split counts share one shared-memory
+    limit per kernel; a larger split count after a smaller one (the limit
+    set lower in between) must still launch."""
+    B = batch
+    op = pk.SparseDecode(B["idx"], B["sae"], heads_per_unit=B["G"], unique_cap=512 / B["N"])
+    op.route(B["Q"])
+    ref = op.attention(B["Q"], B["K"], B["V"], splits=1).float().clone()
+    for s in (16, 3, 16, 8, 2, 12, 16):
+        out = op.attention(B["Q"], B["K"], B["V"], splits=s).float()
+        assert rel_l2(out.cpu().numpy(), ref.cpu().numpy()) < 5e-3, s
+
+
 def test_sequence_shard_partials_merge(pk, batch):
     """Emulates the sequence-sharded decode on one GPU: each shard attends
     over its own id range and the LSE merge of the partials equals the
