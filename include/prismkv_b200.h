@@ -99,6 +99,27 @@ int pk_route_qact(uint64_t q, int q_dtype, uint64_t units, int n_units,
                   uint64_t order, uint64_t n_order, int order_stride,
                   uint64_t score, uint64_t topk, uint64_t stream);
 
+/* Feature-sharded q_activation routing: the same order as pk_route_qact
+ * (core.py:131-139) with the encode split over P ranks by feature range.
+ * pk_route_qact_shard encodes features [f_lo, f_hi) of every head (the
+ * bound-filtered path: w_bf16 and w_norm required) and writes each head's
+ * exact positive top-k among them, in rank order, to picks[U*G, k] as int32
+ * (value bits, feature id) pairs; unused slots hold (0, INT32_MAX).
+ * pk_route_qact_merge takes picks[P, U*G, k] of P disjoint ranges covering
+ * all F features (after an all-gather), ranks each head's entries
+ * exactly (value desc, feature asc) and finishes the route as
+ * pk_route_qact: order[u, 0..n_order[u]), counts[U, F] marking live
+ * buckets, score[U, F] optional.  No counterpart in the reference, whose
+ * route runs on one device (src/prismkv/core.py:131-139). */
+size_t pk_route_qact_shard_workspace_bytes(int U, int G, int F_local, int k);
+int pk_route_qact_shard(uint64_t q, int q_dtype, uint64_t w_enc, uint64_t b_enc, uint64_t w_bf16, uint64_t w_norm,
+                        float query_scale, int U, int G, int d, int F, int k, int f_lo, int f_hi,
+                        uint64_t workspace, uint64_t workspace_bytes, uint64_t picks, uint64_t stream);
+size_t pk_route_qact_merge_workspace_bytes(int U, int G, int k);
+int pk_route_qact_merge(uint64_t picks, int P, uint64_t counts, int U, int G, int F, int k,
+                        uint64_t workspace, uint64_t workspace_bytes, uint64_t order, uint64_t n_order,
+                        int order_stride, uint64_t score, uint64_t stream);
+
 /* ------------------------------------------------------------------------
  * moments routing (a9).
  * Replaces pack + torch.bmm + fused_norm_top / HopperTop16
@@ -144,8 +165,12 @@ int pk_union(uint64_t offsets, uint64_t lens, uint64_t ids, int64_t ids_stride,
  *   row(p)  = base(u) + p * kv_row_stride       (elements)
  * which covers both [U, total, d] and slot-major [slot, cap, H_kv, d].
  * Rows attended: ids[u, 0..count[u]) then history[u]..length[u]-1.
+ * ids holds U rows of ids_stride int32 each; the kernel may read any
+ * element of a row (entries past count[u] are read ahead and ignored).
  * length[u] == 0 marks an inactive unit (output zeros).  q, k, v and out
- * share `dtype`.  splits <= 0 picks a split count for the machine.
+ * share `dtype`.  splits <= 0 picks a split count for the machine: about
+ * two CTAs per SM over all units, whole clusters of 8 above 8 splits, at
+ * most 64.
  * With partial != 0 the kernel writes per-(u, head) partials
  * (m, l, o[d]) fp32 to partial[U*G, d+2] instead of out (for pk_lse_merge).
  * ------------------------------------------------------------------------ */

@@ -674,6 +674,48 @@ struct FastSmem {
     int all_live[256];
 };
 
+// The unit's share of the routing once a head's m positive picks are in
+// sm.q (sel / selkey in rank order): kCluster -- the G head CTAs of the unit
+// form a cluster, each copies every head's picks from the others' shared
+// memory, computes all entries' scores (the arithmetic of the single-CTA
+// aggregation) and ranks and writes the order slots of its own head's
+// entries; otherwise the picks go through global memory and the unit's last
+// CTA to arrive builds the whole order (head_finish).  Every thread calls it.
+template <bool kCluster>
+__device__ void qact_unit_tail(int u, int g, int G, int F, int k, int m, FastSmem& sm, uint32_t* sA,
+                               const int* __restrict__ counts, int* __restrict__ head_ids,
+                               float* __restrict__ head_val, int* __restrict__ unit_done, int* __restrict__ order,
+                               int* __restrict__ n_order, int order_stride, float* __restrict__ score) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    if constexpr (kCluster) {
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        head_picks(G, k, m, sm.q, sm.hid, sm.hv);
+        __syncthreads();
+        for (int r = tid; r < k; r += nt) {
+            const int f = sm.hid[r];
+            sm.hlive[r] = f != INT32_MAX && counts[(int64_t)u * F + f] > 0;
+        }
+        cluster.sync();   // every head's picks are in its CTA's shared memory
+        const int E = G * k;
+        for (int e = tid; e < E; e += nt) {
+            const int h = e / k, r = e - h * k;
+            sm.all_id[e] = cluster.map_shared_rank(sm.hid, h)[r];
+            sm.all_v[e] = cluster.map_shared_rank(sm.hv, h)[r];
+            sm.all_live[e] = cluster.map_shared_rank(sm.hlive, h)[r];
+        }
+        cluster.sync();   // no CTA exits while another still reads its picks
+        float* sc = reinterpret_cast<float*>(sA);
+        int* cand = reinterpret_cast<int*>(sA) + E;
+        unit_scores(u, G, F, k, sm.all_id, sm.all_v, sm.all_live, counts, sc, cand, g * k, (g + 1) * k, score);
+        const int tot = unit_rank(u, E, sc, cand, g * k, (g + 1) * k, sm.q.tk.scan, order, order_stride);
+        if (g == 0 && tid == 0) n_order[u] = tot;
+    } else {
+        head_finish(u, g, G, F, k, m, sm.q, sA, counts, head_ids, head_val, unit_done, order, n_order, order_stride,
+                    score);
+    }
+}
+
 // Per (unit, head), the exact top-k of the activations from the bounds of
 // qact_approx_kernel (L_f <= exact_f <= U_f):
 //   lambda' = the k-th largest of the per-group maxima of L.  At least k
@@ -701,7 +743,7 @@ qact_select_fast_kernel(const QT* __restrict__ q, const float* __restrict__ uppe
                         const float* __restrict__ W, const float* __restrict__ bias, float query_scale, int F, int k,
                         const int* __restrict__ counts, int* __restrict__ head_ids, float* __restrict__ head_val,
                         int* __restrict__ unit_done, int* __restrict__ order, int* __restrict__ n_order,
-                        int order_stride, float* __restrict__ score) {
+                        int order_stride, float* __restrict__ score, int f_base, int* __restrict__ picks) {
     // sA[F]: exact values when every feature is recomputed; head_finish's
     // aggregation scratch.
     extern __shared__ __align__(16) uint32_t sA[];
@@ -867,38 +909,76 @@ qact_select_fast_kernel(const QT* __restrict__ q, const float* __restrict__ uppe
             sm.q.selkey, sm.q.tk);
     }
     __syncthreads();
-    if constexpr (kCluster) {
-        namespace cg = cooperative_groups;
-        cg::cluster_group cluster = cg::this_cluster();
-        head_picks(G, k, m, sm.q, sm.hid, sm.hv);
-        __syncthreads();
-        for (int r = tid; r < k; r += nt) {
-            const int f = sm.hid[r];
-            sm.hlive[r] = f != INT32_MAX && counts[(int64_t)u * F + f] > 0;
+    if constexpr (!kCluster) {
+        if (picks) {
+            // Feature-sharded routing: this shard's picks of the head, in rank
+            // order, as (value bits, feature id); unused slots (0, INT32_MAX).
+            int* hp = picks + ((int64_t)u * G + g) * k * 2;
+            for (int r = tid; r < k; r += nt) {
+                hp[2 * r] = r < m ? (int)sm.q.selkey[r] : 0;
+                hp[2 * r + 1] = r < m ? sm.q.sel[r] + f_base : INT32_MAX;
+            }
+            return;
         }
-        cluster.sync();   // every head's picks are in its CTA's shared memory
-        const int E = G * k;
-        for (int e = tid; e < E; e += nt) {
-            const int h = e / k, r = e - h * k;
-            sm.all_id[e] = cluster.map_shared_rank(sm.hid, h)[r];
-            sm.all_v[e] = cluster.map_shared_rank(sm.hv, h)[r];
-            sm.all_live[e] = cluster.map_shared_rank(sm.hlive, h)[r];
-        }
-        cluster.sync();   // no CTA exits while another still reads its picks
-        float* sc = reinterpret_cast<float*>(sA);
-        int* cand = reinterpret_cast<int*>(sA) + E;
-        unit_scores(u, G, F, k, sm.all_id, sm.all_v, sm.all_live, counts, sc, cand, g * k, (g + 1) * k, score);
-        const int tot = unit_rank(u, E, sc, cand, g * k, (g + 1) * k, sm.q.tk.scan, order, order_stride);
-        if (g == 0 && tid == 0) n_order[u] = tot;
-    } else {
-        head_finish(u, g, G, F, k, m, sm.q, sA, counts, head_ids, head_val, unit_done, order, n_order, order_stride,
-                    score);
     }
+    qact_unit_tail<kCluster>(u, g, G, F, k, m, sm, sA, counts, head_ids, head_val, unit_done, order, n_order,
+                             order_stride, score);
 }
 
 __global__ void zero_rows_kernel(float* __restrict__ score, const int* __restrict__ units, int F) {
     const int u = units ? units[blockIdx.x] : blockIdx.x;
     for (int i = threadIdx.x; i < F; i += blockDim.x) score[(int64_t)u * F + i] = 0.f;
+}
+
+// Feature-sharded routing, second half.  picks[P][U*G][k] holds, per shard
+// and head, the shard's positive top-k as (value bits, feature id) in rank
+// order (pk_route_qact_shard), the shards covering disjoint feature ranges.
+// Each shard's list holds every feature of its range that can reach the
+// head's top-k, so the exact rank (value desc, feature asc, core.py:134) of
+// the positive entries over all lists is the unsharded ranking; the first k
+// are the head's picks.  The unit's normalisation, aggregation and order
+// then follow as in the unsharded route (qact_unit_tail).  One CTA per
+// (unit, head); P * k <= kCandCap.
+template <bool kCluster>
+__global__ void __launch_bounds__(kSelThreads)
+qact_merge_kernel(const int* __restrict__ picks, int P, int G, int F, int k, const int* __restrict__ counts,
+                  int* __restrict__ head_ids, float* __restrict__ head_val, int* __restrict__ unit_done,
+                  int* __restrict__ order, int* __restrict__ n_order, int order_stride, float* __restrict__ score) {
+    extern __shared__ __align__(16) uint32_t sA[];   // the tail's aggregation scratch
+    __shared__ FastSmem sm;
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
+    const int u = blockIdx.x / G, g = blockIdx.x % G;
+    const int64_t n_heads = gridDim.x;
+    const int n = P * k;
+    int npos = 0;
+    for (int c = tid; c < n; c += nt) {
+        const int r = c / k, j = c - r * k;
+        const int* e = picks + (((int64_t)r * n_heads + blockIdx.x) * k + j) * 2;
+        const float v = __uint_as_float((uint32_t)__ldg(e));
+        sm.cval[c] = v;
+        sm.cand[c] = __ldg(e + 1);
+        npos += v > 0.f;
+    }
+    npos = warp_sum(npos);
+    if (lane == 0) sm.wc[warp] = npos;
+    __syncthreads();
+    int all_pos = 0;
+    for (int w = 0; w < nw; ++w) all_pos += sm.wc[w];
+    const int m = min(k, all_pos);
+    for (int c = tid; c < n; c += nt) {
+        const float vc = sm.cval[c];
+        if (!(vc > 0.f)) continue;
+        const int fc = sm.cand[c];
+        int r = 0;
+        for (int j = 0; j < n; ++j) {
+            const float vj = sm.cval[j];
+            r += (vj > vc) || (vj == vc && sm.cand[j] < fc);
+        }
+        if (r < m) { sm.q.sel[r] = fc; sm.q.selkey[r] = __float_as_uint(vc); }
+    }
+    __syncthreads();
+    qact_unit_tail<kCluster>(u, g, G, F, k, m, sm, sA, counts, head_ids, head_val, unit_done, order, n_order,
+                             order_stride, score);
 }
 
 // ---------------------------------------------------------------------------
@@ -1125,7 +1205,7 @@ extern "C" int pk_route_qact(uint64_t q, int q_dtype, uint64_t units, int n_unit
             const cudaError_t e_ = cudaLaunchKernelEx(                                                           \
                 &cfg, fn, (const QT*)q, (const float*)act, (const uint32_t*)gmax, ngroups, ul, G,                \
                 (const float*)w_enc, (const float*)b_enc, query_scale, F, k, (const int*)counts, hid, hval,      \
-                done, (int*)order, (int*)n_order, order_stride, (float*)score);                                  \
+                done, (int*)order, (int*)n_order, order_stride, (float*)score, 0, (int*)nullptr);                \
             if (e_ != cudaSuccess) return (int)e_;                                                               \
         } else {                                                                                                 \
             auto fn = qact_select_fast_kernel<ORD, QT, MINB, false>;                                             \
@@ -1133,7 +1213,7 @@ extern "C" int pk_route_qact(uint64_t q, int q_dtype, uint64_t units, int n_unit
             fn<<<n_units * G, kSelThreads, fsmem, st>>>(                                                         \
                 (const QT*)q, act, gmax, ngroups, ul, G, (const float*)w_enc, (const float*)b_enc, query_scale,  \
                 F, k, (const int*)counts, hid, hval, done, (int*)order, (int*)n_order, order_stride,             \
-                (float*)score);                                                                                  \
+                (float*)score, 0, (int*)nullptr);                                                                \
         }                                                                                                        \
     } while (0)
 #define PK_LAUNCH_FAST(ORD, QT)                                                                                  \
@@ -1179,6 +1259,139 @@ extern "C" int pk_route_qact(uint64_t q, int q_dtype, uint64_t units, int n_unit
     qact_select_kernel<<<n_units * G, 256, ssmem, st>>>(act, ul, G, F, k, (const int*)counts, hid, hval, done,
                                                         (int*)order, (int*)n_order, order_stride, (float*)score,
                                                         (int*)topk);
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Feature-sharded q_activation routing: each of P ranks encodes the features
+// [f_lo, f_hi) of every head and exports its picks; after an all-gather of
+// the picks every rank merges them into the same order.
+// ---------------------------------------------------------------------------
+
+extern "C" size_t pk_route_qact_shard_workspace_bytes(int U, int G, int F_local, int k) {
+    if (U < 1 || G < 1 || F_local < 1 || k < 1) return 0;
+    const size_t act = (size_t)U * G * F_local * sizeof(float);
+    const size_t groups = (size_t)U * G * route_groups(F_local, k) * sizeof(uint32_t);
+    return (act + 255) / 256 * 256 + (groups + 255) / 256 * 256;
+}
+
+extern "C" int pk_route_qact_shard(uint64_t q, int q_dtype, uint64_t w_enc, uint64_t b_enc, uint64_t w_bf16,
+                                   uint64_t w_norm, float query_scale, int U, int G, int d, int F, int k, int f_lo,
+                                   int f_hi, uint64_t workspace, uint64_t workspace_bytes, uint64_t picks,
+                                   uint64_t stream) {
+    if (U < 1 || G < 1 || F < 1 || k < 1 || k > 256 || !(query_scale > 0.f)) return PK_ERR_ARG;
+    if (f_lo < 0 || f_hi <= f_lo || f_hi > F) return PK_ERR_ARG;
+    if (d != kEncD) return PK_ERR_UNSUPPORTED;
+    const int Fl = f_hi - f_lo;
+    if ((size_t)Fl * sizeof(uint32_t) > 200 * 1024) return PK_ERR_UNSUPPORTED;
+    if (workspace_bytes < pk_route_qact_shard_workspace_bytes(U, G, Fl, k)) return PK_ERR_WORKSPACE;
+    if (!q || !w_enc || !b_enc || !w_bf16 || !w_norm || !workspace || !picks) return PK_ERR_ARG;
+    if (q_dtype != PK_BF16 && q_dtype != PK_F32) return PK_ERR_ARG;
+    if (q % 16 || w_bf16 % 16) return PK_ERR_ARG;   // 16-byte row loads
+    cudaStream_t st = (cudaStream_t)stream;
+    char* ws = (char*)workspace;
+    float* act = (float*)ws;
+    uint32_t* gmax = (uint32_t*)(ws + ((size_t)U * G * Fl * sizeof(float) + 255) / 256 * 256);
+    const int kl = k < Fl ? k : Fl;
+    const int gs = select_group_size(Fl, kl);
+    const int ngroups = (int)route_groups(Fl, k);
+    // This shard's rows of the SAE (rows are 256 and 512 bytes: the offsets
+    // keep the 16-byte alignment of the row loads).
+    const __nv_bfloat16* wb = (const __nv_bfloat16*)w_bf16 + (int64_t)f_lo * kEncD;
+    const float* wf = (const float*)w_enc + (int64_t)f_lo * kEncD;
+    const float* bl = (const float*)b_enc + f_lo;
+    const float* wn = (const float*)w_norm + f_lo;
+    dim3 ag((Fl + kApxFeat - 1) / kApxFeat, (U * G + kApxHeads - 1) / kApxHeads);
+    const int asmem = (kApxHeads + kApxFeat) * 256;
+    if (q_dtype == PK_BF16) {
+        cudaFuncSetAttribute(qact_approx_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, asmem);
+        qact_approx_kernel<__nv_bfloat16><<<ag, kApxThreads, asmem, st>>>(
+            (const __nv_bfloat16*)q, nullptr, U, G, wb, bl, wn, query_scale, Fl, gs, ngroups, act, gmax);
+    } else {
+        cudaFuncSetAttribute(qact_approx_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, asmem);
+        qact_approx_kernel<float><<<ag, kApxThreads, asmem, st>>>(
+            (const float*)q, nullptr, U, G, wb, bl, wn, query_scale, Fl, gs, ngroups, act, gmax);
+    }
+    PK_CHECK_LAUNCH();
+    const size_t fsmem = (size_t)4 * Fl;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const bool wide = U * G > sms;
+    const bool inter = G >= 2 && G <= 5;   // the order F.linear takes for a [G, d] block
+#define PK_LAUNCH_SHARD(ORD, QT, MINB)                                                                           \
+    do {                                                                                                         \
+        auto fn = qact_select_fast_kernel<ORD, QT, MINB, false>;                                                 \
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem);                       \
+        fn<<<U * G, kSelThreads, fsmem, st>>>((const QT*)q, act, gmax, ngroups, nullptr, G, wf, bl, query_scale, \
+                                               Fl, k, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0,   \
+                                               nullptr, f_lo, (int*)picks);                                     \
+    } while (0)
+#define PK_LAUNCH_SHARD2(ORD, QT)                                                                                \
+    do {                                                                                                         \
+        if (wide) PK_LAUNCH_SHARD(ORD, QT, 2); else PK_LAUNCH_SHARD(ORD, QT, 1);                                 \
+    } while (0)
+    if (q_dtype == PK_BF16) {
+        if (inter) PK_LAUNCH_SHARD2(kInterleaved16, __nv_bfloat16); else PK_LAUNCH_SHARD2(kSequential, __nv_bfloat16);
+    } else {
+        if (inter) PK_LAUNCH_SHARD2(kInterleaved16, float); else PK_LAUNCH_SHARD2(kSequential, float);
+    }
+#undef PK_LAUNCH_SHARD2
+#undef PK_LAUNCH_SHARD
+    PK_CHECK_LAUNCH();
+    return PK_OK;
+}
+
+extern "C" size_t pk_route_qact_merge_workspace_bytes(int U, int G, int k) {
+    if (U < 1 || G < 1 || k < 1) return 0;
+    const size_t heads = (size_t)U * G * k * (sizeof(int) + sizeof(float));
+    const size_t done = (size_t)U * sizeof(int);
+    return (heads + 255) / 256 * 256 + (done + 255) / 256 * 256;
+}
+
+extern "C" int pk_route_qact_merge(uint64_t picks, int P, uint64_t counts, int U, int G, int F, int k,
+                                   uint64_t workspace, uint64_t workspace_bytes, uint64_t order, uint64_t n_order,
+                                   int order_stride, uint64_t score, uint64_t stream) {
+    if (P < 1 || U < 1 || G < 1 || F < 1 || k < 1) return PK_ERR_ARG;
+    if (G * k > 256 || order_stride < G * k || P * k > kCandCap) return PK_ERR_ARG;
+    if (workspace_bytes < pk_route_qact_merge_workspace_bytes(U, G, k)) return PK_ERR_WORKSPACE;
+    if (!picks || !counts || !workspace || !order || !n_order) return PK_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    char* ws = (char*)workspace;
+    int* hid = (int*)ws;
+    float* hval = (float*)(hid + (size_t)U * G * k);
+    int* done = (int*)(ws + ((size_t)U * G * k * (sizeof(int) + sizeof(float)) + 255) / 256 * 256);
+    if (score) {
+        zero_rows_kernel<<<U, 256, 0, st>>>((float*)score, nullptr, F);
+        PK_CHECK_LAUNCH();
+    }
+    const size_t msmem = (size_t)16 * G * k;   // the tail's aggregation scratch
+    if (G <= 8) {
+        // The G head CTAs of a unit as one cluster (portable sizes).
+        auto fn = qact_merge_kernel<true>;
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(U * G);
+        cfg.blockDim = dim3(kSelThreads);
+        cfg.dynamicSmemBytes = msmem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = G;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, (const int*)picks, P, G, F, k, (const int*)counts, hid,
+                                                 hval, done, (int*)order, (int*)n_order, order_stride, (float*)score);
+        if (e != cudaSuccess) return (int)e;
+    } else {
+        auto fn = qact_merge_kernel<false>;
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem);
+        fn<<<U * G, kSelThreads, msmem, st>>>((const int*)picks, P, G, F, k, (const int*)counts, hid, hval, done,
+                                               (int*)order, (int*)n_order, order_stride, (float*)score);
+    }
     PK_CHECK_LAUNCH();
     return PK_OK;
 }

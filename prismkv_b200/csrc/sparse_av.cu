@@ -6,17 +6,23 @@
 // bf16 path: a CTA of four warps streams its split's rows in tiles of 64 K
 // rows and 64 V rows, three stages deep.  Each warp gathers its own 16 rows of
 // every tile with 16-byte cp.async (rows addressed through the id list).  For
-// G <= 8 heads the warp also computes on those rows alone, so the warps
-// pipeline independently (no CTA barrier per tile): its 16 key rows fill the
-// M = 16 of mma.sync m16n8k16 and the heads its N = 8 (S^T = K Q^T, then
-// O^T += V^T P^T with P^T formed by movmatrix).  For 9..16 heads the heads
-// fill M, with a CTA barrier per tile.  Softmax is online in fp32 and P
-// enters the PV product in bf16.  The S split CTAs of a unit form a
-// thread-block cluster and merge their states through distributed shared
-// memory; above 8 splits the last CTA of a unit to finish merges partials
-// from global memory.  The _append entry point fuses the decode KV append:
-// the unit's new rows are attended in place of its newest tail row and
-// written into the cache by its first split CTA.
+// G <= 8 heads the tiles of a unit's row list are dealt to its S split CTAs
+// round robin (split s takes tiles s, s + S, ...), so a split's first tiles
+// are known before the unit's row count: their ids are read in parallel with
+// the count, and each later tile's ids one tile ahead, into registers.  The
+// warp also computes on its rows alone, so the warps pipeline independently
+// (no CTA barrier per tile): its 16 key rows fill the M = 16 of mma.sync
+// m16n8k16 and the heads its N = 8 (S^T = K Q^T, then O^T += V^T P^T with
+// P^T formed by movmatrix).  For 9..16 heads the heads fill M, with a CTA
+// barrier per tile.  Softmax is online in fp32 and P enters the PV product in
+// bf16.  The split CTAs of a unit merge in thread-block clusters of up to 8
+// through distributed shared memory; with more splits than one cluster holds,
+// each cluster's merged state goes to global memory and, per output slice,
+// the last cluster to finish merges the clusters' states.  Without a cluster
+// the last CTA of a unit merges the split partials from global memory.  The
+// _append entry point fuses the decode KV append: the unit's new rows are
+// attended in place of its newest tail row and written into the cache by its
+// first split CTA.
 #include <cooperative_groups.h>
 
 #include <mutex>
@@ -34,6 +40,8 @@ constexpr int kAvStageBytes = kAvTile * kAvRowBytes * 2;   // K + V
 constexpr int kAvMaxG = 16;
 constexpr int kAvIdsCap = 2048;   // row ids staged per CTA (longer splits read the rest directly)
 constexpr int kAvMaxCluster = 16; // splits merged through distributed shared memory
+constexpr int kAvGroupMax = 8;    // CTAs per cluster when clusters are merged through global memory
+constexpr int kAvCounters = 8;    // arrival counters per unit (one per cluster rank)
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct AvParams {
@@ -48,8 +56,9 @@ struct AvParams {
     const int* history;
     const int* length;
     int G, S;
-    float* part;    // [U*G, S, D+2] split partials (log2 domain)
-    int* done;      // [U] arrival counters
+    int C;          // CTAs per cluster (G <= 8 kernel; S is a multiple of C)
+    float* part;    // [U*G, S, D+2] split partials (log2 domain); cluster states [U, S/C, 3, G*D]
+    int* done;      // [U, kAvCounters] arrival counters
     void* out;      // [U, G, D] (dtype of q)
     float* xpart;   // [U*G, D+2] exported partial (natural-log m), or null
     // Fused decode append, or null: unit u's new K/V rows k_new/v_new[u, D]
@@ -176,7 +185,7 @@ __device__ void av_finish(const AvParams& p, int u, int s, float* red, int nwarp
     if (S == 1) return;
     __threadfence();
     __syncthreads();
-    if (tid == 0) is_last = atomicAdd(&p.done[u], 1) == S - 1;
+    if (tid == 0) is_last = atomicAdd(&p.done[u * kAvCounters], 1) == S - 1;
     __syncthreads();
     if (!is_last) return;
     __threadfence();
@@ -244,7 +253,7 @@ __device__ void av_finish(const AvParams& p, int u, int s, float* red, int nwarp
         }
     }
     emit(hcur, O);
-    if (tid == 0) p.done[u] = 0;
+    if (tid == 0) p.done[u * kAvCounters] = 0;
 }
 
 // Cluster merge: the CTA combines its warps' states into shared memory
@@ -315,25 +324,44 @@ __device__ void av_finish_cluster(const AvParams& p, int u, int s, const float* 
 }
 
 
-// Push merge (used with the cluster launch of sparse_av_bf16_kernel): output
-// element e = h*D + d of the unit belongs to CTA e / per of the cluster.
-// Each CTA combines its warps' states, stores its (o) of every element and
-// its (m, l) of every head into the owning CTA's receive buffer (pbuf:
-// o_in[S][per], then ml_in[S][G][2]), and after one cluster barrier merges
-// the S states of its own elements from its own shared memory, in split
-// order: the arithmetic of av_finish_cluster, with one barrier fewer and
-// remote stores instead of remote loads.  The caller arrived on the cluster
-// barrier at kernel start; the wait here, before the first remote store,
-// makes sure every CTA of the cluster is running.
+// Output of one merged (u, h, d) state: the result, or the exported partial
+// (natural-log m) for the sequence-sharded merge.
+template <typename OT>
+__device__ __forceinline__ void av_emit(const AvParams& p, int64_t uh, int d, float M, float L, float O) {
+    if (p.xpart) {
+        float* xp = p.xpart + uh * (kAvD + 2);
+        if (d == 0) { xp[0] = M == -INFINITY ? -INFINITY : M / kLog2e; xp[1] = L; }
+        xp[2 + d] = O;
+    } else {
+        OT* o = (OT*)p.out + uh * kAvD;
+        o[d] = to_out<OT>(L > 0.f ? O / L : 0.f);
+    }
+}
+
+// Push merge (used with the cluster launch of sparse_av_bf16_kernel): the
+// C = p.C split CTAs of a cluster share out the unit's G*D output elements,
+// element e belonging to cluster rank e / per.  Each CTA combines its warps'
+// states, stores its (o) of every element and its (m, l) of every head into
+// the owning CTA's receive buffer (pbuf: o_in[C][per], then ml_in[C][G][2]),
+// and after one cluster barrier merges the C states of its own elements from
+// its own shared memory, in rank order (remote stores instead of remote
+// loads, one barrier).  The caller arrived on the cluster barrier at kernel
+// start; the wait here, before the first remote store, makes sure every CTA
+// of the cluster is running.  With one cluster per unit the merged states
+// are the result.  With NC = S / C clusters, each owner stores its elements'
+// cluster state (m, l, o) in global memory and counts itself in on its rank's
+// arrival counter; the last of the NC owners of a slice merges the NC cluster
+// states in cluster order and resets the counter.
 template <typename OT>
 __device__ void av_finish_push(const AvParams& p, int u, int s, const float* red, int nwarps, float* ml_loc,
                                float* pbuf) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
-    const int G = p.G, S = p.S, tid = threadIdx.x;
-    const int GD = G * kAvD, per = (GD + S - 1) / S;
+    const int G = p.G, C = p.C, tid = threadIdx.x;
+    const int j = (int)cluster.block_rank(), c = s / C, NC = p.S / C;
+    const int GD = G * kAvD, per = (GD + C - 1) / C;
     float* o_in = pbuf;
-    float* ml_in = pbuf + S * per;
+    float* ml_in = pbuf + C * per;
     const float* rm = red;
     const float* rl = red + nwarps * kAvMaxG;
     const float* ro = red + 2 * nwarps * kAvMaxG;
@@ -352,92 +380,121 @@ __device__ void av_finish_push(const AvParams& p, int u, int s, const float* red
         if (dim == 0) { ml_loc[2 * h] = M; ml_loc[2 * h + 1] = L; }
         const int e = h * kAvD + dim, owner = e / per;
         float* dst = cluster.map_shared_rank(o_in, owner);
-        dst[s * per + (e - owner * per)] = O;
+        dst[j * per + (e - owner * per)] = O;
     }
     __syncthreads();
-    for (int i = tid; i < 2 * G * S; i += kAvThreads) {
-        const int r = i / (2 * G), j = i % (2 * G);
+    for (int i = tid; i < 2 * G * C; i += kAvThreads) {
+        const int r = i / (2 * G), jj = i % (2 * G);
         float* dst = cluster.map_shared_rank(ml_in, r);
-        dst[s * 2 * G + j] = ml_loc[j];
+        dst[j * 2 * G + jj] = ml_loc[jj];
     }
     cluster.sync();
-    for (int jj = tid; jj < per && s * per + jj < GD; jj += kAvThreads) {
-        const int e = s * per + jj, h = e / kAvD, d = e % kAvD;
+    float* cst = p.part + (int64_t)(u * NC + c) * 3 * GD;   // this cluster's states [3][GD]
+    for (int jj = tid; jj < per && j * per + jj < GD; jj += kAvThreads) {
+        const int e = j * per + jj, h = e / kAvD, d = e % kAvD;
         float M = -INFINITY;
-        for (int j = 0; j < S; ++j) M = fmaxf(M, ml_in[(j * G + h) * 2]);
+        for (int r = 0; r < C; ++r) M = fmaxf(M, ml_in[(r * G + h) * 2]);
         float L = 0.f, O = 0.f;
-        for (int j = 0; j < S; ++j) {
-            const float mj = ml_in[(j * G + h) * 2];
-            const float sc = (mj == -INFINITY) ? 0.f : exp2f(mj - M);
-            L = fmaf(sc, ml_in[(j * G + h) * 2 + 1], L);
-            O = fmaf(sc, o_in[j * per + jj], O);
+        for (int r = 0; r < C; ++r) {
+            const float mr = ml_in[(r * G + h) * 2];
+            const float sc = (mr == -INFINITY) ? 0.f : exp2f(mr - M);
+            L = fmaf(sc, ml_in[(r * G + h) * 2 + 1], L);
+            O = fmaf(sc, o_in[r * per + jj], O);
         }
-        const int64_t uh = (int64_t)u * G + h;
-        if (p.xpart) {
-            float* xp = p.xpart + uh * (kAvD + 2);
-            if (d == 0) { xp[0] = M == -INFINITY ? -INFINITY : M / kLog2e; xp[1] = L; }
-            xp[2 + d] = O;
+        if (NC == 1) {
+            av_emit<OT>(p, (int64_t)u * G + h, d, M, L, O);
         } else {
-            OT* o = (OT*)p.out + uh * kAvD;
-            o[d] = to_out<OT>(L > 0.f ? O / L : 0.f);
+            cst[e] = M;
+            cst[GD + e] = L;
+            cst[2 * GD + e] = O;
         }
     }
+    if (NC == 1) return;
+    __shared__ int is_last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) is_last = atomicAdd(&p.done[u * kAvCounters + j], 1) == NC - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const float* ust = p.part + (int64_t)u * NC * 3 * GD;
+    for (int jj = tid; jj < per && j * per + jj < GD; jj += kAvThreads) {
+        const int e = j * per + jj, h = e / kAvD, d = e % kAvD;
+        float M = -INFINITY;
+        for (int r = 0; r < NC; ++r) M = fmaxf(M, __ldcg(ust + (int64_t)r * 3 * GD + e));
+        float L = 0.f, O = 0.f;
+        for (int r = 0; r < NC; ++r) {
+            const float* sr = ust + (int64_t)r * 3 * GD;
+            const float mr = __ldcg(sr + e);
+            const float sc = (mr == -INFINITY) ? 0.f : exp2f(mr - M);
+            L = fmaf(sc, __ldcg(sr + GD + e), L);
+            O = fmaf(sc, __ldcg(sr + 2 * GD + e), O);
+        }
+        av_emit<OT>(p, (int64_t)u * G + h, d, M, L, O);
+    }
+    if (tid == 0) p.done[u * kAvCounters + j] = 0;
 }
 
 // Receive buffer of av_finish_push, in floats.
 __host__ __device__ constexpr int av_push_floats(int G, int S) { return S * ((G * kAvD + S - 1) / S) + 2 * G * S; }
 
 // G <= 8 heads.  Warp w owns rows [16w, 16w + 16) of every tile: it copies
-// them in and computes on them, so each warp's stages are its own.
+// them in and computes on them, so each warp's stages are its own.  Split s
+// takes the unit's tiles s, s + S, s + 2S, ...
 template <bool kCluster>
 __global__ void __launch_bounds__(kAvThreads, 2)
 sparse_av_bf16_kernel(AvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int s = blockIdx.x, u = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int G = p.G;
+    const int G = p.G, S = p.S;
     if constexpr (kCluster) asm volatile("barrier.cluster.arrive.relaxed;\n" ::: "memory");
+    const int* idp = p.ids + (int64_t)u * p.ids_stride;
+    // Each warp stages the ids of its own rows (16w..16w+15 of each tile) of
+    // the split's first tiles in shared memory before the row count is known
+    // (within the id row's stride; entries past the count are not used), so
+    // the count and the ids arrive in one round trip.  Tiles past the staged
+    // ones (more than kAvIdsCap / 64 per split) read their ids directly.
+    int* sids = reinterpret_cast<int*>(smem + kAvStages * kAvStageBytes);
+    constexpr int kStagedTiles = kAvIdsCap / kAvTile;
+    auto list_pos = [&](int j, int row) -> int64_t { return (int64_t)(s + (int64_t)j * S) * kAvTile + row; };
+    {
+        const int64_t tiles_in_stride = (p.ids_stride + kAvTile - 1) / kAvTile;
+        const int64_t jcan = s < tiles_in_stride ? (tiles_in_stride - 1 - s) / S + 1 : 0;
+        const int jst = (int)(jcan < kStagedTiles ? jcan : kStagedTiles);
+        for (int i = lane; i < jst * 16; i += 32) {
+            const int j = i >> 4, row = warp * 16 + (i & 15);
+            const int64_t r = list_pos(j, row);
+            if (r < p.ids_stride) cp_async4(smem_u32(sids + j * kAvTile + row), idp + r);
+        }
+        cp_async_commit();
+    }
     const int H = p.history[u], len = p.length[u], cnt = p.count[u];
     const int rows = len > 0 ? cnt + max(len - H, 0) : 0;
-    // Whole tiles split evenly: the splits differ by at most one tile.
     const int nt_all = (rows + kAvTile - 1) / kAvTile;
-    const int r0 = min(rows, (int)((int64_t)s * nt_all / p.S) * kAvTile);
-    const int r1 = min(rows, (int)((int64_t)(s + 1) * nt_all / p.S) * kAvTile);
-    const int ntiles = (r1 - r0 + kAvTile - 1) / kAvTile;
+    const int ntiles = s < nt_all ? (nt_all - 1 - s) / S + 1 : 0;
+    // Cache position of row `row` of the split's tile j (-1: past the
+    // rows): a listed id below the count, then the tail history..length-1.
+    auto pos_of = [&](int j, int row) -> int {
+        const int64_t r = list_pos(j, row);
+        if (r >= rows) return -1;
+        if (r >= cnt) return H + (int)(r - cnt);
+        return j < kStagedTiles ? sids[j * kAvTile + row] : __ldg(idp + r);
+    };
     const int64_t ubase = (int64_t)(u / p.kv_heads) * p.kv_batch_stride + (int64_t)(u % p.kv_heads) * p.kv_head_stride;
     const __nv_bfloat16* kb = (const __nv_bfloat16*)p.k + ubase;
     const __nv_bfloat16* vb = (const __nv_bfloat16*)p.v + ubase;
-    const int* idp = p.ids + (int64_t)u * p.ids_stride;
     const __nv_bfloat16* qp = (const __nv_bfloat16*)p.q + (int64_t)u * G * kAvD;
     const int fresh = fresh_row(p, H, len);
     const __nv_bfloat16* knew = fresh >= 0 ? (const __nv_bfloat16*)p.k_new + (int64_t)u * kAvD : kb;
     const __nv_bfloat16* vnew = fresh >= 0 ? (const __nv_bfloat16*)p.v_new + (int64_t)u * kAvD : vb;
     append_fresh_row<__nv_bfloat16>(p, u, ubase, fresh);
     const int g = lane >> 2, q4 = lane & 3;
-
-    // Q^T as the MMA B operand: n = head g, k = dims.
-    uint32_t qb[8][2];
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
-#pragma unroll
-        for (int r = 0; r < 2; ++r)
-            qb[kk][r] = g < G ? *reinterpret_cast<const uint32_t*>(qp + g * kAvD + kk * 16 + r * 8 + 2 * q4) : 0u;
-
-    // The split's row ids, staged once in shared memory (all copies in flight
-    // together) so that issuing a tile's copies never waits on a global load.
-    int* sids = reinterpret_cast<int*>(smem + kAvStages * kAvStageBytes);
-    const int n_staged = min(max(0, min(r1, cnt) - r0), kAvIdsCap);
-    for (int i = tid; i < n_staged; i += kAvThreads) cp_async4(smem_u32(sids + i), idp + r0 + i);
-    cp_async_commit();
     cp_async_wait<0>();
-    __syncthreads();
-    auto pos_of = [&](int r) -> int {
-        if (r >= r1) return -1;
-        if (r >= cnt) return H + (r - cnt);
-        return r - r0 < kAvIdsCap ? sids[r - r0] : idp[r];
-    };
+    __syncwarp();   // the warp's staged ids are visible to all its lanes
+
     // Loader: the warp's 16 rows, two 256-byte rows per instruction (16
-    // lanes x 16 bytes per row: fully coalesced); rows past the split end
+    // lanes x 16 bytes per row: fully coalesced); rows past the unit's rows
     // are zero-filled.
     const int ld_sub = lane >> 4, ld_ch = lane & 15;
     auto issue = [&](int t) {
@@ -446,7 +503,7 @@ sparse_av_bf16_kernel(AvParams p) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int row = warp * 16 + 2 * i + ld_sub;
-            const int pos = pos_of(r0 + t * kAvTile + row);
+            const int pos = pos_of(t, row);
             const bool valid = pos >= 0, nw = valid && pos == fresh;
             const int64_t off = valid && !nw ? (int64_t)pos * p.kv_row_stride : 0;
             cp_async16(kd + tile_off(row, ld_ch), (nw ? knew : kb) + off + ld_ch * 8, valid);
@@ -457,6 +514,14 @@ sparse_av_bf16_kernel(AvParams p) {
     cp_async_commit();
     if (1 < ntiles) issue(1);
     cp_async_commit();
+
+    // Q^T as the MMA B operand: n = head g, k = dims.
+    uint32_t qb[8][2];
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+            qb[kk][r] = g < G ? *reinterpret_cast<const uint32_t*>(qp + g * kAvD + kk * 16 + r * 8 + 2 * q4) : 0u;
 
     // Online softmax state of heads 2*q4 and 2*q4 + 1 (lanes with the same
     // q4 agree); O^T accumulators oc[mt] hold dims mt*16 + g (+8) of them.
@@ -484,10 +549,10 @@ sparse_av_bf16_kernel(AvParams p) {
             if (kk & 1) mma_bf16(sb, a, qb[kk][0], qb[kk][1]);
             else mma_bf16(sa, a, qb[kk][0], qb[kk][1]);
         }
-        // Scale, mask rows past the split end (c0/c1: key g, heads 2q4 and
+        // Scale, mask rows past the unit's rows (c0/c1: key g, heads 2q4 and
         // 2q4+1; c2/c3: key g+8), online softmax per head.
-        const int base_r = r0 + t * kAvTile + wrow;
-        const bool ok0 = base_r + g < r1, ok1 = base_r + g + 8 < r1;
+        const int64_t base_r = list_pos(t, wrow);
+        const bool ok0 = base_r + g < rows, ok1 = base_r + g + 8 < rows;
         const float s0 = ok0 ? (sa[0] + sb[0]) * scale : -INFINITY;
         const float s1 = ok0 ? (sa[1] + sb[1]) * scale : -INFINITY;
         const float s2 = ok1 ? (sa[2] + sb[2]) * scale : -INFINITY;
@@ -905,12 +970,25 @@ int default_splits(int U) {
         sms = sms_of[dev];
     }
     cudaGetLastError();
-    // About one wave of two CTAs per SM across all units, at most 8 splits
-    // (portable clusters, merged on chip): each split pays a fixed prologue
-    // (ids, Q, first tile), so more splits than resident slots only add
-    // overhead, and clusters above 8 CTAs schedule poorly.
+    // About one wave of two CTAs per SM across all units: each split pays a
+    // fixed prologue (ids, Q, first tile), so more splits than resident slots
+    // only add overhead.  Up to 8 splits form one cluster merged on chip;
+    // above that, whole clusters of 8 (merged on chip, then across clusters
+    // through global memory), at most 64 splits.
     const int s = (2 * sms) / U;
-    return s < 1 ? 1 : (s > 8 ? 8 : s);
+    if (s < 1) return 1;
+    return s <= kAvGroupMax ? s : (s / kAvGroupMax * kAvGroupMax > 64 ? 64 : s / kAvGroupMax * kAvGroupMax);
+}
+
+// CTAs per cluster of the G <= 8 kernel for S splits: all of them up to 8,
+// else the largest divisor of S in [3, 8] (the clusters' states then merge
+// through global memory); 0 when there is none (no cluster: the last CTA of
+// a unit merges the S split partials).
+int av_cluster_size(int S) {
+    if (S <= kAvGroupMax) return S;
+    for (int c = kAvGroupMax; c >= 3; --c)
+        if (S % c == 0) return c;
+    return 0;
 }
 
 }  // namespace pk
@@ -919,8 +997,11 @@ using namespace pk;
 
 extern "C" size_t pk_sparse_av_workspace_bytes(int U, int G, int d, int splits) {
     if (splits <= 0) splits = 256;
+    // Split partials [U*G, S, d+2] (the cluster states [U, S/C, 3, G*d] of a
+    // clustered launch fit in the same bytes for C >= 3), then kAvCounters
+    // arrival counters per unit.
     const size_t part = (size_t)U * G * splits * (d + 2) * sizeof(float);
-    return (part + 255) / 256 * 256 + ((size_t)U * sizeof(int) + 255) / 256 * 256;
+    return (part + 255) / 256 * 256 + ((size_t)U * kAvCounters * sizeof(int) + 255) / 256 * 256;
 }
 
 static int sparse_av_launch(uint64_t q, uint64_t k, uint64_t v, int dtype, int kv_heads, int64_t kv_batch_stride,
@@ -952,13 +1033,19 @@ static int sparse_av_launch(uint64_t q, uint64_t k, uint64_t v, int dtype, int k
     p.v_new = (const void*)v_new;
     cudaStream_t st = (cudaStream_t)stream;
     dim3 grid(splits, U);
+    p.C = 1;
     if (dtype == PK_BF16) {
         if (kv_row_stride % 8 || kv_batch_stride % 8 || kv_head_stride % 8 || (k | v) % 16) return PK_ERR_ARG;
         const int which = G <= 8 ? 0 : 1;
         const int base_smem = kAvStages * kAvStageBytes + kAvIdsCap * (int)sizeof(int);
+        // Cluster size: the G <= 8 kernel merges clusters of av_cluster_size
+        // splits on chip (and the clusters through global memory); the
+        // 9..16-head kernel takes all its splits (up to 16) in one cluster.
+        const int C = which == 0 ? av_cluster_size(splits) : splits;
         // The cluster form of the G <= 8 kernel adds the push-merge receive buffer.
-        const int csmem = base_smem + (which == 0 ? av_push_floats(G, splits) * (int)sizeof(float) : 0);
-        if (splits >= 2 && cluster_fits(which, splits, csmem)) {
+        const int csmem = base_smem + (which == 0 && C >= 2 ? av_push_floats(G, C) * (int)sizeof(float) : 0);
+        if (splits >= 2 && C >= 2 && cluster_fits(which, C, csmem)) {
+            p.C = C;
             // The shared-memory limit is one attribute per kernel, shared by
             // every split count: set it for this launch's size.
             auto cfn = which == 0 ? sparse_av_bf16_kernel<true> : sparse_av_bf16_g16_kernel<true>;
@@ -971,7 +1058,7 @@ static int sparse_av_launch(uint64_t q, uint64_t k, uint64_t v, int dtype, int k
             cfg.stream = st;
             cudaLaunchAttribute attr[1];
             attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = splits;
+            attr[0].val.clusterDim.x = C;
             attr[0].val.clusterDim.y = 1;
             attr[0].val.clusterDim.z = 1;
             cfg.attrs = attr;
@@ -1097,7 +1184,8 @@ extern "C" int pk_sparse_av_noalloc(uint64_t q, uint64_t k, uint64_t v, int dtyp
         // the previous call left, so clear them on this call's stream.
         const size_t part = (size_t)U * G * splits * (d + 2) * sizeof(float);
         const size_t counters = (part + 255) / 256 * 256;
-        cudaError_t e = cudaMemsetAsync((char*)scratch + counters, 0, (size_t)U * sizeof(int), (cudaStream_t)stream);
+        cudaError_t e = cudaMemsetAsync((char*)scratch + counters, 0, (size_t)U * kAvCounters * sizeof(int),
+                                        (cudaStream_t)stream);
         if (e != cudaSuccess) return (int)e;
     }
     return pk_sparse_av(q, k, v, dtype, kv_heads, kv_batch_stride, kv_head_stride, kv_row_stride, ids, ids_stride,

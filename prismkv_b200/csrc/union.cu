@@ -21,10 +21,11 @@
 //      its tokens are turned on, and each token turned on decrements the
 //      counts of the later buckets holding it (one barrier per accepted
 //      bucket).  When the tail or the hash does not fit in shared memory,
-//      rounds run instead: every remaining bucket's count is retaken from
-//      the bitmap, the first that fits is accepted, and a bucket whose count
-//      exceeds the remaining budget is dropped for good (its count can
-//      shrink by at most what the budget shrinks).
+//      rounds run instead: the counts of the next 32 live buckets are
+//      retaken from the bitmap (a warp each), the first that fits is
+//      accepted, and a bucket whose count exceeds the remaining budget is
+//      dropped for good (its count can shrink by at most what the budget
+//      shrinks).
 #include "common.cuh"
 #include "mma.cuh"
 
@@ -41,6 +42,7 @@ struct UnionSmem {
     int cand_pre[kMaxCand + 1];   // exclusive prefix of the list lengths
     int newc[kMaxCand];
     unsigned char dead[kMaxCand];
+    int cand_pre_win[32];         // the fallback rounds' window of live buckets
     int scan[40];
     int red[32];
     int flags[8];
@@ -407,9 +409,31 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
             }
             cpos = n;
         }
+        // Rounds over a window of the next nw live buckets (one warp each):
+        // their exact counts against the bitmap, then the first that fits is
+        // accepted and the next window starts after it.  Every window member
+        // over the budget is dropped for good: a count shrinks by at most
+        // what the remaining budget shrinks, so a bucket over the budget now
+        // never fits later.
         while (cpos < n) {
-            for (int c = cpos + warp; c < n; c += nw) {
-                if (sm.dead[c]) continue;
+            if (warp == 0) {
+                // The window: the next nw buckets from cpos that are not dead.
+                int got = 0;
+                for (int base = cpos; base < n && got < nw; base += 32) {
+                    const int c = base + lane;
+                    const bool live = c < n && !sm.dead[c];
+                    const unsigned lm = __ballot_sync(0xffffffffu, live);
+                    const int at = got + __popc(lm & ((1u << lane) - 1u));
+                    if (live && at < nw) sm.cand_pre_win[at] = c;
+                    got += __popc(lm);
+                }
+                if (lane == 0) sm.flags[1] = min(got, nw);
+            }
+            __syncthreads();
+            const int nwin = sm.flags[1];
+            if (nwin == 0) break;
+            if (warp < nwin) {
+                const int c = sm.cand_pre_win[warp];
                 const int L = sm.cand_len[c];
                 int m = 0;
                 for (int i = lane; i < L; i += 32) {
@@ -422,22 +446,23 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
             __syncthreads();
             if (warp == 0) {
                 const long long rem = lim - count;
-                int first = n;
-                for (int base = cpos; base < n; base += 32) {
-                    const int c = base + lane;
-                    bool fits = false;
-                    if (c < n && !sm.dead[c]) {
-                        if ((long long)sm.newc[c] <= rem) fits = true;
-                        else sm.dead[c] = 1;
-                    }
-                    const unsigned fm = __ballot_sync(0xffffffffu, fits);
-                    if (fm && first == n) first = base + __ffs(fm) - 1;
+                const int c = lane < nwin ? sm.cand_pre_win[lane] : n;
+                const bool fits = lane < nwin && (long long)sm.newc[c] <= rem;
+                const unsigned fm = __ballot_sync(0xffffffffu, fits);
+                const int first_lane = fm ? __ffs(fm) - 1 : nwin;
+                // Window members over the budget are dropped.
+                if (lane < nwin && !fits) sm.dead[c] = 1;
+                if (lane == 0) {
+                    sm.flags[0] = fm ? sm.cand_pre_win[first_lane] : -1;
+                    sm.flags[2] = sm.cand_pre_win[nwin - 1];
                 }
-                if (lane == 0) sm.flags[0] = first;
             }
             __syncthreads();
             const int c = sm.flags[0];
-            if (c >= n) break;
+            if (c < 0) {
+                cpos = sm.flags[2] + 1;
+                continue;
+            }
             or_bucket(c);
             count += sm.newc[c];
             raw_acc += sm.cand_len[c];

@@ -38,6 +38,21 @@ def kv_layout(k: torch.Tensor, v: torch.Tensor, U: int, d: int):
     return kv
 
 
+def default_splits(U: int, rows: int | None, device) -> int:
+    """Split count of the sparse attention for U units of about ``rows`` rows
+    each: one wave of two CTAs per SM over all units, at least two 64-row
+    tiles per split, and above 8 splits whole clusters of 8 (at most 64),
+    the library's own default (pk_sparse_av with splits <= 0) when rows is
+    None."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    s = (2 * sms) // max(1, U)
+    if rows is not None:
+        s = min(s, max(1, (rows + 63) // 64 // 2))
+    if s > 8:
+        s = min(64, s // 8 * 8)
+    return max(1, s)
+
+
 def kv_append(k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
               positions: torch.Tensor) -> None:
     """Decode KV append (the reference's ``batch_append``,
@@ -150,9 +165,49 @@ class SparseDecode:
             nv.call("pk_route_moments", q, nv.dtype_code(q), idx.mean, idx.var, counts, bits, U, G, d, F, k,
                     self.ws.get(("moments", U, G, F), nbytes), nbytes, self.score, self.order, self.n_order,
                     self.width)
+        self.union()
+
+    def union(self) -> None:
+        """The budgeted union of the routed order (core.py:152-164) for every
+        unit: ids, accepted buckets, raw sizes and counts."""
+        idx = self.index
         nv.call("pk_union", idx.offsets, idx.lens, idx.ids, idx.ids.stride(0), self.order, self.n_order, self.width,
-                self.history, self.limit, U, F, self.max_history, self.ids, self.ids.shape[1], self.count,
+                self.history, self.limit, self.U, self.F, self.max_history, self.ids, self.ids.shape[1], self.count,
                 self.features, self.n_features, self.raw, self.status)
+
+    # ---------------------------------------------- feature-sharded routing
+    def route_shard_picks(self, q: torch.Tensor, f_lo: int, f_hi: int, picks: torch.Tensor) -> torch.Tensor:
+        """q_activation routing over the features [f_lo, f_hi) only: each
+        head's positive top-k among them, exact, in rank order, as int32
+        (value bits, feature id) pairs in picks [U*G, k, 2] (unused slots
+        (0, INT32_MAX)).  The first half of the feature-sharded route; the
+        picks of every feature range go to route_merge."""
+        U, G, d, F, k = self.U, self.G, self.d, self.F, self.k
+        if self.router != "q_activation" or self.prep[0] is None:
+            raise ValueError("feature-sharded routing needs the bound-filtered q_activation router")
+        if q.shape != (U, G, d) or not q.is_contiguous():
+            raise ValueError(f"contiguous Q[{U},{G},{d}] required")
+        if tuple(picks.shape) != (U * G, k, 2) or picks.dtype != torch.int32 or not picks.is_contiguous():
+            raise ValueError(f"picks must be a contiguous int32 [{U * G}, {k}, 2] tensor")
+        nbytes = nv.query("pk_route_qact_shard_workspace_bytes", U, G, f_hi - f_lo, k)
+        nv.call("pk_route_qact_shard", q, nv.dtype_code(q), self.sae.W_enc, self.sae.b_enc, self.prep[0], self.prep[1],
+                self.query_scale, U, G, d, F, k, f_lo, f_hi,
+                self.ws.get(("qact_shard", U, G, f_hi - f_lo, k), nbytes), nbytes, picks)
+        return picks
+
+    def route_merge(self, gathered: torch.Tensor) -> None:
+        """The second half of the feature-sharded route: gathered [P, U*G,
+        k, 2] holds the picks of P disjoint feature ranges covering all F
+        features; every head's exact top-k over them, then the unit's
+        normalisation, aggregation and order (core.py:134-139), equal to the
+        unsharded route's.  Bucket liveness comes from this index."""
+        U, G, F, k = self.U, self.G, self.F, self.k
+        P = gathered.shape[0]
+        if tuple(gathered.shape[1:]) != (U * G, k, 2) or gathered.dtype != torch.int32 or not gathered.is_contiguous():
+            raise ValueError(f"gathered picks must be a contiguous int32 [P, {U * G}, {k}, 2] tensor")
+        nbytes = nv.query("pk_route_qact_merge_workspace_bytes", U, G, k)
+        nv.call("pk_route_qact_merge", gathered, P, self.index.lens, U, G, F, k,
+                self.ws.get(("qact_merge", U, G, k), nbytes), nbytes, self.order, self.n_order, self.width, None)
 
     # ------------------------------------------------------------ attention
     def attention(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, length=None, splits=None,
@@ -189,10 +244,8 @@ class SparseDecode:
             lt = length
         S = splits or self.splits or 0
         if S <= 0:
-            # The library's default: one wave of two CTAs per SM over all
-            # units, at most 8 splits (one on-chip merged cluster per unit).
-            sms = torch.cuda.get_device_properties(q.device).multi_processor_count
-            S = max(1, min(8, (2 * sms) // U))
+            # Rows per unit: at most the id width plus the tail.
+            S = default_splits(U, self.id_width + max(0, total - self.index.history), q.device)
         nbytes = nv.query("pk_sparse_av_workspace_bytes", U, G, d, S)
         if partial is not None:
             out = None

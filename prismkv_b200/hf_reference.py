@@ -39,7 +39,7 @@ from dataclasses import dataclass
 import torch
 
 from . import native as nv
-from .decode import SparseDecode
+from .decode import SparseDecode, default_splits
 from .index import DeviceIndex, SAEParams
 
 SUPPORTED_MODULES = ("Qwen3Attention", "Qwen3_5Attention", "LlamaAttention")
@@ -407,8 +407,7 @@ class HFReference:
         count = torch.full((U,), history, dtype=torch.int32, device=Qb.device)
         hist = torch.full((U,), history, dtype=torch.int32, device=Qb.device)
         length = torch.full((U,), total, dtype=torch.int32, device=Qb.device)
-        sms = torch.cuda.get_device_properties(Qb.device).multi_processor_count
-        S = max(1, min(8, (2 * sms) // U))
+        S = default_splits(U, total, Qb.device)
         nbytes = nv.query("pk_sparse_av_workspace_bytes", U, G, d, S)
         out = torch.empty(U, G, d, dtype=Qb.dtype, device=Qb.device)
         nv.call("pk_sparse_av", Qb, Kb, Vb, nv.dtype_code(Qb), 1, Kb.stride(0), 0, Kb.stride(1), ids, ids.shape[1],

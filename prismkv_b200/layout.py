@@ -8,7 +8,7 @@ from __future__ import annotations
 import torch
 
 from . import native as nv
-from .decode import SparseDecode, kv_layout
+from .decode import SparseDecode, default_splits, kv_layout
 
 
 def gather_kv(k: torch.Tensor, v: torch.Tensor, ids: torch.Tensor, count: torch.Tensor, history: torch.Tensor,
@@ -75,8 +75,7 @@ def layout_probe(op: SparseDecode, q: torch.Tensor, k: torch.Tensor, v: torch.Te
         vu = v[u] if v.dim() == 3 else v[u // kv_heads, :, u % kv_heads]
         if not torch.equal(pk_[u, :c + t], ku[pos]) or not torch.equal(pv_[u, :c + t], vu[pos]):
             raise RuntimeError("packed rows differ from the selection and tail")
-    sms = torch.cuda.get_device_properties(q.device).multi_processor_count
-    S = splits or max(1, min(8, (2 * sms) // U))
+    S = splits or default_splits(U, P, q.device)
     ident = torch.arange(max(P, 1), dtype=torch.int32, device=q.device).repeat(U, 1).contiguous()
     p_len = rows.int()
     nbytes = nv.query("pk_sparse_av_workspace_bytes", U, G, d, S)

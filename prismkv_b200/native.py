@@ -37,6 +37,10 @@ SIGNATURES = {
     "pk_supported_head_dim": ("i", ctypes.c_int),
     "pk_route_qact_workspace_bytes": ("iiii", ctypes.c_size_t),
     "pk_route_qact": ("PiPiPPPPfPiiiiiPPPPiPPP", ctypes.c_int),
+    "pk_route_qact_shard_workspace_bytes": ("iiii", ctypes.c_size_t),
+    "pk_route_qact_shard": ("PiPPPPfiiiiiiiPPPP", ctypes.c_int),
+    "pk_route_qact_merge_workspace_bytes": ("iii", ctypes.c_size_t),
+    "pk_route_qact_merge": ("PiPiiiiPPPPiPP", ctypes.c_int),
     "pk_sae_prepare": ("PiiPPP", ctypes.c_int),
     "pk_sae_prepare_half": ("PiiPP", ctypes.c_int),
     "pk_route_moments_workspace_bytes": ("iii", ctypes.c_size_t),

@@ -4,10 +4,14 @@ split along the token axis over the ranks of a process group.
 Rank r of P owns tokens [lo_r, hi_r) of the history (``token_ranges``); the
 dense tail of generated tokens lives on the last rank.  One decode step is:
 
-1. routing, replicated on every rank (the q_activation scores depend only on
-   the query and the SAE, core.py:131-139, bucket liveness being local; the
-   moments router, core.py:117-130, reads the whole sequence's bucket moments
-   and sizes, attach_global_moments, so every rank takes the same buckets);
+1. routing.  q_activation (core.py:131-139) is split by features: rank r
+   encodes the features of its range (``feature_ranges``) for every query
+   head and keeps each head's exact positive top-k among them; one
+   all-gather of those picks (a few KB) and an exact merge give every rank
+   the unsharded per-head top-k and the same order (bucket liveness is
+   local).  The moments router (core.py:117-130) runs replicated: it reads
+   the whole sequence's bucket moments and sizes (attach_global_moments), so
+   every rank takes the same buckets;
 2. the union of the routed buckets' shard-local lists (core.py:152-164) with
    the per-shard budget ``budget // P`` -- in the unbudgeted mode the shards'
    unions are exactly the global union cut at the shard boundaries;
@@ -17,7 +21,8 @@ dense tail of generated tokens lives on the last rank.  One decode step is:
    log-sum-exp merge on every rank (pk_lse_merge), the split-KV merge of the
    reference's kernels (kernels/ppu_8b/av_tuned.cu) applied across ranks.
 
-There is no other collective on the path.
+The two all-gathers (routing picks, attention partials) are the only
+collectives on the path.
 """
 from __future__ import annotations
 
@@ -76,6 +81,12 @@ def shard_index(index: DeviceIndex, lo: int, hi: int) -> DeviceIndex:
     out.center.copy_(index.center)
     out.history = hi - lo
     return out
+
+
+def feature_ranges(F: int, P: int) -> list:
+    """Contiguous feature ranges [lo, hi) of the feature-sharded route, in
+    rank order (sizes differ by at most one)."""
+    return token_ranges(F, P)
 
 
 def gather_partials(part: torch.Tensor, out: torch.Tensor, group=None) -> torch.Tensor:
@@ -176,7 +187,7 @@ class ShardedDecode:
     def __init__(self, local_index: DeviceIndex, sae, *, group=None, heads_per_unit: int = 4,
                  router: str = "q_activation", query_scale: float = 1.0, query_topk: int | None = None,
                  budget: int | None = None, splits: int | None = None, max_history: int | None = None,
-                 workspace: nv.Workspace | None = None):
+                 workspace: nv.Workspace | None = None, split_route: bool | None = None):
         self.group = group
         init = dist.is_initialized()
         self.P = dist.get_world_size(group) if init else 1
@@ -196,6 +207,17 @@ class ShardedDecode:
         self.part = torch.empty(U * G, d + 2, dtype=torch.float32, device=dev)
         self.gathered = torch.empty(self.P, U * G, d + 2, dtype=torch.float32, device=dev)
         self.out = None
+        # q_activation routing split by features over the ranks (default
+        # with more than one rank); replicated otherwise.
+        if split_route is None:
+            split_route = self.P > 1 and router == "q_activation" and self.op.prep[0] is not None
+        if split_route and (router != "q_activation" or self.op.prep[0] is None):
+            raise ValueError("split_route needs the bound-filtered q_activation router")
+        self.split_route = bool(split_route)
+        if self.split_route:
+            self.f_range = feature_ranges(self.op.F, self.P)[self.rank]
+            self.picks = torch.empty(U * G, self.op.k, 2, dtype=torch.int32, device=dev)
+            self.all_picks = torch.empty(self.P, U * G, self.op.k, 2, dtype=torch.int32, device=dev)
 
     @property
     def is_tail_rank(self) -> bool:
@@ -203,7 +225,13 @@ class ShardedDecode:
 
     def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, length=None) -> torch.Tensor:
         U, G, d = self.op.U, self.op.G, self.op.d
-        self.op.route(q)
+        if self.split_route:
+            self.op.route_shard_picks(q, *self.f_range, self.picks)
+            _gather(self.picks, self.all_picks, self.group)
+            self.op.route_merge(self.all_picks)
+            self.op.union()
+        else:
+            self.op.route(q)
         self.op.attention(q, k, v, length=length, partial=self.part)
         gather_partials(self.part, self.gathered, self.group)
         if self.out is None or self.out.dtype != q.dtype:

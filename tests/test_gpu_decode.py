@@ -338,6 +338,15 @@ def test_union_greedy_matches_oracle_on_large_buckets(pk, oracle, seed):
                 (0, 500, 4096, 20000, 10 ** 9))
 
 
+def test_union_matches_oracle_at_a_million_token_history(pk, oracle):
+    """Config 4's union size: a 2^20-token history, whose bitmap leaves room
+    to stage only part of the 256 candidates' lists, so the tail runs the
+    windowed recount rounds; against the oracle's greedy."""
+    rs = np.random.RandomState(41)
+    _union_case(pk, oracle, rs, 2, 1 << 20, 600, 256, [64, 256, 1024], [0.3, 0.5, 0.2], 4000,
+                (0, 8192, 30000, 10 ** 9))
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_bound_filtered_build_equals_exact_build(pk, dtype):
     """Tensor-core bounds + exact recompute of the undecided band give the
@@ -367,9 +376,12 @@ def test_bound_filtered_build_equals_exact_build(pk, dtype):
 @pytest.mark.parametrize("G", [1, 3, 8, 12, 16])
 def test_attention_head_counts_and_split_forms_match_oracle(pk, oracle, G):
     """Both bf16 attention kernels -- heads in the MMA's N for G <= 8, in its
-    M for 9..16 -- with one split, a cluster of splits merged on chip, and
-    more than 8 splits merged through global memory, against the oracle's
-    attend (core.py:170-183) on the same bf16 inputs."""
+    M for 9..16 -- with one split, a cluster of splits merged on chip, more
+    splits than one cluster holds (for G <= 8: clusters of 8, 6 or 5 merged
+    on chip and then across clusters through global memory; a prime count
+    takes the last-CTA merge of every split), against the oracle's attend
+    (core.py:170-183) on the same bf16 inputs.  Each workspace is used twice
+    in a row (the arrival counters must be left at zero)."""
     from prismkv_b200 import native as nv
     rs = np.random.RandomState(11 + G)
     U, N, tail, d = 3, 2048, 5, 128
@@ -393,13 +405,19 @@ def test_attention_head_counts_and_split_forms_match_oracle(pk, oracle, G):
     hist = torch.full((U,), N, dtype=torch.int32, device=dev)
     length = torch.full((U,), N + tail, dtype=torch.int32, device=dev)
     refs = [oracle.attend(q[u], keys[u], vals[u], sel[u], N) for u in range(U)]
-    for splits in (1, 4, 8, 13):
+    for splits in (1, 4, 8, 13, 12, 16, 20, 24, 64):
         nbytes = nv.query("pk_sparse_av_workspace_bytes", U, G, d, splits)
         ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
-        out = torch.full((U, G, d), float("nan"), dtype=torch.bfloat16, device=dev)
-        nv.call("pk_sparse_av", Q, K, V, nv.PK_BF16, 1, K.stride(0), 0, K.stride(1), tid, width, count, hist, length,
-                U, G, d, splits, ws, nbytes, out, None)
-        torch.cuda.synchronize()
+        first = None
+        for rep in range(2):
+            out = torch.full((U, G, d), float("nan"), dtype=torch.bfloat16, device=dev)
+            nv.call("pk_sparse_av", Q, K, V, nv.PK_BF16, 1, K.stride(0), 0, K.stride(1), tid, width, count, hist,
+                    length, U, G, d, splits, ws, nbytes, out, None)
+            torch.cuda.synchronize()
+            if first is None:
+                first = out.clone()
+            else:
+                assert torch.equal(out, first), (G, splits)
         got = out.float().cpu().numpy()
         for u in range(U):
             assert rel_l2(got[u], refs[u]) < TOL_BF16, (G, splits, u)

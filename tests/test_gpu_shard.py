@@ -276,3 +276,71 @@ def test_two_rank_nccl_sharded_moments_router():
     assert all(p.exitcode == 0 for p in procs)
     res = dict(q.get(timeout=5) for _ in range(2))
     assert all(s and e < 2e-2 for s, e in res.values()), res
+
+
+@pytest.mark.parametrize("P", [2, 3, 8])
+def test_feature_split_route_equals_unsharded(pk, P):
+    """The feature-sharded q_activation route: each feature range's picks
+    (pk_route_qact_shard), stacked as an all-gather would, merged on one
+    device (pk_route_qact_merge) give the unsharded route's order and, with
+    it, the same budgeted union (integer outputs, bit-exact)."""
+    from prismkv_b200.shard import feature_ranges
+    c = make_case(23)
+    U, N, G, d, F, k = c["U"], c["N"], c["G"], c["d"], c["F"], c["k"]
+    dev = torch.device("cuda")
+    K = torch.from_numpy(c["keys"]).to(dev).bfloat16()
+    Q = torch.from_numpy(c["q"]).to(dev).bfloat16().contiguous()
+    sae = pk.SAEParams(torch.from_numpy(c["W"]).to(dev), torch.zeros(F, device=dev), key_mean=8, query_topk=k)
+    idx = pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=False)
+    ref = pk.SparseDecode(idx, sae, heads_per_unit=G, budget=1500)
+    ref.route(Q)
+    op = pk.SparseDecode(idx, sae, heads_per_unit=G, budget=1500)
+    gathered = torch.empty(P, U * G, k, 2, dtype=torch.int32, device=dev)
+    for r, (lo, hi) in enumerate(feature_ranges(F, P)):
+        op.route_shard_picks(Q, lo, hi, gathered[r])
+    op.route_merge(gathered)
+    op.union()
+    torch.cuda.synchronize()
+    ref.check()
+    op.check()
+    assert torch.equal(op.n_order, ref.n_order)
+    for u in range(U):
+        n = int(ref.n_order[u])
+        assert torch.equal(op.order[u, :n], ref.order[u, :n]), u
+        c_ = int(ref.count[u])
+        assert int(op.count[u]) == c_ and torch.equal(op.ids[u, :c_], ref.ids[u, :c_]), u
+
+
+def test_feature_split_route_config4_shape(pk):
+    """The feature-sharded route at config 4's routing shape (F = 32768,
+    64 features per query head, 8 units of 4 heads) over 8 feature ranges
+    equals the unsharded route's order bit for bit."""
+    from prismkv_b200.shard import feature_ranges
+    rs = np.random.RandomState(29)
+    U, G, d, F, k, N, C = 8, 4, 128, 32768, 64, 16384, 256
+    centers = rs.standard_normal((U, C, d)).astype(np.float32)
+    cid = rs.randint(0, C, size=(U, N))
+    keys = (centers[np.arange(U)[:, None], cid] + np.float32(0.3) * rs.standard_normal((U, N, d))).astype(np.float32)
+    q = (centers[np.arange(U)[:, None], rs.randint(0, C, size=(U, G))]
+         + np.float32(0.3) * rs.standard_normal((U, G, d))).astype(np.float32)
+    W = (rs.standard_normal((F, d)) / np.sqrt(d)).astype(np.float32)
+    dev = torch.device("cuda")
+    K = torch.from_numpy(keys).to(dev).bfloat16()
+    Q = torch.from_numpy(q).to(dev).bfloat16().contiguous()
+    sae = pk.SAEParams(torch.from_numpy(W).to(dev), torch.zeros(F, device=dev), key_mean=8, query_topk=k)
+    idx = pk.DeviceIndex.build(K, sae, 1.0, moments=False)
+    ref = pk.SparseDecode(idx, sae, heads_per_unit=G, budget=8192)
+    ref.route(Q)
+    op = pk.SparseDecode(idx, sae, heads_per_unit=G, budget=8192)
+    P = 8
+    gathered = torch.empty(P, U * G, k, 2, dtype=torch.int32, device=dev)
+    for r, (lo, hi) in enumerate(feature_ranges(F, P)):
+        op.route_shard_picks(Q, lo, hi, gathered[r])
+    op.route_merge(gathered)
+    op.union()
+    torch.cuda.synchronize()
+    assert torch.equal(op.n_order, ref.n_order) and torch.equal(op.count, ref.count)
+    for u in range(U):
+        n, c_ = int(ref.n_order[u]), int(ref.count[u])
+        assert torch.equal(op.order[u, :n], ref.order[u, :n]), u
+        assert torch.equal(op.ids[u, :c_], ref.ids[u, :c_]), u
