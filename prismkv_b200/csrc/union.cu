@@ -521,7 +521,9 @@ static int union_launch(uint64_t offsets, uint64_t lens, uint64_t ids, int64_t i
         return PK_ERR_ARG;
     const int Wmax = (max_history + 31) / 32;
     const size_t bitmap = (size_t)((Wmax + 3) & ~3) * 4;
-    const size_t cap = 200 * 1024;
+    // Dynamic shared memory: all a block may hold (227 KB) less the static
+    // scratch, rounded down to KB.
+    const size_t cap = (227 * 1024 - sizeof(UnionSmem)) / 1024 * 1024;
     // The bitmap, then as many staged list entries as fit (at least 2048).
     if (bitmap + 2048 * 4 > cap) return PK_ERR_UNSUPPORTED;
     const int stage_cap = (int)((cap - bitmap) / 4);
