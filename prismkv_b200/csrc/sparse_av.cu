@@ -5,11 +5,12 @@
 //
 // bf16 path: a CTA of four warps streams its split's rows in tiles of 64 K
 // rows and 64 V rows, three stages deep.  Each warp gathers its own 16 rows of
-// every tile with 16-byte cp.async (rows addressed through the id list).  For
-// G <= 8 heads the tiles of a unit's row list are dealt to its S split CTAs
-// round robin (split s takes tiles s, s + S, ...), so a split's first tiles
-// are known before the unit's row count: their ids are read in parallel with
-// the count, and each later tile's ids one tile ahead, into registers.  The
+// every tile with 16-byte cp.async (rows addressed through the id list, staged
+// in shared memory).  For G <= 8 heads, when a unit's splits span several
+// clusters its tiles are dealt to the S split CTAs round robin (split s takes
+// tiles s, s + S, ...), so a split's tiles are known before the unit's row
+// count and their ids are staged in parallel with it; otherwise each split is
+// a contiguous run of tiles.  The
 // warp also computes on its rows alone, so the warps pipeline independently
 // (no CTA barrier per tile): its 16 key rows fill the M = 16 of mma.sync
 // m16n8k16 and the heads its N = 8 (S^T = K Q^T, then O^T += V^T P^T with
@@ -57,6 +58,7 @@ struct AvParams {
     const int* length;
     int G, S;
     int C;          // CTAs per cluster (G <= 8 kernel; S is a multiple of C)
+    int rr;         // G <= 8 kernel: tiles dealt round robin (several clusters per unit)
     float* part;    // [U*G, S, D+2] split partials (log2 domain); cluster states [U, S/C, 3, G*D]
     int* done;      // [U, kAvCounters] arrival counters
     void* out;      // [U, G, D] (dtype of q)
@@ -440,7 +442,8 @@ __host__ __device__ constexpr int av_push_floats(int G, int S) { return S * ((G 
 
 // G <= 8 heads.  Warp w owns rows [16w, 16w + 16) of every tile: it copies
 // them in and computes on them, so each warp's stages are its own.  Split s
-// takes the unit's tiles s, s + S, s + 2S, ...
+// takes a contiguous run of the unit's tiles, or, with several clusters per
+// unit, the tiles s, s + S, s + 2S, ...
 template <bool kCluster>
 __global__ void __launch_bounds__(kAvThreads, 2)
 sparse_av_bf16_kernel(AvParams p) {
@@ -450,21 +453,37 @@ sparse_av_bf16_kernel(AvParams p) {
     const int G = p.G, S = p.S;
     if constexpr (kCluster) asm volatile("barrier.cluster.arrive.relaxed;\n" ::: "memory");
     const int* idp = p.ids + (int64_t)u * p.ids_stride;
-    // Each warp stages the ids of its own rows (16w..16w+15 of each tile) of
-    // the split's first tiles in shared memory before the row count is known
-    // (within the id row's stride; entries past the count are not used), so
-    // the count and the ids arrive in one round trip.  Tiles past the staged
-    // ones (more than kAvIdsCap / 64 per split) read their ids directly.
+    const __nv_bfloat16* qp = (const __nv_bfloat16*)p.q + (int64_t)u * G * kAvD;
+    const int g = lane >> 2, q4 = lane & 3;
+    // Q^T as the MMA B operand: n = head g, k = dims.
+    uint32_t qb[8][2];
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+            qb[kk][r] = g < G ? *reinterpret_cast<const uint32_t*>(qp + g * kAvD + kk * 16 + r * 8 + 2 * q4) : 0u;
+    // Tile j of the split covers 64 consecutive list positions.  With
+    // one cluster (or none) per unit the split is a contiguous run of whole
+    // tiles [r0, r1); with several clusters (p.rr) the unit's tiles are
+    // dealt round robin (split s takes tiles s, s + S, ...), so the split's
+    // tiles are known before the unit's row count and their ids are staged
+    // in parallel with it: each warp stages the ids of its own rows (16w ..
+    // 16w + 15 of each tile) within the id row's stride (entries past the
+    // count are not used).  Tiles past the staged ones (more than
+    // kAvIdsCap / 64 per split) read their ids directly.
     int* sids = reinterpret_cast<int*>(smem + kAvStages * kAvStageBytes);
     constexpr int kStagedTiles = kAvIdsCap / kAvTile;
-    auto list_pos = [&](int j, int row) -> int64_t { return (int64_t)(s + (int64_t)j * S) * kAvTile + row; };
-    {
+    const bool rr = p.rr != 0;
+    // List position of row `row` of the split's tile j: base0 + j * tstep + row.
+    int base0 = rr ? s * kAvTile : 0;
+    const int tstep = rr ? S * kAvTile : kAvTile;
+    if (rr) {
         const int64_t tiles_in_stride = (p.ids_stride + kAvTile - 1) / kAvTile;
         const int64_t jcan = s < tiles_in_stride ? (tiles_in_stride - 1 - s) / S + 1 : 0;
         const int jst = (int)(jcan < kStagedTiles ? jcan : kStagedTiles);
         for (int i = lane; i < jst * 16; i += 32) {
             const int j = i >> 4, row = warp * 16 + (i & 15);
-            const int64_t r = list_pos(j, row);
+            const int64_t r = (int64_t)base0 + (int64_t)j * tstep + row;
             if (r < p.ids_stride) cp_async4(smem_u32(sids + j * kAvTile + row), idp + r);
         }
         cp_async_commit();
@@ -472,26 +491,42 @@ sparse_av_bf16_kernel(AvParams p) {
     const int H = p.history[u], len = p.length[u], cnt = p.count[u];
     const int rows = len > 0 ? cnt + max(len - H, 0) : 0;
     const int nt_all = (rows + kAvTile - 1) / kAvTile;
-    const int ntiles = s < nt_all ? (nt_all - 1 - s) / S + 1 : 0;
+    int ntiles, lim;
+    if (rr) {
+        ntiles = s < nt_all ? (nt_all - 1 - s) / S + 1 : 0;
+        lim = rows;
+        cp_async_wait<0>();
+        __syncwarp();   // the warp's staged ids are visible to all its lanes
+    } else {
+        // Whole tiles split evenly: the splits differ by at most one tile.
+        const int r0 = min(rows, (int)((int64_t)s * nt_all / S) * kAvTile);
+        const int r1 = min(rows, (int)((int64_t)(s + 1) * nt_all / S) * kAvTile);
+        base0 = r0;
+        ntiles = (r1 - r0 + kAvTile - 1) / kAvTile;
+        lim = r1;
+        // The split's ids, staged by the whole CTA (coalesced, all copies in
+        // flight together).
+        const int n_staged = min(max(0, min(r1, cnt) - r0), kAvIdsCap);
+        for (int i = tid; i < n_staged; i += kAvThreads) cp_async4(smem_u32(sids + i), idp + r0 + i);
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+    }
     // Cache position of row `row` of the split's tile j (-1: past the
-    // rows): a listed id below the count, then the tail history..length-1.
+    // split): a listed id below the count, then the tail history..length-1.
     auto pos_of = [&](int j, int row) -> int {
-        const int64_t r = list_pos(j, row);
-        if (r >= rows) return -1;
-        if (r >= cnt) return H + (int)(r - cnt);
+        const int r = base0 + j * tstep + row;
+        if (r >= lim) return -1;
+        if (r >= cnt) return H + (r - cnt);
         return j < kStagedTiles ? sids[j * kAvTile + row] : __ldg(idp + r);
     };
     const int64_t ubase = (int64_t)(u / p.kv_heads) * p.kv_batch_stride + (int64_t)(u % p.kv_heads) * p.kv_head_stride;
     const __nv_bfloat16* kb = (const __nv_bfloat16*)p.k + ubase;
     const __nv_bfloat16* vb = (const __nv_bfloat16*)p.v + ubase;
-    const __nv_bfloat16* qp = (const __nv_bfloat16*)p.q + (int64_t)u * G * kAvD;
     const int fresh = fresh_row(p, H, len);
     const __nv_bfloat16* knew = fresh >= 0 ? (const __nv_bfloat16*)p.k_new + (int64_t)u * kAvD : kb;
     const __nv_bfloat16* vnew = fresh >= 0 ? (const __nv_bfloat16*)p.v_new + (int64_t)u * kAvD : vb;
     append_fresh_row<__nv_bfloat16>(p, u, ubase, fresh);
-    const int g = lane >> 2, q4 = lane & 3;
-    cp_async_wait<0>();
-    __syncwarp();   // the warp's staged ids are visible to all its lanes
 
     // Loader: the warp's 16 rows, two 256-byte rows per instruction (16
     // lanes x 16 bytes per row: fully coalesced); rows past the unit's rows
@@ -514,14 +549,6 @@ sparse_av_bf16_kernel(AvParams p) {
     cp_async_commit();
     if (1 < ntiles) issue(1);
     cp_async_commit();
-
-    // Q^T as the MMA B operand: n = head g, k = dims.
-    uint32_t qb[8][2];
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
-#pragma unroll
-        for (int r = 0; r < 2; ++r)
-            qb[kk][r] = g < G ? *reinterpret_cast<const uint32_t*>(qp + g * kAvD + kk * 16 + r * 8 + 2 * q4) : 0u;
 
     // Online softmax state of heads 2*q4 and 2*q4 + 1 (lanes with the same
     // q4 agree); O^T accumulators oc[mt] hold dims mt*16 + g (+8) of them.
@@ -551,8 +578,8 @@ sparse_av_bf16_kernel(AvParams p) {
         }
         // Scale, mask rows past the unit's rows (c0/c1: key g, heads 2q4 and
         // 2q4+1; c2/c3: key g+8), online softmax per head.
-        const int64_t base_r = list_pos(t, wrow);
-        const bool ok0 = base_r + g < rows, ok1 = base_r + g + 8 < rows;
+        const int base_r = base0 + t * tstep + wrow;
+        const bool ok0 = base_r + g < lim, ok1 = base_r + g + 8 < lim;
         const float s0 = ok0 ? (sa[0] + sb[0]) * scale : -INFINITY;
         const float s1 = ok0 ? (sa[1] + sb[1]) * scale : -INFINITY;
         const float s2 = ok1 ? (sa[2] + sb[2]) * scale : -INFINITY;
@@ -1034,6 +1061,7 @@ static int sparse_av_launch(uint64_t q, uint64_t k, uint64_t v, int dtype, int k
     cudaStream_t st = (cudaStream_t)stream;
     dim3 grid(splits, U);
     p.C = 1;
+    p.rr = 0;
     if (dtype == PK_BF16) {
         if (kv_row_stride % 8 || kv_batch_stride % 8 || kv_head_stride % 8 || (k | v) % 16) return PK_ERR_ARG;
         const int which = G <= 8 ? 0 : 1;
@@ -1046,6 +1074,7 @@ static int sparse_av_launch(uint64_t q, uint64_t k, uint64_t v, int dtype, int k
         const int csmem = base_smem + (which == 0 && C >= 2 ? av_push_floats(G, C) * (int)sizeof(float) : 0);
         if (splits >= 2 && C >= 2 && cluster_fits(which, C, csmem)) {
             p.C = C;
+            p.rr = which == 0 && C < splits;
             // The shared-memory limit is one attribute per kernel, shared by
             // every split count: set it for this launch's size.
             auto cfn = which == 0 ? sparse_av_bf16_kernel<true> : sparse_av_bf16_g16_kernel<true>;

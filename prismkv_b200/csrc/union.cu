@@ -43,7 +43,6 @@ struct UnionSmem {
     int newc[kMaxCand];
     unsigned char dead[kMaxCand];
     int cand_pre_win[32];         // the fallback rounds' window of live buckets
-    int scan[40];
     int red[32];
     int flags[8];
     long long lred[2];
@@ -201,6 +200,29 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
             if ((unsigned)t < (unsigned)H) set_bit(bm, t);
         }
     };
+    // Calls fn(t) for every token of bucket c from one warp (lanes take
+    // consecutive entries): a staged list from shared memory, any other from
+    // global memory with eight loads a lane in flight (entries past the list
+    // give t = -1).
+    auto warp_tokens = [&](int c, auto&& fn) {
+        const int L = sm.cand_len[c];
+        if (c >= ws0 && c < ws1) {
+            const uint32_t* src = stage + (sm.cand_pre[c] - sm.cand_pre[ws0]);
+            for (int i = lane; i < L; i += 32) fn((int)(src[i] & ~kFlipFlag));
+        } else {
+            const int* src = uid + sm.cand_start[c];
+            for (int i0 = 0; i0 < L; i0 += 256) {
+                int tk[8];
+#pragma unroll
+                for (int b = 0; b < 8; ++b) {
+                    const int i = i0 + 32 * b + lane;
+                    tk[b] = i < L ? __ldg(src + i) : -1;
+                }
+#pragma unroll
+                for (int b = 0; b < 8; ++b) fn(tk[b]);
+            }
+        }
+    };
     stage_from(0);
 
     const long long raw_total = sm.cand_pre[n];
@@ -208,13 +230,10 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
     int nf = 0;
     if (raw_total <= lim) {
         // Every candidate fits whatever the overlap: the unbudgeted union.
-        for (int c = warp; c < n; c += nw) {
-            const int L = sm.cand_len[c];
-            for (int i = lane; i < L; i += 32) {
-                const int t = token(c, i);
+        for (int c = warp; c < n; c += nw)
+            warp_tokens(c, [&](int t) {
                 if ((unsigned)t < (unsigned)H) set_bit(bm, t);
-            }
-        }
+            });
         for (int c = tid; c < n; c += nt) feat[c] = sm.cand_bucket[c];
         nf = n;
         raw_acc = raw_total;
@@ -232,16 +251,13 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
             }
         }
         int flips = 0;
-        for (int c = warp; c < sure; c += nw) {
-            const int L = sm.cand_len[c];
-            for (int i = lane; i < L; i += 32) {
-                const int t = token(c, i);
+        for (int c = warp; c < sure; c += nw)
+            warp_tokens(c, [&](int t) {
                 if ((unsigned)t < (unsigned)H) {
                     const uint32_t bit = 1u << (t & 31);
                     flips += (atomicOr(&bm[t >> 5], bit) & bit) ? 0 : 1;
                 }
-            }
-        }
+            });
         long long count = block_sum(flips, sm.red);
         // Galloping probes from there; the first range is sized by the
         // overlap seen so far (tokens per listed entry).
@@ -434,12 +450,8 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
             if (nwin == 0) break;
             if (warp < nwin) {
                 const int c = sm.cand_pre_win[warp];
-                const int L = sm.cand_len[c];
                 int m = 0;
-                for (int i = lane; i < L; i += 32) {
-                    const int t = token(c, i);
-                    m += ((unsigned)t < (unsigned)H && !test_bit(bm, t)) ? 1 : 0;
-                }
+                warp_tokens(c, [&](int t) { m += ((unsigned)t < (unsigned)H && !test_bit(bm, t)) ? 1 : 0; });
                 m = warp_sum(m);
                 if (lane == 0) sm.newc[c] = m;
             }
@@ -474,24 +486,41 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
     }
     __syncthreads();
 
-    // Compaction: each thread owns a contiguous run of words.
-    const int per = (W + nt - 1) / nt;
-    const int w0 = min(W, tid * per), w1 = min(W, w0 + per);
-    int pop = 0;
-    for (int w = w0; w < w1; ++w) pop += __popc(bm[w]);
-    int total;
-    int at = block_exclusive_scan(pop, sm.scan, &total);
+    // Compaction: each warp owns a contiguous run of words, read 32
+    // consecutive words at a time (conflict-free); a count pass, the warps'
+    // offsets, then the emit pass in word order.
+    const int wper = ((W + nw - 1) / nw + 31) & ~31;
+    const int ww0 = min(W, warp * wper), ww1 = min(W, ww0 + wper);
+    int wpop = 0;
+    for (int base = ww0; base < ww1; base += 32) {
+        const int w = base + lane;
+        wpop += w < ww1 ? __popc(bm[w]) : 0;
+    }
+    wpop = warp_sum(wpop);
+    if (lane == 0) sm.red[warp] = wpop;
+    __syncthreads();
+    int at = 0, total = 0;
+    for (int i = 0; i < nw; ++i) {
+        const int c = sm.red[i];
+        at += i < warp ? c : 0;
+        total += c;
+    }
     int* dst = out_ids + (int64_t)u * out_stride;
     bool overflow = false;
-    for (int w = w0; w < w1; ++w) {
-        uint32_t m = bm[w];
+    for (int base = ww0; base < ww1; base += 32) {
+        const int w = base + lane;
+        uint32_t m = w < ww1 ? bm[w] : 0u;
+        const int c = __popc(m);
+        const int inc = warp_inclusive_scan(c);
+        int pos = at + inc - c;
         while (m) {
             const int bit = __ffs(m) - 1;
             m &= m - 1;
-            if (at < out_stride) dst[at] = w * 32 + bit;
+            if (pos < out_stride) dst[pos] = w * 32 + bit;
             else overflow = true;
-            ++at;
+            ++pos;
         }
+        at += __shfl_sync(0xffffffffu, inc, 31);
     }
     if (overflow && status) atomicOr(status, PK_STATUS_OUT_FULL);
     if (tid == 0) {
