@@ -887,7 +887,8 @@ def seqshard_measure(a, ctx) -> dict:
                    "tokens_per_shard": n_local, "build_s": round(build_s, 2),
                    "index_build": "exact BatchTopK over the whole sequence (build_sharded)",
                    "parallelism": f"seq{world}", "graph": graph[0] is not None,
-                   "collective": "one NCCL all-gather of the (m, l, o) partials per step" if world > 1 else None,
+                   "collective": ("NCCL all-gathers of the routing picks and of the (m, l, o) partials, one of each "
+                                  "per step") if world > 1 else None,
                    "l2": "KV rows gathered per step are scattered over >> L2"},
         "e2e": {"value": round(tokens / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(U * G * d * 2) * world, "d2h_bytes_per_step": int(U * G * d * 2) * world},
