@@ -67,6 +67,8 @@ def parse():
     p.add_argument("--parity-units", type=int, default=1,
                    help="units of layer 0 recomputed by the CPU oracle after timing (0: none)")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--exchange", choices=["p2p", "nccl"], default=None,
+                   help="config 4 on several GPUs: the step's all-gathers over NVLink peer memory (default) or NCCL")
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
 
@@ -801,7 +803,8 @@ def seqshard_measure(a, ctx) -> dict:
     for key in [k_ for k_ in ws.buffers if isinstance(k_, tuple) and k_[0] in ("build", "shard_build")]:
         del ws.buffers[key]
     torch.cuda.empty_cache()
-    sd = ShardedDecode(idx, sae, heads_per_unit=G, budget=budget, max_history=n_local, workspace=ws)
+    sd = ShardedDecode(idx, sae, heads_per_unit=G, budget=budget, max_history=n_local, workspace=ws,
+                       exchange=a.exchange)
     q_static = Q[0].clone()
     len_static = torch.full((U,), n_local + (1 if tail else 0), dtype=torch.int32, device=dev)
 
@@ -887,8 +890,9 @@ def seqshard_measure(a, ctx) -> dict:
                    "tokens_per_shard": n_local, "build_s": round(build_s, 2),
                    "index_build": "exact BatchTopK over the whole sequence (build_sharded)",
                    "parallelism": f"seq{world}", "graph": graph[0] is not None,
-                   "collective": ("NCCL all-gathers of the routing picks and of the (m, l, o) partials, one of each "
-                                  "per step") if world > 1 else None,
+                   "collective": (f"all-gathers of the routing picks and of the (m, l, o) partials, one of each "
+                                  f"per step, over {'NVLink peer memory (pk_p2p_allgather)' if sd.exchange == 'p2p' else 'NCCL'}")
+                                 if world > 1 else None,
                    "l2": "KV rows gathered per step are scattered over >> L2"},
         "e2e": {"value": round(tokens / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(U * G * d * 2) * world, "d2h_bytes_per_step": int(U * G * d * 2) * world},
@@ -896,6 +900,7 @@ def seqshard_measure(a, ctx) -> dict:
         "clocks": clocks.summary(t0, t1),
     }
     graph[0] = None   # a graph holding NCCL calls is released before the group
+    sd.close()        # the peer-memory exchanges (collective)
     del sd, idx, K, V
     torch.cuda.synchronize()
     torch.cuda.empty_cache()

@@ -52,6 +52,7 @@ extern "C" {
 #define PK_STATUS_OUT_FULL 16         /* union: output row too short            */
 #define PK_STATUS_HISTORY_TOO_LONG 32 /* union: history above max_history       */
 #define PK_STATUS_NEEDS_EXACT 64      /* build: bounds undecided, rerun exactly  */
+#define PK_STATUS_EXCHANGE_TIMEOUT 128 /* p2p all-gather: a peer never published */
 
 /* Element types. */
 #define PK_F32 0
@@ -196,6 +197,27 @@ int pk_sparse_av_append(uint64_t q, uint64_t k, uint64_t v, int dtype,
                         int U, int G, int d, int splits,
                         uint64_t workspace, uint64_t workspace_bytes,
                         uint64_t out, uint64_t partial, uint64_t k_new, uint64_t v_new, uint64_t stream);
+
+/* All-gather of a small device buffer between the P <= 8 ranks of one node
+ * over NVLink peer memory (no counterpart in the reference, which runs on
+ * one device; the exchange step of the sequence-sharded decode).  Each rank
+ * allocates an exchange region of pk_p2p_region_bytes(P, bytes) with
+ * pk_p2p_alloc (zeroed device memory), exports it with pk_p2p_handle (a
+ * 64-byte CUDA IPC handle), and opens every peer's with pk_p2p_open.
+ * pk_p2p_allgather then copies src[bytes] (16-byte multiple) of every rank
+ * into out[P, bytes] on every rank: peer_bases is a host array of the P
+ * regions' addresses as mapped here (its rank-th entry local_base).  Every
+ * rank must issue the same sequence of calls on its region.  A peer that
+ * does not publish within max_spins polls (~64 ns each) sets
+ * PK_STATUS_EXCHANGE_TIMEOUT in *status and the call completes. */
+size_t pk_p2p_region_bytes(int P, int64_t bytes);
+int pk_p2p_alloc(uint64_t bytes, uint64_t ptr_out);
+int pk_p2p_free(uint64_t ptr);
+int pk_p2p_handle(uint64_t ptr, uint64_t handle_out);
+int pk_p2p_open(uint64_t handle, uint64_t ptr_out);
+int pk_p2p_close(uint64_t ptr);
+int pk_p2p_allgather(uint64_t src, int64_t bytes, int rank, int P, uint64_t peer_bases, uint64_t local_base,
+                     uint64_t out, uint64_t status, int64_t max_spins, uint64_t stream);
 
 /* Log-sum-exp merge of P partial states partial[P, UG, d+2] (m, l, o[d]) into
  * out[UG, d] (dtype).  The cross-GPU step of the sequence-sharded decode;

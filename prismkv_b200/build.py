@@ -19,7 +19,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB = PKG / "libprismkv_b200.so"
-SOURCES = ["capi.cu", "route.cu", "union.cu", "sparse_av.cu", "build.cu", "layout.cu"]
+SOURCES = ["capi.cu", "route.cu", "union.cu", "sparse_av.cu", "build.cu", "layout.cu", "p2p.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--fmad=false", "-Xcompiler", "-fPIC", "--extended-lambda"]

@@ -20,6 +20,7 @@ PK_TERM_COUNT, PK_TERM_MEAN, PK_TERM_VARIANCE = 1, 2, 4
 STATUS_BUCKET_FULL, STATUS_BOUNDARY_FULL, STATUS_MEMBERS_FULL = 1, 2, 4
 STATUS_BUCKET_TOO_BIG, STATUS_OUT_FULL, STATUS_HISTORY_TOO_LONG = 8, 16, 32
 STATUS_NEEDS_EXACT = 64
+STATUS_EXCHANGE_TIMEOUT = 128
 STATUS_BITS = {
     1: "bucket region full (append)",
     2: "boundary buffer full (build)",
@@ -28,6 +29,7 @@ STATUS_BITS = {
     16: "union output row too short",
     32: "history longer than the union bitmap",
     64: "bounds could not bracket the threshold: exact build needed",
+    128: "peer exchange timed out: a rank did not publish its buffer",
 }
 
 # name: (argument codes including the trailing stream, restype).
@@ -50,6 +52,13 @@ SIGNATURES = {
     "pk_sparse_av": ("PPPiilllPlPPPiiiiPPPPP", ctypes.c_int),
     "pk_sparse_av_append": ("PPPiilllPlPPPiiiiPPPPPPP", ctypes.c_int),
     "pk_lse_merge": ("PiiiPiP", ctypes.c_int),
+    "pk_p2p_region_bytes": ("il", ctypes.c_size_t),
+    "pk_p2p_alloc": ("PP", ctypes.c_int),
+    "pk_p2p_free": ("P", ctypes.c_int),
+    "pk_p2p_handle": ("PP", ctypes.c_int),
+    "pk_p2p_open": ("PP", ctypes.c_int),
+    "pk_p2p_close": ("P", ctypes.c_int),
+    "pk_p2p_allgather": ("PliiPPPPlP", ctypes.c_int),
     "pk_gather_kv": ("PPiilllPlPPPiilPPPP", ctypes.c_int),
     "pk_kv_append": ("PPPPiilllPiiiP", ctypes.c_int),
     "pk_sparse_av_noalloc": ("PPPiilllPlPPPiiiiPP", ctypes.c_int),
@@ -70,7 +79,8 @@ SIGNATURES = {
 _CT = {"P": ctypes.c_uint64, "i": ctypes.c_int, "l": ctypes.c_int64, "f": ctypes.c_float, "d": ctypes.c_double}
 # Entry points that take the stream as their last argument.
 _ASYNC = {n for n, (c, r) in SIGNATURES.items() if r is ctypes.c_int and c.endswith("P") and n not in
-          ("pk_version", "pk_supported_head_dim", "pk_build_shard_layout")}
+          ("pk_version", "pk_supported_head_dim", "pk_build_shard_layout", "pk_p2p_alloc", "pk_p2p_free",
+           "pk_p2p_handle", "pk_p2p_open", "pk_p2p_close")}
 
 _lib = None
 

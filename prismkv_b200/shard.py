@@ -22,10 +22,14 @@ dense tail of generated tokens lives on the last rank.  One decode step is:
    reference's kernels (kernels/ppu_8b/av_tuned.cu) applied across ranks.
 
 The two all-gathers (routing picks, attention partials) are the only
-collectives on the path.
+exchanges on the path.  Between GPUs of one node they run over NVLink peer
+memory (``PeerExchange``: plain peer stores and one flag per rank, a kernel
+of the library); with exchange="nccl", or on CPU process groups, they are
+library all-gathers.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -104,6 +108,96 @@ def gather_partials(part: torch.Tensor, out: torch.Tensor, group=None) -> torch.
     else:
         dist.all_gather(list(out.unbind(0)), part, group=group)
     return out
+
+
+class PeerExchange:
+    """All-gather of a fixed-size device buffer between the P <= 8 ranks of
+    one node over NVLink peer memory (pk_p2p_allgather).  Each rank
+    allocates an exchange region in its own device memory and opens every
+    peer's through a CUDA IPC handle (handles are exchanged once, at
+    construction, over the process group).  ``all_gather(src, out)`` copies
+    every rank's ``src`` into ``out[P, ...]``: one kernel, graph-capturable,
+    no host synchronisation; every rank must make the same sequence of
+    calls.  A peer that does not publish within ``max_spins`` polls (~64 ns
+    each) sets a status bit that ``check()`` raises on."""
+
+    def __init__(self, nbytes: int, group=None, device=None, max_spins: int = 1 << 23):
+        if nbytes <= 0 or nbytes % 16:
+            raise ValueError("the exchanged buffer must be a positive multiple of 16 bytes")
+        self.group = group
+        self.P = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.P > 8:
+            raise ValueError("PeerExchange joins at most 8 ranks")
+        self.nbytes = int(nbytes)
+        self.max_spins = int(max_spins)
+        self.device = torch.device(device or "cuda")
+        region = int(nv.query("pk_p2p_region_bytes", self.P, self.nbytes))
+        ptr = ctypes.c_uint64(0)
+        with torch.cuda.device(self.device):
+            _check(nv.query("pk_p2p_alloc", region, ctypes.addressof(ptr)), "pk_p2p_alloc")
+        self.base = int(ptr.value)
+        self._opened = []
+        try:
+            handle = (ctypes.c_uint8 * 64)()
+            _check(nv.query("pk_p2p_handle", self.base, ctypes.addressof(handle)), "pk_p2p_handle")
+            handles = [bytes(handle)]
+            if self.P > 1:
+                handles = [None] * self.P
+                dist.all_gather_object(handles, bytes(handle), group=group)
+            bases = []
+            for q, h in enumerate(handles):
+                if q == self.rank:
+                    bases.append(self.base)
+                    continue
+                hb = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+                p = ctypes.c_uint64(0)
+                with torch.cuda.device(self.device):
+                    _check(nv.query("pk_p2p_open", ctypes.addressof(hb), ctypes.addressof(p)), "pk_p2p_open")
+                self._opened.append(int(p.value))
+                bases.append(int(p.value))
+        except Exception:
+            self.close(collective=False)
+            raise
+        self._bases = (ctypes.c_uint64 * self.P)(*bases)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def all_gather(self, src: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        if src.numel() * src.element_size() != self.nbytes or not src.is_contiguous():
+            raise ValueError(f"src must be a contiguous buffer of {self.nbytes} bytes")
+        if out.shape[0] != self.P or out.numel() * out.element_size() != self.P * self.nbytes \
+                or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous [{self.P}, ...] buffer of {self.P * self.nbytes} bytes")
+        nv.call("pk_p2p_allgather", src, self.nbytes, self.rank, self.P, ctypes.addressof(self._bases), self.base,
+                out, self.status, self.max_spins)
+        return out
+
+    def check(self) -> None:
+        nv.check_status(self.status, "peer exchange")
+
+    def close(self, collective: bool = True) -> None:
+        """Unmaps the peers' regions and frees this rank's: a collective call
+        (every rank, nothing in flight); the barriers keep any rank from
+        freeing its region while a peer may still write to it."""
+        if not getattr(self, "base", 0) and not getattr(self, "_opened", None):
+            return
+        torch.cuda.synchronize(self.device)
+        sync = collective and self.P > 1 and dist.is_initialized()
+        if sync:
+            dist.barrier(group=self.group)
+        for p in getattr(self, "_opened", []):
+            nv.query("pk_p2p_close", p)
+        self._opened = []
+        if sync:
+            dist.barrier(group=self.group)
+        if getattr(self, "base", 0):
+            nv.query("pk_p2p_free", self.base)
+            self.base = 0
+
+
+def _check(rc: int, what: str) -> None:
+    if rc:
+        raise RuntimeError(f"{what}: {'argument error' if rc < 0 else 'CUDA error'} {rc}")
 
 
 def shard_budget(budget, P: int):
@@ -187,7 +281,8 @@ class ShardedDecode:
     def __init__(self, local_index: DeviceIndex, sae, *, group=None, heads_per_unit: int = 4,
                  router: str = "q_activation", query_scale: float = 1.0, query_topk: int | None = None,
                  budget: int | None = None, splits: int | None = None, max_history: int | None = None,
-                 workspace: nv.Workspace | None = None, split_route: bool | None = None):
+                 workspace: nv.Workspace | None = None, split_route: bool | None = None,
+                 exchange: str | None = None):
         self.group = group
         init = dist.is_initialized()
         self.P = dist.get_world_size(group) if init else 1
@@ -218,6 +313,18 @@ class ShardedDecode:
             self.f_range = feature_ranges(self.op.F, self.P)[self.rank]
             self.picks = torch.empty(U * G, self.op.k, 2, dtype=torch.int32, device=dev)
             self.all_picks = torch.empty(self.P, U * G, self.op.k, 2, dtype=torch.int32, device=dev)
+        # The exchanges: NVLink peer memory between the GPUs of one node
+        # (default with more than one CUDA rank), or the group's all-gather.
+        if exchange is None:
+            exchange = "p2p" if self.P > 1 and dev.type == "cuda" and dist.get_backend(group) == "nccl" else "nccl"
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError("exchange must be 'p2p' or 'nccl'")
+        self.exchange = exchange
+        self._px_part = self._px_picks = None
+        if exchange == "p2p" and self.P > 1:
+            self._px_part = PeerExchange(self.part.numel() * 4, group, dev)
+            if self.split_route:
+                self._px_picks = PeerExchange(self.picks.numel() * 4, group, dev)
 
     @property
     def is_tail_rank(self) -> bool:
@@ -227,13 +334,19 @@ class ShardedDecode:
         U, G, d = self.op.U, self.op.G, self.op.d
         if self.split_route:
             self.op.route_shard_picks(q, *self.f_range, self.picks)
-            _gather(self.picks, self.all_picks, self.group)
+            if self._px_picks is not None:
+                self._px_picks.all_gather(self.picks, self.all_picks)
+            else:
+                _gather(self.picks, self.all_picks, self.group)
             self.op.route_merge(self.all_picks)
             self.op.union()
         else:
             self.op.route(q)
         self.op.attention(q, k, v, length=length, partial=self.part)
-        gather_partials(self.part, self.gathered, self.group)
+        if self._px_part is not None:
+            self._px_part.all_gather(self.part, self.gathered)
+        else:
+            gather_partials(self.part, self.gathered, self.group)
         if self.out is None or self.out.dtype != q.dtype:
             self.out = torch.empty(U, G, d, dtype=q.dtype, device=q.device)
         nv.call("pk_lse_merge", self.gathered, self.P, U * G, d, self.out, nv.dtype_code(q))
@@ -241,6 +354,16 @@ class ShardedDecode:
 
     def check(self) -> None:
         self.op.check()
+        for px in (self._px_part, self._px_picks):
+            if px is not None:
+                px.check()
+
+    def close(self) -> None:
+        """Releases the peer-memory exchanges (every rank, nothing in flight)."""
+        for px in (self._px_part, self._px_picks):
+            if px is not None:
+                px.close()
+        self._px_part = self._px_picks = None
 
 
 # ---------------------------------------------------------------------------
