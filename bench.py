@@ -69,6 +69,8 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--exchange", choices=["p2p", "nccl"], default=None,
                    help="config 4 on several GPUs: the step's all-gathers over NVLink peer memory (default) or NCCL")
+    p.add_argument("--split-route", action="store_true",
+                   help="config 4 on several GPUs: q_activation routing split by features over the ranks")
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
 
@@ -804,7 +806,7 @@ def seqshard_measure(a, ctx) -> dict:
         del ws.buffers[key]
     torch.cuda.empty_cache()
     sd = ShardedDecode(idx, sae, heads_per_unit=G, budget=budget, max_history=n_local, workspace=ws,
-                       exchange=a.exchange)
+                       exchange=a.exchange, split_route=a.split_route or None)
     q_static = Q[0].clone()
     len_static = torch.full((U,), n_local + (1 if tail else 0), dtype=torch.int32, device=dev)
 
@@ -889,9 +891,11 @@ def seqshard_measure(a, ctx) -> dict:
                    "budget": budget, "budget_per_shard": budget // world, "clusters": C,
                    "tokens_per_shard": n_local, "build_s": round(build_s, 2),
                    "index_build": "exact BatchTopK over the whole sequence (build_sharded)",
+                   "routing": "split by features over the ranks" if sd.split_route else "replicated on every rank",
                    "parallelism": f"seq{world}", "graph": graph[0] is not None,
-                   "collective": (f"all-gathers of the routing picks and of the (m, l, o) partials, one of each "
-                                  f"per step, over {'NVLink peer memory (pk_p2p_allgather)' if sd.exchange == 'p2p' else 'NCCL'}")
+                   "collective": (("all-gathers of the routing picks and of the (m, l, o) partials, one of each "
+                                   "per step" if sd.split_route else "one all-gather of the (m, l, o) partials per step")
+                                  + f", over {'NVLink peer memory (pk_p2p_allgather)' if sd.exchange == 'p2p' else 'NCCL'}")
                                  if world > 1 else None,
                    "l2": "KV rows gathered per step are scattered over >> L2"},
         "e2e": {"value": round(tokens / (e2e_ms / 1e3), 2), "unit": "tokens/s",

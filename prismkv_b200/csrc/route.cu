@@ -200,8 +200,10 @@ __device__ void head_picks(int G, int k, int m, QactSmem& sm, int* hid, float* h
     for (int r = tid; r < k; r += nt) {
         if (r < m) {
             const int f = sm.sel[r];
+            // Position in feature order (a repeated id, which only a
+            // malformed merge input can produce, takes the next slot).
             int pos = 0;
-            for (int r2 = 0; r2 < m; ++r2) pos += sm.sel[r2] < f;
+            for (int r2 = 0; r2 < m; ++r2) pos += sm.sel[r2] < f || (sm.sel[r2] == f && r2 < r);
             float v = __uint_as_float(sm.selkey[r]);
             v = __fdiv_rn(v, s);
             v = __fdiv_rn(v, (float)G);
@@ -281,7 +283,9 @@ __device__ int unit_rank(int u, int E, const float* sc, const int* cand, int e_l
                 const int f2 = cand[e2];
                 if (f2 < 0) continue;
                 const float v2 = sc[e2];
-                r += (v2 > v) || (v2 == v && f2 < f);
+                // (A repeated feature id, from a malformed merge input only,
+                // ranks by entry: the slots stay distinct.)
+                r += (v2 > v) || (v2 == v && (f2 < f || (f2 == f && e2 < e)));
             }
         }
         for (int o = 1; o < P; o <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
@@ -402,11 +406,18 @@ __device__ __forceinline__ float fkey_inv(uint32_t k) {
 }
 
 // Features per group for the routing threshold estimate: the largest of
-// 128..8 that still leaves at least k groups (at most kMaxGroups), 0 if none.
+// 128..8 that leaves at least 4k groups (the k-th largest group maximum is
+// then a tight threshold), else the smallest that leaves at least k groups,
+// at most kMaxGroups groups either way; 0 if none.
 __host__ __device__ __forceinline__ int select_group_size(int F, int k) {
-    for (int gs = 128; gs >= 8; gs >>= 1)
-        if ((F + gs - 1) / gs >= k && (F + gs - 1) / gs <= kMaxGroups) return gs;
-    return 0;
+    int best = 0;
+    for (int gs = 128; gs >= 8; gs >>= 1) {
+        const int ng = (F + gs - 1) / gs;
+        if (ng > kMaxGroups) break;
+        if (ng >= k) best = gs;
+        if (ng >= 4 * k) return gs;
+    }
+    return best;
 }
 
 // Eight consecutive query values as floats (16-byte bf16 or 2x16-byte fp32
@@ -950,31 +961,96 @@ qact_merge_kernel(const int* __restrict__ picks, int P, int G, int F, int k, con
     const int u = blockIdx.x / G, g = blockIdx.x % G;
     const int64_t n_heads = gridDim.x;
     const int n = P * k;
-    int npos = 0;
     for (int c = tid; c < n; c += nt) {
         const int r = c / k, j = c - r * k;
         const int* e = picks + (((int64_t)r * n_heads + blockIdx.x) * k + j) * 2;
-        const float v = __uint_as_float((uint32_t)__ldg(e));
-        sm.cval[c] = v;
+        sm.cval[c] = __uint_as_float((uint32_t)__ldg(e));
         sm.cand[c] = __ldg(e + 1);
-        npos += v > 0.f;
     }
-    npos = warp_sum(npos);
-    if (lane == 0) sm.wc[warp] = npos;
     __syncthreads();
-    int all_pos = 0;
-    for (int w = 0; w < nw; ++w) all_pos += sm.wc[w];
-    const int m = min(k, all_pos);
-    for (int c = tid; c < n; c += nt) {
-        const float vc = sm.cval[c];
-        if (!(vc > 0.f)) continue;
+    // An entry counts if its value is positive and its feature id lies in
+    // [0, F).  Each shard's list is in rank order (value descending,
+    // feature ascending) with its counting entries first, so an entry's rank
+    // over all lists is its position plus, per other list, a binary search
+    // for the entries ahead of it.  Lists that break that form -- only a
+    // malformed input can -- take the quadratic rank instead, whose order
+    // (value, feature, then entry) keeps the ranks of any input distinct, so
+    // the kernel's memory accesses never depend on a malformed input.
+    __shared__ int list_len[kCandCap / 8];   // counting entries per list (k >= 8)
+    __shared__ int malformed;
+    if (tid == 0) malformed = 0;
+    for (int r = tid; r < P; r += nt) list_len[r] = k;
+    __syncthreads();
+    auto counts_ = [&](int c) {
         const int fc = sm.cand[c];
-        int r = 0;
-        for (int j = 0; j < n; ++j) {
-            const float vj = sm.cval[j];
-            r += (vj > vc) || (vj == vc && sm.cand[j] < fc);
+        return sm.cval[c] > 0.f && fc >= 0 && fc < F;
+    };
+    for (int c = tid; c < n; c += nt) {
+        const int r = c / k, j = c - r * k;
+        const bool ok = counts_(c);
+        if (!ok) atomicMin(&list_len[r], j);
+        if (j + 1 < k) {
+            const bool okn = counts_(c + 1);
+            const float v = sm.cval[c], vn = sm.cval[c + 1];
+            const int f = sm.cand[c], fn = sm.cand[c + 1];
+            if (okn && (!ok || !(v > vn || (v == vn && f < fn)))) malformed = 1;
         }
-        if (r < m) { sm.q.sel[r] = fc; sm.q.selkey[r] = __float_as_uint(vc); }
+    }
+    __syncthreads();
+    int m;
+    if (!malformed) {
+        int all_pos = 0;
+        for (int r = 0; r < P; ++r) all_pos += list_len[r];
+        m = min(k, all_pos);
+        for (int c = tid; c < n; c += nt) {
+            const int r = c / k, j = c - r * k;
+            if (j >= list_len[r]) continue;
+            const float v = sm.cval[c];
+            const int f = sm.cand[c];
+            int rank = j;
+            for (int r2 = 0; r2 < P && rank < m; ++r2) {
+                if (r2 == r) continue;
+                const float* lv = sm.cval + r2 * k;
+                const int* lf = sm.cand + r2 * k;
+                int lo = 0, hi = list_len[r2];
+                while (lo < hi) {
+                    const int mid = (lo + hi) >> 1;
+                    const float ve = lv[mid];
+                    const int fe = lf[mid];
+                    if (ve > v || (ve == v && (fe < f || (fe == f && r2 < r)))) lo = mid + 1;
+                    else hi = mid;
+                }
+                rank += lo;
+            }
+            if (rank < m) { sm.q.sel[rank] = f; sm.q.selkey[rank] = __float_as_uint(v); }
+        }
+    } else {
+        int npos = 0;
+        for (int c = tid; c < n; c += nt) {
+            const bool ok = counts_(c);
+            npos += ok ? 1 : 0;
+        }
+        __syncthreads();
+        for (int c = tid; c < n; c += nt)
+            if (!counts_(c)) sm.cval[c] = 0.f;
+        npos = warp_sum(npos);
+        if (lane == 0) sm.wc[warp] = npos;
+        __syncthreads();
+        int all_pos = 0;
+        for (int w = 0; w < nw; ++w) all_pos += sm.wc[w];
+        m = min(k, all_pos);
+        for (int c = tid; c < n; c += nt) {
+            const float vc = sm.cval[c];
+            if (!(vc > 0.f)) continue;
+            const int fc = sm.cand[c];
+            int r = 0;
+            for (int j = 0; j < n; ++j) {
+                const float vj = sm.cval[j];
+                const int fj = sm.cand[j];
+                r += (vj > vc) || (vj == vc && (fj < fc || (fj == fc && j < c)));
+            }
+            if (r < m) { sm.q.sel[r] = fc; sm.q.selkey[r] = __float_as_uint(vc); }
+        }
     }
     __syncthreads();
     qact_unit_tail<kCluster>(u, g, G, F, k, m, sm, sA, counts, head_ids, head_val, unit_done, order, n_order,
@@ -1354,7 +1430,7 @@ extern "C" int pk_route_qact_merge(uint64_t picks, int P, uint64_t counts, int U
                                    uint64_t workspace, uint64_t workspace_bytes, uint64_t order, uint64_t n_order,
                                    int order_stride, uint64_t score, uint64_t stream) {
     if (P < 1 || U < 1 || G < 1 || F < 1 || k < 1) return PK_ERR_ARG;
-    if (G * k > 256 || order_stride < G * k || P * k > kCandCap) return PK_ERR_ARG;
+    if (G * k > 256 || order_stride < G * k || P * k > kCandCap || P > kCandCap / 8) return PK_ERR_ARG;
     if (workspace_bytes < pk_route_qact_merge_workspace_bytes(U, G, k)) return PK_ERR_WORKSPACE;
     if (!picks || !counts || !workspace || !order || !n_order) return PK_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;

@@ -128,7 +128,9 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
     const int* uid = ids + (int64_t)u * ids_stride;
     int* feat = features + (int64_t)u * order_stride;
 
-    for (int i = tid; i < W; i += nt) bm[i] = 0u;
+    // The bitmap's words, zeroed up to a multiple of 4 (the compaction reads
+    // 16 bytes at a time).
+    for (int i = tid; i < ((W + 3) & ~3); i += nt) bm[i] = 0u;
     for (int c = tid; c < n; c += nt) {
         const int b = order[(int64_t)u * order_stride + c];
         sm.cand_bucket[c] = b;
@@ -448,10 +450,27 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
             __syncthreads();
             const int nwin = sm.flags[1];
             if (nwin == 0) break;
+            // A list of at most 256 entries that is not staged stays in the
+            // counting warp's registers: if its bucket is accepted, that warp
+            // ORs it in without reading it again.
+            int tk[8];
             if (warp < nwin) {
                 const int c = sm.cand_pre_win[warp];
+                const int L = sm.cand_len[c];
                 int m = 0;
-                warp_tokens(c, [&](int t) { m += ((unsigned)t < (unsigned)H && !test_bit(bm, t)) ? 1 : 0; });
+                if (L <= 256 && !(c >= ws0 && c < ws1)) {
+                    const int* src = uid + sm.cand_start[c];
+#pragma unroll
+                    for (int b = 0; b < 8; ++b) {
+                        const int i = 32 * b + lane;
+                        tk[b] = i < L ? __ldg(src + i) : -1;
+                    }
+#pragma unroll
+                    for (int b = 0; b < 8; ++b)
+                        m += ((unsigned)tk[b] < (unsigned)H && !test_bit(bm, tk[b])) ? 1 : 0;
+                } else {
+                    warp_tokens(c, [&](int t) { m += ((unsigned)t < (unsigned)H && !test_bit(bm, t)) ? 1 : 0; });
+                }
                 m = warp_sum(m);
                 if (lane == 0) sm.newc[c] = m;
             }
@@ -467,6 +486,7 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
                 if (lane == 0) {
                     sm.flags[0] = fm ? sm.cand_pre_win[first_lane] : -1;
                     sm.flags[2] = sm.cand_pre_win[nwin - 1];
+                    sm.flags[3] = first_lane;
                 }
             }
             __syncthreads();
@@ -475,7 +495,16 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
                 cpos = sm.flags[2] + 1;
                 continue;
             }
-            or_bucket(c);
+            const int c_warp = sm.flags[3];
+            if (sm.cand_len[c] <= 256 && !(c >= ws0 && c < ws1)) {
+                if (warp == c_warp) {
+#pragma unroll
+                    for (int b = 0; b < 8; ++b)
+                        if ((unsigned)tk[b] < (unsigned)H) set_bit(bm, tk[b]);
+                }
+            } else {
+                or_bucket(c);
+            }
             count += sm.newc[c];
             raw_acc += sm.cand_len[c];
             if (tid == 0) feat[nf] = sm.cand_bucket[c];
@@ -486,15 +515,20 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
     }
     __syncthreads();
 
-    // Compaction: each warp owns a contiguous run of words, read 32
-    // consecutive words at a time (conflict-free); a count pass, the warps'
-    // offsets, then the emit pass in word order.
-    const int wper = ((W + nw - 1) / nw + 31) & ~31;
-    const int ww0 = min(W, warp * wper), ww1 = min(W, ww0 + wper);
+    // Compaction: each warp owns a contiguous run of words, each lane
+    // reading four consecutive words (16 bytes: conflict-free) of a
+    // 128-word chunk; a count pass, the warps' offsets, then the emit pass
+    // in word order.  Words past W are zero.
+    const int W4 = (W + 3) & ~3;
+    const int wper = ((W4 + nw - 1) / nw + 127) & ~127;
+    const int ww0 = min(W4, warp * wper), ww1 = min(W4, ww0 + wper);
     int wpop = 0;
-    for (int base = ww0; base < ww1; base += 32) {
-        const int w = base + lane;
-        wpop += w < ww1 ? __popc(bm[w]) : 0;
+    for (int base = ww0; base < ww1; base += 128) {
+        const int w = base + 4 * lane;
+        if (w < ww1) {
+            const uint4 m4 = *reinterpret_cast<const uint4*>(bm + w);
+            wpop += __popc(m4.x) + __popc(m4.y) + __popc(m4.z) + __popc(m4.w);
+        }
     }
     wpop = warp_sum(wpop);
     if (lane == 0) sm.red[warp] = wpop;
@@ -507,18 +541,23 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
     }
     int* dst = out_ids + (int64_t)u * out_stride;
     bool overflow = false;
-    for (int base = ww0; base < ww1; base += 32) {
-        const int w = base + lane;
-        uint32_t m = w < ww1 ? bm[w] : 0u;
-        const int c = __popc(m);
+    for (int base = ww0; base < ww1; base += 128) {
+        const int w = base + 4 * lane;
+        const uint4 m4 = w < ww1 ? *reinterpret_cast<const uint4*>(bm + w) : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t mw[4] = {m4.x, m4.y, m4.z, m4.w};
+        const int c = __popc(m4.x) + __popc(m4.y) + __popc(m4.z) + __popc(m4.w);
         const int inc = warp_inclusive_scan(c);
         int pos = at + inc - c;
-        while (m) {
-            const int bit = __ffs(m) - 1;
-            m &= m - 1;
-            if (pos < out_stride) dst[pos] = w * 32 + bit;
-            else overflow = true;
-            ++pos;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t m = mw[j];
+            while (m) {
+                const int bit = __ffs(m) - 1;
+                m &= m - 1;
+                if (pos < out_stride) dst[pos] = (w + j) * 32 + bit;
+                else overflow = true;
+                ++pos;
+            }
         }
         at += __shfl_sync(0xffffffffu, inc, 31);
     }

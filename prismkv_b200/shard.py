@@ -4,14 +4,16 @@ split along the token axis over the ranks of a process group.
 Rank r of P owns tokens [lo_r, hi_r) of the history (``token_ranges``); the
 dense tail of generated tokens lives on the last rank.  One decode step is:
 
-1. routing.  q_activation (core.py:131-139) is split by features: rank r
-   encodes the features of its range (``feature_ranges``) for every query
-   head and keeps each head's exact positive top-k among them; one
-   all-gather of those picks (a few KB) and an exact merge give every rank
-   the unsharded per-head top-k and the same order (bucket liveness is
-   local).  The moments router (core.py:117-130) runs replicated: it reads
-   the whole sequence's bucket moments and sizes (attach_global_moments), so
-   every rank takes the same buckets;
+1. routing, replicated on every rank by default (the q_activation scores
+   depend only on the query and the SAE, core.py:131-139, bucket liveness
+   being local; the moments router, core.py:117-130, reads the whole
+   sequence's bucket moments and sizes, attach_global_moments, so every rank
+   takes the same buckets).  With split_route=True, q_activation is split by
+   features instead: rank r encodes the features of its range
+   (``feature_ranges``) for every query head and keeps each head's exact
+   positive top-k among them; one all-gather of those picks (a few KB) and
+   an exact merge give every rank the unsharded per-head top-k and the same
+   order;
 2. the union of the routed buckets' shard-local lists (core.py:152-164) with
    the per-shard budget ``budget // P`` -- in the unbudgeted mode the shards'
    unions are exactly the global union cut at the shard boundaries;
@@ -302,10 +304,11 @@ class ShardedDecode:
         self.part = torch.empty(U * G, d + 2, dtype=torch.float32, device=dev)
         self.gathered = torch.empty(self.P, U * G, d + 2, dtype=torch.float32, device=dev)
         self.out = None
-        # q_activation routing split by features over the ranks (default
-        # with more than one rank); replicated otherwise.
+        # q_activation routing split by features over the ranks on request;
+        # replicated by default (measured faster on B200s at config 4: the
+        # split's merge and exchange cost more than the encode it saves).
         if split_route is None:
-            split_route = self.P > 1 and router == "q_activation" and self.op.prep[0] is not None
+            split_route = False
         if split_route and (router != "q_activation" or self.op.prep[0] is None):
             raise ValueError("split_route needs the bound-filtered q_activation router")
         self.split_route = bool(split_route)

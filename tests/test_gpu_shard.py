@@ -114,7 +114,8 @@ def _rank_main(rank, world, port, q, exchange="nccl"):
                            query_topk=c["k"])
         idx = pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=False)
         lo, hi = token_ranges(N, world)[rank]
-        sd = ShardedDecode(shard_index(idx, lo, hi), sae, heads_per_unit=G, budget=None, exchange=exchange)
+        sd = ShardedDecode(shard_index(idx, lo, hi), sae, heads_per_unit=G, budget=None, exchange=exchange,
+                           split_route=True)
         assert sd.exchange == exchange and sd.split_route
         rows = slice(lo, hi + c["tail"]) if sd.is_tail_rank else slice(lo, hi)
         Ks, Vs = K[:, rows].contiguous(), V[:, rows].contiguous()
@@ -473,3 +474,45 @@ def test_peer_exchange_single_rank_gathers_itself(pk):
             assert torch.equal(out[0], src)
     finally:
         px.close()
+
+
+def test_feature_split_merge_ignores_repeated_and_out_of_range_picks(pk):
+    """pk_route_qact_merge ignores ids outside [0, F), ranks a list out of
+    rank order by the quadratic path and ranks repeated ids without gaps
+    (the lists it expects are disjoint and in rank order; this keeps a
+    malformed input from steering its memory accesses): the picks of the
+    whole feature range followed by copies with their ids pushed out of
+    range, or reversed, merge into the one-device route's order, and the
+    same picks repeated three times merge without a fault."""
+    c = make_case(31)
+    U, N, G, d, F, k = c["U"], c["N"], c["G"], c["d"], c["F"], c["k"]
+    dev = torch.device("cuda")
+    K = torch.from_numpy(c["keys"]).to(dev).bfloat16()
+    Q = torch.from_numpy(c["q"]).to(dev).bfloat16().contiguous()
+    sae = pk.SAEParams(torch.from_numpy(c["W"]).to(dev), torch.zeros(F, device=dev), key_mean=8, query_topk=k)
+    idx = pk.DeviceIndex.build(K[:, :N], sae, 1.0, moments=False)
+    ref = pk.SparseDecode(idx, sae, heads_per_unit=G, budget=1500)
+    ref.route(Q)
+    op = pk.SparseDecode(idx, sae, heads_per_unit=G, budget=1500)
+    picks = torch.empty(U * G, k, 2, dtype=torch.int32, device=dev)
+    op.route_shard_picks(Q, 0, F, picks)
+    bad = picks.clone()
+    bad[..., 1] += F
+    worse = picks.clone()
+    worse[..., 1] = -worse[..., 1] - 1
+    op.route_merge(torch.stack([picks, bad, worse]).contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(op.n_order, ref.n_order)
+    for u in range(U):
+        n = int(ref.n_order[u])
+        assert torch.equal(op.order[u, :n], ref.order[u, :n]), u
+    # A list out of rank order takes the quadratic rank: the same order.
+    op.route_merge(picks.flip(1).contiguous().unsqueeze(0))
+    torch.cuda.synchronize()
+    assert torch.equal(op.n_order, ref.n_order)
+    for u in range(U):
+        n = int(ref.n_order[u])
+        assert torch.equal(op.order[u, :n], ref.order[u, :n]), u
+    op.route_merge(torch.stack([picks, picks, picks]).contiguous())
+    torch.cuda.synchronize()
+    assert bool((op.n_order >= 0).all()) and bool((op.n_order <= op.width).all())
