@@ -12,7 +12,10 @@
 // then ties at that value by ascending flat index, positives only.  The dot
 // products run as one sequential FMA chain over d, the order the reference's
 // F.linear takes for a many-row block, so memberships are bit-identical.
+#include <cstring>
+#include <cuda.h>
 #include <cuda_fp16.h>
+#include <cudaTypedefs.h>
 
 #include "common.cuh"
 #include "mma.cuh"
@@ -674,28 +677,31 @@ struct TileSample {
     int tb_stride, ft_stride;   // MODE 0: token blocks and feature tiles sampled
 };
 
-// The tile images the passes stream through shared memory, built once per
-// call: per 256-feature tile, W_half's rows in the tensor core's shared
-// memory layout (two 128-byte-swizzled K-atoms of 256 rows) and a side record
-// of the tile's norms, biases (zero past F) and, per 128 features, the
-// largest |W_f| and b_f for the epilogue's row tests.  W rows out of fp16
-// range raise PK_STATUS_NEEDS_EXACT.
+// Built once per call, per 256-feature tile: a side record of the tile's
+// norms, biases (zero past F) and, per 128 features, the largest |W_f| and
+// b_f for the epilogue's row tests; and, only when W_half cannot be loaded
+// through a tensor map, an image of its rows in the tensor core's shared
+// memory layout (two 128-byte-swizzled K-atoms of 256 rows).  W rows out of
+// fp16 range raise PK_STATUS_NEEDS_EXACT.
 constexpr int kTcFeat = 256;
 constexpr int kTcWBytes = kTcFeat * 256;            // 2 K-atoms x 256 rows x 128 B
 constexpr int kTcSideBytes = 2 * kTcFeat * 4 + 16;  // norms, biases, 2 x (max |W_f|, max b_f)
 
 __global__ void __launch_bounds__(256)
 build_tiles_kernel(const __half* __restrict__ Wh, const float* __restrict__ wn, const float* __restrict__ bias,
-                   int F, uint8_t* __restrict__ tiles, uint8_t* __restrict__ sides, int* __restrict__ status) {
+                   int F, uint8_t* __restrict__ tiles, uint8_t* __restrict__ sides, int* __restrict__ status,
+                   int write_images) {
     const int t = blockIdx.x, row = threadIdx.x, lane = row & 31, warp = row >> 5;
     const int f = t * kTcFeat + row;
     const bool valid = f < F;
-    uint8_t* img = tiles + (int64_t)t * kTcWBytes;
-    const uint4* src = reinterpret_cast<const uint4*>(Wh + (int64_t)(valid ? f : 0) * kBD);
+    if (write_images) {   // (not needed when the passes load W through a tensor map)
+        uint8_t* img = tiles + (int64_t)t * kTcWBytes;
+        const uint4* src = reinterpret_cast<const uint4*>(Wh + (int64_t)(valid ? f : 0) * kBD);
 #pragma unroll
-    for (int ch = 0; ch < 16; ++ch) {
-        const uint4 val = valid ? src[ch] : make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(img + (ch >> 3) * (kTcFeat * 128) + sw128_off(row, ch & 7)) = val;
+        for (int ch = 0; ch < 16; ++ch) {
+            const uint4 val = valid ? src[ch] : make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4*>(img + (ch >> 3) * (kTcFeat * 128) + sw128_off(row, ch & 7)) = val;
+        }
     }
     float* sw = reinterpret_cast<float*>(sides + (int64_t)t * kTcSideBytes);
     const float w = valid ? wn[f] : 0.f, b = valid ? bias[f] : -INFINITY;
@@ -721,8 +727,10 @@ build_tiles_kernel(const __half* __restrict__ Wh, const float* __restrict__ wn, 
 
 // The passes run on the 5th-generation tensor cores, one CTA per 128-token
 // block of a unit (one CTA per SM), warp-specialised:
-//   warp 8 (one thread): streams tile j's image and side record into
-//     shared-memory buffer j & 1 with two bulk copies, and issues the eight
+//   warp 8 (one thread): loads tile j's W rows straight from W_half with two
+//     tensor-map TMA boxes (the K-atoms, 128-byte swizzled by the copy
+//     engine) and its side record with a bulk copy into shared-memory buffer
+//     j & 1, and issues the eight
 //     K=16 MMAs of tile j into TMEM accumulator j & 1 once the copy has
 //     landed and the epilogue of tile j-2 has drained that accumulator;
 //   warps 0-15: the epilogue of tile j from TMEM -- one token row and 64
@@ -754,11 +762,20 @@ __host__ __device__ constexpr int tc_smem(int mode) {
            (mode == 0 ? kFBins * 4 : 2 * kFWin * 4) + 10 * 8 + 16 + (mode == 1 ? kTcStage * 16 : 0);
 }
 
+// The W operand's source: a tensor map over W_half [F, d] fp16 (the
+// tile's two 128-byte-swizzled K-atoms, 256 feature rows each, loaded by
+// the TMA straight into the tensor core's layout; rows past F are filled
+// with zeros), or, without one, the tile images of build_tiles_kernel.
+struct WSource {
+    CUtensorMap map;   // valid when use_map
+    int use_map;
+};
+
 template <int MODE, typename T>
 __global__ void __launch_bounds__(kTcThreads, 1)
 build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t row_stride, int64_t N,
                      const float* __restrict__ center, float key_scale, int F, FastWs fw, TileSample smp,
-                     int* __restrict__ status) {
+                     int* __restrict__ status, const __grid_constant__ WSource wsrc) {
     extern __shared__ uint8_t tc_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* Xs = base;
@@ -768,7 +785,7 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
     int* hA = reinterpret_cast<int*>(xn + kTcTokens);                        // MODE 0: [kFBins]; MODE 1: L [kFWin]
     int* hB = hA + kFWin;                                                    // MODE 1: U [kFWin]
     uint64_t* bars = reinterpret_cast<uint64_t*>(hA + (MODE == 0 ? kFBins : 2 * kFWin));
-    uint64_t* full = bars;          // [2] tile image landed
+    uint64_t* full = bars;          // [2] W tile landed
     uint64_t* mma_done = bars + 2;  // [2] MMAs of the tile complete
     uint64_t* tmem_empty = bars + 4; // [2] epilogue drained the accumulator
     uint64_t* side_full = bars + 6;  // [4] side record landed (slot j % 4)
@@ -793,7 +810,14 @@ build_tile_tc_kernel(const T* __restrict__ keys, int64_t unit_stride, int64_t ro
         const int t = ft_first + j * fstep;
         const uint32_t wbar = smem_addr(&full[j & 1]), sbar = smem_addr(&side_full[j % kTcSideSlots]);
         mbar_expect_tx(wbar, kTcWBytes);
-        bulk_g2s(smem_addr(Wt + (j & 1) * kTcWBytes), fw.tiles + (int64_t)t * kTcWBytes, kTcWBytes, wbar);
+        const uint32_t wdst = smem_addr(Wt + (j & 1) * kTcWBytes);
+        if (wsrc.use_map) {
+            // Two boxes of 64 fp16 x 256 rows: the K-atoms of d 0..63, 64..127.
+            tma_load_2d(wdst, &wsrc.map, 0, t * kTcFeat, wbar);
+            tma_load_2d(wdst + kTcFeat * 128, &wsrc.map, 64, t * kTcFeat, wbar);
+        } else {
+            bulk_g2s(wdst, fw.tiles + (int64_t)t * kTcWBytes, kTcWBytes, wbar);
+        }
         mbar_expect_tx(sbar, kTcSideBytes);
         bulk_g2s(smem_addr(side + (j % kTcSideSlots) * kTcSideBytes), fw.sides + (int64_t)t * kTcSideBytes,
                  kTcSideBytes, sbar);
@@ -1490,6 +1514,37 @@ TileSample sample_plan(int64_t N, int F, long long count, int* nsample_out) {
     return smp;
 }
 
+// A tensor map over W_half [F, d] fp16 (rows of 256 bytes, 16-byte aligned):
+// boxes of 64 x 256 with the 128-byte swizzle the MMA's K-major descriptors
+// read.  Encoded through the driver entry point (no link to libcuda);
+// use_map stays 0 when the entry point or the encode is refused, and the
+// kernels then copy build_tiles_kernel's images instead.
+static WSource make_wsource(const __half* Wh, int F) {
+    WSource w;
+    memset(&w, 0, sizeof(w));
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static bool looked_up = false;
+    if (!looked_up) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+        cudaGetLastError();
+        looked_up = true;
+    }
+    if (!encode || !Wh || (uintptr_t)Wh % 16 || F < 1) return w;
+    const cuuint64_t dims[2] = {(cuuint64_t)kBD, (cuuint64_t)F};
+    const cuuint64_t strides[1] = {(cuuint64_t)kBD * sizeof(__half)};
+    const cuuint32_t box[2] = {64, (cuuint32_t)kTcFeat};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(&w.map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)Wh, dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    w.use_map = r == CUDA_SUCCESS ? 1 : 0;
+    return w;
+}
+
 template <typename T>
 int run_encode_select_fast(const T* keys, int64_t unit_stride, int64_t row_stride, int64_t N, const float* center,
                            float key_scale, const float* W, const __half* Wh, const float* wn,
@@ -1504,17 +1559,18 @@ int run_encode_select_fast(const T* keys, int64_t unit_stride, int64_t row_strid
     const TileSample smp = sample_plan(N, F, count, &nsample);
     const double frac = fmin(1.0, (double)nsample * 128.0 / (double)N) / (double)smp.ft_stride;
     const TileSample none = {1, 1};
-    build_tiles_kernel<<<nft, 256, 0, st>>>(Wh, wn, b, F, fw.tiles, fw.sides, status);
+    const WSource wsrc = make_wsource(Wh, F);
+    build_tiles_kernel<<<nft, 256, 0, st>>>(Wh, wn, b, F, fw.tiles, fw.sides, status, !wsrc.use_map);
     PK_CHECK_LAUNCH();
     cudaFuncSetAttribute(build_tile_tc_kernel<0, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(0));
     cudaFuncSetAttribute(build_tile_tc_kernel<1, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(1));
     build_tile_tc_kernel<0, T><<<dim3(nsample, U), kTcThreads, tc_smem(0), st>>>(
-        keys, unit_stride, row_stride, N, center, key_scale, F, fw, smp, status);
+        keys, unit_stride, row_stride, N, center, key_scale, F, fw, smp, status, wsrc);
     PK_CHECK_LAUNCH();
     build_floor_kernel<<<U, 32, 0, st>>>(fw, count, frac);
     PK_CHECK_LAUNCH();
     build_tile_tc_kernel<1, T><<<dim3(nblocks, U), kTcThreads, tc_smem(1), st>>>(
-        keys, unit_stride, row_stride, N, center, key_scale, F, fw, none, status);
+        keys, unit_stride, row_stride, N, center, key_scale, F, fw, none, status, wsrc);
     PK_CHECK_LAUNCH();
     build_fast_cut_kernel<<<U, 32, 0, st>>>(fw, count, status);
     PK_CHECK_LAUNCH();
@@ -1820,11 +1876,12 @@ int shard_phase(int phase, const T* keys, int64_t us, int64_t rs, const float* c
         // The sample is planned on this shard's own share of the budget.
         int ns = 0;
         const TileSample plan = sample_plan(N, F, local_count, &ns);
-        build_tiles_kernel<<<nft, 256, 0, st>>>(Wh, wn, b, F, fw.tiles, fw.sides, status);
+        const WSource wsrc = make_wsource(Wh, F);
+        build_tiles_kernel<<<nft, 256, 0, st>>>(Wh, wn, b, F, fw.tiles, fw.sides, status, !wsrc.use_map);
         PK_CHECK_LAUNCH();
         cudaFuncSetAttribute(build_tile_tc_kernel<0, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(0));
         build_tile_tc_kernel<0, T><<<dim3(ns, U), kTcThreads, tc_smem(0), st>>>(
-            keys, us, rs, N, center, key_scale, F, fw, plan, status);
+            keys, us, rs, N, center, key_scale, F, fw, plan, status, wsrc);
         PK_CHECK_LAUNCH();
         set_ints_kernel<<<1, 1, 0, st>>>(sample_info, ns, plan.ft_stride);
         PK_CHECK_LAUNCH();
@@ -1836,7 +1893,7 @@ int shard_phase(int phase, const T* keys, int64_t us, int64_t rs, const float* c
         PK_CHECK_LAUNCH();
         cudaFuncSetAttribute(build_tile_tc_kernel<1, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(1));
         build_tile_tc_kernel<1, T><<<dim3(nblocks, U), kTcThreads, tc_smem(1), st>>>(
-            keys, us, rs, N, center, key_scale, F, fw, none, status);
+            keys, us, rs, N, center, key_scale, F, fw, none, status, make_wsource(Wh, F));
         PK_CHECK_LAUNCH();
         return PK_OK;
     }
