@@ -17,15 +17,16 @@
 //   2. after i*, the tail: each remaining bucket's count of tokens missing
 //      from the bitmap is taken once, and a chained hash maps every missing
 //      token to the tail entries that hold it.  The block then walks the
-//      buckets in order: the next bucket whose exact count fits is accepted,
-//      its tokens are turned on, and each token turned on decrements the
-//      counts of the later buckets holding it (one barrier per accepted
-//      bucket).  When the tail or the hash does not fit in shared memory,
-//      rounds run instead: the counts of the next 32 live buckets are
-//      retaken from the bitmap (a warp each), the first that fits is
-//      accepted, and a bucket whose count exceeds the remaining budget is
-//      dropped for good (its count can shrink by at most what the budget
-//      shrinks).
+//      buckets in order, a batch at a time: the next buckets whose exact
+//      counts fit, for as long as their summed counts fit too, are all
+//      accepted (each is what the one-at-a-time rule accepts), their tokens
+//      are turned on, and each token turned on decrements the counts of the
+//      later buckets holding it (two barriers per batch).  When the tail or
+//      the hash does not fit in shared memory, rounds run instead: the
+//      counts of the next 32 live buckets are retaken from the bitmap (a
+//      warp each) and a batch of them is accepted the same way.  A bucket
+//      whose count exceeds the remaining budget is dropped for good (its
+//      count can shrink by at most what the budget shrinks).
 #include "common.cuh"
 #include "mma.cuh"
 
@@ -45,6 +46,7 @@ struct UnionSmem {
     int cand_pre_win[32];         // the fallback rounds' window of live buckets
     int red[32];
     int flags[8];
+    int flip3[3];                 // accepted batches' new-token counts, rotating
     long long lred[2];
 };
 
@@ -384,55 +386,92 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
                 m = warp_sum(m);
                 if (lane == 0) sm.newc[c] = m;
             }
+            if (tid == 0) sm.flip3[0] = sm.flip3[1] = sm.flip3[2] = 0;
             __syncthreads();
-            // Every warp finds the same next bucket whose exact count fits
-            // (ballots over the counts), then the whole block adds its tokens
-            // and, for each token it turns on, decrements the counts of the
-            // later buckets holding it.  One barrier per accepted bucket: the
-            // decrements touch only buckets after it, so a warp still
-            // scanning for it finds the same bucket and reads its count
-            // unchanged.
+            // The walk accepts a batch of buckets per step: from c on, the
+            // buckets whose exact counts fit the room left (rem), in order,
+            // for as long as their summed counts fit rem too.  Each member is
+            // what the one-at-a-time rule accepts: at its turn its count is at
+            // most its count now (counts only shrink), and the room left is at
+            // least rem less the earlier members' counts now.  A bucket passed
+            // over because its count exceeds rem never fits later (a count
+            // shrinks by at most what the room shrinks).  Warp 0 finds the
+            // batch [c, cend); the block adds its tokens, and for each token
+            // it turns on decrements the counts of the buckets from cend on
+            // that hold it.  The members' counts are not touched meanwhile,
+            // so every thread tells a member by its count.  Two barriers per
+            // batch; the exact growth of the union is the number of bits the
+            // batch turned on.
             long long cnt = count;
-            for (int c = cpos; c < n; ++c) {
+            for (int c = cpos, it = 0; c < n; ++it) {
                 const long long rem = lim - cnt;
-                int next = n;
-                for (int b = c; b < n; b += 32) {
-                    const int cc = b + lane;
-                    const unsigned fm = __ballot_sync(0xffffffffu, cc < n && (long long)sm.newc[cc] <= rem);
-                    if (fm) {
-                        next = b + __ffs(fm) - 1;
-                        break;
+                if (warp == 0) {
+                    long long run = 0, radd = 0;
+                    int cend = n, nadd = 0;
+                    for (int b = c; b < n; b += 32) {
+                        const int cc = b + lane;
+                        const int v = cc < n ? sm.newc[cc] : 0;
+                        const bool fit = cc < n && (long long)v <= rem;
+                        long long x = fit ? v : 0;
+#pragma unroll
+                        for (int o = 1; o < 32; o <<= 1) {
+                            const long long y = __shfl_up_sync(0xffffffffu, x, o);
+                            if (lane >= o) x += y;
+                        }
+                        const unsigned stop = __ballot_sync(0xffffffffu, fit && run + x > rem);
+                        const unsigned below = stop ? (1u << (__ffs(stop) - 1)) - 1u : 0xffffffffu;
+                        const unsigned mem = __ballot_sync(0xffffffffu, fit) & below;
+                        const bool is_mem = (mem >> lane) & 1u;
+                        if (is_mem) feat[nf + nadd + __popc(mem & ((1u << lane) - 1u))] = sm.cand_bucket[cc];
+                        radd += warp_sum(is_mem ? (long long)sm.cand_len[cc] : 0ll);
+                        nadd += __popc(mem);
+                        if (stop) {
+                            cend = b + __ffs(stop) - 1;
+                            break;
+                        }
+                        run += __shfl_sync(0xffffffffu, x, 31);
                     }
-                }
-                if (next >= n) break;
-                c = next;
-                const int miss = sm.newc[c];
-                cnt += miss;
-                raw_acc += sm.cand_len[c];
-                if (tid == 0) feat[nf] = sm.cand_bucket[c];
-                ++nf;
-                const int L = sm.cand_len[c];
-                const int e0 = sm.cand_pre[c] - sm.cand_pre[cpos];
-                for (int i = tid; i < L; i += nt) {
-                    const uint32_t t = tail[e0 + i] & ~kFlipFlag;
-                    if (t >= (uint32_t)H) continue;
-                    const uint32_t bit = 1u << (t & 31);
-                    if (atomicOr(&bm[t >> 5], bit) & bit) continue;
-                    for (int e = heads[slot(t)]; e >= 0; e = nxt[e]) {
-                        const int oc = own[e];
-                        if (oc > c && (tail[e] & ~kFlipFlag) == t) atomicSub(&sm.newc[oc], 1);
+                    if (lane == 0) {
+                        sm.flags[4] = cend;
+                        sm.flags[5] = nadd;
+                        sm.lred[0] = radd;
                     }
                 }
                 __syncthreads();
+                const int cend = sm.flags[4];
+                nf += sm.flags[5];
+                raw_acc += sm.lred[0];
+                int flips = 0;
+                const int e_lo = sm.cand_pre[c] - sm.cand_pre[cpos], e_hi = sm.cand_pre[cend] - sm.cand_pre[cpos];
+                for (int e = e_lo + tid; e < e_hi; e += nt) {
+                    const uint32_t t = tail[e] & ~kFlipFlag;
+                    if (t >= (uint32_t)H) continue;
+                    const uint32_t bit = 1u << (t & 31);
+                    // A bit still off was off when the counts were taken, so
+                    // the entry is chained and own[e] names its bucket.
+                    if (bm[t >> 5] & bit) continue;
+                    if ((long long)sm.newc[own[e]] > rem) continue;
+                    if (atomicOr(&bm[t >> 5], bit) & bit) continue;
+                    ++flips;
+                    for (int ce = heads[slot(t)]; ce >= 0; ce = nxt[ce]) {
+                        const int oc = own[ce];
+                        if (oc >= cend && (tail[ce] & ~kFlipFlag) == t) atomicSub(&sm.newc[oc], 1);
+                    }
+                }
+                flips = warp_sum(flips);
+                if (lane == 0 && flips) atomicAdd(&sm.flip3[it % 3], flips);
+                if (tid == 0) sm.flip3[(it + 1) % 3] = 0;
+                __syncthreads();
+                cnt += sm.flip3[it % 3];
+                c = cend;
             }
             cpos = n;
         }
         // Rounds over a window of the next nw live buckets (one warp each):
-        // their exact counts against the bitmap, then the first that fits is
-        // accepted and the next window starts after it.  Every window member
-        // over the budget is dropped for good: a count shrinks by at most
-        // what the remaining budget shrinks, so a bucket over the budget now
-        // never fits later.
+        // their exact counts against the bitmap, then a batch of those that
+        // fit is accepted.  Every window member over the budget is dropped
+        // for good: a count shrinks by at most what the remaining budget
+        // shrinks, so a bucket over the budget now never fits later.
         while (cpos < n) {
             if (warp == 0) {
                 // The window: the next nw buckets from cpos that are not dead.
@@ -474,43 +513,68 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
                 m = warp_sum(m);
                 if (lane == 0) sm.newc[c] = m;
             }
+            if (tid == 0) sm.flip3[0] = 0;
             __syncthreads();
+            // The batch, as in the walk: the window's buckets that fit, in
+            // order, while their summed counts fit the room left.  Members
+            // over the room are dropped for good; the next window starts at
+            // the first bucket that fits alone but not after the batch.
             if (warp == 0) {
                 const long long rem = lim - count;
                 const int c = lane < nwin ? sm.cand_pre_win[lane] : n;
-                const bool fits = lane < nwin && (long long)sm.newc[c] <= rem;
-                const unsigned fm = __ballot_sync(0xffffffffu, fits);
-                const int first_lane = fm ? __ffs(fm) - 1 : nwin;
-                // Window members over the budget are dropped.
-                if (lane < nwin && !fits) sm.dead[c] = 1;
-                if (lane == 0) {
-                    sm.flags[0] = fm ? sm.cand_pre_win[first_lane] : -1;
-                    sm.flags[2] = sm.cand_pre_win[nwin - 1];
-                    sm.flags[3] = first_lane;
-                }
-            }
-            __syncthreads();
-            const int c = sm.flags[0];
-            if (c < 0) {
-                cpos = sm.flags[2] + 1;
-                continue;
-            }
-            const int c_warp = sm.flags[3];
-            if (sm.cand_len[c] <= 256 && !(c >= ws0 && c < ws1)) {
-                if (warp == c_warp) {
+                const int v = lane < nwin ? sm.newc[c] : 0;
+                const bool fits = lane < nwin && (long long)v <= rem;
+                long long x = fits ? v : 0;
 #pragma unroll
-                    for (int b = 0; b < 8; ++b)
-                        if ((unsigned)tk[b] < (unsigned)H) set_bit(bm, tk[b]);
+                for (int o = 1; o < 32; o <<= 1) {
+                    const long long y = __shfl_up_sync(0xffffffffu, x, o);
+                    if (lane >= o) x += y;
                 }
-            } else {
-                or_bucket(c);
+                const unsigned stop = __ballot_sync(0xffffffffu, fits && x > rem);
+                const unsigned below = stop ? (1u << (__ffs(stop) - 1)) - 1u : 0xffffffffu;
+                const unsigned mem = __ballot_sync(0xffffffffu, fits) & below;
+                const bool is_mem = (mem >> lane) & 1u;
+                if (lane < nwin && !fits) sm.dead[c] = 1;
+                if (is_mem) feat[nf + __popc(mem & ((1u << lane) - 1u))] = sm.cand_bucket[c];
+                const long long radd = warp_sum(is_mem ? (long long)sm.cand_len[c] : 0ll);
+                if (lane == 0) {
+                    sm.flags[0] = (int)mem;
+                    sm.flags[2] = stop ? sm.cand_pre_win[__ffs(stop) - 1] : sm.cand_pre_win[nwin - 1] + 1;
+                    sm.lred[0] = radd;
+                }
             }
-            count += sm.newc[c];
-            raw_acc += sm.cand_len[c];
-            if (tid == 0) feat[nf] = sm.cand_bucket[c];
-            ++nf;
-            cpos = c + 1;
             __syncthreads();
+            const unsigned mem = (unsigned)sm.flags[0];
+            nf += __popc(mem);
+            raw_acc += sm.lred[0];
+            cpos = sm.flags[2];
+            // Members of at most 256 entries that are not staged are ORed by
+            // the warp holding them; longer ones by the whole block.
+            int flips = 0;
+            auto flip = [&](int t) {
+                if ((unsigned)t < (unsigned)H) {
+                    const uint32_t bit = 1u << (t & 31);
+                    flips += (atomicOr(&bm[t >> 5], bit) & bit) ? 0 : 1;
+                }
+            };
+            auto held = [&](int c) { return sm.cand_len[c] <= 256 && !(c >= ws0 && c < ws1); };
+            if (warp < nwin && ((mem >> warp) & 1u)) {
+                const int c = sm.cand_pre_win[warp];
+                if (held(c) && sm.newc[c] > 0) {
+#pragma unroll
+                    for (int b = 0; b < 8; ++b) flip(tk[b]);
+                }
+            }
+            for (unsigned rest = mem; rest; rest &= rest - 1) {
+                const int c = sm.cand_pre_win[__ffs(rest) - 1];
+                if (held(c) || sm.newc[c] == 0) continue;
+                const int L = sm.cand_len[c];
+                for (int i = tid; i < L; i += nt) flip(token(c, i));
+            }
+            flips = warp_sum(flips);
+            if (lane == 0 && flips) atomicAdd(&sm.flip3[0], flips);
+            __syncthreads();
+            count += sm.flip3[0];
         }
     }
     __syncthreads();
