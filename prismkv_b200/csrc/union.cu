@@ -42,12 +42,11 @@ struct UnionSmem {
     int cand_len[kMaxCand];
     int cand_pre[kMaxCand + 1];   // exclusive prefix of the list lengths
     int newc[kMaxCand];
-    unsigned char dead[kMaxCand];
+    unsigned char dead[kMaxCand]; // 1: dropped for good; 2: accepted by the walk or a round
     int cand_pre_win[32];         // the fallback rounds' window of live buckets
     int red[32];
     int flags[8];
     int flip3[3];                 // accepted batches' new-token counts, rotating
-    long long lred[2];
 };
 
 __device__ __forceinline__ bool test_bit(const uint32_t* bm, int t) { return (bm[t >> 5] >> (t & 31)) & 1u; }
@@ -63,6 +62,49 @@ __device__ __forceinline__ int block_sum(int v, int* red) {
     int s = 0;
     for (int w = 0; w < nw; ++w) s += red[w];
     return s;
+}
+
+// One block of 32 consecutive candidates of a batch (lane = candidate):
+// fit says the candidate's count v fits the room rem.  Returns the members:
+// the fitting lanes before the first fitting lane at which the running sum
+// of the fitting counts (run, carried across blocks, equal in every lane)
+// exceeds rem; stop_lane is that lane, or -1 when the whole block joins.
+// Counts below 2^26 take 32-bit reductions (a block whose fitting counts
+// all fit needs no scan).
+__device__ __forceinline__ unsigned batch_block(bool fit, int v, long long rem, long long& run, int& stop_lane) {
+    const int lane = threadIdx.x & 31;
+    const unsigned fm = __ballot_sync(0xffffffffu, fit);
+    unsigned st;
+    if (rem < (1ll << 26)) {
+        const unsigned tot = __reduce_add_sync(0xffffffffu, fit ? (unsigned)v : 0u);
+        if (run + (long long)tot <= rem) {
+            run += tot;
+            stop_lane = -1;
+            return fm;
+        }
+        int x = fit ? v : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        st = __ballot_sync(0xffffffffu, fit && run + x > rem);
+    } else {
+        long long x = fit ? v : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const long long y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        st = __ballot_sync(0xffffffffu, fit && run + x > rem);
+        if (!st) {
+            run += __shfl_sync(0xffffffffu, x, 31);
+            stop_lane = -1;
+            return fm;
+        }
+    }
+    stop_lane = __ffs(st) - 1;
+    return fm & ((1u << stop_lane) - 1u);
 }
 
 struct UnionArgs {
@@ -406,41 +448,31 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
             for (int c = cpos, it = 0; c < n; ++it) {
                 const long long rem = lim - cnt;
                 if (warp == 0) {
-                    long long run = 0, radd = 0;
+                    long long run = 0;
                     int cend = n, nadd = 0;
                     for (int b = c; b < n; b += 32) {
                         const int cc = b + lane;
                         const int v = cc < n ? sm.newc[cc] : 0;
-                        const bool fit = cc < n && (long long)v <= rem;
-                        long long x = fit ? v : 0;
-#pragma unroll
-                        for (int o = 1; o < 32; o <<= 1) {
-                            const long long y = __shfl_up_sync(0xffffffffu, x, o);
-                            if (lane >= o) x += y;
+                        int stop_lane;
+                        const unsigned mem = batch_block(cc < n && (long long)v <= rem, v, rem, run, stop_lane);
+                        if ((mem >> lane) & 1u) {
+                            feat[nf + nadd + __popc(mem & ((1u << lane) - 1u))] = sm.cand_bucket[cc];
+                            sm.dead[cc] = 2;
                         }
-                        const unsigned stop = __ballot_sync(0xffffffffu, fit && run + x > rem);
-                        const unsigned below = stop ? (1u << (__ffs(stop) - 1)) - 1u : 0xffffffffu;
-                        const unsigned mem = __ballot_sync(0xffffffffu, fit) & below;
-                        const bool is_mem = (mem >> lane) & 1u;
-                        if (is_mem) feat[nf + nadd + __popc(mem & ((1u << lane) - 1u))] = sm.cand_bucket[cc];
-                        radd += warp_sum(is_mem ? (long long)sm.cand_len[cc] : 0ll);
                         nadd += __popc(mem);
-                        if (stop) {
-                            cend = b + __ffs(stop) - 1;
+                        if (stop_lane >= 0) {
+                            cend = b + stop_lane;
                             break;
                         }
-                        run += __shfl_sync(0xffffffffu, x, 31);
                     }
                     if (lane == 0) {
                         sm.flags[4] = cend;
                         sm.flags[5] = nadd;
-                        sm.lred[0] = radd;
                     }
                 }
                 __syncthreads();
                 const int cend = sm.flags[4];
                 nf += sm.flags[5];
-                raw_acc += sm.lred[0];
                 int flips = 0;
                 const int e_lo = sm.cand_pre[c] - sm.cand_pre[cpos], e_hi = sm.cand_pre[cend] - sm.cand_pre[cpos];
                 for (int e = e_lo + tid; e < e_hi; e += nt) {
@@ -524,29 +556,22 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
                 const int c = lane < nwin ? sm.cand_pre_win[lane] : n;
                 const int v = lane < nwin ? sm.newc[c] : 0;
                 const bool fits = lane < nwin && (long long)v <= rem;
-                long long x = fits ? v : 0;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const long long y = __shfl_up_sync(0xffffffffu, x, o);
-                    if (lane >= o) x += y;
-                }
-                const unsigned stop = __ballot_sync(0xffffffffu, fits && x > rem);
-                const unsigned below = stop ? (1u << (__ffs(stop) - 1)) - 1u : 0xffffffffu;
-                const unsigned mem = __ballot_sync(0xffffffffu, fits) & below;
-                const bool is_mem = (mem >> lane) & 1u;
+                long long run = 0;
+                int stop_lane;
+                const unsigned mem = batch_block(fits, v, rem, run, stop_lane);
                 if (lane < nwin && !fits) sm.dead[c] = 1;
-                if (is_mem) feat[nf + __popc(mem & ((1u << lane) - 1u))] = sm.cand_bucket[c];
-                const long long radd = warp_sum(is_mem ? (long long)sm.cand_len[c] : 0ll);
+                if ((mem >> lane) & 1u) {
+                    feat[nf + __popc(mem & ((1u << lane) - 1u))] = sm.cand_bucket[c];
+                    sm.dead[c] = 2;
+                }
                 if (lane == 0) {
                     sm.flags[0] = (int)mem;
-                    sm.flags[2] = stop ? sm.cand_pre_win[__ffs(stop) - 1] : sm.cand_pre_win[nwin - 1] + 1;
-                    sm.lred[0] = radd;
+                    sm.flags[2] = stop_lane >= 0 ? sm.cand_pre_win[stop_lane] : sm.cand_pre_win[nwin - 1] + 1;
                 }
             }
             __syncthreads();
             const unsigned mem = (unsigned)sm.flags[0];
             nf += __popc(mem);
-            raw_acc += sm.lred[0];
             cpos = sm.flags[2];
             // Members of at most 256 entries that are not staged are ORed by
             // the warp holding them; longer ones by the whole block.
@@ -626,6 +651,13 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
         at += __shfl_sync(0xffffffffu, inc, 31);
     }
     if (overflow && status) atomicOr(status, PK_STATUS_OUT_FULL);
+    if (warp == 0) {
+        // Raw sizes of the buckets the walk or the rounds accepted (marked 2).
+        long long r = 0;
+        for (int c = lane; c < n; c += 32)
+            if (sm.dead[c] == 2) r += sm.cand_len[c];
+        raw_acc += warp_sum(r);
+    }
     if (tid == 0) {
         out_count[u] = total;
         n_features[u] = nf;
