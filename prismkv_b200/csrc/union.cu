@@ -44,7 +44,7 @@ struct UnionSmem {
     int newc[kMaxCand];
     unsigned char dead[kMaxCand]; // 1: dropped for good; 2: accepted by the walk or a round
     int cand_pre_win[32];         // the fallback rounds' window of live buckets
-    int red[32];
+    int red[64];
     int flags[8];
     int flip3[3];                 // accepted batches' new-token counts, rotating
 };
@@ -52,16 +52,18 @@ struct UnionSmem {
 __device__ __forceinline__ bool test_bit(const uint32_t* bm, int t) { return (bm[t >> 5] >> (t & 31)) & 1u; }
 __device__ __forceinline__ void set_bit(uint32_t* bm, int t) { atomicOr(&bm[t >> 5], 1u << (t & 31)); }
 
-// Sum of one int per thread, returned to every thread (two barriers).
-__device__ __forceinline__ int block_sum(int v, int* red) {
+// Sum of one non-negative int per thread, returned to every thread: one
+// barrier, the warps' sums alternating between two halves of red[64] (a
+// half is written again only two calls later, after every thread passed
+// the barrier of the call in between).
+__device__ __forceinline__ int block_sum(int v, int* red, int& parity) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    v = warp_sum(v);
+    int* half = red + 32 * parity;
+    parity ^= 1;
+    v = (int)__reduce_add_sync(0xffffffffu, (unsigned)v);
+    if (lane == 0) half[warp] = v;
     __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    int s = 0;
-    for (int w = 0; w < nw; ++w) s += red[w];
-    return s;
+    return (int)__reduce_add_sync(0xffffffffu, lane < nw ? (unsigned)half[lane] : 0u);
 }
 
 // One block of 32 consecutive candidates of a batch (lane = candidate):
@@ -153,6 +155,7 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
     const int tid = threadIdx.x, nt = blockDim.x;
     const int lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
     const int H = history[u];
+    int red_parity = 0;   // block_sum's half of sm.red
     if (H > max_history || H < 0) {
         // The bitmap was sized for max_history: refuse rather than truncate.
         if (tid == 0) {
@@ -237,7 +240,7 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
             const int t = token(c, i);
             m += ((unsigned)t < (unsigned)H && !test_bit(bm, t)) ? 1 : 0;
         }
-        return block_sum(m, sm.red);
+        return block_sum(m, sm.red, red_parity);
     };
     auto or_bucket = [&](int c) {
         const int L = sm.cand_len[c];
@@ -297,14 +300,21 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
             }
         }
         int flips = 0;
-        for (int c = warp; c < sure; c += nw)
-            warp_tokens(c, [&](int t) {
-                if ((unsigned)t < (unsigned)H) {
-                    const uint32_t bit = 1u << (t & 31);
-                    flips += (atomicOr(&bm[t >> 5], bit) & bit) ? 0 : 1;
-                }
-            });
-        long long count = block_sum(flips, sm.red);
+        auto flip = [&](int t) {
+            if ((unsigned)t < (unsigned)H) {
+                const uint32_t bit = 1u << (t & 31);
+                flips += (atomicOr(&bm[t >> 5], bit) & bit) ? 0 : 1;
+            }
+        };
+        if (ws0 == 0 && sure <= ws1) {
+            // Staged: the prefix's entries are one contiguous run, shared
+            // evenly by all threads (a long list is not left to one warp).
+            const int e1 = sm.cand_pre[sure];
+            for (int e = tid; e < e1; e += nt) flip((int)(stage[e] & ~kFlipFlag));
+        } else {
+            for (int c = warp; c < sure; c += nw) warp_tokens(c, flip);
+        }
+        long long count = block_sum(flips, sm.red, red_parity);
         // Galloping probes from there; the first range is sized by the
         // overlap seen so far (tokens per listed entry).
         int lo = sure, fail_hi = n + 1, istar = n;
@@ -362,7 +372,7 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
                         }
                     }
                 }
-                const int m = block_sum(flips, sm.red);
+                const int m = block_sum(flips, sm.red, red_parity);
                 if (count + m <= lim) {
                     count += m;
                     lo = hi;
@@ -413,20 +423,36 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
             for (int i = tid; i < (1 << hb_bits); i += nt) heads[i] = -1;
             __syncthreads();
             auto slot = [&](uint32_t t) { return (int)((t * 2654435761u) >> (32 - hb_bits)); };
+            // Every entry's bucket (own), and the counts zeroed; then one
+            // flat pass over the tail's entries shared evenly by all threads:
+            // an entry whose token is missing is chained, and the lanes of a
+            // warp holding entries of one bucket add their missing tokens to
+            // its count with one shared-memory atomic.
             for (int c = cpos + warp; c < n; c += nw) {
                 const int L = sm.cand_len[c];
                 const int e0 = sm.cand_pre[c] - sm.cand_pre[cpos];
-                int m = 0;
-                for (int i = lane; i < L; i += 32) {
-                    const uint32_t t = tail[e0 + i] & ~kFlipFlag;
+                for (int i = lane; i < L; i += 32) own[e0 + i] = (unsigned char)c;
+                if (lane == 0) sm.newc[c] = 0;
+            }
+            __syncthreads();
+            for (int base = warp * 32; base < T; base += nt) {
+                const int e = base + lane;
+                int c = -1;
+                bool miss = false;
+                if (e < T) {
+                    c = own[e];
+                    const uint32_t t = tail[e] & ~kFlipFlag;
                     if (t < (uint32_t)H && !test_bit(bm, (int)t)) {
-                        ++m;
-                        own[e0 + i] = (unsigned char)c;
-                        nxt[e0 + i] = atomicExch(&heads[slot(t)], e0 + i);
+                        miss = true;
+                        nxt[e] = atomicExch(&heads[slot(t)], e);
                     }
                 }
-                m = warp_sum(m);
-                if (lane == 0) sm.newc[c] = m;
+                const unsigned grp = __match_any_sync(0xffffffffu, c);
+                const unsigned mm = __ballot_sync(0xffffffffu, miss);
+                if (c >= 0 && lane == __ffs(grp) - 1) {
+                    const int k2 = __popc(grp & mm);
+                    if (k2) atomicAdd(&sm.newc[c], k2);
+                }
             }
             if (tid == 0) sm.flip3[0] = sm.flip3[1] = sm.flip3[2] = 0;
             __syncthreads();
@@ -622,12 +648,9 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
     wpop = warp_sum(wpop);
     if (lane == 0) sm.red[warp] = wpop;
     __syncthreads();
-    int at = 0, total = 0;
-    for (int i = 0; i < nw; ++i) {
-        const int c = sm.red[i];
-        at += i < warp ? c : 0;
-        total += c;
-    }
+    const int cw = lane < nw ? sm.red[lane] : 0;
+    int at = (int)__reduce_add_sync(0xffffffffu, lane < warp ? (unsigned)cw : 0u);
+    const int total = (int)__reduce_add_sync(0xffffffffu, (unsigned)cw);
     int* dst = out_ids + (int64_t)u * out_stride;
     bool overflow = false;
     for (int base = ww0; base < ww1; base += 128) {
