@@ -44,6 +44,7 @@ struct UnionSmem {
     int newc[kMaxCand];
     unsigned char dead[kMaxCand]; // 1: dropped for good; 2: accepted by the walk or a round
     int cand_pre_win[32];         // the fallback rounds' window of live buckets
+    int win_pre[33];              // exclusive prefix of the window lists' 256-entry chunks
     int red[64];
     int flags[8];
     int flip3[3];                 // accepted batches' new-token counts, rotating
@@ -525,51 +526,86 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
             }
             cpos = n;
         }
-        // Rounds over a window of the next nw live buckets (one warp each):
-        // their exact counts against the bitmap, then a batch of those that
-        // fit is accepted.  Every window member over the budget is dropped
-        // for good: a count shrinks by at most what the remaining budget
-        // shrinks, so a bucket over the budget now never fits later.
+        // Rounds over a window of the next 32 live buckets: their exact
+        // counts against the bitmap, then a batch of those that fit is
+        // accepted.  Every window member over the budget is dropped for good:
+        // a count shrinks by at most what the remaining budget shrinks, so a
+        // bucket over the budget now never fits later.  The window's lists
+        // are cut into chunks of 256 entries dealt to the warps (a long list
+        // is shared by several warps); a chunk's tokens are read eight a lane
+        // at a time and, when every warp holds at most one chunk, kept in
+        // registers for the accepted buckets' OR.
         while (cpos < n) {
             if (warp == 0) {
-                // The window: the next nw buckets from cpos that are not dead.
+                // The window: the next 32 buckets from cpos that are not dead,
+                // their chunk counts' prefix, their counts zeroed.
                 int got = 0;
-                for (int base = cpos; base < n && got < nw; base += 32) {
+                for (int base = cpos; base < n && got < 32; base += 32) {
                     const int c = base + lane;
                     const bool live = c < n && !sm.dead[c];
                     const unsigned lm = __ballot_sync(0xffffffffu, live);
                     const int at = got + __popc(lm & ((1u << lane) - 1u));
-                    if (live && at < nw) sm.cand_pre_win[at] = c;
+                    if (live && at < 32) sm.cand_pre_win[at] = c;
                     got += __popc(lm);
                 }
-                if (lane == 0) sm.flags[1] = min(got, nw);
+                const int nwin = min(got, 32);
+                __syncwarp();
+                const int c = lane < nwin ? sm.cand_pre_win[lane] : -1;
+                const int nch = c >= 0 ? (sm.cand_len[c] + 255) >> 8 : 0;
+                sm.win_pre[lane + 1] = warp_inclusive_scan(nch);
+                if (c >= 0) sm.newc[c] = 0;
+                if (lane == 0) {
+                    sm.win_pre[0] = 0;
+                    sm.flags[1] = nwin;
+                }
             }
             __syncthreads();
             const int nwin = sm.flags[1];
             if (nwin == 0) break;
-            // A list of at most 256 entries that is not staged stays in the
-            // counting warp's registers: if its bucket is accepted, that warp
-            // ORs it in without reading it again.
-            int tk[8];
-            if (warp < nwin) {
-                const int c = sm.cand_pre_win[warp];
+            const int nchunks = sm.win_pre[nwin];
+            // Window slot of chunk q: the last slot whose chunks start at or
+            // before q (slots without entries own no chunk).
+            auto chunk_slot = [&](int q) {
+                int lo = 0, hi = nwin;
+                while (hi - lo > 1) {
+                    const int mid = (lo + hi) >> 1;
+                    if (sm.win_pre[mid] <= q) lo = mid;
+                    else hi = mid;
+                }
+                return lo;
+            };
+            auto chunk_tokens = [&](int q, int s, int (&tk)[8]) {
+                const int c = sm.cand_pre_win[s];
                 const int L = sm.cand_len[c];
-                int m = 0;
-                if (L <= 256 && !(c >= ws0 && c < ws1)) {
+                const int i0 = (q - sm.win_pre[s]) << 8;
+                if (c >= ws0 && c < ws1) {
+                    const uint32_t* src = stage + (sm.cand_pre[c] - sm.cand_pre[ws0]);
+#pragma unroll
+                    for (int b = 0; b < 8; ++b) {
+                        const int i = i0 + 32 * b + lane;
+                        tk[b] = i < L ? (int)(src[i] & ~kFlipFlag) : -1;
+                    }
+                } else {
                     const int* src = uid + sm.cand_start[c];
 #pragma unroll
                     for (int b = 0; b < 8; ++b) {
-                        const int i = 32 * b + lane;
+                        const int i = i0 + 32 * b + lane;
                         tk[b] = i < L ? __ldg(src + i) : -1;
                     }
-#pragma unroll
-                    for (int b = 0; b < 8; ++b)
-                        m += ((unsigned)tk[b] < (unsigned)H && !test_bit(bm, tk[b])) ? 1 : 0;
-                } else {
-                    warp_tokens(c, [&](int t) { m += ((unsigned)t < (unsigned)H && !test_bit(bm, t)) ? 1 : 0; });
                 }
-                m = warp_sum(m);
-                if (lane == 0) sm.newc[c] = m;
+            };
+            const bool keep = nchunks <= nw;
+            int tk[8];
+            int my_slot = -1;
+            for (int q = warp; q < nchunks; q += nw) {
+                const int s = chunk_slot(q);
+                chunk_tokens(q, s, tk);
+                int m = 0;
+#pragma unroll
+                for (int b = 0; b < 8; ++b) m += ((unsigned)tk[b] < (unsigned)H && !test_bit(bm, tk[b])) ? 1 : 0;
+                m = (int)__reduce_add_sync(0xffffffffu, (unsigned)m);
+                if (lane == 0 && m) atomicAdd(&sm.newc[sm.cand_pre_win[s]], m);
+                my_slot = s;
             }
             if (tid == 0) sm.flip3[0] = 0;
             __syncthreads();
@@ -590,39 +626,36 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
                     feat[nf + __popc(mem & ((1u << lane) - 1u))] = sm.cand_bucket[c];
                     sm.dead[c] = 2;
                 }
+                // Members with tokens to add.
+                const unsigned add = __ballot_sync(0xffffffffu, ((mem >> lane) & 1u) && v > 0);
                 if (lane == 0) {
                     sm.flags[0] = (int)mem;
+                    sm.flags[3] = (int)add;
                     sm.flags[2] = stop_lane >= 0 ? sm.cand_pre_win[stop_lane] : sm.cand_pre_win[nwin - 1] + 1;
                 }
             }
             __syncthreads();
             const unsigned mem = (unsigned)sm.flags[0];
+            const unsigned add = (unsigned)sm.flags[3];
             nf += __popc(mem);
             cpos = sm.flags[2];
-            // Members of at most 256 entries that are not staged are ORed by
-            // the warp holding them; longer ones by the whole block.
             int flips = 0;
-            auto flip = [&](int t) {
-                if ((unsigned)t < (unsigned)H) {
-                    const uint32_t bit = 1u << (t & 31);
-                    flips += (atomicOr(&bm[t >> 5], bit) & bit) ? 0 : 1;
-                }
-            };
-            auto held = [&](int c) { return sm.cand_len[c] <= 256 && !(c >= ws0 && c < ws1); };
-            if (warp < nwin && ((mem >> warp) & 1u)) {
-                const int c = sm.cand_pre_win[warp];
-                if (held(c) && sm.newc[c] > 0) {
+            if (add) {
+                for (int q = warp; q < nchunks; q += nw) {
+                    const int s = keep ? my_slot : chunk_slot(q);
+                    if (!((add >> s) & 1u)) continue;
+                    if (!keep) chunk_tokens(q, s, tk);
 #pragma unroll
-                    for (int b = 0; b < 8; ++b) flip(tk[b]);
+                    for (int b = 0; b < 8; ++b) {
+                        const int t = tk[b];
+                        if ((unsigned)t < (unsigned)H) {
+                            const uint32_t bit = 1u << (t & 31);
+                            flips += (atomicOr(&bm[t >> 5], bit) & bit) ? 0 : 1;
+                        }
+                    }
                 }
             }
-            for (unsigned rest = mem; rest; rest &= rest - 1) {
-                const int c = sm.cand_pre_win[__ffs(rest) - 1];
-                if (held(c) || sm.newc[c] == 0) continue;
-                const int L = sm.cand_len[c];
-                for (int i = tid; i < L; i += nt) flip(token(c, i));
-            }
-            flips = warp_sum(flips);
+            flips = (int)__reduce_add_sync(0xffffffffu, (unsigned)flips);
             if (lane == 0 && flips) atomicAdd(&sm.flip3[0], flips);
             __syncthreads();
             count += sm.flip3[0];
