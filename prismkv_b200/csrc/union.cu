@@ -503,13 +503,16 @@ __device__ __forceinline__ void union_unit(const UnionArgs& A, int u, uint32_t* 
                 int flips = 0;
                 const int e_lo = sm.cand_pre[c] - sm.cand_pre[cpos], e_hi = sm.cand_pre[cend] - sm.cand_pre[cpos];
                 for (int e = e_lo + tid; e < e_hi; e += nt) {
+                    // Entries of buckets passed over, or of members with
+                    // nothing to add, are skipped before their token is read.
+                    const int oc0 = sm.newc[own[e]];
+                    if (oc0 == 0 || (long long)oc0 > rem) continue;
                     const uint32_t t = tail[e] & ~kFlipFlag;
                     if (t >= (uint32_t)H) continue;
                     const uint32_t bit = 1u << (t & 31);
                     // A bit still off was off when the counts were taken, so
-                    // the entry is chained and own[e] names its bucket.
+                    // the entry is chained.
                     if (bm[t >> 5] & bit) continue;
-                    if ((long long)sm.newc[own[e]] > rem) continue;
                     if (atomicOr(&bm[t >> 5], bit) & bit) continue;
                     ++flips;
                     for (int ce = heads[slot(t)]; ce >= 0; ce = nxt[ce]) {
